@@ -1,0 +1,147 @@
+/*
+ * ps_attn.h -- C ABI of the B200 paged split-KV ("PS") attention library.
+ *
+ * libps_attn.so replaces the two GPU calls that vLLM's FlashAttention backend
+ * makes per decoder layer (vllm/v1/attention/backends/flash_attn.py):
+ *
+ *   do_kv_cache_update -> reshape_and_cache_flash      (flash_attn.py:874-883)
+ *   forward            -> flash_attn_varlen_func(...)   (flash_attn.py:796-817)
+ *
+ * Conventions shared by every entry point:
+ *   - plain device pointers, element strides (not bytes) and sizes; no
+ *     framework types cross this boundary;
+ *   - work is enqueued on `stream` (a cudaStream_t; NULL = legacy default);
+ *     nothing synchronises the host, nothing allocates device memory;
+ *   - the return value is a ps_status; on failure ps_last_error() returns a
+ *     message for the calling thread;
+ *   - device-side range checks never trap: they set bits in a caller-owned
+ *     int32 status word (PS_DEV_*) and skip the offending access.
+ */
+#ifndef PS_ATTN_H_
+#define PS_ATTN_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PS_ATTN_ABI_VERSION 1
+
+/* host-side return codes */
+typedef enum {
+  PS_OK = 0,
+  PS_ERR_INVALID_ARGUMENT = 1, /* shape, stride, alignment or pointer error */
+  PS_ERR_UNSUPPORTED = 2,      /* valid request this build does not handle */
+  PS_ERR_WORKSPACE = 3,        /* workspace missing or too small */
+  PS_ERR_CUDA = 4              /* a CUDA runtime/driver call failed */
+} ps_status;
+
+/* bits of the device status word */
+#define PS_DEV_SLOT_OUT_OF_RANGE 0x1  /* kv_append: slot >= num_blocks*block_size */
+#define PS_DEV_BLOCK_OUT_OF_RANGE 0x2 /* attention: block_table entry outside the pool */
+#define PS_DEV_WAIT_TIMEOUT 0x4       /* a bounded device wait gave up */
+#define PS_DEV_BAD_METADATA 0x8       /* seq_lens / query_start_loc inconsistent */
+
+/* element types */
+typedef enum { PS_DTYPE_FP16 = 0, PS_DTYPE_BF16 = 1, PS_DTYPE_FP32 = 2 } ps_dtype;
+
+int ps_abi_version(void);
+const char* ps_last_error(void);
+
+/*
+ * KV append.  Replaces torch.ops._C_cache_ops.reshape_and_cache_flash
+ * (vllm/_custom_ops.py:2591-2610; semantics of its readable twin
+ * vllm/v1/attention/ops/triton_reshape_and_cache_flash.py:44-87, NHD layout):
+ *
+ *   for t < num_tokens with s = slot_mapping[t] >= 0:
+ *     key_cache  [s / block_size, s % block_size, h, :] = key  [t, h, :]
+ *     value_cache[s / block_size, s % block_size, h, :] = value[t, h, :]
+ *
+ * An exact byte copy for any element size (2 or 4 bytes).  key/value may hold
+ * more than num_tokens rows (vLLM pads them); slot_mapping's length rules.
+ * The last dimension of every tensor is contiguous.  status (nullable) gets
+ * PS_DEV_SLOT_OUT_OF_RANGE for slots beyond the pool; those rows are skipped.
+ */
+int ps_kv_append(const void* key, int64_t key_stride_token, int64_t key_stride_head,
+                 const void* value, int64_t value_stride_token, int64_t value_stride_head,
+                 void* key_cache, void* value_cache, int64_t cache_stride_block,
+                 int64_t cache_stride_slot, int64_t cache_stride_head, int64_t num_blocks,
+                 const int64_t* slot_mapping, int64_t num_tokens, int num_kv_heads,
+                 int head_size, int block_size, int elem_bytes, int32_t* status, void* stream);
+
+/*
+ * A batch of paged attention problems: the argument set of
+ * flash_attn_varlen_func's paged branch (vllm/vllm_flash_attn/
+ * flash_attn_interface.py:176-394) as the FlashAttention backend calls it.
+ * Sequence b owns query rows [query_start_loc[b], query_start_loc[b+1]) and
+ * the first seq_lens[b] tokens of its pages; page p of sequence b is cache
+ * block block_table[b * block_table_stride + p].  Attention is causal with
+ * bottom-right alignment (query row i of a q_len-row sequence sees keys
+ * j <= seq_len - q_len + i), which for decode (q_len = 1) is all seq_len keys.
+ */
+typedef struct {
+  /* query [num_tokens, num_q_heads, head_size] */
+  const void* q;
+  int64_t q_stride_token, q_stride_head;
+  /* paged cache: key_cache/value_cache [num_blocks, block_size, num_kv_heads,
+     head_size] (the two halves of vLLM's [2, num_blocks, ...] tensor) */
+  const void* key_cache;
+  const void* value_cache;
+  int64_t cache_stride_block, cache_stride_slot, cache_stride_head;
+  int64_t num_blocks;
+  /* metadata (device) */
+  const int32_t* block_table;     /* [num_seqs, max_blocks_per_seq] */
+  int64_t block_table_stride;
+  int32_t max_blocks_per_seq;
+  const int32_t* seq_lens;        /* [num_seqs], includes the new tokens */
+  const int32_t* query_start_loc; /* [num_seqs + 1]; NULL = one query row per sequence */
+  int32_t num_seqs;
+  /* output [num_tokens, num_q_heads, head_size], same dtype as q */
+  void* out;
+  int64_t out_stride_token, out_stride_head;
+  /* natural-log LSE, fp32, nullable: lse[h * lse_stride_head + t * lse_stride_token] */
+  float* lse;
+  int64_t lse_stride_head, lse_stride_token;
+  /* shape */
+  int32_t num_q_heads, num_kv_heads, head_size, block_size;
+  int32_t dtype; /* ps_dtype of q, cache and out */
+  float softmax_scale;
+} ps_paged_problem;
+
+/*
+ * Bytes of workspace ps_paged_decode needs for up to num_seqs sequences on
+ * the current device.  The size does not depend on sequence lengths, so one
+ * buffer sized for max_num_seqs serves every step and every CUDA-graph
+ * replay.  The buffer must be zeroed once before first use (the kernel keeps
+ * its counters at zero between calls); its first int32 is the status word.
+ */
+int64_t ps_paged_decode_workspace_size(int32_t num_seqs, int32_t num_q_heads,
+                                       int32_t num_kv_heads, int32_t head_size);
+
+/*
+ * Paged decode: one query row per sequence (q_len 1; a sequence with q_len 0
+ * is skipped).  Replaces flash_attn_varlen_func(..., block_table=...,
+ * seqused_k=seq_lens, fa_version=4) for max_seqlen_q == 1
+ * (flash_attn.py:796-817 -> vllm/vllm_flash_attn/cute/interface.py:289-1063)
+ * and the split combine FA4 launches after it (cute/interface.py:1052-1060,
+ * cute/flash_fwd_combine.py:21-698), which here is fused: the last split of a
+ * (sequence, kv head) to finish merges all splits.
+ */
+int ps_paged_decode(const ps_paged_problem* problem, void* workspace, int64_t workspace_bytes,
+                    void* stream);
+
+/*
+ * Chunked prefill: any q_len >= 1 per sequence, causal bottom-right, over the
+ * same paged cache.  Replaces flash_attn_varlen_func for max_seqlen_q > 1
+ * (flash_attn.py:796-817 -> cute/flash_fwd_sm100.py).  Tensor-core path:
+ * tcgen05 MMA with TMEM accumulators.  No workspace.
+ */
+int ps_chunked_prefill(const ps_paged_problem* problem, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PS_ATTN_H_ */

@@ -1,0 +1,226 @@
+"""CPU oracle for the paged split-KV ("PS") attention path.
+
+TEST INFRASTRUCTURE ONLY.  Nothing in the product imports this module; only
+``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline leg use
+it, and only as the checker.  It is a numpy restatement of the reference
+semantics of vLLM 0.22's FlashAttention backend on sm_100 (the path prime-rl's
+inference server runs):
+
+* KV append  -- ``vllm/v1/attention/ops/triton_reshape_and_cache_flash.py:44-87``
+  (NHD branch; the compiled ``reshape_and_cache_flash`` has the same contract,
+  ``vllm/_custom_ops.py:2591-2610``).
+* page gather through ``block_table`` -- the addressing FA4 uses for paged KV,
+  ``vllm/vllm_flash_attn/cute/paged_kv.py:17-246``.
+* attention  -- ``vllm/vllm_flash_attn/cute/testing.py:326-455`` (``attention_ref``:
+  fp32 upcast, GQA head repeat, bottom-right causal mask, natural-log LSE).
+* split-KV combine ("PS postprocess") --
+  ``vllm/vllm_flash_attn/cute/flash_fwd_combine.py:521-567`` (LSE merge) and
+  ``:633-640`` (weighted sum of partial outputs).
+* split heuristic -- ``vllm/vllm_flash_attn/cute/interface.py:257-265``.
+
+Parity pin: ``tests/golden/`` holds vectors produced by vLLM's own
+``attention_ref`` (loaded by file path) and by vLLM's own Triton append kernel
+run under the Triton CPU interpreter; ``tests/test_oracle.py`` checks this
+module against them.
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+
+LOG2E = math.log2(math.e)
+LN2 = math.log(2.0)
+
+
+# --------------------------------------------------------------------------
+# KV append
+# --------------------------------------------------------------------------
+def kv_append(key, value, key_cache, value_cache, slot_mapping):
+    """Scatter ``key``/``value`` rows into the paged cache in place.
+
+    Follows ``triton_reshape_and_cache_flash.py:44-87`` (NHD layout):
+    ``slot < 0`` is a padding token and is skipped (:46-48);
+    ``block = slot // block_size``, ``offset = slot % block_size`` (:50-51);
+    the whole ``[num_heads, head_size]`` row is copied (:78-87, :112-123).
+    ``slot_mapping.shape[0]`` is the token count; key/value may be longer
+    (``flash_attn.py:869-873``).
+
+    key, value: [T', Hkv, D]; key_cache, value_cache: [NB, bs, Hkv, D].
+    Works on any dtype because it is a byte copy.
+    """
+    slot_mapping = np.asarray(slot_mapping, dtype=np.int64)
+    bs = key_cache.shape[1]
+    for t, slot in enumerate(slot_mapping.tolist()):
+        if slot < 0:
+            continue
+        blk, off = divmod(slot, bs)
+        key_cache[blk, off] = key[t]
+        value_cache[blk, off] = value[t]
+
+
+def gather_pages(cache, block_table_row, seq_len):
+    """Return the first ``seq_len`` token rows of one sequence: [L, Hkv, D].
+
+    Page ``p`` of the sequence lives in cache block ``block_table_row[p]``;
+    token ``i`` is row ``i % bs`` of page ``i // bs`` (``paged_kv.py:17-246``).
+    """
+    bs = cache.shape[1]
+    npages = (seq_len + bs - 1) // bs
+    if npages == 0:
+        return cache[:0, 0]
+    blocks = np.asarray(block_table_row[:npages], dtype=np.int64)
+    rows = cache[blocks].reshape(npages * bs, *cache.shape[2:])
+    return rows[:seq_len]
+
+
+# --------------------------------------------------------------------------
+# attention (attention_ref restated)
+# --------------------------------------------------------------------------
+def attention_ref(q, k, v, causal=True, softmax_scale=None):
+    """Single-sequence attention, fp32, as ``testing.py:326-455``.
+
+    q: [Sq, Hq, D]; k, v: [Sk, Hkv, D].  Returns (out [Sq, Hq, D] fp32,
+    lse [Hq, Sq] fp32, natural log).
+
+    * fp32 upcast (``upcast=True``, :352-354);
+    * K/V heads repeated ``Hq // Hkv`` times, GQA group = consecutive q heads
+      (:369-370);
+    * ``scores = (q * scale) @ k^T`` (:375);
+    * causal mask is bottom-right aligned: query row ``i`` may see key ``j``
+      iff ``j <= i + Sk - Sq`` (``construct_local_mask`` :278-279 with
+      ``window_size = (None, 0)``, :349-350);
+    * ``lse = logsumexp(scores)`` (:428), ``out = softmax(scores) @ v`` (:430, :452);
+    * a fully masked row gives ``out = 0`` (``attention.masked_fill`` at :438)
+      and ``lse = -inf``.
+    """
+    q = np.asarray(q, dtype=np.float32)
+    k = np.asarray(k, dtype=np.float32)
+    v = np.asarray(v, dtype=np.float32)
+    sq, hq, d = q.shape
+    sk, hkv, _ = k.shape
+    g = hq // hkv
+    if softmax_scale is None:
+        softmax_scale = 1.0 / math.sqrt(d)
+    out = np.zeros((sq, hq, d), dtype=np.float32)
+    lse = np.full((hq, sq), -np.inf, dtype=np.float32)
+    if sk == 0 or sq == 0:
+        return out, lse
+    kk = np.repeat(k, g, axis=1)  # [Sk, Hq, D]
+    vv = np.repeat(v, g, axis=1)
+    # [Hq, Sq, Sk]
+    scores = np.einsum("thd,shd->hts", q * np.float32(softmax_scale), kk, dtype=np.float32)
+    if causal:
+        row = np.arange(sq)[:, None]
+        col = np.arange(sk)[None, :]
+        masked = col > row + sk - sq
+        scores = np.where(masked[None], np.float32(-np.inf), scores)
+    mx = scores.max(axis=-1, keepdims=True)
+    mx_safe = np.where(np.isfinite(mx), mx, np.float32(0.0))
+    e = np.exp(scores - mx_safe, dtype=np.float32)
+    ssum = e.sum(axis=-1, keepdims=True, dtype=np.float32)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        lse = (np.log(ssum) + mx_safe)[..., 0].astype(np.float32)
+        p = np.where(ssum > 0, e / ssum, np.float32(0.0)).astype(np.float32)
+    lse = np.where(ssum[..., 0] > 0, lse, np.float32(-np.inf))
+    out = np.einsum("hts,shd->thd", p, vv, dtype=np.float32)
+    return out.astype(np.float32), lse.astype(np.float32)
+
+
+def paged_attention(q, key_cache, value_cache, block_table, seq_lens, query_start_loc,
+                    softmax_scale, causal=True):
+    """Varlen paged attention over a batch, the reference forward path.
+
+    ``FlashAttentionImpl.forward`` (``flash_attn.py:787-817``) passes
+    ``cu_seqlens_q = query_start_loc``, ``seqused_k = seq_lens`` and the
+    block table to ``flash_attn_varlen_func``; sequence ``b`` owns query rows
+    ``[qsl[b], qsl[b+1])`` and its first ``seq_lens[b]`` cached tokens.
+
+    Returns (out [T, Hq, D] fp32, lse [Hq, T] fp32).
+    """
+    q = np.asarray(q, dtype=np.float32)
+    t_total, hq, d = q.shape
+    out = np.zeros((t_total, hq, d), dtype=np.float32)
+    lse = np.full((hq, t_total), -np.inf, dtype=np.float32)
+    qsl = np.asarray(query_start_loc, dtype=np.int64)
+    for b, L in enumerate(np.asarray(seq_lens, dtype=np.int64).tolist()):
+        t0, t1 = int(qsl[b]), int(qsl[b + 1])
+        if t1 <= t0:
+            continue
+        kb = gather_pages(key_cache, block_table[b], L)
+        vb = gather_pages(value_cache, block_table[b], L)
+        o, l = attention_ref(q[t0:t1], kb, vb, causal=causal, softmax_scale=softmax_scale)
+        out[t0:t1] = o
+        lse[:, t0:t1] = l
+    return out, lse
+
+
+# --------------------------------------------------------------------------
+# split-KV partials and the combine ("PS postprocess")
+# --------------------------------------------------------------------------
+def split_partials(q, k, v, splits, softmax_scale):
+    """Per-split normalised partial outputs and LSEs of one decode query.
+
+    q: [Hq, D] (the single decode token), k/v: [L, Hkv, D].  ``splits`` is a
+    list of ``(start, end)`` key ranges.  An empty split has ``lse = -inf``
+    and ``O = 0`` (``softmax.py:147-158`` zero-sum guard).
+    Returns (o [S, Hq, D], lse [S, Hq]).
+    """
+    outs, lses = [], []
+    for s0, s1 in splits:
+        o, l = attention_ref(q[None], k[s0:s1], v[s0:s1], causal=False,
+                             softmax_scale=softmax_scale)
+        outs.append(o[0])
+        lses.append(l[:, 0])
+    return np.stack(outs).astype(np.float32), np.stack(lses).astype(np.float32)
+
+
+def combine(o_partial, lse_partial):
+    """Merge split partials, restating ``flash_fwd_combine.py``.
+
+    o_partial: [S, ...rows, D] fp32 (normalised per split);
+    lse_partial: [S, ...rows] fp32 natural-log LSE.
+
+    * ``lse_max = max_s lse_s``; if every split is ``-inf`` the max used for
+      the exponent is 0 (:541-547);
+    * ``scale_s = exp2(lse_s*log2e - lse_max_cur*log2e)`` (:548-554);
+    * ``lse = log(sum_s scale_s) + lse_max`` -- note: ``lse_max``, so an
+      all-empty row yields ``-inf`` (:558);
+    * ``inv_sum = 0`` when the sum is 0 or NaN, else ``1/sum`` (:560-562);
+    * ``O = sum_s scale_s*inv_sum * O_s`` over splits with positive scale
+      (:633-640).
+    Returns (o [...rows, D], lse [...rows]).
+    """
+    o_partial = np.asarray(o_partial, dtype=np.float32)
+    lse_partial = np.asarray(lse_partial, dtype=np.float32)
+    lse_max = lse_partial.max(axis=0)
+    lse_max_cur = np.where(lse_max == -np.inf, np.float32(0.0), lse_max)
+    with np.errstate(over="ignore", invalid="ignore"):
+        scale = np.exp2(lse_partial * np.float32(LOG2E) - lse_max_cur * np.float32(LOG2E),
+                        dtype=np.float32)
+    ssum = scale.sum(axis=0, dtype=np.float32)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        lse = (np.log(ssum) + lse_max).astype(np.float32)
+        inv = np.where((ssum == 0) | np.isnan(ssum), np.float32(0.0), np.float32(1.0) / ssum)
+    w = scale * inv
+    w = np.where(w > 0, w, np.float32(0.0))
+    o = (w[..., None] * o_partial).sum(axis=0, dtype=np.float32)
+    return o.astype(np.float32), lse
+
+
+def num_splits_heuristic(total_mblocks, num_sms, num_n_blocks, max_splits):
+    """FA4's split count when ``num_splits < 1`` (``interface.py:257-265``)."""
+    if num_n_blocks <= 4:
+        return 1
+    return min(num_sms // total_mblocks, max_splits, num_n_blocks)
+
+
+# --------------------------------------------------------------------------
+# seeded inputs for the benchmark configurations
+# --------------------------------------------------------------------------
+def decode_slots(block_table, seq_lens, block_size):
+    """slot of the newest token of each sequence: ``bt[b, (L-1)//bs]*bs + (L-1)%bs``."""
+    bt = np.asarray(block_table, dtype=np.int64)
+    L = np.asarray(seq_lens, dtype=np.int64)
+    pos = L - 1
+    return bt[np.arange(len(L)), pos // block_size] * block_size + pos % block_size

@@ -1,0 +1,90 @@
+// KV append: scatter the new tokens' key/value rows into the paged cache.
+//
+// Semantics of vLLM's reshape_and_cache_flash (NHD layout), as spelled out by
+// its Triton twin vllm/v1/attention/ops/triton_reshape_and_cache_flash.py:
+//   slot < 0 -> padding token, skipped                      (:46-48)
+//   block = slot / block_size, offset = slot % block_size   (:50-51)
+//   cache[block, offset, h, :] = src[t, h, :] for all heads (:78-87, :112-123)
+//
+// B200 layout: a CTA handles one token per iteration (grid-stride over
+// tokens); its threads walk the token's 2 * num_heads head rows in VEC-byte
+// vectors, head_size bytes contiguous per head row, so each warp moves whole
+// 512-byte runs (16-byte vectors) on both the load and the store side.  The
+// payload is never touched by arithmetic: the copy is bit-exact.
+#include "ps_common.cuh"
+#include "ps_launch.h"
+
+namespace ps {
+
+template <int VEC>
+struct VecT;
+template <>
+struct VecT<16> {
+  using T = uint4;
+};
+template <>
+struct VecT<8> {
+  using T = uint2;
+};
+template <>
+struct VecT<4> {
+  using T = uint32_t;
+};
+template <>
+struct VecT<2> {
+  using T = uint16_t;
+};
+
+template <int VEC>
+__global__ void __launch_bounds__(256) kv_append_kernel(AppendArgs a) {
+  using V = typename VecT<VEC>::T;
+  const int per_tensor = a.num_heads * a.vecs_per_head;
+  const int per_token = 2 * per_tensor;
+  for (int64_t t = blockIdx.x; t < a.num_tokens; t += gridDim.x) {
+    const int64_t slot = __ldg(a.slot_mapping + t);
+    if (slot < 0) continue;  // padding token
+    if (slot >= a.num_slots) {
+      if (threadIdx.x == 0) set_status(a.status, PS_DEV_SLOT_OUT_OF_RANGE);
+      continue;
+    }
+    const int64_t blk = slot / a.block_size;
+    const int64_t off = slot - blk * a.block_size;
+    const int64_t dst_tok = blk * a.c_sblock + off * a.c_sslot;
+    for (int j = threadIdx.x; j < per_token; j += blockDim.x) {
+      const bool is_v = j >= per_tensor;
+      const int r = is_v ? j - per_tensor : j;
+      const int h = r / a.vecs_per_head;
+      const int c = r - h * a.vecs_per_head;
+      const char* src = is_v ? a.value + t * a.val_st + h * a.val_sh
+                             : a.key + t * a.key_st + h * a.key_sh;
+      char* dst = (is_v ? a.value_cache : a.key_cache) + dst_tok + h * a.c_shead;
+      const V v = __ldg(reinterpret_cast<const V*>(src) + c);
+      reinterpret_cast<V*>(dst)[c] = v;
+    }
+  }
+}
+
+}  // namespace ps
+
+int ps_launch_kv_append(const ps::AppendArgs& a, int vec, int sm_count, cudaStream_t stream) {
+  if (a.num_tokens == 0) return 0;
+  const int threads = 256;
+  int64_t blocks = a.num_tokens;
+  const int64_t cap = static_cast<int64_t>(sm_count) * 8;
+  if (blocks > cap) blocks = cap;
+  switch (vec) {
+    case 16:
+      ps::kv_append_kernel<16><<<static_cast<int>(blocks), threads, 0, stream>>>(a);
+      break;
+    case 8:
+      ps::kv_append_kernel<8><<<static_cast<int>(blocks), threads, 0, stream>>>(a);
+      break;
+    case 4:
+      ps::kv_append_kernel<4><<<static_cast<int>(blocks), threads, 0, stream>>>(a);
+      break;
+    default:
+      ps::kv_append_kernel<2><<<static_cast<int>(blocks), threads, 0, stream>>>(a);
+      break;
+  }
+  return static_cast<int>(cudaGetLastError());
+}

@@ -1,0 +1,288 @@
+// C ABI of libps_attn.so: argument validation, TMA descriptor encoding and
+// kernel launches.  Declarations and contracts live in include/ps_attn.h.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "ps_common.cuh"
+#include "ps_launch.h"
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(PS_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+// SM count of the current device, cached per device ordinal.
+int sm_count_current(int* out_dev) {
+  static std::mutex mu;
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+  if (out_dev) *out_dev = dev;
+  std::lock_guard<std::mutex> lk(mu);
+  if (dev < 64 && cache[dev] > 0) return cache[dev];
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return -1;
+  if (dev < 64) cache[dev] = n;
+  return n;
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+// Tensor map over one cache half viewed as [num_blocks][block_size][Hkv][128]
+// 16-bit elements; box = one 16-token page of one head, 64 dims (128 B) wide,
+// 128-byte swizzle.
+int make_page_map(CUtensorMap* map, const void* base, int64_t num_blocks, int block_size,
+                  int num_kv_heads, int64_t s_block, int64_t s_slot, int64_t s_head) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(PS_ERR_CUDA, "cuTensorMapEncodeTiled unavailable from the driver");
+  cuuint64_t dims[4] = {128, static_cast<cuuint64_t>(num_kv_heads),
+                        static_cast<cuuint64_t>(block_size), static_cast<cuuint64_t>(num_blocks)};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(s_head) * 2, static_cast<cuuint64_t>(s_slot) * 2,
+                           static_cast<cuuint64_t>(s_block) * 2};
+  cuuint32_t box[4] = {64, 1, 16, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 4, const_cast<void*>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(PS_ERR_INVALID_ARGUMENT,
+                "cuTensorMapEncodeTiled failed (%d): cache strides must be multiples of 16 "
+                "bytes and the base 16-byte aligned",
+                static_cast<int>(r));
+  return PS_OK;
+}
+
+bool aligned(const void* p, int bytes) {
+  return (reinterpret_cast<uintptr_t>(p) % static_cast<uintptr_t>(bytes)) == 0;
+}
+
+int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
+
+struct DecodeWorkspaceLayout {
+  int64_t counters_off, part_lse_off, part_o_off, total;
+};
+
+DecodeWorkspaceLayout decode_layout(int num_seqs, int num_q_heads, int num_kv_heads, int sm_count) {
+  const int group = num_q_heads / num_kv_heads;
+  const int kg = group <= 8 ? 8 : 16;
+  const int64_t slots = ps_decode_partial_slots(num_seqs, num_kv_heads, sm_count);
+  DecodeWorkspaceLayout l;
+  l.counters_off = 256;  // [0, 256): status word and reserved
+  l.part_lse_off = round_up(l.counters_off + static_cast<int64_t>(num_seqs) * num_kv_heads * 4, 256);
+  l.part_o_off = round_up(l.part_lse_off + slots * kg * 4, 256);
+  l.total = round_up(l.part_o_off + slots * kg * 128 * 4, 256);
+  return l;
+}
+
+int validate_problem(const ps_paged_problem* pr, bool decode) {
+  if (!pr) return fail(PS_ERR_INVALID_ARGUMENT, "problem is NULL");
+  if (pr->num_seqs < 0) return fail(PS_ERR_INVALID_ARGUMENT, "num_seqs < 0");
+  if (pr->num_seqs == 0) return PS_OK;
+  if (!pr->q || !pr->key_cache || !pr->value_cache || !pr->block_table || !pr->seq_lens ||
+      !pr->out)
+    return fail(PS_ERR_INVALID_ARGUMENT, "a required pointer is NULL");
+  if (!decode && !pr->query_start_loc)
+    return fail(PS_ERR_INVALID_ARGUMENT, "chunked prefill needs query_start_loc");
+  if (pr->dtype != PS_DTYPE_BF16 && pr->dtype != PS_DTYPE_FP16)
+    return fail(PS_ERR_UNSUPPORTED, "attention supports fp16 and bf16 only (dtype %d)", pr->dtype);
+  if (pr->head_size != 128)
+    return fail(PS_ERR_UNSUPPORTED, "head_size %d unsupported (this build: 128)", pr->head_size);
+  if (pr->block_size <= 0 || pr->block_size % 16 != 0 || pr->block_size > 256)
+    return fail(PS_ERR_INVALID_ARGUMENT, "block_size %d must be a multiple of 16 in [16, 256]",
+                pr->block_size);
+  if (pr->num_kv_heads <= 0 || pr->num_q_heads <= 0 || pr->num_q_heads % pr->num_kv_heads != 0)
+    return fail(PS_ERR_INVALID_ARGUMENT, "num_q_heads %d must be a positive multiple of num_kv_heads %d",
+                pr->num_q_heads, pr->num_kv_heads);
+  const int group = pr->num_q_heads / pr->num_kv_heads;
+  if (group > 16)
+    return fail(PS_ERR_UNSUPPORTED, "GQA group %d > 16 unsupported", group);
+  if (pr->num_blocks <= 0 || pr->num_blocks > INT32_MAX)
+    return fail(PS_ERR_INVALID_ARGUMENT, "num_blocks out of range");
+  if (pr->max_blocks_per_seq < 0 || pr->block_table_stride < pr->max_blocks_per_seq)
+    return fail(PS_ERR_INVALID_ARGUMENT, "block_table_stride < max_blocks_per_seq");
+  // 16-byte rows for TMA / vector access
+  if (!aligned(pr->key_cache, 16) || !aligned(pr->value_cache, 16) ||
+      pr->cache_stride_head % 8 || pr->cache_stride_slot % 8 || pr->cache_stride_block % 8)
+    return fail(PS_ERR_INVALID_ARGUMENT, "cache base/strides must be 16-byte aligned");
+  if (!aligned(pr->q, 16) || pr->q_stride_head % 8 || pr->q_stride_token % 8)
+    return fail(PS_ERR_INVALID_ARGUMENT, "q base/strides must be 16-byte aligned");
+  if (!aligned(pr->out, 16) || pr->out_stride_head % 8 || pr->out_stride_token % 8)
+    return fail(PS_ERR_INVALID_ARGUMENT, "out base/strides must be 16-byte aligned");
+  if (!(pr->softmax_scale > 0.f))
+    return fail(PS_ERR_INVALID_ARGUMENT, "softmax_scale must be positive");
+  return PS_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int ps_abi_version(void) { return PS_ATTN_ABI_VERSION; }
+
+const char* ps_last_error(void) { return g_err; }
+
+int ps_kv_append(const void* key, int64_t key_stride_token, int64_t key_stride_head,
+                 const void* value, int64_t value_stride_token, int64_t value_stride_head,
+                 void* key_cache, void* value_cache, int64_t cache_stride_block,
+                 int64_t cache_stride_slot, int64_t cache_stride_head, int64_t num_blocks,
+                 const int64_t* slot_mapping, int64_t num_tokens, int num_kv_heads, int head_size,
+                 int block_size, int elem_bytes, int32_t* status, void* stream) {
+  if (num_tokens < 0) return fail(PS_ERR_INVALID_ARGUMENT, "num_tokens < 0");
+  if (num_tokens == 0) return PS_OK;
+  if (!key || !value || !key_cache || !value_cache || !slot_mapping)
+    return fail(PS_ERR_INVALID_ARGUMENT, "a required pointer is NULL");
+  if (elem_bytes != 2 && elem_bytes != 4 && elem_bytes != 1)
+    return fail(PS_ERR_UNSUPPORTED, "elem_bytes %d unsupported", elem_bytes);
+  if (num_kv_heads <= 0 || head_size <= 0 || block_size <= 0 || num_blocks <= 0)
+    return fail(PS_ERR_INVALID_ARGUMENT, "non-positive shape");
+  const int64_t row = static_cast<int64_t>(head_size) * elem_bytes;
+  // widest vector every address and stride admits
+  int vec = 16;
+  auto ok = [&](int v) {
+    if (row % v) return false;
+    const void* ps[4] = {key, value, key_cache, value_cache};
+    for (const void* p : ps)
+      if (!aligned(p, v)) return false;
+    const int64_t st[7] = {key_stride_token, key_stride_head, value_stride_token, value_stride_head,
+                           cache_stride_block, cache_stride_slot, cache_stride_head};
+    for (int64_t s : st)
+      if ((s * elem_bytes) % v) return false;
+    return true;
+  };
+  while (vec > 1 && !ok(vec)) vec >>= 1;
+  if (vec < 2) return fail(PS_ERR_INVALID_ARGUMENT, "rows are not 2-byte aligned");
+  int dev = 0;
+  const int sms = sm_count_current(&dev);
+  if (sms <= 0) return fail(PS_ERR_CUDA, "no CUDA device");
+  ps::AppendArgs a;
+  a.key = static_cast<const char*>(key);
+  a.value = static_cast<const char*>(value);
+  a.key_cache = static_cast<char*>(key_cache);
+  a.value_cache = static_cast<char*>(value_cache);
+  a.slot_mapping = slot_mapping;
+  a.key_st = key_stride_token * elem_bytes;
+  a.key_sh = key_stride_head * elem_bytes;
+  a.val_st = value_stride_token * elem_bytes;
+  a.val_sh = value_stride_head * elem_bytes;
+  a.c_sblock = cache_stride_block * elem_bytes;
+  a.c_sslot = cache_stride_slot * elem_bytes;
+  a.c_shead = cache_stride_head * elem_bytes;
+  a.num_slots = num_blocks * block_size;
+  a.num_tokens = num_tokens;
+  a.num_heads = num_kv_heads;
+  a.block_size = block_size;
+  a.vecs_per_head = static_cast<int32_t>(row / vec);
+  a.status = status;
+  const int e = ps_launch_kv_append(a, vec, sms, static_cast<cudaStream_t>(stream));
+  if (e != 0) return cuda_fail(static_cast<cudaError_t>(e), "kv_append launch");
+  return PS_OK;
+}
+
+int64_t ps_paged_decode_workspace_size(int32_t num_seqs, int32_t num_q_heads,
+                                       int32_t num_kv_heads, int32_t head_size) {
+  if (num_seqs < 0 || num_kv_heads <= 0 || num_q_heads <= 0 || head_size != 128) {
+    fail(PS_ERR_INVALID_ARGUMENT, "workspace size: bad shape");
+    return -1;
+  }
+  const int sms = sm_count_current(nullptr);
+  if (sms <= 0) {
+    fail(PS_ERR_CUDA, "no CUDA device");
+    return -1;
+  }
+  return decode_layout(num_seqs, num_q_heads, num_kv_heads, sms).total;
+}
+
+int ps_paged_decode(const ps_paged_problem* pr, void* workspace, int64_t workspace_bytes,
+                    void* stream) {
+  int rc = validate_problem(pr, true);
+  if (rc != PS_OK) return rc;
+  if (pr->num_seqs == 0) return PS_OK;
+  if (pr->num_seqs > ps::kDecodeMaxSeqs)
+    return fail(PS_ERR_UNSUPPORTED, "num_seqs %d > %d per decode launch", pr->num_seqs,
+                ps::kDecodeMaxSeqs);
+  int dev = 0;
+  const int sms = sm_count_current(&dev);
+  if (sms <= 0) return fail(PS_ERR_CUDA, "no CUDA device");
+  const DecodeWorkspaceLayout lay = decode_layout(pr->num_seqs, pr->num_q_heads, pr->num_kv_heads, sms);
+  if (!workspace || workspace_bytes < lay.total || !aligned(workspace, 256))
+    return fail(PS_ERR_WORKSPACE, "decode workspace must be >= %lld bytes, 256-byte aligned",
+                static_cast<long long>(lay.total));
+  CUtensorMap kmap, vmap;
+  rc = make_page_map(&kmap, pr->key_cache, pr->num_blocks, pr->block_size, pr->num_kv_heads,
+                     pr->cache_stride_block, pr->cache_stride_slot, pr->cache_stride_head);
+  if (rc != PS_OK) return rc;
+  rc = make_page_map(&vmap, pr->value_cache, pr->num_blocks, pr->block_size, pr->num_kv_heads,
+                     pr->cache_stride_block, pr->cache_stride_slot, pr->cache_stride_head);
+  if (rc != PS_OK) return rc;
+  char* ws = static_cast<char*>(workspace);
+  ps::DecodeParams p;
+  p.q = pr->q;
+  p.q_st = pr->q_stride_token;
+  p.q_sh = pr->q_stride_head;
+  p.block_table = pr->block_table;
+  p.bt_stride = pr->block_table_stride;
+  p.max_blocks_per_seq = pr->max_blocks_per_seq;
+  p.seq_lens = pr->seq_lens;
+  p.qsl = pr->query_start_loc;
+  p.num_seqs = pr->num_seqs;
+  p.out = pr->out;
+  p.o_st = pr->out_stride_token;
+  p.o_sh = pr->out_stride_head;
+  p.lse = pr->lse;
+  p.lse_sh = pr->lse_stride_head;
+  p.lse_st = pr->lse_stride_token;
+  p.num_q_heads = pr->num_q_heads;
+  p.num_kv_heads = pr->num_kv_heads;
+  p.group = pr->num_q_heads / pr->num_kv_heads;
+  p.block_size = pr->block_size;
+  p.num_blocks = pr->num_blocks;
+  p.scale_log2 = pr->softmax_scale * 1.4426950408889634f;
+  p.status = reinterpret_cast<int32_t*>(ws);
+  p.counters = reinterpret_cast<int32_t*>(ws + lay.counters_off);
+  p.part_lse = reinterpret_cast<float*>(ws + lay.part_lse_off);
+  p.part_o = reinterpret_cast<float*>(ws + lay.part_o_off);
+  p.num_part_slots = ps_decode_partial_slots(pr->num_seqs, pr->num_kv_heads, sms);
+  const int e = ps_launch_paged_decode(p, kmap, vmap, pr->dtype == PS_DTYPE_BF16, sms,
+                                       static_cast<cudaStream_t>(stream));
+  if (e != 0) return cuda_fail(static_cast<cudaError_t>(e), "paged_decode launch");
+  return PS_OK;
+}
+
+int ps_chunked_prefill(const ps_paged_problem* pr, void* stream) {
+  (void)stream;
+  const int rc = validate_problem(pr, false);
+  if (rc != PS_OK) return rc;
+  return fail(PS_ERR_UNSUPPORTED, "chunked prefill not built yet");
+}
+
+}  // extern "C"

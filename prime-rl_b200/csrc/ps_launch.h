@@ -1,0 +1,68 @@
+// Internal launch interfaces between the C-ABI layer (ps_attn_api.cu) and the
+// kernel translation units.  Not part of the public ABI.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace ps {
+
+struct AppendArgs {
+  const char* key;
+  const char* value;
+  char* key_cache;
+  char* value_cache;
+  const int64_t* slot_mapping;
+  int64_t key_st, key_sh, val_st, val_sh;  // bytes
+  int64_t c_sblock, c_sslot, c_shead;      // bytes
+  int64_t num_slots;                       // num_blocks * block_size
+  int64_t num_tokens;
+  int32_t num_heads;
+  int32_t block_size;
+  int32_t vecs_per_head;  // head_size * elem_bytes / VEC
+  int32_t* status;
+};
+
+// Paged decode launch parameters (device-visible copy of ps_paged_problem plus
+// derived values).  Strides are in elements.
+struct DecodeParams {
+  const void* q;
+  int64_t q_st, q_sh;
+  const int32_t* block_table;
+  int64_t bt_stride;
+  int32_t max_blocks_per_seq;
+  const int32_t* seq_lens;
+  const int32_t* qsl;
+  int32_t num_seqs;
+  void* out;
+  int64_t o_st, o_sh;
+  float* lse;
+  int64_t lse_sh, lse_st;
+  int32_t num_q_heads, num_kv_heads, group;  // group = q heads per kv head
+  int32_t block_size;                        // tokens per cache block (multiple of 16)
+  int64_t num_blocks;
+  float scale_log2;                          // softmax_scale * log2(e)
+  // workspace
+  int32_t* status;
+  int32_t* counters;     // [num_seqs * num_kv_heads]
+  float* part_o;         // [slots, group, 128]
+  float* part_lse;       // [slots, group]
+  int64_t num_part_slots;
+};
+
+// Static sizing of the decode kernel, shared by the workspace-size query.
+constexpr int kDecodeWarps = 8;      // warps per CTA
+constexpr int kDecodeStages = 3;     // pages in flight per warp
+constexpr int kDecodeMaxSeqs = 4096; // sequences per launch (prefix table in smem)
+
+}  // namespace ps
+
+int ps_launch_kv_append(const ps::AppendArgs& a, int vec, int sm_count, cudaStream_t stream);
+
+// Returns a cudaError_t value.
+int ps_launch_paged_decode(const ps::DecodeParams& p, const CUtensorMap& kmap,
+                           const CUtensorMap& vmap, int dtype_bf16, int sm_count,
+                           cudaStream_t stream);
+
+int64_t ps_decode_partial_slots(int num_seqs, int num_kv_heads, int sm_count);

@@ -1,0 +1,145 @@
+"""ctypes binding of libps_attn.so (declarations: include/ps_attn.h).
+
+There is no fallback: if the library is missing or fails to load, every op
+raises.  ``load()`` builds the library first when its sources are newer.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from pathlib import Path
+
+_LIB = None
+_LOCK = threading.Lock()
+
+PS_OK = 0
+PS_ERR_INVALID_ARGUMENT = 1
+PS_ERR_UNSUPPORTED = 2
+PS_ERR_WORKSPACE = 3
+PS_ERR_CUDA = 4
+
+PS_DEV_SLOT_OUT_OF_RANGE = 0x1
+PS_DEV_BLOCK_OUT_OF_RANGE = 0x2
+PS_DEV_WAIT_TIMEOUT = 0x4
+PS_DEV_BAD_METADATA = 0x8
+
+PS_DTYPE_FP16 = 0
+PS_DTYPE_BF16 = 1
+PS_DTYPE_FP32 = 2
+
+ABI_VERSION = 1
+
+# every symbol include/ps_attn.h declares
+EXPORTED_SYMBOLS = (
+    "ps_abi_version",
+    "ps_last_error",
+    "ps_kv_append",
+    "ps_paged_decode_workspace_size",
+    "ps_paged_decode",
+    "ps_chunked_prefill",
+)
+
+
+class PSError(RuntimeError):
+    """A libps_attn call returned a non-zero ps_status."""
+
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"ps_attn error {code}: {msg}")
+        self.code = code
+
+
+class PagedProblem(ctypes.Structure):
+    """Mirror of ``ps_paged_problem`` in include/ps_attn.h (same field order)."""
+
+    _fields_ = [
+        ("q", ctypes.c_void_p),
+        ("q_stride_token", ctypes.c_int64),
+        ("q_stride_head", ctypes.c_int64),
+        ("key_cache", ctypes.c_void_p),
+        ("value_cache", ctypes.c_void_p),
+        ("cache_stride_block", ctypes.c_int64),
+        ("cache_stride_slot", ctypes.c_int64),
+        ("cache_stride_head", ctypes.c_int64),
+        ("num_blocks", ctypes.c_int64),
+        ("block_table", ctypes.c_void_p),
+        ("block_table_stride", ctypes.c_int64),
+        ("max_blocks_per_seq", ctypes.c_int32),
+        ("seq_lens", ctypes.c_void_p),
+        ("query_start_loc", ctypes.c_void_p),
+        ("num_seqs", ctypes.c_int32),
+        ("out", ctypes.c_void_p),
+        ("out_stride_token", ctypes.c_int64),
+        ("out_stride_head", ctypes.c_int64),
+        ("lse", ctypes.c_void_p),
+        ("lse_stride_head", ctypes.c_int64),
+        ("lse_stride_token", ctypes.c_int64),
+        ("num_q_heads", ctypes.c_int32),
+        ("num_kv_heads", ctypes.c_int32),
+        ("head_size", ctypes.c_int32),
+        ("block_size", ctypes.c_int32),
+        ("dtype", ctypes.c_int32),
+        ("softmax_scale", ctypes.c_float),
+    ]
+
+
+def lib_path() -> Path:
+    return Path(__file__).resolve().parent / "libps_attn.so"
+
+
+def _declare(lib):
+    c = ctypes
+    lib.ps_abi_version.restype = c.c_int
+    lib.ps_abi_version.argtypes = []
+    lib.ps_last_error.restype = c.c_char_p
+    lib.ps_last_error.argtypes = []
+    lib.ps_kv_append.restype = c.c_int
+    lib.ps_kv_append.argtypes = [
+        c.c_void_p, c.c_int64, c.c_int64,  # key
+        c.c_void_p, c.c_int64, c.c_int64,  # value
+        c.c_void_p, c.c_void_p, c.c_int64, c.c_int64, c.c_int64, c.c_int64,  # caches
+        c.c_void_p, c.c_int64, c.c_int, c.c_int, c.c_int, c.c_int,  # slots, shape
+        c.c_void_p, c.c_void_p,  # status, stream
+    ]
+    lib.ps_paged_decode_workspace_size.restype = c.c_int64
+    lib.ps_paged_decode_workspace_size.argtypes = [c.c_int32] * 4
+    lib.ps_paged_decode.restype = c.c_int
+    lib.ps_paged_decode.argtypes = [c.POINTER(PagedProblem), c.c_void_p, c.c_int64, c.c_void_p]
+    lib.ps_chunked_prefill.restype = c.c_int
+    lib.ps_chunked_prefill.argtypes = [c.POINTER(PagedProblem), c.c_void_p]
+
+
+def load(build_if_stale: bool = True):
+    """Load (and, if its sources changed, rebuild) libps_attn.so."""
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    with _LOCK:
+        if _LIB is not None:
+            return _LIB
+        path = lib_path()
+        if build_if_stale and os.environ.get("PS_ATTN_NO_BUILD", "0") != "1":
+            from . import _build
+
+            if _build.needs_build():
+                try:
+                    _build.build()
+                except RuntimeError:
+                    if not path.exists():
+                        raise
+        if not path.exists():
+            raise RuntimeError(
+                f"libps_attn.so not found at {path}; build it with "
+                "`python -m ps_attn._build` (needs nvcc)")
+        lib = ctypes.CDLL(str(path))
+        _declare(lib)
+        if lib.ps_abi_version() != ABI_VERSION:
+            raise RuntimeError(f"libps_attn ABI {lib.ps_abi_version()} != {ABI_VERSION}")
+        _LIB = lib
+        return lib
+
+
+def check(rc: int):
+    if rc != PS_OK:
+        msg = _LIB.ps_last_error().decode(errors="replace") if _LIB is not None else ""
+        raise PSError(rc, msg)

@@ -1,0 +1,220 @@
+"""Torch-facing ops over libps_attn.so.
+
+These functions mirror the two GPU calls vLLM's FlashAttention backend makes
+per decoder layer and keep their argument meaning:
+
+* :func:`kv_append` -- ``reshape_and_cache_flash(key, value, key_cache,
+  value_cache, slot_mapping, ...)`` (``vllm/_custom_ops.py:2591-2610``);
+* :func:`paged_attention` -- ``flash_attn_varlen_func(q, k_cache, v_cache, out,
+  cu_seqlens_q, max_seqlen_q, seqused_k, max_seqlen_k, softmax_scale,
+  causal=True, block_table=...)`` as called at
+  ``vllm/v1/attention/backends/flash_attn.py:796-817``.  It dispatches to
+  :func:`paged_decode` (``max_seqlen_q == 1``) or :func:`chunked_prefill`.
+
+Tensors stay on the device; the work is enqueued on the current CUDA stream;
+nothing here synchronises or allocates except :class:`DecodeWorkspace`
+construction.  All validation failures raise :class:`ps_attn._lib.PSError` or
+``ValueError``; there is no non-CUDA path.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+
+_DTYPES = {
+    torch.float16: _lib.PS_DTYPE_FP16,
+    torch.bfloat16: _lib.PS_DTYPE_BF16,
+    torch.float32: _lib.PS_DTYPE_FP32,
+}
+
+
+def _stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _require_cuda(*tensors):
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise ValueError("ps_attn ops take CUDA tensors only (no CPU path)")
+
+
+def kv_append(key: torch.Tensor, value: torch.Tensor, key_cache: torch.Tensor,
+              value_cache: torch.Tensor, slot_mapping: torch.Tensor,
+              status: torch.Tensor | None = None) -> None:
+    """Write ``key``/``value`` rows into the paged cache at ``slot_mapping``.
+
+    key, value: [T', Hkv, D] (T' >= len(slot_mapping)); key_cache,
+    value_cache: [num_blocks, block_size, Hkv, D]; slot_mapping: int64 [T].
+    Negative slots are skipped.  Bit-exact copy.
+    """
+    lib = _lib.load()
+    _require_cuda(key, value, key_cache, value_cache, slot_mapping)
+    if slot_mapping.dtype != torch.int64:
+        raise ValueError("slot_mapping must be int64")
+    if key.dtype != key_cache.dtype or value.dtype != value_cache.dtype or key.dtype != value.dtype:
+        raise ValueError("key/value/cache dtypes must match (no fp8 cache in this build)")
+    if key_cache.stride() != value_cache.stride() or key_cache.shape != value_cache.shape:
+        raise ValueError("key_cache and value_cache must have the same shape and strides")
+    if key.stride(-1) != 1 or value.stride(-1) != 1 or key_cache.stride(-1) != 1:
+        raise ValueError("last dimension must be contiguous")
+    if not slot_mapping.is_contiguous():
+        raise ValueError("slot_mapping must be contiguous")
+    T = slot_mapping.shape[0]
+    if key.shape[0] < T or value.shape[0] < T:
+        raise ValueError("key/value have fewer rows than slot_mapping")
+    nb, bs, hkv, d = key_cache.shape
+    if key.shape[1:] != (hkv, d) or value.shape[1:] != (hkv, d):
+        raise ValueError(f"key/value shape {tuple(key.shape)} does not match cache {tuple(key_cache.shape)}")
+    _lib.check(lib.ps_kv_append(
+        key.data_ptr(), key.stride(0), key.stride(1),
+        value.data_ptr(), value.stride(0), value.stride(1),
+        key_cache.data_ptr(), value_cache.data_ptr(),
+        key_cache.stride(0), key_cache.stride(1), key_cache.stride(2), nb,
+        slot_mapping.data_ptr(), T, hkv, d, bs, key.element_size(),
+        status.data_ptr() if status is not None else None,
+        _stream_ptr(key.device)))
+
+
+class DecodeWorkspace:
+    """Fixed-size device workspace for :func:`paged_decode`.
+
+    Sized for ``max_num_seqs`` once (independent of sequence lengths, so one
+    buffer serves every step and every CUDA-graph replay) and zeroed at
+    creation; the kernel leaves its counters at zero.  ``status()`` reads and
+    ``clear_status()`` resets the device status word (PS_DEV_* bits).
+    """
+
+    def __init__(self, max_num_seqs: int, num_q_heads: int, num_kv_heads: int,
+                 head_size: int, device: torch.device | str | int | None = None):
+        lib = _lib.load()
+        dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        if dev.type != "cuda":
+            raise ValueError("DecodeWorkspace lives on a CUDA device")
+        with torch.cuda.device(dev):
+            nbytes = lib.ps_paged_decode_workspace_size(max_num_seqs, num_q_heads, num_kv_heads, head_size)
+        if nbytes < 0:
+            _lib.check(_lib.PS_ERR_INVALID_ARGUMENT)
+        self.max_num_seqs = max_num_seqs
+        self.num_q_heads = num_q_heads
+        self.num_kv_heads = num_kv_heads
+        self.nbytes = int(nbytes)
+        self.buffer = torch.zeros(self.nbytes, dtype=torch.uint8, device=dev)
+
+    def status(self) -> int:
+        return int(self.buffer[:4].view(torch.int32).item())
+
+    def clear_status(self) -> None:
+        self.buffer[:4].zero_()
+
+
+_WS_CACHE: dict = {}
+
+
+def get_workspace(num_seqs: int, num_q_heads: int, num_kv_heads: int, head_size: int,
+                  device: torch.device) -> DecodeWorkspace:
+    """Process-wide workspace per (device, heads), grown to the largest batch seen."""
+    key = (device.index, num_q_heads, num_kv_heads, head_size)
+    ws = _WS_CACHE.get(key)
+    if ws is None or ws.max_num_seqs < num_seqs:
+        cap = max(num_seqs, 256 if ws is None else 2 * ws.max_num_seqs)
+        ws = DecodeWorkspace(cap, num_q_heads, num_kv_heads, head_size, device)
+        _WS_CACHE[key] = ws
+    return ws
+
+
+def _problem(q, key_cache, value_cache, block_table, seq_lens, query_start_loc,
+             softmax_scale, out, lse) -> _lib.PagedProblem:
+    _require_cuda(q, key_cache, value_cache, block_table, seq_lens, out, query_start_loc, lse)
+    if q.dtype not in (torch.float16, torch.bfloat16):
+        raise ValueError(f"attention dtype {q.dtype} unsupported (fp16/bf16)")
+    if key_cache.dtype != q.dtype or value_cache.dtype != q.dtype or out.dtype != q.dtype:
+        raise ValueError("q, caches and out must share one dtype")
+    if key_cache.stride() != value_cache.stride() or key_cache.shape != value_cache.shape:
+        raise ValueError("key_cache and value_cache must have the same shape and strides")
+    if block_table.dtype != torch.int32 or seq_lens.dtype != torch.int32:
+        raise ValueError("block_table and seq_lens must be int32")
+    if query_start_loc is not None and query_start_loc.dtype != torch.int32:
+        raise ValueError("query_start_loc must be int32")
+    if block_table.stride(-1) != 1 or not seq_lens.is_contiguous():
+        raise ValueError("block_table rows and seq_lens must be contiguous")
+    if q.stride(-1) != 1 or out.stride(-1) != 1 or key_cache.stride(-1) != 1:
+        raise ValueError("last dimension must be contiguous")
+    if lse is not None and lse.dtype != torch.float32:
+        raise ValueError("lse must be float32 [num_q_heads, num_tokens]")
+    nb, bs, hkv, d = key_cache.shape
+    hq = q.shape[1]
+    pr = _lib.PagedProblem()
+    pr.q = q.data_ptr()
+    pr.q_stride_token, pr.q_stride_head = q.stride(0), q.stride(1)
+    pr.key_cache = key_cache.data_ptr()
+    pr.value_cache = value_cache.data_ptr()
+    pr.cache_stride_block, pr.cache_stride_slot, pr.cache_stride_head = key_cache.stride()[:3]
+    pr.num_blocks = nb
+    pr.block_table = block_table.data_ptr()
+    pr.block_table_stride = block_table.stride(0)
+    pr.max_blocks_per_seq = block_table.shape[1]
+    pr.seq_lens = seq_lens.data_ptr()
+    pr.query_start_loc = query_start_loc.data_ptr() if query_start_loc is not None else None
+    pr.num_seqs = seq_lens.shape[0]
+    pr.out = out.data_ptr()
+    pr.out_stride_token, pr.out_stride_head = out.stride(0), out.stride(1)
+    if lse is not None:
+        pr.lse = lse.data_ptr()
+        pr.lse_stride_head, pr.lse_stride_token = lse.stride(0), lse.stride(1)
+    pr.num_q_heads = hq
+    pr.num_kv_heads = hkv
+    pr.head_size = d
+    pr.block_size = bs
+    pr.dtype = _DTYPES[q.dtype]
+    pr.softmax_scale = float(softmax_scale)
+    return pr
+
+
+def paged_decode(q: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Tensor,
+                 block_table: torch.Tensor, seq_lens: torch.Tensor, softmax_scale: float,
+                 out: torch.Tensor, lse: torch.Tensor | None = None,
+                 query_start_loc: torch.Tensor | None = None,
+                 workspace: DecodeWorkspace | None = None) -> torch.Tensor:
+    """Decode attention, one query row per sequence, written into ``out``.
+
+    q/out: [T, Hq, D]; caches [num_blocks, block_size, Hkv, D]; block_table
+    int32 [B, P]; seq_lens int32 [B] (including the new token);
+    query_start_loc int32 [B+1] or None (row b for sequence b); lse fp32
+    [Hq, T] or None (natural log).
+    """
+    lib = _lib.load()
+    B = seq_lens.shape[0]
+    if workspace is None:
+        workspace = get_workspace(B, q.shape[1], key_cache.shape[2], key_cache.shape[3], q.device)
+    elif workspace.max_num_seqs < B:
+        raise ValueError(f"workspace sized for {workspace.max_num_seqs} sequences < {B}")
+    pr = _problem(q, key_cache, value_cache, block_table, seq_lens, query_start_loc,
+                  softmax_scale, out, lse)
+    _lib.check(lib.ps_paged_decode(ctypes.byref(pr), workspace.buffer.data_ptr(),
+                                   workspace.nbytes, _stream_ptr(q.device)))
+    return out
+
+
+def chunked_prefill(q: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Tensor,
+                    block_table: torch.Tensor, seq_lens: torch.Tensor,
+                    query_start_loc: torch.Tensor, softmax_scale: float, out: torch.Tensor,
+                    lse: torch.Tensor | None = None) -> torch.Tensor:
+    """Causal (bottom-right) varlen attention over the paged cache; any q_len >= 1."""
+    lib = _lib.load()
+    pr = _problem(q, key_cache, value_cache, block_table, seq_lens, query_start_loc,
+                  softmax_scale, out, lse)
+    _lib.check(lib.ps_chunked_prefill(ctypes.byref(pr), _stream_ptr(q.device)))
+    return out
+
+
+def paged_attention(q, key_cache, value_cache, out, query_start_loc, max_query_len, seq_lens,
+                    softmax_scale, block_table, lse=None, workspace=None):
+    """``flash_attn_varlen_func``'s paged, causal call shape: route by ``max_query_len``."""
+    if max_query_len <= 1:
+        return paged_decode(q, key_cache, value_cache, block_table, seq_lens, softmax_scale, out,
+                            lse=lse, query_start_loc=query_start_loc, workspace=workspace)
+    return chunked_prefill(q, key_cache, value_cache, block_table, seq_lens, query_start_loc,
+                           softmax_scale, out, lse=lse)

@@ -1,0 +1,160 @@
+"""Generate the golden vectors in this directory from the reference's own code.
+
+Run in a container where vLLM 0.22 is installed (not needed at test time):
+
+    python tests/golden/make_golden.py
+
+* Attention: vLLM's FA4 torch reference ``attention_ref``
+  (``vllm/vllm_flash_attn/cute/testing.py:326-455``), loaded by file path
+  because importing the ``vllm.vllm_flash_attn`` package needs its CUDA
+  extensions.  It is evaluated in fp32 (inputs upcast first) on the pages each
+  sequence's block table names, with ``causal=True`` as
+  ``flash_attn.py:796-817`` passes it.
+* KV append: vLLM's Triton kernel ``reshape_and_cache_kernel_flash``
+  (``vllm/v1/attention/ops/triton_reshape_and_cache_flash.py:17-124``) run on CPU
+  tensors under the Triton interpreter (``TRITON_INTERPRET=1``).
+
+Inputs are regenerated at test time from the seeds recorded here by
+``ps_attn.workloads.make_batch`` (CPU generator); a checksum of the inputs is
+stored so a generator change is detected instead of silently comparing
+different data.
+"""
+from __future__ import annotations
+
+import importlib.util
+import json
+import os
+import sys
+from pathlib import Path
+
+os.environ.setdefault("TRITON_INTERPRET", "1")
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+HERE = Path(__file__).resolve().parent
+REPO = HERE.parent.parent
+sys.path.insert(0, str(REPO / "prime-rl_b200"))
+
+from ps_attn import workloads  # noqa: E402
+
+VLLM = Path(importlib.util.find_spec("vllm").origin).parent
+
+
+def load_attention_ref():
+    path = VLLM / "vllm_flash_attn" / "cute" / "testing.py"
+    spec = importlib.util.spec_from_file_location("fa4_testing_ref", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod.attention_ref
+
+
+# (name, make_batch kwargs) -- every attention case applies the append first
+ATTN_CASES = {
+    "cfg1": dict(cfg=1),
+    "gqa1": dict(q_lens=[1, 1, 1], seq_lens=[1, 17, 100], num_q_heads=2, num_kv_heads=2, seed=11),
+    "gqa2": dict(q_lens=[1, 1, 1, 1], seq_lens=[16, 33, 250, 64], num_q_heads=4, num_kv_heads=2, seed=12),
+    "gqa4": dict(q_lens=[1, 1], seq_lens=[47, 300], num_q_heads=8, num_kv_heads=2, seed=13),
+    "gqa8": dict(q_lens=[1, 1, 1], seq_lens=[129, 5, 512], num_q_heads=16, num_kv_heads=2, seed=14),
+    "gqa16": dict(q_lens=[1, 1], seq_lens=[80, 31], num_q_heads=16, num_kv_heads=1, seed=15),
+    "bs32": dict(q_lens=[1, 1, 1], seq_lens=[70, 32, 200], num_q_heads=8, num_kv_heads=2,
+                 block_size=32, seed=16),
+    "prefill": dict(q_lens=[5, 37, 1, 16], seq_lens=[5, 90, 33, 200], num_q_heads=8,
+                    num_kv_heads=2, seed=17),
+    "grpo": dict(q_lens=[1] * 8, seq_lens=[70, 80, 65, 99, 64 + 1, 130, 77, 66], num_q_heads=8,
+                 num_kv_heads=2, share_groups=4, shared_prefix_tokens=64, seed=18),
+}
+
+
+def build_case(spec, dtype=torch.bfloat16):
+    spec = dict(spec)
+    if "cfg" in spec:
+        return workloads.make_config(spec["cfg"], device="cpu")
+    spec.setdefault("dtype", dtype)
+    return workloads.make_batch(device="cpu", **spec)
+
+
+def checksum(batch):
+    parts = [batch.q, batch.key, batch.value, batch.kv_cache]
+    return float(sum(p.double().sum().item() for p in parts))
+
+
+def torch_append(batch):
+    """Index-put append used to prepare the cache for the attention goldens."""
+    kc, vc = batch.kv_cache[0], batch.kv_cache[1]
+    nb, bs, h, d = kc.shape
+    ok = batch.slot_mapping >= 0
+    kc.view(-1, h, d)[batch.slot_mapping[ok]] = batch.key[ok]
+    vc.view(-1, h, d)[batch.slot_mapping[ok]] = batch.value[ok]
+
+
+def attention_golden(name, spec, attention_ref):
+    batch = build_case(spec)
+    cs = checksum(batch)
+    torch_append(batch)
+    kc, vc = batch.kv_cache[0], batch.kv_cache[1]
+    bs = kc.shape[1]
+    T, hq, d = batch.q.shape
+    out = torch.zeros(T, hq, d, dtype=torch.float32)
+    lse = torch.full((hq, T), float("-inf"), dtype=torch.float32)
+    qsl = batch.query_start_loc.tolist()
+    for b, L in enumerate(batch.seq_lens.tolist()):
+        t0, t1 = qsl[b], qsl[b + 1]
+        if t1 <= t0:
+            continue
+        npg = (L + bs - 1) // bs
+        blocks = batch.block_table[b, :npg].long()
+        k = kc[blocks].reshape(npg * bs, *kc.shape[2:])[:L].float()
+        v = vc[blocks].reshape(npg * bs, *vc.shape[2:])[:L].float()
+        q = batch.q[t0:t1].float()
+        o, _, l = attention_ref(q[None], k[None], v[None], causal=True, return_lse=True)
+        out[t0:t1] = o[0]
+        lse[:, t0:t1] = l[0]
+    return dict(out=out.numpy(), lse=lse.numpy()), cs
+
+
+def append_golden(triton_mod, dtype, seed):
+    """Run vLLM's Triton append kernel under the interpreter on a small cache."""
+    g = torch.Generator().manual_seed(seed)
+    T, H, D, NB, bs = 9, 2, 128, 6, 16
+    # key/value are views into a wider qkv row (token stride > H*D), like vLLM's
+    qkv = torch.randn(T + 2, (4 + 2 * H) * D, generator=g).to(dtype)
+    key = qkv[:, 4 * D:(4 + H) * D].view(T + 2, H, D)
+    value = qkv[:, (4 + H) * D:].view(T + 2, H, D)
+    kc = torch.randn(NB, bs, H, D, generator=g).to(dtype)
+    vc = torch.randn(NB, bs, H, D, generator=g).to(dtype)
+    kc0, vc0 = kc.clone(), vc.clone()
+    slots = torch.tensor([3, -1, 17, 40, 95, 0, -1, 64, 33], dtype=torch.int64)
+    n = H * D
+    run_dtype = torch.int16 if dtype == torch.bfloat16 else dtype
+    kc_r, vc_r = kc.view(run_dtype), vc.view(run_dtype)
+    key_r, value_r = key.view(run_dtype), value.view(run_dtype)
+    triton_mod.reshape_and_cache_kernel_flash[(T, 1)](
+        key_r, value_r, kc_r, vc_r, slots, torch.ones(1), torch.ones(1),
+        key_r.stride(0), value_r.stride(0), kc_r.stride(0), kc_r.stride(2), 0, 0, kc_r.stride(1),
+        H, D, bs, 1, False, False, 256)
+    as_np = (lambda t: t.view(torch.int16).numpy()) if dtype == torch.bfloat16 else (lambda t: t.numpy())
+    return dict(qkv=as_np(qkv), key_cache_in=as_np(kc0), value_cache_in=as_np(vc0),
+                slot_mapping=slots.numpy(), key_cache_out=as_np(kc), value_cache_out=as_np(vc))
+
+
+def main():
+    attention_ref = load_attention_ref()
+    meta = {"attention": {}, "append": {}}
+    for name, spec in ATTN_CASES.items():
+        arrays, cs = attention_golden(name, spec, attention_ref)
+        np.savez_compressed(HERE / f"attn_{name}.npz", **arrays)
+        meta["attention"][name] = {"spec": {k: v for k, v in spec.items()}, "input_checksum": cs}
+        print(f"attn_{name}: out {arrays['out'].shape} checksum {cs:.6f}")
+    from vllm.v1.attention.ops import triton_reshape_and_cache_flash as triton_mod
+
+    for name, dtype, seed in (("bf16", torch.bfloat16, 21), ("fp32", torch.float32, 22)):
+        arrays = append_golden(triton_mod, dtype, seed)
+        np.savez_compressed(HERE / f"append_{name}.npz", **arrays)
+        meta["append"][name] = {"dtype": str(dtype), "seed": seed}
+        print(f"append_{name}: written")
+    (HERE / "golden_meta.json").write_text(json.dumps(meta, indent=1, default=str) + "\n")
+
+
+if __name__ == "__main__":
+    main()

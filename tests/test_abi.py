@@ -1,0 +1,91 @@
+"""CPU: the C-ABI library loads, exports every declared symbol and validates
+arguments on the host (no kernel is launched here)."""
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from ps_attn import _lib
+
+HEADER = Path(__file__).resolve().parent.parent / "include" / "ps_attn.h"
+
+
+def declared_functions():
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    return sorted(set(re.findall(r"\b(ps_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_and_binding_agree():
+    assert declared_functions() == sorted(_lib.EXPORTED_SYMBOLS)
+
+
+def test_library_loads_and_exports_every_symbol():
+    lib = _lib.load()
+    for name in declared_functions():
+        assert hasattr(lib, name), f"{name} missing from libps_attn.so"
+    assert lib.ps_abi_version() == _lib.ABI_VERSION
+
+
+def test_struct_layout_matches_header_order():
+    fields = [f for f, _ in _lib.PagedProblem._fields_]
+    text = HEADER.read_text()
+    body = text[text.index("typedef struct {"):text.index("} ps_paged_problem;")]
+    body = re.sub(r"/\*.*?\*/", "", body, flags=re.S)
+    names = []
+    for decl in body.split(";"):
+        decl = decl.strip()
+        if not decl or decl.startswith("typedef"):
+            decl = decl.replace("typedef struct {", "").strip()
+        if not decl:
+            continue
+        toks = decl.replace("*", " ").replace(",", " ").split()
+        # drop the type tokens: everything up to the first field name
+        for i, tok in enumerate(toks):
+            if tok not in ("const", "void", "int64_t", "int32_t", "float"):
+                names.extend(toks[i:])
+                break
+    assert names == fields
+
+
+def test_host_validation_errors_without_gpu():
+    lib = _lib.load()
+    # NULL problem -> invalid argument, message set
+    rc = lib.ps_paged_decode(None, None, 0, None)
+    assert rc == _lib.PS_ERR_INVALID_ARGUMENT
+    assert b"NULL" in lib.ps_last_error()
+    # zero tokens is a no-op success, negative is rejected
+    args = [None, 0, 0, None, 0, 0, None, None, 0, 0, 0, 1, None, 0, 8, 128, 16, 2, None, None]
+    assert lib.ps_kv_append(*args) == _lib.PS_OK
+    args[13] = -1
+    assert lib.ps_kv_append(*args) == _lib.PS_ERR_INVALID_ARGUMENT
+    # unsupported dtype is reported as such (checked before any device query)
+    pr = _lib.PagedProblem()
+    for f in ("q", "key_cache", "value_cache", "block_table", "seq_lens", "out"):
+        setattr(pr, f, 4096)
+    pr.num_seqs, pr.dtype, pr.head_size, pr.block_size = 1, _lib.PS_DTYPE_FP32, 128, 16
+    pr.num_q_heads, pr.num_kv_heads, pr.num_blocks = 8, 2, 4
+    assert lib.ps_paged_decode(ctypes.byref(pr), None, 0, None) == _lib.PS_ERR_UNSUPPORTED
+    pr.dtype, pr.head_size = _lib.PS_DTYPE_BF16, 96
+    assert lib.ps_paged_decode(ctypes.byref(pr), None, 0, None) == _lib.PS_ERR_UNSUPPORTED
+    pr.head_size, pr.block_size = 128, 24
+    assert lib.ps_paged_decode(ctypes.byref(pr), None, 0, None) == _lib.PS_ERR_INVALID_ARGUMENT
+    pr.block_size, pr.num_q_heads = 16, 7
+    assert lib.ps_paged_decode(ctypes.byref(pr), None, 0, None) == _lib.PS_ERR_INVALID_ARGUMENT
+    # prefill requires query_start_loc
+    pr.num_q_heads = 8
+    assert lib.ps_chunked_prefill(ctypes.byref(pr), None) == _lib.PS_ERR_INVALID_ARGUMENT
+
+
+def test_ops_refuse_cpu_tensors():
+    import torch
+
+    from ps_attn import ops
+
+    k = torch.zeros(2, 1, 128, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.kv_append(k, k, torch.zeros(1, 16, 1, 128, dtype=torch.bfloat16),
+                      torch.zeros(1, 16, 1, 128, dtype=torch.bfloat16),
+                      torch.zeros(2, dtype=torch.int64))
