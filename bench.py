@@ -227,8 +227,9 @@ def run_ours(args):
     torch.cuda.synchronize(dev)
 
     sampler = ClockSampler(local)
-    sampler.start()
-    time.sleep(0.25)
+    if not args.quick:
+        sampler.start()
+        time.sleep(0.25)
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
@@ -242,7 +243,7 @@ def run_ours(args):
     # keep the same load on the GPU for at least ~1.5 s so the clock sampler sees it
     extra_t = time.perf_counter()
     with torch.cuda.stream(stream):
-        while time.perf_counter() - extra_t < max(0.0, 1.5 - elapsed_ms / 1e3):
+        while not args.quick and time.perf_counter() - extra_t < max(0.0, 1.5 - elapsed_ms / 1e3):
             for _ in range(50):
                 step()
             stream.synchronize()
@@ -258,7 +259,7 @@ def run_ours(args):
     assert ws.status() == 0, f"device status {ws.status():#x}"
 
     # ---- end to end through the public API: host inputs in, host output back ----
-    e2e = run_e2e(batch, ws, dev, args.steps, world)
+    e2e = None if args.quick else run_e2e(batch, ws, dev, args.steps, world)
 
     ms = elapsed_ms / args.steps
     tokens_per_step = B if not sharded else B  # every rank decodes all B tokens (its heads)
@@ -298,7 +299,7 @@ def run_ours(args):
         "e2e": e2e,
         "clocks": clocks,
     }
-    if rank == 0 and world == 1:
+    if rank == 0 and world == 1 and not args.quick:
         res["cpu_baseline"] = cpu_baseline(cfg, budget_s=args.cpu_budget)
     if rank == 0:
         print(json.dumps(res), flush=True)
@@ -468,6 +469,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
+    ap.add_argument("--quick", action="store_true",
+                    help="timed steps only: no end-to-end, CPU baseline or clock sampling")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

@@ -108,6 +108,11 @@ typedef struct {
   int32_t num_q_heads, num_kv_heads, head_size, block_size;
   int32_t dtype; /* ps_dtype of q, cache and out */
   float softmax_scale;
+  /* rows of q / out (the extent chunked prefill's Q tile loads are bounded by) */
+  int64_t num_tokens;
+  /* device status word (PS_DEV_* bits), nullable; ps_paged_decode uses the
+     one in its workspace instead */
+  int32_t* status;
 } ps_paged_problem;
 
 /*
@@ -136,7 +141,9 @@ int ps_paged_decode(const ps_paged_problem* problem, void* workspace, int64_t wo
  * Chunked prefill: any q_len >= 1 per sequence, causal bottom-right, over the
  * same paged cache.  Replaces flash_attn_varlen_func for max_seqlen_q > 1
  * (flash_attn.py:796-817 -> cute/flash_fwd_sm100.py).  Tensor-core path:
- * tcgen05 MMA with TMEM accumulators.  No workspace.
+ * tcgen05 MMA with TMEM accumulators.  No workspace; problem->num_tokens
+ * must be the row count of q/out and problem->status (nullable) receives
+ * PS_DEV_* bits.
  */
 int ps_chunked_prefill(const ps_paged_problem* problem, void* stream);
 

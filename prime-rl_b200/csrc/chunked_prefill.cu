@@ -1,0 +1,495 @@
+// Chunked-prefill paged attention on the sm_100a tensor cores (tcgen05 + TMEM).
+//
+// Semantics: vllm/vllm_flash_attn/cute/testing.py:326-455 (attention_ref) with
+// causal=True, bottom-right aligned: in a sequence of seq_len L with q_len new
+// query rows, query row i sees keys j <= L - q_len + i (construct_local_mask,
+// testing.py:278-279).  Output bf16/fp16, natural-log LSE as FA4's
+// softmax.finalize (cute/softmax.py:147-158).
+//
+// Tiling.  An M tile is 128 rows of (token, q head) pairs of ONE kv head: the
+// GQA group is packed along M (row = token * group + head_in_group), so a KV
+// tile loaded once serves every q head that reads it.  A KV tile is 128 keys =
+// 8 pages of 16 tokens gathered through the block table, one TMA box per page
+// and 64-dim half, 128-byte swizzled (the canonical K-major SW128 layout for
+// K; for V the same bytes are the MN-major SW128 layout of the PV B operand).
+//
+// Warp roles (192 threads, one persistent CTA per SM):
+//   warp 0     TMA producer: Q tile (3-D box over [tokens, heads, dims]), K/V tiles
+//   warp 1     TMEM owner; lane 0 issues tcgen05.mma:
+//                S[b] = Q . K^T   (M128 N128 K16 x 8, S double-buffered in TMEM)
+//                O   += P . V     (M128 N128 K16 x 8, O resident in TMEM)
+//   warps 2-5  softmax + epilogue, one thread per TMEM lane (= M row): S row
+//              from TMEM, causal mask, online softmax in the exp2 domain with
+//              lazy rescaling (the running max moves only when a tile's max
+//              exceeds it by more than 2^8; O in TMEM is rescaled then), P as
+//              bf16 into shared memory, final O / l and LSE to global memory.
+//
+// Every mbarrier wait is bounded (~1 s); on timeout the kernel records
+// PS_DEV_WAIT_TIMEOUT, raises a CTA-wide abort flag that ends every role's
+// loop, and still frees its TMEM.
+#include "ps_common.cuh"
+#include "ps_launch.h"
+#include "tcgen05.cuh"
+
+namespace ps {
+
+constexpr int kKeys = 128;            // keys per KV tile
+constexpr int kRegionBytes = 128 * 128;  // [128 rows][64 x 16-bit], 128B swizzled
+constexpr int kTileBytes = 2 * kRegionBytes;  // both 64-dim halves
+constexpr int kKvStages = 2;
+constexpr float kRescaleThreshold = 8.0f;  // log2 units
+
+struct PrefillSmem {
+  // all tiles 1024-byte aligned (offsets from the aligned base)
+  static constexpr int q_off = 0;
+  static constexpr int k_off = q_off + kTileBytes;
+  static constexpr int v_off = k_off + kKvStages * kTileBytes;
+  static constexpr int p_off = v_off + kKvStages * kTileBytes;
+  static constexpr int bar_off = p_off + kTileBytes;
+  // barriers
+  static constexpr int n_bars = 2 /*q*/ + 3 * kKvStages /*kfull vfull kvempty*/ +
+                                2 * 2 /*s_full s_empty*/ + 2 /*p_full pv_done*/;
+  static constexpr int misc_off = bar_off + n_bars * 8;  // tmem base, abort flag
+  static constexpr int table_off = misc_off + 16;
+  static constexpr int bytes_before_table = table_off;
+};
+
+struct PBars {
+  uint64_t* q_full;
+  uint64_t* q_empty;
+  uint64_t* kfull;   // [kKvStages]
+  uint64_t* vfull;   // [kKvStages]
+  uint64_t* kvempty; // [kKvStages]
+  uint64_t* s_full;  // [2]
+  uint64_t* s_empty; // [2]
+  uint64_t* p_full;
+  uint64_t* pv_done;
+};
+
+struct UnitInfo {
+  int b, h, t0, t1;   // sequence, kv head, token range [t0, t1) within the q chunk
+  int qrow0;          // first global q row of the sequence
+  int ctx;            // L - q_len
+  int L;
+  int kv_end;         // keys [0, kv_end) are visible to some row of the unit
+  int ntiles;
+};
+
+__device__ __forceinline__ UnitInfo unit_info(const PrefillParams& p, const int* prefix, int u) {
+  UnitInfo ui;
+  const int pu = u / p.num_kv_heads;
+  ui.h = u - pu * p.num_kv_heads;
+  int lo = 0, hi = p.num_seqs - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (prefix[mid] <= pu) lo = mid; else hi = mid - 1;
+  }
+  ui.b = lo;
+  const int mt = pu - prefix[lo];
+  ui.qrow0 = __ldg(p.qsl + lo);
+  const int qlen = __ldg(p.qsl + lo + 1) - ui.qrow0;
+  ui.L = __ldg(p.seq_lens + lo);
+  ui.ctx = ui.L - qlen;
+  ui.t0 = mt * p.tokens_per_tile;
+  ui.t1 = min(qlen, ui.t0 + p.tokens_per_tile);
+  ui.kv_end = ui.ctx + ui.t1;
+  ui.ntiles = (ui.kv_end + kKeys - 1) / kKeys;
+  return ui;
+}
+
+// bounded wait that also observes the CTA abort flag; returns false to abort
+__device__ __forceinline__ bool pwait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                      int32_t* status) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (clock64() - t0 > kWaitLimitCycles) {
+      *abort_flag = 1;
+      set_status(status, PS_DEV_WAIT_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, uint64_t* bar,
+                                            int c0, int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cta.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+      : "memory");
+}
+
+template <bool kBF16>
+__global__ void __launch_bounds__(192, 1)
+    chunked_prefill_kernel(const __grid_constant__ PrefillParams p,
+                           const __grid_constant__ CUtensorMap qmap,
+                           const __grid_constant__ CUtensorMap kmap,
+                           const __grid_constant__ CUtensorMap vmap) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  using L = PrefillSmem;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + L::bar_off);
+  PBars bars;
+  bars.q_full = bar + 0;
+  bars.q_empty = bar + 1;
+  bars.kfull = bar + 2;
+  bars.vfull = bar + 2 + kKvStages;
+  bars.kvempty = bar + 2 + 2 * kKvStages;
+  bars.s_full = bar + 2 + 3 * kKvStages;
+  bars.s_empty = bar + 4 + 3 * kKvStages;
+  bars.p_full = bar + 6 + 3 * kKvStages;
+  bars.pv_done = bar + 7 + 3 * kKvStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::misc_off);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::misc_off + 4);
+  int* prefix = reinterpret_cast<int*>(smem + L::table_off);
+  __shared__ int s_warp_tot[6];
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int B = p.num_seqs;
+  const int G = p.group;
+
+  // ---- prologue: M tiles per sequence, exclusive prefix ------------------------
+  const int per = (B + blockDim.x - 1) / blockDim.x;
+  const int b_lo = min(B, tid * per), b_hi = min(B, b_lo + per);
+  int local = 0;
+  for (int b = b_lo; b < b_hi; ++b) {
+    const int qlen = __ldg(p.qsl + b + 1) - __ldg(p.qsl + b);
+    local += qlen > 0 ? (qlen + p.tokens_per_tile - 1) / p.tokens_per_tile : 0;
+  }
+  int incl = local;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += v;
+  }
+  if (lane == 31) s_warp_tot[warp] = incl;
+  if (tid == 0) {
+    *abort_flag = 0;
+    mbar_init(bars.q_full, 1);
+    mbar_init(bars.q_empty, 1);
+    for (int s = 0; s < kKvStages; ++s) {
+      mbar_init(bars.kfull + s, 1);
+      mbar_init(bars.vfull + s, 1);
+      mbar_init(bars.kvempty + s, 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(bars.s_full + s, 1);
+      mbar_init(bars.s_empty + s, 4);
+    }
+    mbar_init(bars.p_full, 4);
+    mbar_init(bars.pv_done, 1);
+    fence_mbar_init();
+    tma_prefetch_desc(&qmap);
+    tma_prefetch_desc(&kmap);
+    tma_prefetch_desc(&vmap);
+  }
+  if (warp == 1) {  // TMEM: S0 [0,128) S1 [128,256) O [256,384)
+    tc::tmem_alloc(tmem_slot, 512);
+    tc::tmem_relinquish();
+  }
+  __syncthreads();
+  {
+    int warp_off = 0;
+    for (int w = 0; w < warp; ++w) warp_off += s_warp_tot[w];
+    int run = warp_off + incl - local;
+    for (int b = b_lo; b < b_hi; ++b) {
+      prefix[b] = run;
+      const int qlen = __ldg(p.qsl + b + 1) - __ldg(p.qsl + b);
+      run += qlen > 0 ? (qlen + p.tokens_per_tile - 1) / p.tokens_per_tile : 0;
+    }
+    if (tid == blockDim.x - 1) prefix[B] = warp_off + incl;
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+  const int total_units = prefix[B] * p.num_kv_heads;
+
+  uint8_t* sQ = smem + L::q_off;
+  uint8_t* sK = smem + L::k_off;
+  uint8_t* sV = smem + L::v_off;
+  uint8_t* sP = smem + L::p_off;
+  const int spb = p.block_size / 16;
+
+  if (warp == 0) {
+    // =========================== TMA producer ===========================
+    if (lane == 0) {
+      int t = 0, uit = 0;
+      for (int u = blockIdx.x; u < total_units && !*abort_flag; u += gridDim.x, ++uit) {
+        const UnitInfo ui = unit_info(p, prefix, u);
+        if (!pwait(bars.q_empty, (uit & 1) ^ 1, abort_flag, p.status)) break;
+        // the box always spans tokens_per_tile tokens (rows past the sequence are
+        // the next sequence's or zero fill) and TMA delivers the whole box
+        mbar_arrive_expect_tx(bars.q_full, p.tokens_per_tile * G * 2 * 128);
+        tma_load_3d(sQ, &qmap, bars.q_full, 0, ui.h * G, ui.qrow0 + ui.t0);
+        tma_load_3d(sQ + kRegionBytes, &qmap, bars.q_full, 64, ui.h * G, ui.qrow0 + ui.t0);
+        const int npages_needed = (ui.kv_end + 15) / 16;
+        const int* bt = p.block_table + static_cast<int64_t>(ui.b) * p.bt_stride;
+        bool ok = true;
+        for (int j = 0; j < ui.ntiles; ++j, ++t) {
+          const int s = t % kKvStages;
+          const uint32_t n = static_cast<uint32_t>(t / kKvStages);
+          if (!pwait(bars.kvempty + s, (n & 1) ^ 1, abort_flag, p.status)) { ok = false; break; }
+          const int pg0 = j * 8;
+          const int npg = min(8, npages_needed - pg0);
+          const uint32_t bytes = static_cast<uint32_t>(npg) * 2 * 2048;
+          uint8_t* kd = sK + s * kTileBytes;
+          uint8_t* vd = sV + s * kTileBytes;
+          mbar_arrive_expect_tx(bars.kfull + s, bytes);
+          mbar_arrive_expect_tx(bars.vfull + s, bytes);
+          for (int i = 0; i < npg; ++i) {
+            const int pg = pg0 + i;
+            const int bi = pg / spb;
+            int blk = bi < p.max_blocks_per_seq ? __ldg(bt + bi) : -1;
+            if (blk < 0 || blk >= p.num_blocks) {
+              set_status(p.status, PS_DEV_BLOCK_OUT_OF_RANGE);
+              blk = 0;
+            }
+            const int tok = (pg % spb) * 16;
+            tma_load_4d(kd + i * 2048, &kmap, bars.kfull + s, 0, ui.h, tok, blk);
+            tma_load_4d(kd + kRegionBytes + i * 2048, &kmap, bars.kfull + s, 64, ui.h, tok, blk);
+            tma_load_4d(vd + i * 2048, &vmap, bars.vfull + s, 0, ui.h, tok, blk);
+            tma_load_4d(vd + kRegionBytes + i * 2048, &vmap, bars.vfull + s, 64, ui.h, tok, blk);
+          }
+        }
+        if (!ok) break;
+      }
+    }
+  } else if (warp == 1) {
+    // =========================== MMA issuer ===========================
+    if (lane == 0) {
+      const uint32_t idesc_qk = tc::idesc_f16(kBF16, 128, 128, false, false);
+      const uint32_t idesc_pv = tc::idesc_f16(kBF16, 128, 128, false, true);
+      const uint32_t q_addr = smem_u32(sQ), k_addr = smem_u32(sK), v_addr = smem_u32(sV),
+                     p_addr = smem_u32(sP);
+      int t = 0, uit = 0;
+      int pend_t = -1, pend_j = 0;  // tile whose PV is still to be issued
+      auto issue_pv = [&](int tt, int jj) -> bool {
+        const int s = tt % kKvStages;
+        if (!pwait(bars.p_full, static_cast<uint32_t>(tt & 1), abort_flag, p.status)) return false;
+        if (!pwait(bars.vfull + s, static_cast<uint32_t>((tt / kKvStages) & 1), abort_flag, p.status))
+          return false;
+        tc::fence_after_sync();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint64_t ad = tc::sw128_desc(p_addr + (kk >> 2) * kRegionBytes + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = tc::sw128_desc(v_addr + s * kTileBytes + kk * 2048, kRegionBytes, 1024);
+          tc::mma_f16_ss(tmem + 256, ad, bd, idesc_pv, (jj > 0 || kk > 0) ? 1u : 0u);
+        }
+        tc::commit(bars.pv_done);
+        tc::commit(bars.kvempty + s);
+        return true;
+      };
+      bool ok = true;
+      for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x, ++uit) {
+        const UnitInfo ui = unit_info(p, prefix, u);
+        if (!pwait(bars.q_full, static_cast<uint32_t>(uit & 1), abort_flag, p.status)) break;
+        tc::fence_after_sync();
+        for (int j = 0; j < ui.ntiles; ++j, ++t) {
+          const int s = t % kKvStages;
+          const int sb = t & 1;
+          const uint32_t n = static_cast<uint32_t>(t / kKvStages);
+          if (!pwait(bars.kfull + s, n & 1, abort_flag, p.status)) { ok = false; break; }
+          if (!pwait(bars.s_empty + sb, (static_cast<uint32_t>(t >> 1) & 1) ^ 1, abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
+          tc::fence_after_sync();
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint32_t off = (kk >> 2) * kRegionBytes + (kk & 3) * 32;
+            const uint64_t ad = tc::sw128_desc(q_addr + off, 16, 1024);
+            const uint64_t bd = tc::sw128_desc(k_addr + s * kTileBytes + off, 16, 1024);
+            tc::mma_f16_ss(tmem + sb * 128, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
+          }
+          tc::commit(bars.s_full + sb);
+          if (j == ui.ntiles - 1) tc::commit(bars.q_empty);
+          if (pend_t >= 0 && !issue_pv(pend_t, pend_j)) { ok = false; break; }
+          pend_t = t;
+          pend_j = j;
+        }
+        if (ok && pend_t >= 0) {
+          if (!issue_pv(pend_t, pend_j)) ok = false;
+          pend_t = -1;
+        }
+      }
+    }
+  } else {
+    // =========================== softmax + epilogue ===========================
+    const int quarter = warp & 3;             // TMEM lane quarter this warp may access
+    const int row = quarter * 32 + lane;      // M row == TMEM lane
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    const float sl2 = p.scale_log2;
+    int t = 0;
+    for (int u = blockIdx.x; u < total_units; u += gridDim.x) {
+      const UnitInfo ui = unit_info(p, prefix, u);
+      const int tok = ui.t0 + row / G;
+      const int hin = row - (row / G) * G;
+      const bool row_valid = row < p.tokens_per_tile * G && tok < ui.t1;
+      const int limit = row_valid ? ui.ctx + tok : -1;  // last visible key
+      float m_run = -INFINITY, l_run = 0.f;
+      bool ok = true;
+      for (int j = 0; j < ui.ntiles; ++j, ++t) {
+        const int sb = t & 1;
+        if (!pwait(bars.s_full + sb, static_cast<uint32_t>(t >> 1) & 1, abort_flag, p.status)) { ok = false; break; }
+        tc::fence_after_sync();
+        float s[128];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r[32];
+          tc::ld_32x32b_x32(lane_addr + sb * 128 + c * 32, r);
+          tc::wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(r[i]);
+        }
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bars.s_empty + sb);
+        // scale + causal mask, row max
+        const int key0 = j * kKeys;
+        float mx = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < 128; ++c) {
+          const float v = (key0 + c <= limit) ? s[c] * sl2 : -INFINITY;
+          s[c] = v;
+          mx = fmaxf(mx, v);
+        }
+        float m_new = m_run, factor = 1.f;
+        if (mx > m_run + kRescaleThreshold || (m_run == -INFINITY && mx > -INFINITY)) {
+          m_new = mx;
+          factor = ex2(m_run - m_new);  // 0 when m_run == -inf
+        }
+        float rs = 0.f;
+        uint32_t pk[64];
+#pragma unroll
+        for (int c = 0; c < 64; ++c) {
+          const float p0 = (m_new == -INFINITY) ? 0.f : ex2(s[2 * c] - m_new);
+          const float p1 = (m_new == -INFINITY) ? 0.f : ex2(s[2 * c + 1] - m_new);
+          rs += p0 + p1;
+          pk[c] = pack2<kBF16>(p0, p1);
+        }
+        l_run = l_run * factor + rs;
+        m_run = m_new;
+        // P and O are single-buffered: PV of the previous tile must be done
+        if (t > 0 && !pwait(bars.pv_done, static_cast<uint32_t>((t - 1) & 1), abort_flag, p.status)) {
+          ok = false;
+          break;
+        }
+        tc::fence_after_sync();
+        if (j > 0 && __any_sync(0xffffffffu, factor != 1.f)) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t r[32];
+            tc::ld_32x32b_x32(lane_addr + 256 + c * 32, r);
+            tc::wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * factor);
+            tc::st_32x32b_x32(lane_addr + 256 + c * 32, r);
+          }
+          tc::wait_st();
+        }
+        // P row -> shared memory, K-major 128B-swizzled [128 rows][64 keys] x 2
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          const int region = c >> 3;
+          const int phys = (c & 7) ^ (row & 7);
+          uint4 v = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+          *reinterpret_cast<uint4*>(sP + region * kRegionBytes + row * 128 + phys * 16) = v;
+        }
+        // last tile of the unit: V rows at or past kv_end must be finite (zero)
+        if (j == ui.ntiles - 1) {
+          const int z0 = ui.kv_end - key0;
+          if (z0 < kKeys) {
+            const int s = t % kKvStages;
+            if (!pwait(bars.vfull + s, static_cast<uint32_t>((t / kKvStages) & 1), abort_flag, p.status)) {
+              ok = false;
+              break;
+            }
+            uint8_t* vd = sV + s * kTileBytes;
+            const int nchunks = (kKeys - z0) * 16;  // 16-byte chunks over both regions
+            for (int i = row; i < nchunks; i += 128) {
+              const int rr = z0 + (i >> 4);
+              const int region = (i >> 3) & 1;
+              *reinterpret_cast<uint4*>(vd + region * kRegionBytes + rr * 128 + (i & 7) * 16) =
+                  make_uint4(0u, 0u, 0u, 0u);
+            }
+          }
+        }
+        fence_proxy_async_smem();
+        tc::fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bars.p_full);
+      }
+      if (!ok) break;
+      // ---- epilogue: O / l -> global ----
+      if (!pwait(bars.pv_done, static_cast<uint32_t>((t - 1) & 1), abort_flag, p.status)) break;
+      tc::fence_after_sync();
+      const bool zero = (l_run == 0.f) || (l_run != l_run);
+      const float inv = zero ? 0.f : 1.f / l_run;
+      const int qh = ui.h * G + hin;
+      const int64_t orow = static_cast<int64_t>(ui.qrow0 + tok);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        tc::ld_32x32b_x32(lane_addr + 256 + c * 32, r);
+        tc::wait_ld();
+        if (row_valid) {
+          uint8_t* dst = reinterpret_cast<uint8_t*>(p.out) +
+                         (orow * p.o_st + static_cast<int64_t>(qh) * p.o_sh + c * 32) * 2;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            uint4 v;
+            v.x = pack2<kBF16>(__uint_as_float(r[8 * i + 0]) * inv, __uint_as_float(r[8 * i + 1]) * inv);
+            v.y = pack2<kBF16>(__uint_as_float(r[8 * i + 2]) * inv, __uint_as_float(r[8 * i + 3]) * inv);
+            v.z = pack2<kBF16>(__uint_as_float(r[8 * i + 4]) * inv, __uint_as_float(r[8 * i + 5]) * inv);
+            v.w = pack2<kBF16>(__uint_as_float(r[8 * i + 6]) * inv, __uint_as_float(r[8 * i + 7]) * inv);
+            *reinterpret_cast<uint4*>(dst + i * 16) = v;
+          }
+        }
+      }
+      if (row_valid && p.lse != nullptr)
+        p.lse[static_cast<int64_t>(qh) * p.lse_sh + orow * p.lse_st] =
+            zero ? -INFINITY : (m_run + __log2f(l_run)) * 0.6931471805599453f;
+      tc::fence_before_sync();
+    }
+  }
+
+  // ---- teardown: every role done; TMEM owner frees it ----
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  if (warp == 1) tc::tmem_dealloc(tmem, 512);
+}
+
+template <bool kBF16>
+static int launch_prefill_t(const PrefillParams& p, const CUtensorMap& qmap, const CUtensorMap& kmap,
+                            const CUtensorMap& vmap, int grid, cudaStream_t stream) {
+  const size_t smem = 1024 + PrefillSmem::bytes_before_table + static_cast<size_t>(p.num_seqs + 1) * 4;
+  static bool configured[64] = {false};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev >= 64) return static_cast<int>(cudaErrorInvalidDevice);
+  if (!configured[dev]) {
+    const cudaError_t e = cudaFuncSetAttribute(
+        chunked_prefill_kernel<kBF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        static_cast<int>(1024 + PrefillSmem::bytes_before_table + (kPrefillMaxSeqs + 1) * 4));
+    if (e != cudaSuccess) return static_cast<int>(e);
+    configured[dev] = true;
+  }
+  chunked_prefill_kernel<kBF16><<<grid, 192, smem, stream>>>(p, qmap, kmap, vmap);
+  return static_cast<int>(cudaGetLastError());
+}
+
+}  // namespace ps
+
+int ps_launch_chunked_prefill(const ps::PrefillParams& p, const CUtensorMap& qmap,
+                              const CUtensorMap& kmap, const CUtensorMap& vmap, int dtype_bf16,
+                              int grid, cudaStream_t stream) {
+  return dtype_bf16 ? ps::launch_prefill_t<true>(p, qmap, kmap, vmap, grid, stream)
+                    : ps::launch_prefill_t<false>(p, qmap, kmap, vmap, grid, stream);
+}

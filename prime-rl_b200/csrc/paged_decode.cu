@@ -35,6 +35,16 @@ constexpr int kHeadDim = 128;
 constexpr int kBoxBytes = kPageTokens * 64 * 2;  // 2 KB: 16 rows x 128 bytes
 constexpr int kStageBytes = 4 * kBoxBytes;       // K lo, K hi, V lo, V hi
 
+// Split-slot record: kG output rows of 128 fp32, then kG fp32 LSEs.
+template <int kG>
+__device__ __forceinline__ float* slot_o(const DecodeParams& p, int64_t slot, int row) {
+  return p.part + slot * (kG * (kHeadDim + 1)) + row * kHeadDim;
+}
+template <int kG>
+__device__ __forceinline__ float* slot_lse(const DecodeParams& p, int64_t slot, int row) {
+  return p.part + slot * (kG * (kHeadDim + 1)) + kG * kHeadDim + row;
+}
+
 struct Cursor {
   int b, h, p, P;  // sequence, kv head, page within sequence, pages of sequence
 };
@@ -96,13 +106,13 @@ __device__ void combine_segment(const DecodeParams& p, int b, int h, int64_t slo
   const float kLog2e = 1.4426950408889634f;
   for (int j = 0; j < group; ++j) {
     float mx = -INFINITY;
-    for (int k = lane; k < n; k += 32) mx = fmaxf(mx, __ldcg(p.part_lse + (slot0 + k) * kG + j));
+    for (int k = lane; k < n; k += 32) mx = fmaxf(mx, __ldcg(slot_lse<kG>(p, slot0 + k, j)));
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     const float mx_cur = (mx == -INFINITY) ? 0.f : mx;
     float sum = 0.f;
     for (int k = lane; k < n; k += 32)
-      sum += ex2(__ldcg(p.part_lse + (slot0 + k) * kG + j) * kLog2e - mx_cur * kLog2e);
+      sum += ex2(__ldcg(slot_lse<kG>(p, slot0 + k, j)) * kLog2e - mx_cur * kLog2e);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
     const float lse = __logf(sum) + mx;
@@ -110,11 +120,9 @@ __device__ void combine_segment(const DecodeParams& p, int b, int h, int64_t slo
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int k = 0; k < n; ++k) {
       const float w =
-          ex2(__ldcg(p.part_lse + (slot0 + k) * kG + j) * kLog2e - mx_cur * kLog2e) * inv;
+          ex2(__ldcg(slot_lse<kG>(p, slot0 + k, j)) * kLog2e - mx_cur * kLog2e) * inv;
       if (w > 0.f) {
-        const float4 o = __ldcg(reinterpret_cast<const float4*>(p.part_o + ((slot0 + k) * kG + j) *
-                                                                              kHeadDim) +
-                                lane);
+        const float4 o = __ldcg(reinterpret_cast<const float4*>(slot_o<kG>(p, slot0 + k, j)) + lane);
         acc.x += w * o.x;
         acc.y += w * o.y;
         acc.z += w * o.z;
@@ -135,7 +143,7 @@ __device__ void combine_segment(const DecodeParams& p, int b, int h, int64_t slo
 }
 
 template <bool kBF16, int NT>
-__global__ void __launch_bounds__(kDecodeWarps * 32, 1)
+__global__ void __launch_bounds__(kDecodeWarps * 32, kDecodeCtasPerSm)
     paged_decode_kernel(const __grid_constant__ DecodeParams p,
                         const __grid_constant__ CUtensorMap kmap,
                         const __grid_constant__ CUtensorMap vmap) {
@@ -459,13 +467,13 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 1)
 #pragma unroll
           for (int j = 0; j < 2; ++j) {
             const int col = nt * 8 + 2 * t + j;
-            float* po = p.part_o + (slot * kG + col) * kHeadDim;
+            float* po = slot_o<kG>(p, slot, col);
 #pragma unroll
             for (int mi = 0; mi < 8; ++mi) {
               po[mi * 16 + g] = o[nt][mi][j] * inv[nt][j];
               po[mi * 16 + g + 8] = o[nt][mi][j + 2] * inv[nt][j];
             }
-            if (g == 0) p.part_lse[slot * kG + col] = lse[nt][j];
+            if (g == 0) *slot_lse<kG>(p, slot, col) = lse[nt][j];
           }
         __threadfence();
         __syncwarp();
@@ -506,7 +514,7 @@ static int launch_t(const DecodeParams& p, const CUtensorMap& kmap, const CUtens
     if (e != cudaSuccess) return static_cast<int>(e);
     configured[dev] = true;
   }
-  paged_decode_kernel<kBF16, NT><<<sm_count, kDecodeWarps * 32, smem, stream>>>(p, kmap, vmap);
+  paged_decode_kernel<kBF16, NT><<<sm_count * kDecodeCtasPerSm, kDecodeWarps * 32, smem, stream>>>(p, kmap, vmap);
   return static_cast<int>(cudaGetLastError());
 }
 
@@ -514,7 +522,7 @@ static int launch_t(const DecodeParams& p, const CUtensorMap& kmap, const CUtens
 
 int64_t ps_decode_partial_slots(int num_seqs, int num_kv_heads, int sm_count) {
   // slot = global warp index + (sequence * kv heads + kv head)
-  return static_cast<int64_t>(sm_count) * ps::kDecodeWarps +
+  return static_cast<int64_t>(sm_count) * ps::kDecodeCtasPerSm * ps::kDecodeWarps +
          static_cast<int64_t>(num_seqs) * num_kv_heads;
 }
 

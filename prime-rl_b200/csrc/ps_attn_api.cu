@@ -82,14 +82,41 @@ int make_page_map(CUtensorMap* map, const void* base, int64_t num_blocks, int bl
   return PS_OK;
 }
 
+// Tensor map over q viewed as [num_tokens][num_q_heads][128] 16-bit elements;
+// box = 64 dims x `group` heads x `tokens` tokens, 128-byte swizzle.  Its smem
+// image is row (token * group + head) of 128 bytes: the K-major SW128 layout.
+int make_q_map(CUtensorMap* map, const void* q, int64_t num_tokens, int num_q_heads,
+               int64_t s_token, int64_t s_head, int group, int tokens) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(PS_ERR_CUDA, "cuTensorMapEncodeTiled unavailable from the driver");
+  cuuint64_t dims[3] = {128, static_cast<cuuint64_t>(num_q_heads), static_cast<cuuint64_t>(num_tokens)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(s_head) * 2, static_cast<cuuint64_t>(s_token) * 2};
+  cuuint32_t box[3] = {64, static_cast<cuuint32_t>(group), static_cast<cuuint32_t>(tokens)};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<void*>(q), dims, strides, box,
+                  estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(PS_ERR_INVALID_ARGUMENT, "q tensor map rejected (%d): strides must be multiples of 16 bytes",
+                static_cast<int>(r));
+  return PS_OK;
+}
+
 bool aligned(const void* p, int bytes) {
   return (reinterpret_cast<uintptr_t>(p) % static_cast<uintptr_t>(bytes)) == 0;
 }
 
 int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
 
+// Decode workspace layout.  Every offset is independent of the call's
+// num_seqs, so one buffer serves calls with any batch size up to the one it
+// was sized for without regions of different calls overlapping:
+//   [0, 256)                 status word (+ reserved)
+//   [256, 256 + C)           counters, kDecodeMaxSeqs * num_kv_heads int32
+//   [256 + C, ...)           partial records, one per split slot:
+//                            kg * 128 fp32 output rows, then kg fp32 LSEs
 struct DecodeWorkspaceLayout {
-  int64_t counters_off, part_lse_off, part_o_off, total;
+  int64_t counters_off, part_off, record_bytes, total;
 };
 
 DecodeWorkspaceLayout decode_layout(int num_seqs, int num_q_heads, int num_kv_heads, int sm_count) {
@@ -97,10 +124,10 @@ DecodeWorkspaceLayout decode_layout(int num_seqs, int num_q_heads, int num_kv_he
   const int kg = group <= 8 ? 8 : 16;
   const int64_t slots = ps_decode_partial_slots(num_seqs, num_kv_heads, sm_count);
   DecodeWorkspaceLayout l;
-  l.counters_off = 256;  // [0, 256): status word and reserved
-  l.part_lse_off = round_up(l.counters_off + static_cast<int64_t>(num_seqs) * num_kv_heads * 4, 256);
-  l.part_o_off = round_up(l.part_lse_off + slots * kg * 4, 256);
-  l.total = round_up(l.part_o_off + slots * kg * 128 * 4, 256);
+  l.counters_off = 256;
+  l.part_off = round_up(l.counters_off + static_cast<int64_t>(ps::kDecodeMaxSeqs) * num_kv_heads * 4, 256);
+  l.record_bytes = static_cast<int64_t>(kg) * 129 * 4;
+  l.total = round_up(l.part_off + slots * l.record_bytes, 256);
   return l;
 }
 
@@ -269,8 +296,7 @@ int ps_paged_decode(const ps_paged_problem* pr, void* workspace, int64_t workspa
   p.scale_log2 = pr->softmax_scale * 1.4426950408889634f;
   p.status = reinterpret_cast<int32_t*>(ws);
   p.counters = reinterpret_cast<int32_t*>(ws + lay.counters_off);
-  p.part_lse = reinterpret_cast<float*>(ws + lay.part_lse_off);
-  p.part_o = reinterpret_cast<float*>(ws + lay.part_o_off);
+  p.part = reinterpret_cast<float*>(ws + lay.part_off);
   p.num_part_slots = ps_decode_partial_slots(pr->num_seqs, pr->num_kv_heads, sms);
   const int e = ps_launch_paged_decode(p, kmap, vmap, pr->dtype == PS_DTYPE_BF16, sms,
                                        static_cast<cudaStream_t>(stream));
@@ -279,10 +305,53 @@ int ps_paged_decode(const ps_paged_problem* pr, void* workspace, int64_t workspa
 }
 
 int ps_chunked_prefill(const ps_paged_problem* pr, void* stream) {
-  (void)stream;
-  const int rc = validate_problem(pr, false);
+  int rc = validate_problem(pr, false);
   if (rc != PS_OK) return rc;
-  return fail(PS_ERR_UNSUPPORTED, "chunked prefill not built yet");
+  if (pr->num_seqs == 0 || pr->num_tokens == 0) return PS_OK;
+  if (pr->num_tokens < 0 || pr->num_tokens > INT32_MAX)
+    return fail(PS_ERR_INVALID_ARGUMENT, "num_tokens out of range");
+  if (pr->num_seqs > ps::kPrefillMaxSeqs)
+    return fail(PS_ERR_UNSUPPORTED, "num_seqs %d > %d per prefill launch", pr->num_seqs,
+                ps::kPrefillMaxSeqs);
+  const int sms = sm_count_current(nullptr);
+  if (sms <= 0) return fail(PS_ERR_CUDA, "no CUDA device");
+  const int group = pr->num_q_heads / pr->num_kv_heads;
+  const int tpt = 128 / group;
+  CUtensorMap qmap, kmap, vmap;
+  rc = make_q_map(&qmap, pr->q, pr->num_tokens, pr->num_q_heads, pr->q_stride_token,
+                  pr->q_stride_head, group, tpt);
+  if (rc != PS_OK) return rc;
+  rc = make_page_map(&kmap, pr->key_cache, pr->num_blocks, pr->block_size, pr->num_kv_heads,
+                     pr->cache_stride_block, pr->cache_stride_slot, pr->cache_stride_head);
+  if (rc != PS_OK) return rc;
+  rc = make_page_map(&vmap, pr->value_cache, pr->num_blocks, pr->block_size, pr->num_kv_heads,
+                     pr->cache_stride_block, pr->cache_stride_slot, pr->cache_stride_head);
+  if (rc != PS_OK) return rc;
+  ps::PrefillParams p;
+  p.block_table = pr->block_table;
+  p.bt_stride = pr->block_table_stride;
+  p.max_blocks_per_seq = pr->max_blocks_per_seq;
+  p.seq_lens = pr->seq_lens;
+  p.qsl = pr->query_start_loc;
+  p.num_seqs = pr->num_seqs;
+  p.out = pr->out;
+  p.o_st = pr->out_stride_token;
+  p.o_sh = pr->out_stride_head;
+  p.lse = pr->lse;
+  p.lse_sh = pr->lse_stride_head;
+  p.lse_st = pr->lse_stride_token;
+  p.num_q_heads = pr->num_q_heads;
+  p.num_kv_heads = pr->num_kv_heads;
+  p.group = group;
+  p.tokens_per_tile = tpt;
+  p.block_size = pr->block_size;
+  p.num_blocks = pr->num_blocks;
+  p.scale_log2 = pr->softmax_scale * 1.4426950408889634f;
+  p.status = pr->status;
+  const int e = ps_launch_chunked_prefill(p, qmap, kmap, vmap, pr->dtype == PS_DTYPE_BF16, sms,
+                                          static_cast<cudaStream_t>(stream));
+  if (e != 0) return cuda_fail(static_cast<cudaError_t>(e), "chunked_prefill launch");
+  return PS_OK;
 }
 
 }  // extern "C"

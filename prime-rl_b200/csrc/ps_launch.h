@@ -46,16 +46,49 @@ struct DecodeParams {
   // workspace
   int32_t* status;
   int32_t* counters;     // [num_seqs * num_kv_heads]
-  float* part_o;         // [slots, group, 128]
-  float* part_lse;       // [slots, group]
+  float* part;           // [slots] records: [kg][128] output rows then [kg] LSEs
   int64_t num_part_slots;
 };
 
 // Static sizing of the decode kernel, shared by the workspace-size query.
-constexpr int kDecodeWarps = 8;      // warps per CTA
-constexpr int kDecodeStages = 3;     // pages in flight per warp
-constexpr int kDecodeMaxSeqs = 4096; // sequences per launch (prefix table in smem)
+// The defaults are the tuned values; the macros exist for tuning sweeps.
+#ifndef PS_DECODE_WARPS
+#define PS_DECODE_WARPS 8
+#endif
+#ifndef PS_DECODE_STAGES
+#define PS_DECODE_STAGES 2
+#endif
+#ifndef PS_DECODE_CTAS_PER_SM
+#define PS_DECODE_CTAS_PER_SM 1
+#endif
+constexpr int kDecodeWarps = PS_DECODE_WARPS;           // warps per CTA
+constexpr int kDecodeStages = PS_DECODE_STAGES;         // pages in flight per warp
+constexpr int kDecodeCtasPerSm = PS_DECODE_CTAS_PER_SM; // persistent CTAs per SM
+constexpr int kDecodeMaxSeqs = 4096;                    // sequences per launch (prefix table in smem)
 
+}  // namespace ps
+
+namespace ps {
+// Chunked-prefill launch parameters.  Strides in elements.
+struct PrefillParams {
+  const int32_t* block_table;
+  int64_t bt_stride;
+  int32_t max_blocks_per_seq;
+  const int32_t* seq_lens;
+  const int32_t* qsl;
+  int32_t num_seqs;
+  void* out;
+  int64_t o_st, o_sh;
+  float* lse;
+  int64_t lse_sh, lse_st;
+  int32_t num_q_heads, num_kv_heads, group;
+  int32_t tokens_per_tile;  // floor(128 / group): tokens of one M tile
+  int32_t block_size;
+  int64_t num_blocks;
+  float scale_log2;
+  int32_t* status;
+};
+constexpr int kPrefillMaxSeqs = 4096;
 }  // namespace ps
 
 int ps_launch_kv_append(const ps::AppendArgs& a, int vec, int sm_count, cudaStream_t stream);
@@ -66,3 +99,7 @@ int ps_launch_paged_decode(const ps::DecodeParams& p, const CUtensorMap& kmap,
                            cudaStream_t stream);
 
 int64_t ps_decode_partial_slots(int num_seqs, int num_kv_heads, int sm_count);
+
+int ps_launch_chunked_prefill(const ps::PrefillParams& p, const CUtensorMap& qmap,
+                              const CUtensorMap& kmap, const CUtensorMap& vmap, int dtype_bf16,
+                              int grid, cudaStream_t stream);

@@ -46,17 +46,24 @@ def needs_build() -> bool:
     return any(f.stat().st_mtime > t for f in _inputs())
 
 
-def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = False) -> Path:
-    if not force and not needs_build():
+def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = False,
+          out: Path | None = None, defines: dict | None = None) -> Path:
+    """Compile the library.  ``out``/``defines`` build a tuning variant
+    (e.g. ``{"PS_DECODE_STAGES": 4}``) at another path without touching the
+    in-tree library."""
+    target = Path(out) if out is not None else LIB_PATH
+    if out is None and not defines and not force and not needs_build():
         return LIB_PATH
     nvcc = nvcc_path()
     srcs = [str(CSRC / s) for s in SOURCES if (CSRC / s).exists()]
-    tmp = LIB_PATH.with_suffix(".so.tmp")
+    tmp = target.with_suffix(".so.tmp")
     cmd = [
         nvcc, *ARCH_FLAGS, "-lineinfo", "-O3", "-std=c++17", "--expt-relaxed-constexpr",
         "-Xcompiler", "-fPIC,-O3", "-shared", "-cudart", "static",
         f"-I{INCLUDE}", f"-I{CSRC}", "-o", str(tmp), *srcs,
     ]
+    for k, v in (defines or {}).items():
+        cmd.insert(1, f"-D{k}={v}")
     if ptxas_verbose:
         cmd.insert(1, "-Xptxas=-v")
     if verbose:
@@ -66,8 +73,8 @@ def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = Fals
         raise RuntimeError(f"nvcc failed ({res.returncode}):\n{res.stdout}\n{res.stderr}")
     if verbose or ptxas_verbose:
         print(res.stdout + res.stderr, file=sys.stderr)
-    os.replace(tmp, LIB_PATH)
-    return LIB_PATH
+    os.replace(tmp, target)
+    return target
 
 
 if __name__ == "__main__":

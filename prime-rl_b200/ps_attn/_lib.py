@@ -80,10 +80,16 @@ class PagedProblem(ctypes.Structure):
         ("block_size", ctypes.c_int32),
         ("dtype", ctypes.c_int32),
         ("softmax_scale", ctypes.c_float),
+        ("num_tokens", ctypes.c_int64),
+        ("status", ctypes.c_void_p),
     ]
 
 
 def lib_path() -> Path:
+    """The in-tree library, or a tuning variant named by ``PS_ATTN_LIB``."""
+    override = os.environ.get("PS_ATTN_LIB")
+    if override:
+        return Path(override).resolve()
     return Path(__file__).resolve().parent / "libps_attn.so"
 
 
@@ -118,7 +124,8 @@ def load(build_if_stale: bool = True):
         if _LIB is not None:
             return _LIB
         path = lib_path()
-        if build_if_stale and os.environ.get("PS_ATTN_NO_BUILD", "0") != "1":
+        if (build_if_stale and os.environ.get("PS_ATTN_NO_BUILD", "0") != "1"
+                and not os.environ.get("PS_ATTN_LIB")):
             from . import _build
 
             if _build.needs_build():

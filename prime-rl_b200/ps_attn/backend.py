@@ -1,0 +1,226 @@
+"""vLLM attention backend over libps_attn.so: the drop-in boundary.
+
+Replaces the FlashAttention backend (``vllm/v1/attention/backends/flash_attn.py``)
+for the decoder path prime-rl's inference server runs.  It keeps the
+FlashAttention surface:
+
+* KV cache ``[2, num_blocks, block_size, num_kv_heads, head_size]`` with the NHD
+  stride order (``flash_attn.py:140-171``);
+* ``forward_includes_kv_cache_update = False``: vLLM calls
+  :meth:`PSAttentionImpl.do_kv_cache_update` (``flash_attn.py:850-883``) and then
+  :meth:`PSAttentionImpl.forward` (``flash_attn.py:667-848``), which writes into
+  the preallocated ``output`` in place;
+* metadata built from ``CommonAttentionMetadata`` (``backend.py:353-379``):
+  ``query_start_loc``, ``seq_lens``, ``block_table``, ``slot_mapping``.
+
+Register it as the CUSTOM backend (select with ``--attention-backend CUSTOM``)
+or as an override of FLASH_ATTN::
+
+    from ps_attn.backend import register
+    register()                      # CUSTOM
+    register(override_flash=True)   # FLASH_ATTN -> PS
+
+Batches are reordered decode-first (``reorder_batch_threshold = 1``); decode
+requests run the split-KV decode kernel, the rest the chunked-prefill kernel.
+Unsupported options (ALiBi, sliding window, soft-cap, sinks, fp8 KV cache,
+encoder attention) raise ``NotImplementedError`` at construction.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import ClassVar
+
+import torch
+
+from vllm.v1.attention.backend import (AttentionBackend, AttentionCGSupport, AttentionImpl,
+                                       AttentionMetadataBuilder, AttentionType,
+                                       CommonAttentionMetadata, MultipleOf)
+from vllm.v1.attention.backends.utils import split_decodes_and_prefills
+
+from . import ops
+
+BACKEND_NAME = "CUSTOM"
+
+
+class PSAttentionBackend(AttentionBackend):
+    supported_dtypes: ClassVar[list[torch.dtype]] = [torch.float16, torch.bfloat16]
+    supported_kv_cache_dtypes: ClassVar[list[str]] = ["auto", "float16", "bfloat16"]
+    forward_includes_kv_cache_update: bool = False
+
+    @staticmethod
+    def get_supported_kernel_block_sizes() -> list[int | MultipleOf]:
+        return [MultipleOf(16)]
+
+    @staticmethod
+    def get_name() -> str:
+        return BACKEND_NAME
+
+    @staticmethod
+    def get_impl_cls() -> type["PSAttentionImpl"]:
+        return PSAttentionImpl
+
+    @staticmethod
+    def get_builder_cls() -> type["PSAttentionMetadataBuilder"]:
+        return PSAttentionMetadataBuilder
+
+    @staticmethod
+    def get_kv_cache_shape(num_blocks: int, block_size: int, num_kv_heads: int, head_size: int,
+                           cache_dtype_str: str = "auto") -> tuple[int, ...]:
+        if block_size % 16 != 0:
+            raise ValueError("Block size must be a multiple of 16.")
+        return (2, num_blocks, block_size, num_kv_heads, head_size)
+
+    @staticmethod
+    def get_kv_cache_stride_order(include_num_layers_dimension: bool = False) -> tuple[int, ...]:
+        if include_num_layers_dimension:
+            # (num_blocks, num_layers, 2, block_size, num_kv_heads, head_size)
+            return (2, 0, 1, 3, 4, 5)
+        return (0, 1, 2, 3, 4)
+
+    @classmethod
+    def supports_head_size(cls, head_size: int) -> bool:
+        return head_size == 128
+
+    @classmethod
+    def supports_attn_type(cls, attn_type: str) -> bool:
+        return attn_type == AttentionType.DECODER
+
+    @classmethod
+    def supports_non_causal(cls) -> bool:
+        return False
+
+    @classmethod
+    def supports_sink(cls) -> bool:
+        return False
+
+    @classmethod
+    def supports_compute_capability(cls, capability) -> bool:
+        return (capability.major, capability.minor) == (10, 0)
+
+
+@dataclass
+class PSAttentionMetadata:
+    num_actual_tokens: int
+    max_query_len: int
+    query_start_loc: torch.Tensor   # int32 [B+1]
+    max_seq_len: int
+    seq_lens: torch.Tensor          # int32 [B]
+    block_table: torch.Tensor       # int32 [B, P]
+    slot_mapping: torch.Tensor      # int64 [T]
+    num_decodes: int
+    num_decode_tokens: int
+    num_prefills: int
+    workspace: ops.DecodeWorkspace
+    causal: bool = True
+
+
+class PSAttentionMetadataBuilder(AttentionMetadataBuilder[PSAttentionMetadata]):
+    # decode batches (q_len 1) replay in full CUDA graphs: fixed-size workspace,
+    # no allocation and no host synchronisation inside the kernels
+    _cudagraph_support: ClassVar[AttentionCGSupport] = AttentionCGSupport.UNIFORM_SINGLE_TOKEN_DECODE
+    reorder_batch_threshold: int | None = 1
+    supports_update_block_table: bool = True
+
+    def __init__(self, kv_cache_spec, layer_names, vllm_config, device):
+        super().__init__(kv_cache_spec, layer_names, vllm_config, device)
+        mc, pc = vllm_config.model_config, vllm_config.parallel_config
+        self.num_heads_q = mc.get_num_attention_heads(pc)
+        self.num_heads_kv = mc.get_num_kv_heads(pc)
+        self.head_size = mc.get_head_size()
+        max_seqs = max(vllm_config.scheduler_config.max_num_seqs,
+                       vllm_config.compilation_config.max_cudagraph_capture_size or 0)
+        self.workspace = ops.DecodeWorkspace(max_seqs, self.num_heads_q, self.num_heads_kv,
+                                             self.head_size, device)
+
+    def build(self, common_prefix_len: int, common_attn_metadata: CommonAttentionMetadata,
+              fast_build: bool = False) -> PSAttentionMetadata:
+        m = common_attn_metadata
+        if common_prefix_len > 0:
+            raise NotImplementedError("cascade attention is not used by the PS backend")
+        if not m.causal:
+            raise NotImplementedError("the PS backend is causal-only")
+        nd, npf, ndt, _ = split_decodes_and_prefills(m, decode_threshold=1)
+        return PSAttentionMetadata(
+            num_actual_tokens=m.num_actual_tokens, max_query_len=m.max_query_len,
+            query_start_loc=m.query_start_loc, max_seq_len=m.max_seq_len, seq_lens=m.seq_lens,
+            block_table=m.block_table_tensor, slot_mapping=m.slot_mapping, num_decodes=nd,
+            num_decode_tokens=ndt, num_prefills=npf, workspace=self.workspace, causal=True)
+
+    def update_block_table(self, metadata: PSAttentionMetadata, blk_table: torch.Tensor,
+                           slot_mapping: torch.Tensor) -> PSAttentionMetadata:
+        import copy
+
+        new = copy.copy(metadata)
+        new.block_table = blk_table
+        new.slot_mapping = slot_mapping
+        return new
+
+    def use_cascade_attention(self, *args, **kwargs) -> bool:
+        return False
+
+
+class PSAttentionImpl(AttentionImpl):
+    can_return_lse_for_decode: bool = True
+
+    def __init__(self, num_heads: int, head_size: int, scale: float, num_kv_heads: int,
+                 alibi_slopes: list[float] | None, sliding_window: int | None,
+                 kv_cache_dtype: str, logits_soft_cap: float | None = None,
+                 attn_type: str = AttentionType.DECODER,
+                 kv_sharing_target_layer_name: str | None = None,
+                 sinks: torch.Tensor | None = None) -> None:
+        if alibi_slopes is not None:
+            raise NotImplementedError("ALiBi is not supported by the PS backend")
+        if sliding_window is not None:
+            raise NotImplementedError("sliding window is not supported by the PS backend")
+        if logits_soft_cap:
+            raise NotImplementedError("logits soft-cap is not supported by the PS backend")
+        if sinks is not None:
+            raise NotImplementedError("attention sinks are not supported by the PS backend")
+        if kv_cache_dtype not in ("auto", "float16", "bfloat16"):
+            raise NotImplementedError(f"kv_cache_dtype {kv_cache_dtype} not supported")
+        if attn_type != AttentionType.DECODER:
+            raise NotImplementedError("the PS backend implements decoder attention only")
+        if head_size != 128:
+            raise NotImplementedError(f"head_size {head_size} not supported (128)")
+        self.num_heads = num_heads
+        self.head_size = head_size
+        self.scale = float(scale)
+        self.num_kv_heads = num_kv_heads
+        self.kv_cache_dtype = kv_cache_dtype
+        self.kv_sharing_target_layer_name = kv_sharing_target_layer_name
+        self.attn_type = attn_type
+        self.num_queries_per_kv = num_heads // num_kv_heads
+
+    def do_kv_cache_update(self, layer, key: torch.Tensor, value: torch.Tensor,
+                           kv_cache: torch.Tensor, slot_mapping: torch.Tensor) -> None:
+        key_cache, value_cache = kv_cache.unbind(0)
+        ops.kv_append(key, value, key_cache, value_cache, slot_mapping)
+
+    def forward(self, layer, query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
+                kv_cache: torch.Tensor, attn_metadata: PSAttentionMetadata, output: torch.Tensor,
+                output_scale: torch.Tensor | None = None,
+                output_block_scale: torch.Tensor | None = None) -> torch.Tensor:
+        if output_scale is not None or output_block_scale is not None:
+            raise NotImplementedError("fused output quantization is not supported")
+        if attn_metadata is None:  # profiling run
+            return output.fill_(0)
+        m = attn_metadata
+        key_cache, value_cache = kv_cache.unbind(0)
+        nd, ndt = m.num_decodes, m.num_decode_tokens
+        if nd > 0:
+            ops.paged_decode(query[:ndt], key_cache, value_cache, m.block_table[:nd],
+                             m.seq_lens[:nd], self.scale, output[:ndt],
+                             query_start_loc=m.query_start_loc[:nd + 1], workspace=m.workspace)
+        if m.num_prefills > 0:
+            ops.chunked_prefill(query[:m.num_actual_tokens], key_cache, value_cache,
+                                m.block_table[nd:], m.seq_lens[nd:], m.query_start_loc[nd:],
+                                self.scale, output[:m.num_actual_tokens])
+        return output
+
+
+def register(override_flash: bool = False) -> None:
+    """Register the PS backend with vLLM's backend registry."""
+    from vllm.v1.attention.backends.registry import AttentionBackendEnum, register_backend
+
+    target = AttentionBackendEnum.FLASH_ATTN if override_flash else AttentionBackendEnum.CUSTOM
+    register_backend(target, f"{PSAttentionBackend.__module__}.{PSAttentionBackend.__qualname__}")

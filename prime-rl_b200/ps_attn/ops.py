@@ -126,7 +126,7 @@ def get_workspace(num_seqs: int, num_q_heads: int, num_kv_heads: int, head_size:
 
 
 def _problem(q, key_cache, value_cache, block_table, seq_lens, query_start_loc,
-             softmax_scale, out, lse) -> _lib.PagedProblem:
+             softmax_scale, out, lse, status=None) -> _lib.PagedProblem:
     _require_cuda(q, key_cache, value_cache, block_table, seq_lens, out, query_start_loc, lse)
     if q.dtype not in (torch.float16, torch.bfloat16):
         raise ValueError(f"attention dtype {q.dtype} unsupported (fp16/bf16)")
@@ -170,6 +170,13 @@ def _problem(q, key_cache, value_cache, block_table, seq_lens, query_start_loc,
     pr.block_size = bs
     pr.dtype = _DTYPES[q.dtype]
     pr.softmax_scale = float(softmax_scale)
+    if out.shape[0] < q.shape[0]:
+        raise ValueError("out has fewer rows than q")
+    pr.num_tokens = q.shape[0]
+    if status is not None:
+        if status.dtype != torch.int32 or not status.is_cuda:
+            raise ValueError("status must be a CUDA int32 tensor")
+        pr.status = status.data_ptr()
     return pr
 
 
@@ -201,11 +208,19 @@ def paged_decode(q: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Te
 def chunked_prefill(q: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Tensor,
                     block_table: torch.Tensor, seq_lens: torch.Tensor,
                     query_start_loc: torch.Tensor, softmax_scale: float, out: torch.Tensor,
-                    lse: torch.Tensor | None = None) -> torch.Tensor:
-    """Causal (bottom-right) varlen attention over the paged cache; any q_len >= 1."""
+                    lse: torch.Tensor | None = None,
+                    status: torch.Tensor | None = None) -> torch.Tensor:
+    """Causal (bottom-right) varlen attention over the paged cache; any q_len >= 1.
+
+    ``query_start_loc`` [B+1] holds absolute row offsets into ``q``/``out``
+    (a slice of a larger batch's offsets is fine).  ``status`` (int32 [1],
+    optional) receives PS_DEV_* bits from device-side checks.
+    """
     lib = _lib.load()
+    if query_start_loc is None:
+        raise ValueError("chunked_prefill needs query_start_loc")
     pr = _problem(q, key_cache, value_cache, block_table, seq_lens, query_start_loc,
-                  softmax_scale, out, lse)
+                  softmax_scale, out, lse, status)
     _lib.check(lib.ps_chunked_prefill(ctypes.byref(pr), _stream_ptr(q.device)))
     return out
 

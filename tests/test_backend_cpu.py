@@ -1,0 +1,113 @@
+"""CPU: the vLLM backend surface (static API, metadata split, forward routing).
+
+Kernels are replaced by recorders here; their numerics are covered by the GPU
+tests.  vLLM's own ABCs and ``split_decodes_and_prefills`` are used as-is.
+"""
+from __future__ import annotations
+
+import pytest
+import torch
+
+vllm_backend = pytest.importorskip("vllm.v1.attention.backend")
+
+from ps_attn import backend as psb  # noqa: E402
+
+
+def test_static_api_matches_flash_attention_surface():
+    from vllm.v1.attention.backends.flash_attn import FlashAttentionBackend
+
+    B = psb.PSAttentionBackend
+    for args in [(256, 16, 8, 128), (1000, 32, 1, 128), (7, 64, 4, 128)]:
+        assert B.get_kv_cache_shape(*args) == FlashAttentionBackend.get_kv_cache_shape(*args)
+    with pytest.raises(ValueError):
+        B.get_kv_cache_shape(10, 24, 8, 128)
+    assert B.get_kv_cache_stride_order() == (0, 1, 2, 3, 4)
+    assert B.forward_includes_kv_cache_update is False
+    assert B.get_impl_cls() is psb.PSAttentionImpl
+    assert B.get_builder_cls() is psb.PSAttentionMetadataBuilder
+    assert B.supports_head_size(128) and not B.supports_head_size(64)
+    assert torch.bfloat16 in B.supported_dtypes and torch.float16 in B.supported_dtypes
+    assert B.get_name() == "CUSTOM"
+
+
+def test_registration_overrides_registry():
+    from vllm.v1.attention.backends.registry import AttentionBackendEnum
+
+    psb.register()
+    assert AttentionBackendEnum.CUSTOM.get_class() is psb.PSAttentionBackend
+    AttentionBackendEnum.CUSTOM.clear_override()
+
+
+@pytest.mark.parametrize("kw", [dict(alibi_slopes=[1.0]), dict(sliding_window=128),
+                                dict(logits_soft_cap=30.0), dict(kv_cache_dtype="fp8")])
+def test_impl_rejects_unsupported_options(kw):
+    base = dict(num_heads=16, head_size=128, scale=0.088, num_kv_heads=8, alibi_slopes=None,
+                sliding_window=None, kv_cache_dtype="auto")
+    base.update(kw)
+    with pytest.raises(NotImplementedError):
+        psb.PSAttentionImpl(**base)
+
+
+def _common(q_lens, seq_lens):
+    from vllm.v1.attention.backend import CommonAttentionMetadata
+
+    qsl = torch.zeros(len(q_lens) + 1, dtype=torch.int32)
+    qsl[1:] = torch.cumsum(torch.tensor(q_lens), 0)
+    T = int(qsl[-1])
+    return CommonAttentionMetadata(
+        query_start_loc=qsl, query_start_loc_cpu=qsl.clone(),
+        seq_lens=torch.tensor(seq_lens, dtype=torch.int32), num_reqs=len(q_lens),
+        num_actual_tokens=T, max_query_len=max(q_lens), max_seq_len=max(seq_lens),
+        block_table_tensor=torch.zeros(len(q_lens), 8, dtype=torch.int32),
+        slot_mapping=torch.arange(T, dtype=torch.int64))
+
+
+def _builder():
+    b = psb.PSAttentionMetadataBuilder.__new__(psb.PSAttentionMetadataBuilder)
+    b.workspace = object()
+    return b
+
+
+def test_builder_splits_decode_first_batches():
+    md = _builder().build(0, _common([1, 1, 1, 7, 30], [10, 20, 30, 40, 90]))
+    assert (md.num_decodes, md.num_decode_tokens, md.num_prefills) == (3, 3, 2)
+    md = _builder().build(0, _common([1, 1], [5, 6]))
+    assert (md.num_decodes, md.num_prefills) == (2, 0)
+    with pytest.raises(NotImplementedError):
+        _builder().build(16, _common([1, 1], [5, 6]))
+
+
+def test_forward_routes_decode_and_prefill(monkeypatch):
+    calls = []
+    monkeypatch.setattr(psb.ops, "paged_decode", lambda *a, **k: calls.append(("decode", a, k)))
+    monkeypatch.setattr(psb.ops, "chunked_prefill", lambda *a, **k: calls.append(("prefill", a, k)))
+    impl = psb.PSAttentionImpl(16, 128, 0.088, 8, None, None, "auto")
+    md = _builder().build(0, _common([1, 1, 5], [10, 20, 40]))
+    T = 7
+    q = torch.zeros(T + 2, 16, 128)  # padded rows beyond num_actual_tokens
+    out = torch.zeros(T + 2, 16, 128)
+    kv = torch.zeros(2, 4, 16, 8, 128)
+    impl.forward(None, q, None, None, kv, md, out)
+    assert [c[0] for c in calls] == ["decode", "prefill"]
+    _, a, k = calls[0]
+    assert a[0].shape[0] == 2 and a[3].shape[0] == 2 and a[4].tolist() == [10, 20]
+    assert k["query_start_loc"].tolist() == [0, 1, 2]
+    _, a, k = calls[1]
+    assert a[0].shape[0] == T and a[3].shape[0] == 1 and a[4].tolist() == [40]
+    assert a[5].tolist() == [2, 7]
+    # profiling run: zero output, no kernels
+    calls.clear()
+    out.fill_(3)
+    impl.forward(None, q, None, None, kv, None, out)
+    assert calls == [] and not out.any()
+
+
+def test_kv_update_unbinds_cache(monkeypatch):
+    seen = {}
+    monkeypatch.setattr(psb.ops, "kv_append",
+                        lambda k, v, kc, vc, s: seen.update(kc=kc, vc=vc, s=s))
+    impl = psb.PSAttentionImpl(16, 128, 0.088, 8, None, None, "auto")
+    kv = torch.zeros(2, 4, 16, 8, 128)
+    impl.do_kv_cache_update(None, torch.zeros(3, 8, 128), torch.zeros(3, 8, 128), kv,
+                            torch.arange(3))
+    assert seen["kc"].data_ptr() == kv[0].data_ptr() and seen["vc"].data_ptr() == kv[1].data_ptr()

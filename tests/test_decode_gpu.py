@@ -212,3 +212,16 @@ def test_decode_full_config2_properties(cuda_device):
         ro, rl = ps_oracle.attention_ref(to_np32(sub.q[r:r + 1]), kb, vb,
                                          softmax_scale=1 / math.sqrt(128))
         assert_attn_close(to_np32(out[r:r + 1]), ro, to_np32(lse[:, r:r + 1]), rl)
+
+
+def test_one_workspace_serves_changing_batch_sizes(cuda_device):
+    """Regions of calls with different num_seqs must not overlap in a shared
+    workspace (counters stay zero between calls)."""
+    ws = ops.DecodeWorkspace(64, 16, 8, 128, cuda_device)
+    for lens in ([100, 200, 31, 64, 65, 1000], [2049] * 40 + [17] * 24, [5, 4000], [3000] * 64):
+        batch = workloads.make_batch([1] * len(lens), lens, 16, 8, seed=len(lens))
+        _, (rout, rlse) = oracle_step(batch)
+        out, lse = run_step(batch.to(cuda_device), workspace=ws)
+        torch.cuda.synchronize()
+        assert ws.status() == 0
+        assert_attn_close(to_np32(out), rout, to_np32(lse), rlse)
