@@ -44,8 +44,19 @@ FALLBACK_HBM_GBS = 6650.0
 CONFIG_NAMES = {
     2: "cfg2: Qwen3-0.6B attn (16q/8kv, d128) bf16 paged decode, B=64, ctx U[1024,4096], block 16",
     3: "cfg3: Qwen3-4B attn (32q/8kv, d128) bf16 GRPO decode, 32x8 seqs, shared 1024-token prefix, gen U[0,8192]",
+    4: "cfg4: Qwen3-4B attn (32q/8kv, d128) bf16 mixed batch: 8 chunked-prefill x 2048 on ctx U[0,4096] + 128 decodes ctx U[512,8192]",
     5: "cfg5: Qwen3-32B attn (64q/8kv, d128) bf16 long-context decode, B=512, ctx log-U[2048,32768], KV-head sharded",
 }
+
+
+def prefill_flops(q_lens, seq_lens, num_q_heads, head_size=128):
+    """4 * Hq * D * (unmasked causal (q, k) pairs) over the q_len > 1 sequences."""
+    pairs = 0
+    for n, L in zip(q_lens, seq_lens):
+        if n > 1:
+            c = L - n
+            pairs += n * c + n * (n + 1) // 2
+    return 4 * num_q_heads * head_size * pairs
 
 
 def measured_peaks():
@@ -54,6 +65,13 @@ def measured_peaks():
         d = json.loads(p.read_text())
         return float(d["hbm_gbs"]), "measured"
     return FALLBACK_HBM_GBS, "fallback"
+
+
+def measured_tensor_peak():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        return float(json.loads(p.read_text())["bf16_tflops"])
+    return 1590.0
 
 
 def profile_traffic(kernel_tag: str):
@@ -173,9 +191,25 @@ def run_ours(args):
     def append():
         ops.kv_append(batch.key, batch.value, kc, vc, batch.slot_mapping)
 
+    mixed = cfg == 4
+    if mixed:
+        qlens = (batch.query_start_loc[1:] - batch.query_start_loc[:-1]).tolist()
+        nd = sum(1 for x in qlens if x == 1)
+        assert all(x == 1 for x in qlens[:nd]), "decode-first batch expected"
+        pf_flops = prefill_flops(qlens, batch.seq_lens.tolist(), hq)
+
     def decode():
-        ops.paged_decode(batch.q, kc, vc, batch.block_table, batch.seq_lens, batch.softmax_scale,
-                         out, lse=lse, query_start_loc=batch.query_start_loc, workspace=ws)
+        if not mixed:
+            ops.paged_decode(batch.q, kc, vc, batch.block_table, batch.seq_lens,
+                             batch.softmax_scale, out, lse=lse,
+                             query_start_loc=batch.query_start_loc, workspace=ws)
+            return
+        ops.paged_decode(batch.q[:nd], kc, vc, batch.block_table[:nd], batch.seq_lens[:nd],
+                         batch.softmax_scale, out[:nd], workspace=ws)
+
+    def prefill():
+        ops.chunked_prefill(batch.q, kc, vc, batch.block_table[nd:], batch.seq_lens[nd:],
+                            batch.query_start_loc[nd:], batch.softmax_scale, out)
 
     def gather():
         import torch.distributed as dist
@@ -191,8 +225,12 @@ def run_ours(args):
             append()
             decode()
         stream.synchronize()
+        if mixed:
+            prefill()
+            stream.synchronize()
         if use_graph:
-            for name, fn in (("append", append), ("decode", decode)):
+            fns = [("append", append), ("decode", decode)] + ([("prefill", prefill)] if mixed else [])
+            for name, fn in fns:
                 g = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(g, stream=stream):
                     fn()
@@ -213,6 +251,13 @@ def run_ours(args):
             decode()
         if ev is not None:
             ev[2].record(stream)
+        if mixed:
+            if use_graph:
+                graphs["prefill"].replay()
+            else:
+                prefill()
+            if ev is not None:
+                ev[3].record(stream)
         if sharded:
             gather()
 
@@ -230,7 +275,7 @@ def run_ours(args):
     if not args.quick:
         sampler.start()
         time.sleep(0.25)
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
@@ -256,18 +301,28 @@ def run_ours(args):
         elapsed_ms = float(t.item())
     append_ms = sum(e[0].elapsed_time(e[1]) for e in evs) / args.steps
     decode_ms = sum(e[1].elapsed_time(e[2]) for e in evs) / args.steps
+    prefill_ms = sum(e[2].elapsed_time(e[3]) for e in evs) / args.steps if mixed else None
     assert ws.status() == 0, f"device status {ws.status():#x}"
 
     # ---- end to end through the public API: host inputs in, host output back ----
-    e2e = None if args.quick else run_e2e(batch, ws, dev, args.steps, world)
+    e2e = None if args.quick else run_e2e(batch, ws, dev, args.steps, world,
+                                          nd=nd if mixed else None,
+                                          replicas=1 if sharded else world)
 
     ms = elapsed_ms / args.steps
-    tokens_per_step = B if not sharded else B  # every rank decodes all B tokens (its heads)
+    tokens_per_step = batch.num_tokens  # every rank produces all tokens (its heads when sharded)
     value = (tokens_per_step * (world if not sharded else 1)) / (ms / 1e3)
     peak, peak_kind = measured_peaks()
-    kv_bytes = batch.logical_tokens * hkv * 128 * 2 * batch.kv_cache.element_size()
-    qo_bytes = B * hq * 128 * 2 * batch.q.element_size()
-    meta_bytes = batch.block_table.numel() * 4 + B * 4 * 2
+    if mixed:
+        dec_tokens = int(batch.seq_lens[:nd].sum())
+        kv_bytes = dec_tokens * hkv * 128 * 2 * batch.kv_cache.element_size()
+        qo_bytes = nd * hq * 128 * 2 * batch.q.element_size()
+        meta_bytes = nd * batch.block_table.shape[1] * 4 + nd * 4 * 2
+    else:
+        kv_tokens = batch.unique_tokens if cfg == 3 else batch.logical_tokens
+        kv_bytes = kv_tokens * hkv * 128 * 2 * batch.kv_cache.element_size()
+        qo_bytes = B * hq * 128 * 2 * batch.q.element_size()
+        meta_bytes = batch.block_table.numel() * 4 + B * 4 * 2
     decode_bytes = kv_bytes + qo_bytes + meta_bytes
     step_bytes = workloads.hbm_bytes(batch)
     achieved = decode_bytes / (decode_ms / 1e3) / 1e9
@@ -288,7 +343,7 @@ def run_ours(args):
         },
         "hbm_gbs_step": round(step_bytes / (ms / 1e3) / 1e9, 1),
         "hbm_frac_of_8tbs_step": round(step_bytes / (ms / 1e3) / 1e9 / NOMINAL_HBM_GBS, 4),
-        "gpu_launches": 2 * args.steps,
+        "gpu_launches": (3 if mixed else 2) * args.steps,
         "roofline": {"kernel": "paged_decode", "bound": "hbm", "achieved": round(achieved, 1),
                      "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
                      "frac": round(achieved / peak, 4),
@@ -296,6 +351,12 @@ def run_ours(args):
                      "bytes_per_launch": decode_bytes, "ms_per_launch": round(decode_ms, 5),
                      "traffic": traffic},
         "append_ms": round(append_ms, 5),
+        "prefill": (None if not mixed else {
+            "kernel": "chunked_prefill", "bound": "tensor", "ms_per_launch": round(prefill_ms, 5),
+            "flops_per_launch": pf_flops,
+            "achieved_tflops": round(pf_flops / (prefill_ms / 1e3) / 1e12, 1),
+            "peak_tflops": measured_tensor_peak(), "peak_kind": "measured bf16 dense (cuBLAS)",
+            "frac": round(pf_flops / (prefill_ms / 1e3) / 1e12 / measured_tensor_peak(), 4)}),
         "e2e": e2e,
         "clocks": clocks,
     }
@@ -311,12 +372,14 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
-def run_e2e(batch, ws, dev, steps, world):
+def run_e2e(batch, ws, dev, steps, world, nd=None, replicas=1):
     """Same step through the public ops with per-step host->device inputs
-    (pinned) and the device->host read of the attention output."""
+    (pinned) and the device->host read of the attention output.  ``nd``:
+    number of leading decode sequences of a mixed batch (the rest prefill)."""
     from ps_attn import ops
 
     B, hq = batch.num_seqs, batch.q.shape[1]
+    T = batch.num_tokens
     host = {k: getattr(batch, k).cpu().pin_memory() for k in
             ("q", "key", "value", "slot_mapping", "seq_lens", "block_table", "query_start_loc")}
     dev_in = {k: torch.empty_like(v, device=dev) for k, v in host.items()}
@@ -330,9 +393,16 @@ def run_e2e(batch, ws, dev, steps, world):
         for k, v in host.items():
             dev_in[k].copy_(v, non_blocking=True)
         ops.kv_append(dev_in["key"], dev_in["value"], kc, vc, dev_in["slot_mapping"])
-        ops.paged_decode(dev_in["q"], kc, vc, dev_in["block_table"], dev_in["seq_lens"],
-                         batch.softmax_scale, out, query_start_loc=dev_in["query_start_loc"],
-                         workspace=ws)
+        if nd is None:
+            ops.paged_decode(dev_in["q"], kc, vc, dev_in["block_table"], dev_in["seq_lens"],
+                             batch.softmax_scale, out, query_start_loc=dev_in["query_start_loc"],
+                             workspace=ws)
+        else:
+            ops.paged_decode(dev_in["q"][:nd], kc, vc, dev_in["block_table"][:nd],
+                             dev_in["seq_lens"][:nd], batch.softmax_scale, out[:nd], workspace=ws)
+            ops.chunked_prefill(dev_in["q"], kc, vc, dev_in["block_table"][nd:],
+                                dev_in["seq_lens"][nd:], dev_in["query_start_loc"][nd:],
+                                batch.softmax_scale, out)
         out_host.copy_(out, non_blocking=True)
 
     n = max(3, min(steps, 200))
@@ -353,7 +423,7 @@ def run_e2e(batch, ws, dev, steps, world):
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    return {"value": round(B * world / (ms / 1e3), 1), "unit": "tokens/s",
+    return {"value": round(T * replicas / (ms / 1e3), 1), "unit": "tokens/s",
             "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
             "ms_per_step": round(ms, 5), "steps": n}
 
@@ -416,7 +486,7 @@ def cpu_baseline(cfg, budget_s=20.0, steps=None, warmup=1):
             return torch.from_numpy(o)[None], None, torch.from_numpy(l)[None]
 
     # sequences: seeded prefix subset sized for the time budget
-    sub = {2: 64, 3: 16, 5: 16}[cfg]
+    sub = {2: 64, 3: 16, 4: 16, 5: 16}[cfg]
     batch = workloads.make_config(cfg, device="cpu", max_seqs=sub)
     seqs = list(range(batch.num_seqs))
     for _ in range(warmup):
@@ -465,7 +535,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=20)
-    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 5])
+    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4, 5])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=15.0)

@@ -154,6 +154,7 @@ __global__ void __launch_bounds__(192, 1)
   const int B = p.num_seqs;
   const int G = p.group;
 
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   // ---- prologue: M tiles per sequence, exclusive prefix ------------------------
   const int per = (B + blockDim.x - 1) / blockDim.x;
   const int b_lo = min(B, tid * per), b_hi = min(B, b_lo + per);
@@ -481,8 +482,18 @@ static int launch_prefill_t(const PrefillParams& p, const CUtensorMap& qmap, con
     if (e != cudaSuccess) return static_cast<int>(e);
     configured[dev] = true;
   }
-  chunked_prefill_kernel<kBF16><<<grid, 192, smem, stream>>>(p, qmap, kmap, vmap);
-  return static_cast<int>(cudaGetLastError());
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(192);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, chunked_prefill_kernel<kBF16>, p, qmap, kmap, vmap);
+  return static_cast<int>(e != cudaSuccess ? e : cudaGetLastError());
 }
 
 }  // namespace ps

@@ -38,6 +38,10 @@ struct VecT<2> {
 template <int VEC>
 __global__ void __launch_bounds__(256) kv_append_kernel(AppendArgs a) {
   using V = typename VecT<VEC>::T;
+  // let a programmatic dependent (the attention kernel) get scheduled now; it
+  // still waits for this grid's completion before reading the cache
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int per_tensor = a.num_heads * a.vecs_per_head;
   const int per_token = 2 * per_tensor;
   for (int64_t t = blockIdx.x; t < a.num_tokens; t += gridDim.x) {

@@ -19,8 +19,14 @@
 //
 // Per warp: a private ring of kDecodeStages page buffers in shared memory, each
 // filled by four TMA tensor loads (K lo/hi 64 dims, V lo/hi) of a 16-token
-// page, 128-byte swizzled, completion on an mbarrier.  Compute per page, with
-// tokens on the MMA M axis and the GQA group on N (m16n8k16):
+// page, 128-byte swizzled, completion on an mbarrier.  The first page of a
+// segment also carries the segment's GQA query rows (cp.async.bulk, one
+// 256-byte row per head) into a padded per-warp slot, so a segment start costs
+// no dependent global load.  Block-table entries are fetched 32 at a time into
+// a warp register and handed out by shuffle.
+//
+// Compute per page, with tokens on the MMA M axis and the GQA group on N
+// (m16n8k16):
 //   S^T[16 tok, 8 heads]   = K[16 tok, 128] . Q^T          (8 mma, K via ldmatrix)
 //   online softmax per head column (exp2 domain; 3 xor-shuffles per max)
 //   P^T -> B fragment      via movmatrix.trans (no shared-memory round trip)
@@ -34,6 +40,7 @@ constexpr int kPageTokens = 16;
 constexpr int kHeadDim = 128;
 constexpr int kBoxBytes = kPageTokens * 64 * 2;  // 2 KB: 16 rows x 128 bytes
 constexpr int kStageBytes = 4 * kBoxBytes;       // K lo, K hi, V lo, V hi
+constexpr int kQRowBytes = kHeadDim * 2 + 16;    // padded query row (conflict-free ldmatrix)
 
 // Split-slot record: kG output rows of 128 fp32, then kG fp32 LSEs.
 template <int kG>
@@ -93,17 +100,89 @@ __device__ __forceinline__ void store_out2(void* out, int64_t idx, float v) {
     reinterpret_cast<__half*>(out)[idx] = __float2half_rn(v);
 }
 
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes,
+                                          uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(gsrc)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void fence_acq_rel_gpu() {
+  asm volatile("fence.acq_rel.gpu;" ::: "memory");
+}
+
 // Merge the n partials of segment (b, h) held in slots [slot0, slot0 + n).
 // FA4 combine: lse_max over splits (0 if all -inf), scale_s =
 // exp2((lse_s - lse_max_cur) * log2e), lse = log(sum) + lse_max, inv = 0 for a
 // zero/NaN sum, O = sum_s scale_s * inv * O_s over splits with scale > 0.
 template <bool kBF16, int NT>
-__device__ void combine_segment(const DecodeParams& p, int b, int h, int64_t slot0, int n,
+__device__ __noinline__ void combine_segment(const DecodeParams& p, int b, int h, int64_t slot0,
+                                             int n,
                                 int lane) {
   constexpr int kG = 8 * NT;
   const int group = p.group;
   const int qrow = p.qsl ? __ldg(p.qsl + b) : b;
   const float kLog2e = 1.4426950408889634f;
+  if (n <= 32) {
+    // fast path: lane k owns split k; the loads of a phase are independent.
+    // Heads in chunks of 4 keep the register footprint small.
+    for (int j0 = 0; j0 < group; j0 += 4) {
+      float w[4], lse_out[4];
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) {
+        const int j = j0 + jj;
+        const float ls = (lane < n && j < group) ? __ldcg(slot_lse<kG>(p, slot0 + lane, j)) : -INFINITY;
+        float mx = ls;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        const float mx_cur = (mx == -INFINITY) ? 0.f : mx;
+        const float e = (lane < n) ? ex2(ls * kLog2e - mx_cur * kLog2e) : 0.f;
+        float sum = e;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        lse_out[jj] = __logf(sum) + mx;
+        const float inv = (sum == 0.f || sum != sum) ? 0.f : 1.f / sum;
+        w[jj] = e * inv;
+      }
+      float4 acc[4];
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) acc[jj] = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int k = 0; k < n; ++k) {
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          const float wk = __shfl_sync(0xffffffffu, w[jj], k);
+          if (j0 + jj < group && wk > 0.f) {
+            const float4 o =
+                __ldcg(reinterpret_cast<const float4*>(slot_o<kG>(p, slot0 + k, j0 + jj)) + lane);
+            acc[jj].x += wk * o.x;
+            acc[jj].y += wk * o.y;
+            acc[jj].z += wk * o.z;
+            acc[jj].w += wk * o.w;
+          }
+        }
+      }
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) {
+        const int j = j0 + jj;
+        if (j < group) {
+          const int qh = h * group + j;
+          const int64_t obase = qrow * p.o_st + qh * p.o_sh + lane * 4;
+          uint2 packed;
+          packed.x = pack2<kBF16>(acc[jj].x, acc[jj].y);
+          packed.y = pack2<kBF16>(acc[jj].z, acc[jj].w);
+          if constexpr (kBF16)
+            *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(p.out) + obase) = packed;
+          else
+            *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(p.out) + obase) = packed;
+          if (lane == 0 && p.lse != nullptr) p.lse[qh * p.lse_sh + qrow * p.lse_st] = lse_out[jj];
+        }
+      }
+    }
+    return;
+  }
+  // general path: any number of splits
   for (int j = 0; j < group; ++j) {
     float mx = -INFINITY;
     for (int k = lane; k < n; k += 32) mx = fmaxf(mx, __ldcg(slot_lse<kG>(p, slot0 + k, j)));
@@ -119,8 +198,7 @@ __device__ void combine_segment(const DecodeParams& p, int b, int h, int64_t slo
     const float inv = (sum == 0.f || sum != sum) ? 0.f : 1.f / sum;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int k = 0; k < n; ++k) {
-      const float w =
-          ex2(__ldcg(slot_lse<kG>(p, slot0 + k, j)) * kLog2e - mx_cur * kLog2e) * inv;
+      const float w = ex2(__ldcg(slot_lse<kG>(p, slot0 + k, j)) * kLog2e - mx_cur * kLog2e) * inv;
       if (w > 0.f) {
         const float4 o = __ldcg(reinterpret_cast<const float4*>(slot_o<kG>(p, slot0 + k, j)) + lane);
         acc.x += w * o.x;
@@ -142,6 +220,18 @@ __device__ void combine_segment(const DecodeParams& p, int b, int h, int64_t slo
   }
 }
 
+template <int NT>
+__host__ __device__ constexpr int decode_qslot_bytes() {
+  return 8 * NT * kQRowBytes;
+}
+
+template <int NT>
+__host__ __device__ constexpr int decode_smem_bytes_before_table() {
+  // stages | per-warp query slots | mbarriers
+  return kDecodeWarps * kDecodeStages * kStageBytes +
+         kDecodeWarps * kDecodeStages * decode_qslot_bytes<NT>() + kDecodeWarps * kDecodeStages * 8;
+}
+
 template <bool kBF16, int NT>
 __global__ void __launch_bounds__(kDecodeWarps * 32, kDecodeCtasPerSm)
     paged_decode_kernel(const __grid_constant__ DecodeParams p,
@@ -153,7 +243,9 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, kDecodeCtasPerSm)
   // 1024-byte alignment for the 128B-swizzled TMA destinations.
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kDecodeWarps * D * kStageBytes);
+  uint8_t* qslots = smem + kDecodeWarps * D * kStageBytes;
+  uint64_t* bars =
+      reinterpret_cast<uint64_t*>(qslots + kDecodeWarps * D * decode_qslot_bytes<NT>());
   int* prefix = reinterpret_cast<int*>(bars + kDecodeWarps * D);
   __shared__ int s_warp_tot[kDecodeWarps];
 
@@ -168,6 +260,13 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, kDecodeCtasPerSm)
     tma_prefetch_desc(&kmap);
     tma_prefetch_desc(&vmap);
   }
+  if (lane == 0) {
+    for (int s = 0; s < D; ++s) mbar_init(&bars[warp * D + s], 1);
+    fence_mbar_init();
+  }
+  // Programmatic dependent launch: everything above overlaps the previous
+  // kernel in the stream; global memory is read only after it completes.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 
   // ---- prologue: pages per sequence and their exclusive prefix sum ----------
   const int per = (B + blockDim.x - 1) / blockDim.x;
@@ -220,11 +319,6 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, kDecodeCtasPerSm)
     run += P;
   }
   if (tid == blockDim.x - 1) prefix[B] = warp_off + incl;  // last thread owns the tail
-  // per-warp barrier init
-  if (lane == 0) {
-    for (int s = 0; s < D; ++s) mbar_init(&bars[warp * D + s], 1);
-    fence_mbar_init();
-  }
   __syncthreads();
   if (tid == 0 && any_bad) set_status(p.status, PS_DEV_BAD_METADATA);
 
@@ -253,26 +347,51 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, kDecodeCtasPerSm)
   const int cnt = static_cast<int>(end - start);
 
   uint8_t* wsm = smem + warp * D * kStageBytes;
+  uint8_t* wq = qslots + warp * D * decode_qslot_bytes<NT>();
   uint64_t* wbar = bars + warp * D;
+  const int group = p.group;
 
-  // ---- producer: issue the TMA loads of one page-head into a stage ----------
-  auto issue = [&](int stage, const Cursor& c) {
+  // ---- producer state: block-table entries cached 32 at a time --------------
+  int bt_b = -1, bt_e0 = 0, bt_reg = 0;
+  int pseg = 0;  // segments started on the producer side
+
+  // Issue the TMA loads of page-head c into `stage` (warp-collective).
+  // `seg_start`: c begins a segment for this warp -> also bring its query rows.
+  auto issue = [&](int stage, const Cursor& c, bool seg_start) {
+    const int e = c.p / sub_per_block;
+    if (c.b != bt_b || e < bt_e0 || e >= bt_e0 + 32) {
+      bt_b = c.b;
+      bt_e0 = e;
+      const int idx = e + lane;
+      bt_reg = idx < p.max_blocks_per_seq ? __ldg(p.block_table + c.b * p.bt_stride + idx) : 0;
+    }
+    int blk = __shfl_sync(0xffffffffu, bt_reg, e - bt_e0);
+    const int sub = c.p - e * sub_per_block;
+    uint8_t* dst = wsm + stage * kStageBytes;
+    uint64_t* bar = wbar + stage;
+    const uint32_t qbytes = seg_start ? static_cast<uint32_t>(group) * (kHeadDim * 2) : 0u;
     if (lane == 0) {
-      const int bidx = c.p / sub_per_block;
-      const int sub = c.p - bidx * sub_per_block;
-      int blk = __ldg(p.block_table + c.b * p.bt_stride + bidx);
       if (blk < 0 || blk >= p.num_blocks) {
         set_status(p.status, PS_DEV_BLOCK_OUT_OF_RANGE);
         blk = 0;
       }
-      uint8_t* dst = wsm + stage * kStageBytes;
-      uint64_t* bar = wbar + stage;
-      mbar_arrive_expect_tx(bar, kStageBytes);
+      mbar_arrive_expect_tx(bar, kStageBytes + qbytes);
       const int tok = sub * kPageTokens;
       tma_load_4d(dst + 0 * kBoxBytes, &kmap, bar, 0, c.h, tok, blk);
       tma_load_4d(dst + 1 * kBoxBytes, &kmap, bar, 64, c.h, tok, blk);
       tma_load_4d(dst + 2 * kBoxBytes, &vmap, bar, 0, c.h, tok, blk);
       tma_load_4d(dst + 3 * kBoxBytes, &vmap, bar, 64, c.h, tok, blk);
+    }
+    if (seg_start) {
+      __syncwarp();  // expect_tx is armed before the row copies complete_tx
+      if (lane < group) {
+        const int qrow = p.qsl ? __ldg(p.qsl + c.b) : c.b;
+        const uint16_t* src = reinterpret_cast<const uint16_t*>(p.q) + qrow * p.q_st +
+                              (c.h * group + lane) * p.q_sh;
+        bulk_load(wq + (pseg % D) * decode_qslot_bytes<NT>() + lane * kQRowBytes, src,
+                  kHeadDim * 2, bar);
+      }
+      ++pseg;
     }
   };
 
@@ -283,7 +402,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, kDecodeCtasPerSm)
   const int npre = min(cnt, D);
   for (int k = 0; k < npre; ++k) {
     if (k > 0) cursor_next(pc, cprefix, Hkv);
-    issue(k, pc);
+    issue(k, pc, k == 0 || pc.p == 0);
   }
   int issued = npre;
 
@@ -299,31 +418,10 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, kDecodeCtasPerSm)
   uint32_t qf[NT][8][2];
   float o[NT][8][4];
   float m[NT][2], l[NT][2];
-  for (int k = 0; k < cnt; ++k) {
-    // ---- segment start: load Q fragment, reset state ------------------------
-    if (k == 0 || cc.p == 0) {
-      const int qrow = p.qsl ? __ldg(p.qsl + cc.b) : cc.b;
-      const uint16_t* qb = reinterpret_cast<const uint16_t*>(p.q) + qrow * p.q_st;
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        const int hl = nt * 8 + g;
-        const bool ok = hl < p.group;
-        const uint16_t* qh = qb + (cc.h * p.group + (ok ? hl : 0)) * p.q_sh;
-#pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {
-          qf[nt][ks][0] = ok ? __ldg(reinterpret_cast<const uint32_t*>(qh + ks * 16 + 2 * t)) : 0u;
-          qf[nt][ks][1] =
-              ok ? __ldg(reinterpret_cast<const uint32_t*>(qh + ks * 16 + 8 + 2 * t)) : 0u;
-        }
-#pragma unroll
-        for (int mi = 0; mi < 8; ++mi)
-#pragma unroll
-          for (int c = 0; c < 4; ++c) o[nt][mi][c] = 0.f;
-        m[nt][0] = m[nt][1] = -INFINITY;
-        l[nt][0] = l[nt][1] = 0.f;
-      }
-    }
+  int L = 0;
+  int cseg = 0;  // segments started on the consumer side
 
+  for (int k = 0; k < cnt; ++k) {
     const int stage = k % D;
     const uint32_t phase = static_cast<uint32_t>((k / D) & 1);
     uint8_t* st = wsm + stage * kStageBytes;
@@ -335,7 +433,34 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, kDecodeCtasPerSm)
       return;
     }
 
-    const int L = __ldg(p.seq_lens + cc.b);
+    // ---- segment start: query fragments from the slot, reset state ------------
+    if (k == 0 || cc.p == 0) {
+      L = __ldg(p.seq_lens + cc.b);
+      const uint32_t qbase = smem_u32(wq + (cseg % D) * decode_qslot_bytes<NT>());
+      ++cseg;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        const bool ok = nt * 8 + g < group;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          // matrices: heads nt*8..+7 x dims 32i + 8*(lane/8) .. +7
+          const uint32_t addr = qbase + (nt * 8 + (lane & 7)) * kQRowBytes + (32 * i + 8 * k_mi) * 2;
+          uint32_t r0, r1, r2, r3;
+          ldsm_x4(addr, r0, r1, r2, r3);
+          qf[nt][2 * i][0] = ok ? r0 : 0u;
+          qf[nt][2 * i][1] = ok ? r1 : 0u;
+          qf[nt][2 * i + 1][0] = ok ? r2 : 0u;
+          qf[nt][2 * i + 1][1] = ok ? r3 : 0u;
+        }
+#pragma unroll
+        for (int mi = 0; mi < 8; ++mi)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) o[nt][mi][c] = 0.f;
+        m[nt][0] = m[nt][1] = -INFINITY;
+        l[nt][0] = l[nt][1] = 0.f;
+      }
+    }
+
     const int valid = min(kPageTokens, L - cc.p * kPageTokens);
 
     // ---- S^T = K Q^T -----------------------------------------------------------
@@ -420,7 +545,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, kDecodeCtasPerSm)
     if (issued < cnt) {
       fence_proxy_async_smem();
       cursor_next(pc, cprefix, Hkv);
-      issue(stage, pc);
+      issue(stage, pc, pc.p == 0);
       ++issued;
     }
 
@@ -449,8 +574,8 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, kDecodeCtasPerSm)
 #pragma unroll
           for (int j = 0; j < 2; ++j) {
             const int col = nt * 8 + 2 * t + j;
-            if (col < p.group) {
-              const int qh = h * p.group + col;
+            if (col < group) {
+              const int qh = h * group + col;
               const int64_t ob = qrow * p.o_st + qh * p.o_sh;
 #pragma unroll
               for (int mi = 0; mi < 8; ++mi) {
@@ -475,16 +600,17 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, kDecodeCtasPerSm)
             }
             if (g == 0) *slot_lse<kG>(p, slot, col) = lse[nt][j];
           }
-        __threadfence();
+        // release: the warp's partial is visible (gpu scope) before the count
         __syncwarp();
         int last = 0;
         if (lane == 0) {
+          fence_acq_rel_gpu();
           const int old = atomicAdd(p.counters + b * Hkv + h, 1);
           last = (old == nsplit - 1);
+          if (last) fence_acq_rel_gpu();  // acquire the other splits' partials
         }
         last = __shfl_sync(0xffffffffu, last, 0);
         if (last) {
-          __threadfence();
           combine_segment<kBF16, NT>(p, b, h, first_w + static_cast<int64_t>(b) * Hkv + h, nsplit, lane);
           if (lane == 0) p.counters[b * Hkv + h] = 0;
         }
@@ -497,25 +623,30 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, kDecodeCtasPerSm)
 template <bool kBF16, int NT>
 static int launch_t(const DecodeParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap,
                     int sm_count, cudaStream_t stream) {
-  const size_t smem = 1024 + static_cast<size_t>(kDecodeWarps) * kDecodeStages * kStageBytes +
-                      static_cast<size_t>(kDecodeWarps) * kDecodeStages * 8 +
-                      static_cast<size_t>(p.num_seqs + 1) * 4;
+  const size_t smem = 1024 + decode_smem_bytes_before_table<NT>() + static_cast<size_t>(p.num_seqs + 1) * 4;
   // the attribute is per function and per device
   static bool configured[64] = {false};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev >= 64) return static_cast<int>(cudaErrorInvalidDevice);
   if (!configured[dev]) {
-    const cudaError_t e = cudaFuncSetAttribute(paged_decode_kernel<kBF16, NT>,
-                                               cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               static_cast<int>(1024 + kDecodeWarps * kDecodeStages *
-                                                                           kStageBytes +
-                                                                kDecodeWarps * kDecodeStages * 8 +
-                                                                (kDecodeMaxSeqs + 1) * 4));
+    const cudaError_t e = cudaFuncSetAttribute(
+        paged_decode_kernel<kBF16, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        static_cast<int>(1024 + decode_smem_bytes_before_table<NT>() + (kDecodeMaxSeqs + 1) * 4));
     if (e != cudaSuccess) return static_cast<int>(e);
     configured[dev] = true;
   }
-  paged_decode_kernel<kBF16, NT><<<sm_count * kDecodeCtasPerSm, kDecodeWarps * 32, smem, stream>>>(p, kmap, vmap);
-  return static_cast<int>(cudaGetLastError());
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(sm_count * kDecodeCtasPerSm);
+  cfg.blockDim = dim3(kDecodeWarps * 32);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, paged_decode_kernel<kBF16, NT>, p, kmap, vmap);
+  return static_cast<int>(e != cudaSuccess ? e : cudaGetLastError());
 }
 
 }  // namespace ps
