@@ -220,47 +220,60 @@ __global__ void __launch_bounds__(192, 1)
 
   if (warp == 0) {
     // =========================== TMA producer ===========================
-    if (lane == 0) {
-      int t = 0, uit = 0;
-      for (int u = blockIdx.x; u < total_units && !*abort_flag; u += gridDim.x, ++uit) {
-        const UnitInfo ui = unit_info(p, prefix, u);
-        if (!pwait(bars.q_empty, (uit & 1) ^ 1, abort_flag, p.status)) break;
+    // Warp-wide: block-table entries are fetched 32 at a time into a register
+    // and handed out by shuffle; lane i issues page i of a KV tile.
+    int t = 0, uit = 0;
+    int bt_b = -1, bt_e0 = 0, bt_reg = 0;
+    for (int u = blockIdx.x; u < total_units && !*abort_flag; u += gridDim.x, ++uit) {
+      const UnitInfo ui = unit_info(p, prefix, u);
+      if (!pwait(bars.q_empty, (uit & 1) ^ 1, abort_flag, p.status)) break;
+      if (lane == 0) {
         // the box always spans tokens_per_tile tokens (rows past the sequence are
         // the next sequence's or zero fill) and TMA delivers the whole box
         mbar_arrive_expect_tx(bars.q_full, p.tokens_per_tile * G * 2 * 128);
         tma_load_3d(sQ, &qmap, bars.q_full, 0, ui.h * G, ui.qrow0 + ui.t0);
         tma_load_3d(sQ + kRegionBytes, &qmap, bars.q_full, 64, ui.h * G, ui.qrow0 + ui.t0);
-        const int npages_needed = (ui.kv_end + 15) / 16;
-        const int* bt = p.block_table + static_cast<int64_t>(ui.b) * p.bt_stride;
-        bool ok = true;
-        for (int j = 0; j < ui.ntiles; ++j, ++t) {
-          const int s = t % kKvStages;
-          const uint32_t n = static_cast<uint32_t>(t / kKvStages);
-          if (!pwait(bars.kvempty + s, (n & 1) ^ 1, abort_flag, p.status)) { ok = false; break; }
-          const int pg0 = j * 8;
-          const int npg = min(8, npages_needed - pg0);
+      }
+      const int npages_needed = (ui.kv_end + 15) / 16;
+      const int* bt = p.block_table + static_cast<int64_t>(ui.b) * p.bt_stride;
+      bool ok = true;
+      for (int j = 0; j < ui.ntiles; ++j, ++t) {
+        const int s = t % kKvStages;
+        const uint32_t n = static_cast<uint32_t>(t / kKvStages);
+        const int pg0 = j * 8;
+        const int npg = min(8, npages_needed - pg0);
+        // block-table window covering this tile's entries
+        const int e_first = pg0 / spb, e_last = (pg0 + npg - 1) / spb;
+        if (ui.b != bt_b || e_first < bt_e0 || e_last >= bt_e0 + 32) {
+          bt_b = ui.b;
+          bt_e0 = e_first;
+          const int idx = e_first + lane;
+          bt_reg = idx < p.max_blocks_per_seq ? __ldg(bt + idx) : -1;
+        }
+        const int pg = pg0 + (lane < npg ? lane : 0);
+        int blk = __shfl_sync(0xffffffffu, bt_reg, pg / spb - bt_e0);
+        if (!pwait(bars.kvempty + s, (n & 1) ^ 1, abort_flag, p.status)) { ok = false; break; }
+        uint8_t* kd = sK + s * kTileBytes;
+        uint8_t* vd = sV + s * kTileBytes;
+        if (lane == 0) {
           const uint32_t bytes = static_cast<uint32_t>(npg) * 2 * 2048;
-          uint8_t* kd = sK + s * kTileBytes;
-          uint8_t* vd = sV + s * kTileBytes;
           mbar_arrive_expect_tx(bars.kfull + s, bytes);
           mbar_arrive_expect_tx(bars.vfull + s, bytes);
-          for (int i = 0; i < npg; ++i) {
-            const int pg = pg0 + i;
-            const int bi = pg / spb;
-            int blk = bi < p.max_blocks_per_seq ? __ldg(bt + bi) : -1;
-            if (blk < 0 || blk >= p.num_blocks) {
-              set_status(p.status, PS_DEV_BLOCK_OUT_OF_RANGE);
-              blk = 0;
-            }
-            const int tok = (pg % spb) * 16;
-            tma_load_4d(kd + i * 2048, &kmap, bars.kfull + s, 0, ui.h, tok, blk);
-            tma_load_4d(kd + kRegionBytes + i * 2048, &kmap, bars.kfull + s, 64, ui.h, tok, blk);
-            tma_load_4d(vd + i * 2048, &vmap, bars.vfull + s, 0, ui.h, tok, blk);
-            tma_load_4d(vd + kRegionBytes + i * 2048, &vmap, bars.vfull + s, 64, ui.h, tok, blk);
-          }
         }
-        if (!ok) break;
+        __syncwarp();  // both barriers armed before any copy completes
+        if (lane < npg) {
+          if (blk < 0 || blk >= p.num_blocks) {
+            set_status(p.status, PS_DEV_BLOCK_OUT_OF_RANGE);
+            blk = 0;
+          }
+          const int tok = (pg % spb) * 16;
+          tma_load_4d(kd + lane * 2048, &kmap, bars.kfull + s, 0, ui.h, tok, blk);
+          tma_load_4d(kd + kRegionBytes + lane * 2048, &kmap, bars.kfull + s, 64, ui.h, tok, blk);
+          tma_load_4d(vd + lane * 2048, &vmap, bars.vfull + s, 0, ui.h, tok, blk);
+          tma_load_4d(vd + kRegionBytes + lane * 2048, &vmap, bars.vfull + s, 64, ui.h, tok, blk);
+        }
       }
+      if (!ok) break;
     }
   } else if (warp == 1) {
     // =========================== MMA issuer ===========================
