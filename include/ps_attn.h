@@ -138,6 +138,26 @@ int ps_paged_decode(const ps_paged_problem* problem, void* workspace, int64_t wo
                     void* stream);
 
 /*
+ * Paged decode with library-owned scratch memory.  No counterpart in the
+ * reference: it exists for callers that may not allocate device memory, such
+ * as a backend running inside an inference engine that reserved the GPU's
+ * memory up front (vLLM sizes its KV cache to most of HBM at start-up) and
+ * hands none of it to plugins.  Same semantics and outputs as
+ * ps_paged_decode, but no workspace argument: the split counters and partials
+ * live in a 16 MiB array inside the library, of which every GPU that loads it
+ * holds one copy until the process exits.  Problems whose
+ * ps_paged_decode_workspace_size exceeds 16 MiB are rejected with
+ * PS_ERR_WORKSPACE (with 8 KV heads, GQA group <= 8 and 148 SMs: at most 356
+ * sequences per call).  Allocates nothing (no cudaMalloc / cudaFree).  The
+ * first call on a device looks up the array's device address for that device;
+ * make that first call before any stream capture.  All calls share the one
+ * array: calls that can overlap on the GPU (other streams, other threads)
+ * race and must be serialised by the caller.  problem->status (nullable)
+ * receives this call's PS_DEV_* bits.
+ */
+int ps_paged_decode_static_scratch(const ps_paged_problem* problem, void* stream);
+
+/*
  * Chunked prefill: any q_len >= 1 per sequence, causal bottom-right, over the
  * same paged cache.  Replaces flash_attn_varlen_func for max_seqlen_q > 1
  * (flash_attn.py:796-817 -> cute/flash_fwd_sm100.py).  Tensor-core path:

@@ -172,6 +172,8 @@ int validate_problem(const ps_paged_problem* pr, bool decode) {
 
 }  // namespace
 
+int ps_set_last_error(int code, const char* msg) { return fail(code, "%s", msg); }
+
 extern "C" {
 
 int ps_abi_version(void) { return PS_ATTN_ABI_VERSION; }

@@ -91,6 +91,9 @@ struct PrefillParams {
 constexpr int kPrefillMaxSeqs = 4096;
 }  // namespace ps
 
+// Sets the calling thread's ps_last_error() message; returns `code`.
+int ps_set_last_error(int code, const char* msg);
+
 int ps_launch_kv_append(const ps::AppendArgs& a, int vec, int sm_count, cudaStream_t stream);
 
 // Returns a cudaError_t value.

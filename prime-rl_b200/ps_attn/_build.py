@@ -18,7 +18,8 @@ REPO = PKG_DIR.parent.parent
 INCLUDE = REPO / "include"
 LIB_PATH = PKG_DIR / "libps_attn.so"
 
-SOURCES = ["ps_attn_api.cu", "kv_append.cu", "paged_decode.cu", "chunked_prefill.cu"]
+SOURCES = ["ps_attn_api.cu", "kv_append.cu", "paged_decode.cu", "chunked_prefill.cu",
+           "paged_decode_static.cu"]
 HEADERS = ["ps_common.cuh", "ps_launch.h", "tcgen05.cuh"]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]

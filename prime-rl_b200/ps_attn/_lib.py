@@ -38,6 +38,7 @@ EXPORTED_SYMBOLS = (
     "ps_paged_decode_workspace_size",
     "ps_paged_decode",
     "ps_chunked_prefill",
+    "ps_paged_decode_static_scratch",
 )
 
 
@@ -113,6 +114,8 @@ def _declare(lib):
     lib.ps_paged_decode.argtypes = [c.POINTER(PagedProblem), c.c_void_p, c.c_int64, c.c_void_p]
     lib.ps_chunked_prefill.restype = c.c_int
     lib.ps_chunked_prefill.argtypes = [c.POINTER(PagedProblem), c.c_void_p]
+    lib.ps_paged_decode_static_scratch.restype = c.c_int
+    lib.ps_paged_decode_static_scratch.argtypes = [c.POINTER(PagedProblem), c.c_void_p]
 
 
 def load(build_if_stale: bool = True):
