@@ -113,6 +113,15 @@ __device__ __forceinline__ void fence_acq_rel_gpu() {
   asm volatile("fence.acq_rel.gpu;" ::: "memory");
 }
 
+// Atomic add with release semantics at gpu scope: the caller's earlier writes
+// (and, cumulatively, its warp's, ordered by __syncwarp) are visible before
+// the new count is.
+__device__ __forceinline__ int atomic_add_release_gpu(int* addr, int v) {
+  int old;
+  asm volatile("atom.add.release.gpu.global.s32 %0, [%1], %2;" : "=r"(old) : "l"(addr), "r"(v) : "memory");
+  return old;
+}
+
 // Merge the n partials of segment (b, h) held in slots [slot0, slot0 + n).
 // FA4 combine: lse_max over splits (0 if all -inf), scale_s =
 // exp2((lse_s - lse_max_cur) * log2e), lse = log(sum) + lse_max, inv = 0 for a
@@ -149,11 +158,14 @@ __device__ __noinline__ void combine_segment(const DecodeParams& p, int b, int h
       float4 acc[4];
 #pragma unroll
       for (int jj = 0; jj < 4; ++jj) acc[jj] = make_float4(0.f, 0.f, 0.f, 0.f);
+      // An empty split has weight 0 and an all-zero partial, so every split
+      // can be accumulated unconditionally; the loads then do not wait for
+      // the weights.
       for (int k = 0; k < n; ++k) {
 #pragma unroll
         for (int jj = 0; jj < 4; ++jj) {
           const float wk = __shfl_sync(0xffffffffu, w[jj], k);
-          if (j0 + jj < group && wk > 0.f) {
+          if (j0 + jj < group) {
             const float4 o =
                 __ldcg(reinterpret_cast<const float4*>(slot_o<kG>(p, slot0 + k, j0 + jj)) + lane);
             acc[jj].x += wk * o.x;
@@ -604,8 +616,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, kDecodeCtasPerSm)
         __syncwarp();
         int last = 0;
         if (lane == 0) {
-          fence_acq_rel_gpu();
-          const int old = atomicAdd(p.counters + b * Hkv + h, 1);
+          const int old = atomic_add_release_gpu(p.counters + b * Hkv + h, 1);
           last = (old == nsplit - 1);
           if (last) fence_acq_rel_gpu();  // acquire the other splits' partials
         }
