@@ -39,16 +39,38 @@ constexpr int kTileBytes = 2 * kRegionBytes;  // both 64-dim halves
 constexpr int kKvStages = 2;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
+// Of every 8 exponentials in a softmax row, this many are evaluated on the FMA
+// pipe (exp2_fma) instead of the MUFU unit, which a 128x128 tile otherwise
+// saturates before the tensor core.  Tuned value; the macro exists for sweeps.
+#ifndef PS_PREFILL_EMU_PER8
+#define PS_PREFILL_EMU_PER8 0
+#endif
+
+// 2^x on the FMA/ALU pipes: 2^x = 2^n * 2^f with n = round(x) and
+// f = x - n in [-0.5, 0.5]; 2^f by a cubic fitted for minimum relative error
+// on that interval (Lawson-weighted least squares; max relative error 7.5e-5,
+// far below the 2^-9 rounding of the bf16 P it feeds).  n is read from the
+// mantissa of x + 1.5*2^23 and added to the exponent field.  x < -126
+// (including -inf) returns 0, as ex2 of a masked score must.
+__device__ __forceinline__ float exp2_fma(float x) {
+  const float xc = fmaxf(x, -127.f);
+  const float t = xc + 12582912.f;
+  const float f = xc - (t - 12582912.f);
+  const float p = fmaf(fmaf(fmaf(0.05517132f, f, 0.24261054f), f, 0.69326097f), f, 0.99992812f);
+  const int n = __float_as_int(t) - 0x4B400000;
+  const float r = __int_as_float(__float_as_int(p) + (n << 23));
+  return x < -126.f ? 0.f : r;
+}
+
 struct PrefillSmem {
   // all tiles 1024-byte aligned (offsets from the aligned base)
   static constexpr int q_off = 0;
   static constexpr int k_off = q_off + kTileBytes;
   static constexpr int v_off = k_off + kKvStages * kTileBytes;
-  static constexpr int p_off = v_off + kKvStages * kTileBytes;
-  static constexpr int bar_off = p_off + kTileBytes;
+  static constexpr int bar_off = v_off + kKvStages * kTileBytes;
   // barriers
   static constexpr int n_bars = 2 /*q*/ + 3 * kKvStages /*kfull vfull kvempty*/ +
-                                2 * 2 /*s_full s_empty*/ + 2 /*p_full pv_done*/;
+                                2 /*s_full*/ + 2 /*p_full pv_done*/;
   static constexpr int misc_off = bar_off + n_bars * 8;  // tmem base, abort flag
   static constexpr int table_off = misc_off + 16;
   static constexpr int bytes_before_table = table_off;
@@ -61,7 +83,6 @@ struct PBars {
   uint64_t* vfull;   // [kKvStages]
   uint64_t* kvempty; // [kKvStages]
   uint64_t* s_full;  // [2]
-  uint64_t* s_empty; // [2]
   uint64_t* p_full;
   uint64_t* pv_done;
 };
@@ -140,9 +161,8 @@ __global__ void __launch_bounds__(192, 1)
   bars.vfull = bar + 2 + kKvStages;
   bars.kvempty = bar + 2 + 2 * kKvStages;
   bars.s_full = bar + 2 + 3 * kKvStages;
-  bars.s_empty = bar + 4 + 3 * kKvStages;
-  bars.p_full = bar + 6 + 3 * kKvStages;
-  bars.pv_done = bar + 7 + 3 * kKvStages;
+  bars.p_full = bar + 4 + 3 * kKvStages;
+  bars.pv_done = bar + 5 + 3 * kKvStages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::misc_off);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::misc_off + 4);
   int* prefix = reinterpret_cast<int*>(smem + L::table_off);
@@ -181,7 +201,6 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(bars.s_full + s, 1);
-      mbar_init(bars.s_empty + s, 4);
     }
     mbar_init(bars.p_full, 4);
     mbar_init(bars.pv_done, 1);
@@ -215,7 +234,6 @@ __global__ void __launch_bounds__(192, 1)
   uint8_t* sQ = smem + L::q_off;
   uint8_t* sK = smem + L::k_off;
   uint8_t* sV = smem + L::v_off;
-  uint8_t* sP = smem + L::p_off;
   const int spb = p.block_size / 16;
 
   if (warp == 0) {
@@ -280,8 +298,7 @@ __global__ void __launch_bounds__(192, 1)
     if (lane == 0) {
       const uint32_t idesc_qk = tc::idesc_f16(kBF16, 128, 128, false, false);
       const uint32_t idesc_pv = tc::idesc_f16(kBF16, 128, 128, false, true);
-      const uint32_t q_addr = smem_u32(sQ), k_addr = smem_u32(sK), v_addr = smem_u32(sV),
-                     p_addr = smem_u32(sP);
+      const uint32_t q_addr = smem_u32(sQ), k_addr = smem_u32(sK), v_addr = smem_u32(sV);
       int t = 0, uit = 0;
       int pend_t = -1, pend_j = 0;  // tile whose PV is still to be issued
       auto issue_pv = [&](int tt, int jj) -> bool {
@@ -290,11 +307,13 @@ __global__ void __launch_bounds__(192, 1)
         if (!pwait(bars.vfull + s, static_cast<uint32_t>((tt / kKvStages) & 1), abort_flag, p.status))
           return false;
         tc::fence_after_sync();
+        // A = P, written by the softmax warps as packed 16-bit pairs over the
+        // first 64 columns of this tile's S buffer (keys 16kk.. = columns 8kk..)
+        const uint32_t p_tmem = tmem + (tt & 1) * 128;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          const uint64_t ad = tc::sw128_desc(p_addr + (kk >> 2) * kRegionBytes + (kk & 3) * 32, 16, 1024);
           const uint64_t bd = tc::sw128_desc(v_addr + s * kTileBytes + kk * 2048, kRegionBytes, 1024);
-          tc::mma_f16_ss(tmem + 256, ad, bd, idesc_pv, (jj > 0 || kk > 0) ? 1u : 0u);
+          tc::mma_f16_ts(tmem + 256, p_tmem + kk * 8, bd, idesc_pv, (jj > 0 || kk > 0) ? 1u : 0u);
         }
         tc::commit(bars.pv_done);
         tc::commit(bars.kvempty + s);
@@ -310,10 +329,8 @@ __global__ void __launch_bounds__(192, 1)
           const int sb = t & 1;
           const uint32_t n = static_cast<uint32_t>(t / kKvStages);
           if (!pwait(bars.kfull + s, n & 1, abort_flag, p.status)) { ok = false; break; }
-          if (!pwait(bars.s_empty + sb, (static_cast<uint32_t>(t >> 1) & 1) ^ 1, abort_flag, p.status)) {
-            ok = false;
-            break;
-          }
+          // S buffer sb last held S/P of tile t-2, whose PV was issued before
+          // this MMA; tcgen05 MMAs of one thread execute in issue order.
           tc::fence_after_sync();
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
@@ -354,49 +371,58 @@ __global__ void __launch_bounds__(192, 1)
         if (!pwait(bars.s_full + sb, static_cast<uint32_t>(t >> 1) & 1, abort_flag, p.status)) { ok = false; break; }
         tc::fence_after_sync();
         float s[128];
+        {
+          uint32_t r[4][32];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t r[32];
-          tc::ld_32x32b_x32(lane_addr + sb * 128 + c * 32, r);
+          for (int c = 0; c < 4; ++c) tc::ld_32x32b_x32(lane_addr + sb * 128 + c * 32, r[c]);
           tc::wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(r[i]);
-        }
-        tc::fence_before_sync();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bars.s_empty + sb);
-        // scale + causal mask, row max
-        const int key0 = j * kKeys;
-        float mx = -INFINITY;
+          for (int c = 0; c < 4; ++c)
 #pragma unroll
-        for (int c = 0; c < 128; ++c) {
-          const float v = (key0 + c <= limit) ? s[c] * sl2 : -INFINITY;
-          s[c] = v;
-          mx = fmaxf(mx, v);
+            for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(r[c][i]);
         }
+        // causal mask only on tiles that reach past some row's last visible key
+        const int key0 = j * kKeys;
+        if (!__all_sync(0xffffffffu, key0 + kKeys - 1 <= limit)) {
+#pragma unroll
+          for (int c = 0; c < 128; ++c) s[c] = (key0 + c <= limit) ? s[c] : -INFINITY;
+        }
+        float mxp[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) mxp[i] = s[i];
+#pragma unroll
+        for (int c = 8; c < 128; ++c) mxp[c & 7] = fmaxf(mxp[c & 7], s[c]);
+        float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
+                         fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
+        mx *= sl2;  // scale > 0: max of scaled = scaled max
         float m_new = m_run, factor = 1.f;
         if (mx > m_run + kRescaleThreshold || (m_run == -INFINITY && mx > -INFINITY)) {
           m_new = mx;
           factor = ex2(m_run - m_new);  // 0 when m_run == -inf
         }
-        float rs = 0.f;
+        const float neg_m = (m_new == -INFINITY) ? 0.f : -m_new;  // fully masked row: all p = 0
+        float rsp[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
         uint32_t pk[64];
 #pragma unroll
         for (int c = 0; c < 64; ++c) {
-          const float p0 = (m_new == -INFINITY) ? 0.f : ex2(s[2 * c] - m_new);
-          const float p1 = (m_new == -INFINITY) ? 0.f : ex2(s[2 * c + 1] - m_new);
-          rs += p0 + p1;
+          const float x0 = fmaf(s[2 * c], sl2, neg_m);
+          const float x1 = fmaf(s[2 * c + 1], sl2, neg_m);
+          const float p0 = ((2 * c) % 8 < PS_PREFILL_EMU_PER8) ? exp2_fma(x0) : ex2(x0);
+          const float p1 = ((2 * c + 1) % 8 < PS_PREFILL_EMU_PER8) ? exp2_fma(x1) : ex2(x1);
+          rsp[c & 7] += p0 + p1;
           pk[c] = pack2<kBF16>(p0, p1);
         }
+        const float rs = ((rsp[0] + rsp[1]) + (rsp[2] + rsp[3])) + ((rsp[4] + rsp[5]) + (rsp[6] + rsp[7]));
         l_run = l_run * factor + rs;
         m_run = m_new;
-        // P and O are single-buffered: PV of the previous tile must be done
-        if (t > 0 && !pwait(bars.pv_done, static_cast<uint32_t>((t - 1) & 1), abort_flag, p.status)) {
-          ok = false;
-          break;
-        }
-        tc::fence_after_sync();
+        // O lives in TMEM: rescaling it needs PV of the previous tile done.  The
+        // running max moves rarely (threshold 2^8), so most tiles skip this.
         if (j > 0 && __any_sync(0xffffffffu, factor != 1.f)) {
+          if (!pwait(bars.pv_done, static_cast<uint32_t>((t - 1) & 1), abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
+          tc::fence_after_sync();
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
             uint32_t r[32];
@@ -406,16 +432,19 @@ __global__ void __launch_bounds__(192, 1)
             for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * factor);
             tc::st_32x32b_x32(lane_addr + 256 + c * 32, r);
           }
-          tc::wait_st();
         }
-        // P row -> shared memory, K-major 128B-swizzled [128 rows][64 keys] x 2
+        // P row -> TMEM over the S columns just read (the PV A operand)
+        {
+          uint32_t r0[32], r1[32];
 #pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          const int region = c >> 3;
-          const int phys = (c & 7) ^ (row & 7);
-          uint4 v = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-          *reinterpret_cast<uint4*>(sP + region * kRegionBytes + row * 128 + phys * 16) = v;
+          for (int i = 0; i < 32; ++i) {
+            r0[i] = pk[i];
+            r1[i] = pk[32 + i];
+          }
+          tc::st_32x32b_x32(lane_addr + sb * 128, r0);
+          tc::st_32x32b_x32(lane_addr + sb * 128 + 32, r1);
         }
+        tc::wait_st();
         // last tile of the unit: V rows at or past kv_end must be finite (zero)
         if (j == ui.ntiles - 1) {
           const int z0 = ui.kv_end - key0;
@@ -435,7 +464,7 @@ __global__ void __launch_bounds__(192, 1)
             }
           }
         }
-        fence_proxy_async_smem();
+        fence_proxy_async_smem();  // V tail zeroing (generic) before the MMA reads it
         tc::fence_before_sync();
         __syncwarp();
         if (lane == 0) mbar_arrive(bars.p_full);
