@@ -183,29 +183,37 @@ def run_ours(args):
     out = torch.empty_like(batch.q)
     lse = torch.empty(hq, B, dtype=torch.float32, device=dev)
     kc, vc = batch.kv_cache[0], batch.kv_cache[1]
+    mixed = cfg == 4
+    nd = B
     gathered = None
     if sharded:
         gathered = torch.empty(world, B, hq, 128, dtype=batch.q.dtype, device=dev)
         full_out = torch.empty(B, hq * world, 128, dtype=batch.q.dtype, device=dev)
 
-    def append():
-        ops.kv_append(batch.key, batch.value, kc, vc, batch.slot_mapping)
+    fused = not args.unfused
 
-    mixed = cfg == 4
+    def append():
+        if not fused:
+            ops.kv_append(batch.key, batch.value, kc, vc, batch.slot_mapping)
+        elif mixed:  # prefill tokens still go through the append kernel
+            ops.kv_append(batch.key[nd:], batch.value[nd:], kc, vc, batch.slot_mapping[nd:])
+
     if mixed:
         qlens = (batch.query_start_loc[1:] - batch.query_start_loc[:-1]).tolist()
         nd = sum(1 for x in qlens if x == 1)
         assert all(x == 1 for x in qlens[:nd]), "decode-first batch expected"
         pf_flops = prefill_flops(qlens, batch.seq_lens.tolist(), hq)
 
+    fkw = dict(new_key=batch.key, new_value=batch.value, slot_mapping=batch.slot_mapping) if fused else {}
+
     def decode():
         if not mixed:
             ops.paged_decode(batch.q, kc, vc, batch.block_table, batch.seq_lens,
                              batch.softmax_scale, out, lse=lse,
-                             query_start_loc=batch.query_start_loc, workspace=ws)
+                             query_start_loc=batch.query_start_loc, workspace=ws, **fkw)
             return
         ops.paged_decode(batch.q[:nd], kc, vc, batch.block_table[:nd], batch.seq_lens[:nd],
-                         batch.softmax_scale, out[:nd], workspace=ws)
+                         batch.softmax_scale, out[:nd], workspace=ws, **fkw)
 
     def prefill():
         ops.chunked_prefill(batch.q, kc, vc, batch.block_table[nd:], batch.seq_lens[nd:],
@@ -229,7 +237,8 @@ def run_ours(args):
             prefill()
             stream.synchronize()
         if use_graph:
-            fns = [("append", append), ("decode", decode)] + ([("prefill", prefill)] if mixed else [])
+            fns = ([("append", append)] if (not fused or mixed) else []) + [("decode", decode)] + (
+                [("prefill", prefill)] if mixed else [])
             for name, fn in fns:
                 g = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(g, stream=stream):
@@ -240,7 +249,8 @@ def run_ours(args):
         if ev is not None:
             ev[0].record(stream)
         if use_graph:
-            graphs["append"].replay()
+            if "append" in graphs:
+                graphs["append"].replay()
         else:
             append()
         if ev is not None:
@@ -307,7 +317,7 @@ def run_ours(args):
     # ---- end to end through the public API: host inputs in, host output back ----
     e2e = None if args.quick else run_e2e(batch, ws, dev, args.steps, world,
                                           nd=nd if mixed else None,
-                                          replicas=1 if sharded else world)
+                                          replicas=1 if sharded else world, fused=fused)
 
     ms = elapsed_ms / args.steps
     tokens_per_step = batch.num_tokens  # every rank produces all tokens (its heads when sharded)
@@ -323,7 +333,9 @@ def run_ours(args):
         kv_bytes = kv_tokens * hkv * 128 * 2 * batch.kv_cache.element_size()
         qo_bytes = B * hq * 128 * 2 * batch.q.element_size()
         meta_bytes = batch.block_table.numel() * 4 + B * 4 * 2
-    decode_bytes = kv_bytes + qo_bytes + meta_bytes
+    # a fused append also reads the new K/V rows and writes them into the cache
+    app_bytes = (nd * hkv * 128 * 2 * batch.kv_cache.element_size() * 2) if fused else 0
+    decode_bytes = kv_bytes + qo_bytes + meta_bytes + app_bytes
     step_bytes = workloads.hbm_bytes(batch)
     achieved = decode_bytes / (decode_ms / 1e3) / 1e9
     traffic = profile_traffic(f"paged_decode_cfg{cfg}")
@@ -343,7 +355,8 @@ def run_ours(args):
         },
         "hbm_gbs_step": round(step_bytes / (ms / 1e3) / 1e9, 1),
         "hbm_frac_of_8tbs_step": round(step_bytes / (ms / 1e3) / 1e9 / NOMINAL_HBM_GBS, 4),
-        "gpu_launches": (3 if mixed else 2) * args.steps,
+        "gpu_launches": ((3 if mixed else 2) - (1 if fused and not mixed else 0)) * args.steps,
+        "append_fused_into_decode": fused,
         "roofline": {"kernel": "paged_decode", "bound": "hbm", "achieved": round(achieved, 1),
                      "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
                      "frac": round(achieved / peak, 4),
@@ -372,7 +385,7 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
-def run_e2e(batch, ws, dev, steps, world, nd=None, replicas=1):
+def run_e2e(batch, ws, dev, steps, world, nd=None, replicas=1, fused=True):
     """Same step through the public ops with per-step host->device inputs
     (pinned) and the device->host read of the attention output.  ``nd``:
     number of leading decode sequences of a mixed batch (the rest prefill)."""
@@ -392,14 +405,20 @@ def run_e2e(batch, ws, dev, steps, world, nd=None, replicas=1):
     def one():
         for k, v in host.items():
             dev_in[k].copy_(v, non_blocking=True)
-        ops.kv_append(dev_in["key"], dev_in["value"], kc, vc, dev_in["slot_mapping"])
+        fkw = dict(new_key=dev_in["key"], new_value=dev_in["value"],
+                   slot_mapping=dev_in["slot_mapping"]) if fused else {}
+        if not fused:
+            ops.kv_append(dev_in["key"], dev_in["value"], kc, vc, dev_in["slot_mapping"])
+        elif nd is not None:
+            ops.kv_append(dev_in["key"][nd:], dev_in["value"][nd:], kc, vc, dev_in["slot_mapping"][nd:])
         if nd is None:
             ops.paged_decode(dev_in["q"], kc, vc, dev_in["block_table"], dev_in["seq_lens"],
                              batch.softmax_scale, out, query_start_loc=dev_in["query_start_loc"],
-                             workspace=ws)
+                             workspace=ws, **fkw)
         else:
             ops.paged_decode(dev_in["q"][:nd], kc, vc, dev_in["block_table"][:nd],
-                             dev_in["seq_lens"][:nd], batch.softmax_scale, out[:nd], workspace=ws)
+                             dev_in["seq_lens"][:nd], batch.softmax_scale, out[:nd], workspace=ws,
+                             **fkw)
             ops.chunked_prefill(dev_in["q"], kc, vc, dev_in["block_table"][nd:],
                                 dev_in["seq_lens"][nd:], dev_in["query_start_loc"][nd:],
                                 batch.softmax_scale, out)
@@ -538,6 +557,8 @@ def main():
     ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4, 5])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--unfused", action="store_true",
+                    help="separate append launch instead of the append fused into decode")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--quick", action="store_true",
                     help="timed steps only: no end-to-end, CPU baseline or clock sampling")

@@ -113,6 +113,18 @@ typedef struct {
   /* device status word (PS_DEV_* bits), nullable; ps_paged_decode uses the
      one in its workspace instead */
   int32_t* status;
+  /* Optional KV append fused into ps_paged_decode (NULL new_key = off; the
+     other entry points ignore these fields).  For each sequence b with a
+     query row t, the new key/value rows [t, :, :] are written to the cache at
+     slot_mapping[t] (slot < 0: skipped) -- the contract of ps_kv_append --
+     and attention sees them as the sequence's last token.  The slot must be
+     that of position seq_lens[b] - 1 (it always is for vLLM decode); a
+     mismatch sets PS_DEV_BAD_METADATA. */
+  const void* new_key;
+  int64_t new_key_stride_token, new_key_stride_head;
+  const void* new_value;
+  int64_t new_value_stride_token, new_value_stride_head;
+  const int64_t* slot_mapping;
 } ps_paged_problem;
 
 /*
@@ -132,7 +144,9 @@ int64_t ps_paged_decode_workspace_size(int32_t num_seqs, int32_t num_q_heads,
  * (flash_attn.py:796-817 -> vllm/vllm_flash_attn/cute/interface.py:289-1063)
  * and the split combine FA4 launches after it (cute/interface.py:1052-1060,
  * cute/flash_fwd_combine.py:21-698), which here is fused: the last split of a
- * (sequence, kv head) to finish merges all splits.
+ * (sequence, kv head) to finish merges all splits.  With problem->new_key set
+ * it also performs the KV append of the decode tokens (the caches are then
+ * written), replacing the separate ps_kv_append launch.
  */
 int ps_paged_decode(const ps_paged_problem* problem, void* workspace, int64_t workspace_bytes,
                     void* stream);

@@ -432,6 +432,11 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, kDecodeCtasPerSm)
   float m[NT][2], l[NT][2];
   int L = 0;
   int cseg = 0;  // segments started on the consumer side
+  // fused append: this lane's 16 bytes of the new key (lanes 0-15) or value
+  // (lanes 16-31) row of the current segment's (sequence, kv head)
+  const bool fused = p.new_key != nullptr;
+  uint4 new_row = make_uint4(0u, 0u, 0u, 0u);
+  int64_t new_slot = -1;
 
   for (int k = 0; k < cnt; ++k) {
     const int stage = k % D;
@@ -448,6 +453,17 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, kDecodeCtasPerSm)
     // ---- segment start: query fragments from the slot, reset state ------------
     if (k == 0 || cc.p == 0) {
       L = __ldg(p.seq_lens + cc.b);
+      if (fused) {
+        // fetch the new token's row now; it is written when the segment's last
+        // page comes through this warp (the warp that owns that page)
+        const int qrow = p.qsl ? __ldg(p.qsl + cc.b) : cc.b;
+        new_slot = __ldg(p.slot_mapping + qrow);
+        const int c = lane & 15;
+        const uint16_t* src = lane < 16
+            ? reinterpret_cast<const uint16_t*>(p.new_key) + qrow * p.nk_st + cc.h * p.nk_sh
+            : reinterpret_cast<const uint16_t*>(p.new_value) + qrow * p.nv_st + cc.h * p.nv_sh;
+        new_row = __ldg(reinterpret_cast<const uint4*>(src) + c);
+      }
       const uint32_t qbase = smem_u32(wq + (cseg % D) * decode_qslot_bytes<NT>());
       ++cseg;
 #pragma unroll
@@ -474,6 +490,29 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, kDecodeCtasPerSm)
     }
 
     const int valid = min(kPageTokens, L - cc.p * kPageTokens);
+
+    // ---- fused append: the sequence's last page carries the new token -----
+    if (fused && cc.p == cc.P - 1 && new_slot >= 0) {
+      const int pos = L - 1;
+      const int bidx = pos / p.block_size;
+      const int64_t want = static_cast<int64_t>(__ldg(p.block_table + cc.b * p.bt_stride + bidx)) *
+                               p.block_size + (pos - bidx * p.block_size);
+      if (new_slot == want) {
+        // write the row into this stage's copy of the page (K lanes 0-15, V 16-31)
+        const int r = pos & (kPageTokens - 1);
+        const int c = lane & 15;
+        const int part = (lane < 16 ? 0 : 2) + (c >> 3);  // K lo/hi, V lo/hi box
+        *reinterpret_cast<uint4*>(st + part * kBoxBytes + r * 128 + (((c & 7) ^ (r & 7)) << 4)) = new_row;
+        // and into the cache, as ps_kv_append would
+        const int64_t blk = new_slot / p.block_size, off = new_slot - blk * p.block_size;
+        uint16_t* dst = reinterpret_cast<uint16_t*>(lane < 16 ? p.key_cache : p.value_cache) +
+                        blk * p.c_sblock + off * p.c_sslot + cc.h * p.c_shead;
+        reinterpret_cast<uint4*>(dst)[c] = new_row;
+      } else if (lane == 0) {
+        set_status(p.status, PS_DEV_BAD_METADATA);
+      }
+      __syncwarp();
+    }
 
     // ---- S^T = K Q^T -----------------------------------------------------------
     float s[NT][4];

@@ -300,6 +300,25 @@ int ps_paged_decode(const ps_paged_problem* pr, void* workspace, int64_t workspa
   p.counters = reinterpret_cast<int32_t*>(ws + lay.counters_off);
   p.part = reinterpret_cast<float*>(ws + lay.part_off);
   p.num_part_slots = ps_decode_partial_slots(pr->num_seqs, pr->num_kv_heads, sms);
+  p.new_key = pr->new_key;
+  p.new_value = pr->new_value;
+  p.nk_st = pr->new_key_stride_token;
+  p.nk_sh = pr->new_key_stride_head;
+  p.nv_st = pr->new_value_stride_token;
+  p.nv_sh = pr->new_value_stride_head;
+  p.slot_mapping = pr->slot_mapping;
+  p.key_cache = const_cast<void*>(pr->key_cache);
+  p.value_cache = const_cast<void*>(pr->value_cache);
+  p.c_sblock = pr->cache_stride_block;
+  p.c_sslot = pr->cache_stride_slot;
+  p.c_shead = pr->cache_stride_head;
+  if (pr->new_key != nullptr) {
+    if (!pr->new_value || !pr->slot_mapping)
+      return fail(PS_ERR_INVALID_ARGUMENT, "fused append needs new_key, new_value and slot_mapping");
+    if (!aligned(pr->new_key, 16) || !aligned(pr->new_value, 16) || pr->new_key_stride_token % 8 ||
+        pr->new_key_stride_head % 8 || pr->new_value_stride_token % 8 || pr->new_value_stride_head % 8)
+      return fail(PS_ERR_INVALID_ARGUMENT, "new key/value rows must be 16-byte aligned");
+  }
   const int e = ps_launch_paged_decode(p, kmap, vmap, pr->dtype == PS_DTYPE_BF16, sms,
                                        static_cast<cudaStream_t>(stream));
   if (e != 0) return cuda_fail(static_cast<cudaError_t>(e), "paged_decode launch");

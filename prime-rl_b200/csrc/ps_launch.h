@@ -48,6 +48,14 @@ struct DecodeParams {
   int32_t* counters;     // [num_seqs * num_kv_heads]
   float* part;           // [slots] records: [kg][128] output rows then [kg] LSEs
   int64_t num_part_slots;
+  // fused KV append (new_key == nullptr: off); element strides
+  const void* new_key;
+  const void* new_value;
+  int64_t nk_st, nk_sh, nv_st, nv_sh;
+  const int64_t* slot_mapping;
+  void* key_cache;
+  void* value_cache;
+  int64_t c_sblock, c_sslot, c_shead;
 };
 
 // Static sizing of the decode kernel, shared by the workspace-size query.

@@ -83,6 +83,13 @@ class PagedProblem(ctypes.Structure):
         ("softmax_scale", ctypes.c_float),
         ("num_tokens", ctypes.c_int64),
         ("status", ctypes.c_void_p),
+        ("new_key", ctypes.c_void_p),
+        ("new_key_stride_token", ctypes.c_int64),
+        ("new_key_stride_head", ctypes.c_int64),
+        ("new_value", ctypes.c_void_p),
+        ("new_value_stride_token", ctypes.c_int64),
+        ("new_value_stride_head", ctypes.c_int64),
+        ("slot_mapping", ctypes.c_void_p),
     ]
 
 

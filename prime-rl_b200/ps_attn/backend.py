@@ -6,10 +6,13 @@ FlashAttention surface:
 
 * KV cache ``[2, num_blocks, block_size, num_kv_heads, head_size]`` with the NHD
   stride order (``flash_attn.py:140-171``);
-* ``forward_includes_kv_cache_update = False``: vLLM calls
-  :meth:`PSAttentionImpl.do_kv_cache_update` (``flash_attn.py:850-883``) and then
-  :meth:`PSAttentionImpl.forward` (``flash_attn.py:667-848``), which writes into
-  the preallocated ``output`` in place;
+* KV update: the FlashAttention backend has vLLM call ``do_kv_cache_update``
+  (``flash_attn.py:850-883``) before ``forward`` (``flash_attn.py:667-848``).
+  This backend sets ``forward_includes_kv_cache_update = True`` and does the
+  append inside :meth:`PSAttentionImpl.forward`: decode tokens in the same
+  launch as their attention, prefill tokens through the append kernel.
+  ``do_kv_cache_update`` keeps FlashAttention's contract for callers that use
+  it directly.  ``forward`` writes into the preallocated ``output`` in place;
 * metadata built from ``CommonAttentionMetadata`` (``backend.py:353-379``):
   ``query_start_loc``, ``seq_lens``, ``block_table``, ``slot_mapping``.
 
@@ -45,7 +48,7 @@ BACKEND_NAME = "CUSTOM"
 class PSAttentionBackend(AttentionBackend):
     supported_dtypes: ClassVar[list[torch.dtype]] = [torch.float16, torch.bfloat16]
     supported_kv_cache_dtypes: ClassVar[list[str]] = ["auto", "float16", "bfloat16"]
-    forward_includes_kv_cache_update: bool = False
+    forward_includes_kv_cache_update: bool = True
 
     @staticmethod
     def get_supported_kernel_block_sizes() -> list[int | MultipleOf]:
@@ -207,14 +210,20 @@ class PSAttentionImpl(AttentionImpl):
         m = attn_metadata
         key_cache, value_cache = kv_cache.unbind(0)
         nd, ndt = m.num_decodes, m.num_decode_tokens
+        T = m.num_actual_tokens
+        # key/value are None when this layer shares another layer's cache
+        append = key is not None and value is not None and self.kv_sharing_target_layer_name is None
+        if append and T > ndt:  # prefill tokens: into the cache before their attention
+            ops.kv_append(key[ndt:T], value[ndt:T], key_cache, value_cache, m.slot_mapping[ndt:T])
         if nd > 0:
+            fused = dict(new_key=key, new_value=value, slot_mapping=m.slot_mapping) if append else {}
             ops.paged_decode(query[:ndt], key_cache, value_cache, m.block_table[:nd],
                              m.seq_lens[:nd], self.scale, output[:ndt],
-                             query_start_loc=m.query_start_loc[:nd + 1], workspace=m.workspace)
+                             query_start_loc=m.query_start_loc[:nd + 1], workspace=m.workspace,
+                             **fused)
         if m.num_prefills > 0:
-            ops.chunked_prefill(query[:m.num_actual_tokens], key_cache, value_cache,
-                                m.block_table[nd:], m.seq_lens[nd:], m.query_start_loc[nd:],
-                                self.scale, output[:m.num_actual_tokens])
+            ops.chunked_prefill(query[:T], key_cache, value_cache, m.block_table[nd:],
+                                m.seq_lens[nd:], m.query_start_loc[nd:], self.scale, output[:T])
         return output
 
 

@@ -184,13 +184,19 @@ def paged_decode(q: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Te
                  block_table: torch.Tensor, seq_lens: torch.Tensor, softmax_scale: float,
                  out: torch.Tensor, lse: torch.Tensor | None = None,
                  query_start_loc: torch.Tensor | None = None,
-                 workspace: DecodeWorkspace | None = None) -> torch.Tensor:
+                 workspace: DecodeWorkspace | None = None,
+                 new_key: torch.Tensor | None = None, new_value: torch.Tensor | None = None,
+                 slot_mapping: torch.Tensor | None = None) -> torch.Tensor:
     """Decode attention, one query row per sequence, written into ``out``.
 
     q/out: [T, Hq, D]; caches [num_blocks, block_size, Hkv, D]; block_table
     int32 [B, P]; seq_lens int32 [B] (including the new token);
     query_start_loc int32 [B+1] or None (row b for sequence b); lse fp32
     [Hq, T] or None (natural log).
+
+    ``new_key``/``new_value`` [T, Hkv, D] + ``slot_mapping`` int64 [T] fuse the
+    KV append of the decode tokens into the same launch (same result as
+    :func:`kv_append` followed by this call without them).
     """
     lib = _lib.load()
     B = seq_lens.shape[0]
@@ -200,6 +206,26 @@ def paged_decode(q: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Te
         raise ValueError(f"workspace sized for {workspace.max_num_seqs} sequences < {B}")
     pr = _problem(q, key_cache, value_cache, block_table, seq_lens, query_start_loc,
                   softmax_scale, out, lse)
+    if new_key is not None:
+        _require_cuda(new_key, new_value, slot_mapping)
+        if new_value is None or slot_mapping is None:
+            raise ValueError("fused append needs new_key, new_value and slot_mapping")
+        if slot_mapping.dtype != torch.int64 or not slot_mapping.is_contiguous():
+            raise ValueError("slot_mapping must be contiguous int64")
+        if new_key.dtype != q.dtype or new_value.dtype != q.dtype:
+            raise ValueError("new key/value must have the cache dtype")
+        hkv, d = key_cache.shape[2], key_cache.shape[3]
+        if new_key.shape[1:] != (hkv, d) or new_value.shape[1:] != (hkv, d):
+            raise ValueError("new key/value shape does not match the cache")
+        if new_key.stride(-1) != 1 or new_value.stride(-1) != 1:
+            raise ValueError("last dimension must be contiguous")
+        if slot_mapping.shape[0] < q.shape[0] or new_key.shape[0] < q.shape[0]:
+            raise ValueError("fused append needs a key/value row and a slot per query row")
+        pr.new_key = new_key.data_ptr()
+        pr.new_key_stride_token, pr.new_key_stride_head = new_key.stride(0), new_key.stride(1)
+        pr.new_value = new_value.data_ptr()
+        pr.new_value_stride_token, pr.new_value_stride_head = new_value.stride(0), new_value.stride(1)
+        pr.slot_mapping = slot_mapping.data_ptr()
     _lib.check(lib.ps_paged_decode(ctypes.byref(pr), workspace.buffer.data_ptr(),
                                    workspace.nbytes, _stream_ptr(q.device)))
     return out

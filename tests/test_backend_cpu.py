@@ -22,7 +22,8 @@ def test_static_api_matches_flash_attention_surface():
     with pytest.raises(ValueError):
         B.get_kv_cache_shape(10, 24, 8, 128)
     assert B.get_kv_cache_stride_order() == (0, 1, 2, 3, 4)
-    assert B.forward_includes_kv_cache_update is False
+    # the append runs inside forward (decode tokens fused into the decode launch)
+    assert B.forward_includes_kv_cache_update is True
     assert B.get_impl_cls() is psb.PSAttentionImpl
     assert B.get_builder_cls() is psb.PSAttentionMetadataBuilder
     assert B.supports_head_size(128) and not B.supports_head_size(64)
@@ -100,6 +101,26 @@ def test_forward_routes_decode_and_prefill(monkeypatch):
     out.fill_(3)
     impl.forward(None, q, None, None, kv, None, out)
     assert calls == [] and not out.any()
+
+
+def test_forward_appends_prefill_tokens_and_fuses_decode(monkeypatch):
+    calls = []
+    monkeypatch.setattr(psb.ops, "kv_append", lambda *a, **k: calls.append(("append", a, k)))
+    monkeypatch.setattr(psb.ops, "paged_decode", lambda *a, **k: calls.append(("decode", a, k)))
+    monkeypatch.setattr(psb.ops, "chunked_prefill", lambda *a, **k: calls.append(("prefill", a, k)))
+    impl = psb.PSAttentionImpl(16, 128, 0.088, 8, None, None, "auto")
+    md = _builder().build(0, _common([1, 1, 5], [10, 20, 40]))
+    T = 7
+    q = torch.zeros(T + 1, 16, 128)
+    key = torch.randn(T + 1, 8, 128)
+    val = torch.randn(T + 1, 8, 128)
+    out = torch.zeros(T + 1, 16, 128)
+    impl.forward(None, q, key, val, torch.zeros(2, 4, 16, 8, 128), md, out)
+    assert [c[0] for c in calls] == ["append", "decode", "prefill"]
+    _, a, _ = calls[0]
+    assert a[0].shape[0] == 5 and a[4].tolist() == [2, 3, 4, 5, 6]  # prefill rows only
+    _, _, k = calls[1]
+    assert k["new_key"] is key and k["slot_mapping"] is md.slot_mapping
 
 
 def test_kv_update_unbinds_cache(monkeypatch):

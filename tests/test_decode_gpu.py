@@ -225,3 +225,56 @@ def test_one_workspace_serves_changing_batch_sizes(cuda_device):
         torch.cuda.synchronize()
         assert ws.status() == 0
         assert_attn_close(to_np32(out), rout, to_np32(lse), rlse)
+
+
+@pytest.mark.parametrize("cfg_lens,heads", [
+    ([1, 15, 16, 17, 333, 2049], (16, 8)),
+    ([9000, 3, 40, 700], (8, 4)),
+    ([100, 200], (32, 2)),
+])
+def test_fused_append_equals_append_then_decode(cuda_device, cfg_lens, heads):
+    """The append fused into the decode launch gives bit-identical outputs and
+    cache contents to ps_kv_append followed by the plain decode."""
+    hq, hkv = heads
+    base = workloads.make_batch([1] * len(cfg_lens), cfg_lens, hq, hkv, seed=55).to(cuda_device)
+    a = workloads.PagedBatch(**{**base.__dict__, "kv_cache": base.kv_cache.clone()})
+    b = workloads.PagedBatch(**{**base.__dict__, "kv_cache": base.kv_cache.clone()})
+    out_a, lse_a = run_step(a)
+    out_b = torch.empty_like(b.q)
+    lse_b = torch.empty_like(lse_a)
+    ws = ops.DecodeWorkspace(len(cfg_lens), hq, hkv, 128, cuda_device)
+    ops.paged_decode(b.q, b.kv_cache[0], b.kv_cache[1], b.block_table, b.seq_lens, b.softmax_scale,
+                     out_b, lse=lse_b, query_start_loc=b.query_start_loc, workspace=ws,
+                     new_key=b.key, new_value=b.value, slot_mapping=b.slot_mapping)
+    torch.cuda.synchronize()
+    assert ws.status() == 0
+    assert torch.equal(out_a, out_b) and torch.equal(lse_a, lse_b)
+    assert torch.equal(a.kv_cache, b.kv_cache)
+
+
+def test_fused_append_padding_and_slot_mismatch(cuda_device):
+    batch = workloads.make_batch([1, 1, 1], [40, 17, 64], 8, 2, seed=56).to(cuda_device)
+    # padding token (slot -1): nothing appended for sequence 1, attention unchanged
+    slots = batch.slot_mapping.clone()
+    slots[1] = -1
+    ref = workloads.PagedBatch(**{**batch.__dict__, "kv_cache": batch.kv_cache.clone()})
+    ops.kv_append(ref.key, ref.value, ref.kv_cache[0], ref.kv_cache[1], slots)
+    ref_out = torch.empty_like(ref.q)
+    ops.paged_decode(ref.q, ref.kv_cache[0], ref.kv_cache[1], ref.block_table, ref.seq_lens,
+                     ref.softmax_scale, ref_out)
+    out = torch.empty_like(batch.q)
+    ws = ops.DecodeWorkspace(4, 8, 2, 128, cuda_device)
+    ops.paged_decode(batch.q, batch.kv_cache[0], batch.kv_cache[1], batch.block_table,
+                     batch.seq_lens, batch.softmax_scale, out, workspace=ws, new_key=batch.key,
+                     new_value=batch.value, slot_mapping=slots)
+    torch.cuda.synchronize()
+    assert ws.status() == 0
+    assert torch.equal(out, ref_out) and torch.equal(batch.kv_cache, ref.kv_cache)
+    # a slot that is not the last position is reported, not silently used
+    slots2 = batch.slot_mapping.clone()
+    slots2[2] = slots2[0]
+    ops.paged_decode(batch.q, batch.kv_cache[0], batch.kv_cache[1], batch.block_table,
+                     batch.seq_lens, batch.softmax_scale, out, workspace=ws, new_key=batch.key,
+                     new_value=batch.value, slot_mapping=slots2)
+    torch.cuda.synchronize()
+    assert ws.status() & _lib.PS_DEV_BAD_METADATA

@@ -109,7 +109,8 @@ def test_mixed_batch_through_paged_attention(cuda_device):
 
 
 def test_vllm_impl_forward_mixed_batch(cuda_device):
-    """PSAttentionImpl.forward + do_kv_cache_update on a decode-first mixed batch."""
+    """PSAttentionImpl.forward (which performs the KV append) on a decode-first
+    mixed batch."""
     pytest.importorskip("vllm.v1.attention.backend")
     from ps_attn import backend as psb
 
@@ -125,8 +126,7 @@ def test_vllm_impl_forward_mixed_batch(cuda_device):
         max_seq_len=max(seq_lens), seq_lens=g.seq_lens, block_table=g.block_table,
         slot_mapping=g.slot_mapping, num_decodes=3, num_decode_tokens=3, num_prefills=2,
         workspace=ws)
-    impl.do_kv_cache_update(None, g.key, g.value, g.kv_cache, g.slot_mapping)
-    out = torch.empty_like(g.q)
+    out = torch.empty_like(g.q)  # forward appends (decode tokens fused, prefill tokens first)
     impl.forward(None, g.q, g.key, g.value, g.kv_cache, md, out)
     torch.cuda.synchronize()
     assert ws.status() == 0
