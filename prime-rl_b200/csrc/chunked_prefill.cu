@@ -8,21 +8,27 @@
 //
 // Tiling.  An M tile is 128 rows of (token, q head) pairs of ONE kv head: the
 // GQA group is packed along M (row = token * group + head_in_group), so a KV
-// tile loaded once serves every q head that reads it.  A KV tile is 128 keys =
-// 8 pages of 16 tokens gathered through the block table, one TMA box per page
-// and 64-dim half, 128-byte swizzled (the canonical K-major SW128 layout for
-// K; for V the same bytes are the MN-major SW128 layout of the PV B operand).
+// tile loaded once serves every q head that reads it.  A CTA works on a PAIR of
+// consecutive M tiles (A, B) of the same (sequence, kv head), so every KV tile
+// it loads feeds two 128x128 products.  A KV tile is 128 keys = 8 pages of 16
+// tokens gathered through the block table, one TMA box per page and 64-dim
+// half, 128-byte swizzled (the canonical K-major SW128 layout for K; for V the
+// same bytes are the MN-major SW128 layout of the PV B operand).
 //
-// Warp roles (192 threads, one persistent CTA per SM):
-//   warp 0     TMA producer: Q tile (3-D box over [tokens, heads, dims]), K/V tiles
-//   warp 1     TMEM owner; lane 0 issues tcgen05.mma:
-//                S[b] = Q . K^T   (M128 N128 K16 x 8, S double-buffered in TMEM)
-//                O   += P . V     (M128 N128 K16 x 8, O resident in TMEM)
-//   warps 2-5  softmax + epilogue, one thread per TMEM lane (= M row): S row
-//              from TMEM, causal mask, online softmax in the exp2 domain with
-//              lazy rescaling (the running max moves only when a tile's max
-//              exceeds it by more than 2^8; O in TMEM is rescaled then), P as
-//              bf16 into shared memory, final O / l and LSE to global memory.
+// Warp roles (384 threads, one persistent CTA per SM):
+//   warp 0       TMA producer: Q tiles A and B, K/V tiles
+//   warp 1       TMEM owner; lane 0 issues tcgen05.mma (M128 N128 K16) in the
+//                order S_A(j) S_B(j) PV_A(j) S_A(j+1) PV_B(j) S_B(j+1) ...,
+//                so each softmax group has two MMAs of the other tile to hide in
+//   warps 2-3    idle (keep the softmax groups warpgroup-aligned)
+//   warps 4-7    softmax + epilogue of tile A, warps 8-11 of tile B: one
+//                thread per TMEM lane (= M row); S is read twice from TMEM
+//                (row max, then exp2 + bf16 pack chunk by chunk) and P is
+//                written over the S columns already read, as the A operand of
+//                the PV product.  Online softmax in the exp2 domain with lazy
+//                rescaling (the running max moves only when a tile's max
+//                exceeds it by more than 2^8; O in TMEM is rescaled then).
+// TMEM: S_A [0,128) S_B [128,256) O_A [256,384) O_B [384,512).
 //
 // Every mbarrier wait is bounded (~1 s); on timeout the kernel records
 // PS_DEV_WAIT_TIMEOUT, raises a CTA-wide abort flag that ends every role's
@@ -33,15 +39,15 @@
 
 namespace ps {
 
-constexpr int kKeys = 128;            // keys per KV tile
-constexpr int kRegionBytes = 128 * 128;  // [128 rows][64 x 16-bit], 128B swizzled
+constexpr int kKeys = 128;                    // keys per KV tile
+constexpr int kRegionBytes = 128 * 128;       // [128 rows][64 x 16-bit], 128B swizzled
 constexpr int kTileBytes = 2 * kRegionBytes;  // both 64-dim halves
 constexpr int kKvStages = 2;
+constexpr int kThreads = 384;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 // Of every 8 exponentials in a softmax row, this many are evaluated on the FMA
-// pipe (exp2_fma) instead of the MUFU unit, which a 128x128 tile otherwise
-// saturates before the tensor core.  Tuned value; the macro exists for sweeps.
+// pipe (exp2_fma) instead of the MUFU unit.  The macro exists for sweeps.
 #ifndef PS_PREFILL_EMU_PER8
 #define PS_PREFILL_EMU_PER8 0
 #endif
@@ -64,13 +70,12 @@ __device__ __forceinline__ float exp2_fma(float x) {
 
 struct PrefillSmem {
   // all tiles 1024-byte aligned (offsets from the aligned base)
-  static constexpr int q_off = 0;
-  static constexpr int k_off = q_off + kTileBytes;
+  static constexpr int q_off = 0;  // Q_A then Q_B
+  static constexpr int k_off = q_off + 2 * kTileBytes;
   static constexpr int v_off = k_off + kKvStages * kTileBytes;
   static constexpr int bar_off = v_off + kKvStages * kTileBytes;
-  // barriers
   static constexpr int n_bars = 2 /*q*/ + 3 * kKvStages /*kfull vfull kvempty*/ +
-                                2 /*s_full*/ + 2 /*p_full pv_done*/;
+                                2 /*s_full*/ + 2 /*p_full*/ + 2 /*pv_done*/;
   static constexpr int misc_off = bar_off + n_bars * 8;  // tmem base, abort flag
   static constexpr int table_off = misc_off + 16;
   static constexpr int bytes_before_table = table_off;
@@ -79,23 +84,25 @@ struct PrefillSmem {
 struct PBars {
   uint64_t* q_full;
   uint64_t* q_empty;
-  uint64_t* kfull;   // [kKvStages]
-  uint64_t* vfull;   // [kKvStages]
-  uint64_t* kvempty; // [kKvStages]
-  uint64_t* s_full;  // [2]
-  uint64_t* p_full;
-  uint64_t* pv_done;
+  uint64_t* kfull;    // [kKvStages]
+  uint64_t* vfull;    // [kKvStages]
+  uint64_t* kvempty;  // [kKvStages]
+  uint64_t* s_full;   // [2]: tile A, tile B
+  uint64_t* p_full;   // [2]
+  uint64_t* pv_done;  // [2]
 };
 
 struct UnitInfo {
-  int b, h, t0, t1;   // sequence, kv head, token range [t0, t1) within the q chunk
-  int qrow0;          // first global q row of the sequence
-  int ctx;            // L - q_len
-  int L;
-  int kv_end;         // keys [0, kv_end) are visible to some row of the unit
+  int b, h;         // sequence, kv head
+  int t0;           // first token (within the q chunk) of tile A; tile B starts at t0 + tpt
+  int qlen, qrow0;  // query rows of the sequence, first global q row
+  int ctx;          // L - q_len
+  int kv_end;       // keys [0, kv_end) are visible to some row of the pair
   int ntiles;
 };
 
+// Units are (sequence, M-tile pair, kv head); within a sequence the pairs are
+// enumerated from the last (longest causal range) to the first.
 __device__ __forceinline__ UnitInfo unit_info(const PrefillParams& p, const int* prefix, int u) {
   UnitInfo ui;
   const int pu = u / p.num_kv_heads;
@@ -106,14 +113,15 @@ __device__ __forceinline__ UnitInfo unit_info(const PrefillParams& p, const int*
     if (prefix[mid] <= pu) lo = mid; else hi = mid - 1;
   }
   ui.b = lo;
-  const int mt = pu - prefix[lo];
+  const int npairs = prefix[lo + 1] - prefix[lo];
+  const int mp = npairs - 1 - (pu - prefix[lo]);
   ui.qrow0 = __ldg(p.qsl + lo);
-  const int qlen = __ldg(p.qsl + lo + 1) - ui.qrow0;
-  ui.L = __ldg(p.seq_lens + lo);
-  ui.ctx = ui.L - qlen;
-  ui.t0 = mt * p.tokens_per_tile;
-  ui.t1 = min(qlen, ui.t0 + p.tokens_per_tile);
-  ui.kv_end = ui.ctx + ui.t1;
+  ui.qlen = __ldg(p.qsl + lo + 1) - ui.qrow0;
+  const int L = __ldg(p.seq_lens + lo);
+  ui.ctx = L - ui.qlen;
+  ui.t0 = mp * 2 * p.tokens_per_tile;
+  const int t1 = min(ui.qlen, ui.t0 + 2 * p.tokens_per_tile);
+  ui.kv_end = ui.ctx + t1;
   ui.ntiles = (ui.kv_end + kKeys - 1) / kKeys;
   return ui;
 }
@@ -143,8 +151,17 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* m
       : "memory");
 }
 
+__device__ __forceinline__ void tmem_st_x16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
 template <bool kBF16>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kThreads, 1)
     chunked_prefill_kernel(const __grid_constant__ PrefillParams p,
                            const __grid_constant__ CUtensorMap qmap,
                            const __grid_constant__ CUtensorMap kmap,
@@ -162,27 +179,30 @@ __global__ void __launch_bounds__(192, 1)
   bars.kvempty = bar + 2 + 2 * kKvStages;
   bars.s_full = bar + 2 + 3 * kKvStages;
   bars.p_full = bar + 4 + 3 * kKvStages;
-  bars.pv_done = bar + 5 + 3 * kKvStages;
+  bars.pv_done = bar + 6 + 3 * kKvStages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::misc_off);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::misc_off + 4);
   int* prefix = reinterpret_cast<int*>(smem + L::table_off);
-  __shared__ int s_warp_tot[6];
+  __shared__ int s_warp_tot[kThreads / 32];
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
   const int B = p.num_seqs;
   const int G = p.group;
+  const int tpt = p.tokens_per_tile;
 
   asm volatile("griddepcontrol.wait;" ::: "memory");
-  // ---- prologue: M tiles per sequence, exclusive prefix ------------------------
+  // ---- prologue: M-tile pairs per sequence, exclusive prefix -------------------
   const int per = (B + blockDim.x - 1) / blockDim.x;
   const int b_lo = min(B, tid * per), b_hi = min(B, b_lo + per);
-  int local = 0;
-  for (int b = b_lo; b < b_hi; ++b) {
+  auto pairs_of = [&](int b) {
     const int qlen = __ldg(p.qsl + b + 1) - __ldg(p.qsl + b);
-    local += qlen > 0 ? (qlen + p.tokens_per_tile - 1) / p.tokens_per_tile : 0;
-  }
+    const int mt = qlen > 0 ? (qlen + tpt - 1) / tpt : 0;
+    return (mt + 1) / 2;
+  };
+  int local = 0;
+  for (int b = b_lo; b < b_hi; ++b) local += pairs_of(b);
   int incl = local;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
@@ -199,17 +219,17 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(bars.vfull + s, 1);
       mbar_init(bars.kvempty + s, 1);
     }
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(bars.s_full + s, 1);
+    for (int x = 0; x < 2; ++x) {
+      mbar_init(bars.s_full + x, 1);
+      mbar_init(bars.p_full + x, 4);
+      mbar_init(bars.pv_done + x, 1);
     }
-    mbar_init(bars.p_full, 4);
-    mbar_init(bars.pv_done, 1);
     fence_mbar_init();
     tma_prefetch_desc(&qmap);
     tma_prefetch_desc(&kmap);
     tma_prefetch_desc(&vmap);
   }
-  if (warp == 1) {  // TMEM: S0 [0,128) S1 [128,256) O [256,384)
+  if (warp == 1) {
     tc::tmem_alloc(tmem_slot, 512);
     tc::tmem_relinquish();
   }
@@ -220,8 +240,7 @@ __global__ void __launch_bounds__(192, 1)
     int run = warp_off + incl - local;
     for (int b = b_lo; b < b_hi; ++b) {
       prefix[b] = run;
-      const int qlen = __ldg(p.qsl + b + 1) - __ldg(p.qsl + b);
-      run += qlen > 0 ? (qlen + p.tokens_per_tile - 1) / p.tokens_per_tile : 0;
+      run += pairs_of(b);
     }
     if (tid == blockDim.x - 1) prefix[B] = warp_off + incl;
   }
@@ -246,11 +265,14 @@ __global__ void __launch_bounds__(192, 1)
       const UnitInfo ui = unit_info(p, prefix, u);
       if (!pwait(bars.q_empty, (uit & 1) ^ 1, abort_flag, p.status)) break;
       if (lane == 0) {
-        // the box always spans tokens_per_tile tokens (rows past the sequence are
-        // the next sequence's or zero fill) and TMA delivers the whole box
-        mbar_arrive_expect_tx(bars.q_full, p.tokens_per_tile * G * 2 * 128);
-        tma_load_3d(sQ, &qmap, bars.q_full, 0, ui.h * G, ui.qrow0 + ui.t0);
-        tma_load_3d(sQ + kRegionBytes, &qmap, bars.q_full, 64, ui.h * G, ui.qrow0 + ui.t0);
+        // each box spans tpt tokens (rows past the sequence are the next
+        // sequence's or zero fill) and TMA delivers the whole box
+        mbar_arrive_expect_tx(bars.q_full, 2 * tpt * G * 2 * 128);
+        for (int x = 0; x < 2; ++x) {
+          const int tok = ui.qrow0 + ui.t0 + x * tpt;
+          tma_load_3d(sQ + x * kTileBytes, &qmap, bars.q_full, 0, ui.h * G, tok);
+          tma_load_3d(sQ + x * kTileBytes + kRegionBytes, &qmap, bars.q_full, 64, ui.h * G, tok);
+        }
       }
       const int npages_needed = (ui.kv_end + 15) / 16;
       const int* bt = p.block_table + static_cast<int64_t>(ui.b) * p.bt_stride;
@@ -260,7 +282,6 @@ __global__ void __launch_bounds__(192, 1)
         const uint32_t n = static_cast<uint32_t>(t / kKvStages);
         const int pg0 = j * 8;
         const int npg = min(8, npages_needed - pg0);
-        // block-table window covering this tile's entries
         const int e_first = pg0 / spb, e_last = (pg0 + npg - 1) / spb;
         if (ui.b != bt_b || e_first < bt_e0 || e_last >= bt_e0 + 32) {
           bt_b = ui.b;
@@ -299,99 +320,108 @@ __global__ void __launch_bounds__(192, 1)
       const uint32_t idesc_qk = tc::idesc_f16(kBF16, 128, 128, false, false);
       const uint32_t idesc_pv = tc::idesc_f16(kBF16, 128, 128, false, true);
       const uint32_t q_addr = smem_u32(sQ), k_addr = smem_u32(sK), v_addr = smem_u32(sV);
-      int t = 0, uit = 0;
-      int pend_t = -1, pend_j = 0;  // tile whose PV is still to be issued
-      auto issue_pv = [&](int tt, int jj) -> bool {
+      auto issue_s = [&](int x, int s) {
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t off = (kk >> 2) * kRegionBytes + (kk & 3) * 32;
+          const uint64_t ad = tc::sw128_desc(q_addr + x * kTileBytes + off, 16, 1024);
+          const uint64_t bd = tc::sw128_desc(k_addr + s * kTileBytes + off, 16, 1024);
+          tc::mma_f16_ss(tmem + x * 128, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
+        }
+        tc::commit(bars.s_full + x);
+      };
+      // PV of tile x for global KV tile tt; P sits in S_x's first 64 columns as
+      // packed 16-bit pairs (keys 16kk.. = columns 8kk..)
+      auto issue_pv = [&](int x, int tt, int jj) -> bool {
         const int s = tt % kKvStages;
-        if (!pwait(bars.p_full, static_cast<uint32_t>(tt & 1), abort_flag, p.status)) return false;
-        if (!pwait(bars.vfull + s, static_cast<uint32_t>((tt / kKvStages) & 1), abort_flag, p.status))
+        if (!pwait(bars.p_full + x, static_cast<uint32_t>(tt & 1), abort_flag, p.status)) return false;
+        if (x == 0 &&
+            !pwait(bars.vfull + s, static_cast<uint32_t>((tt / kKvStages) & 1), abort_flag, p.status))
           return false;
         tc::fence_after_sync();
-        // A = P, written by the softmax warps as packed 16-bit pairs over the
-        // first 64 columns of this tile's S buffer (keys 16kk.. = columns 8kk..)
-        const uint32_t p_tmem = tmem + (tt & 1) * 128;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint64_t bd = tc::sw128_desc(v_addr + s * kTileBytes + kk * 2048, kRegionBytes, 1024);
-          tc::mma_f16_ts(tmem + 256, p_tmem + kk * 8, bd, idesc_pv, (jj > 0 || kk > 0) ? 1u : 0u);
+          tc::mma_f16_ts(tmem + 256 + x * 128, tmem + x * 128 + kk * 8, bd, idesc_pv,
+                         (jj > 0 || kk > 0) ? 1u : 0u);
         }
-        tc::commit(bars.pv_done);
-        tc::commit(bars.kvempty + s);
+        tc::commit(bars.pv_done + x);
+        if (x == 1) tc::commit(bars.kvempty + s);  // both PVs of this stage issued
         return true;
       };
+      int t = 0, uit = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x, ++uit) {
         const UnitInfo ui = unit_info(p, prefix, u);
         if (!pwait(bars.q_full, static_cast<uint32_t>(uit & 1), abort_flag, p.status)) break;
         tc::fence_after_sync();
-        for (int j = 0; j < ui.ntiles; ++j, ++t) {
+        {  // S_A(0), S_B(0)
           const int s = t % kKvStages;
-          const int sb = t & 1;
-          const uint32_t n = static_cast<uint32_t>(t / kKvStages);
-          if (!pwait(bars.kfull + s, n & 1, abort_flag, p.status)) { ok = false; break; }
-          // S buffer sb last held S/P of tile t-2, whose PV was issued before
-          // this MMA; tcgen05 MMAs of one thread execute in issue order.
+          if (!pwait(bars.kfull + s, static_cast<uint32_t>((t / kKvStages) & 1), abort_flag, p.status)) break;
           tc::fence_after_sync();
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            const uint32_t off = (kk >> 2) * kRegionBytes + (kk & 3) * 32;
-            const uint64_t ad = tc::sw128_desc(q_addr + off, 16, 1024);
-            const uint64_t bd = tc::sw128_desc(k_addr + s * kTileBytes + off, 16, 1024);
-            tc::mma_f16_ss(tmem + sb * 128, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
+          issue_s(0, s);
+          issue_s(1, s);
+          if (ui.ntiles == 1) tc::commit(bars.q_empty);
+        }
+        for (int j = 0; j < ui.ntiles; ++j) {
+          const int tt = t + j;
+          const bool more = j + 1 < ui.ntiles;
+          const int sn = (tt + 1) % kKvStages;
+          if (!issue_pv(0, tt, j)) { ok = false; break; }
+          if (more) {
+            if (!pwait(bars.kfull + sn, static_cast<uint32_t>(((tt + 1) / kKvStages) & 1), abort_flag,
+                       p.status)) { ok = false; break; }
+            tc::fence_after_sync();
+            issue_s(0, sn);  // S_A(j+1) after PV_A(j): same TMEM columns, issue order
           }
-          tc::commit(bars.s_full + sb);
-          if (j == ui.ntiles - 1) tc::commit(bars.q_empty);
-          if (pend_t >= 0 && !issue_pv(pend_t, pend_j)) { ok = false; break; }
-          pend_t = t;
-          pend_j = j;
+          if (!issue_pv(1, tt, j)) { ok = false; break; }
+          if (more) {
+            issue_s(1, sn);
+            if (j + 1 == ui.ntiles - 1) tc::commit(bars.q_empty);
+          }
         }
-        if (ok && pend_t >= 0) {
-          if (!issue_pv(pend_t, pend_j)) ok = false;
-          pend_t = -1;
-        }
+        t += ui.ntiles;
       }
     }
-  } else {
+  } else if (warp >= 4) {
     // =========================== softmax + epilogue ===========================
+    const int x = (warp >= 8) ? 1 : 0;        // tile A (warps 4-7) or B (8-11)
     const int quarter = warp & 3;             // TMEM lane quarter this warp may access
     const int row = quarter * 32 + lane;      // M row == TMEM lane
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    const uint32_t s_addr = lane_addr + x * 128;
+    const uint32_t o_addr = lane_addr + 256 + x * 128;
     const float sl2 = p.scale_log2;
     int t = 0;
     for (int u = blockIdx.x; u < total_units; u += gridDim.x) {
       const UnitInfo ui = unit_info(p, prefix, u);
-      const int tok = ui.t0 + row / G;
+      const int tok = ui.t0 + x * tpt + row / G;
       const int hin = row - (row / G) * G;
-      const bool row_valid = row < p.tokens_per_tile * G && tok < ui.t1;
+      const bool row_valid = row < tpt * G && tok < ui.qlen;
       const int limit = row_valid ? ui.ctx + tok : -1;  // last visible key
       float m_run = -INFINITY, l_run = 0.f;
       bool ok = true;
       for (int j = 0; j < ui.ntiles; ++j, ++t) {
-        const int sb = t & 1;
-        if (!pwait(bars.s_full + sb, static_cast<uint32_t>(t >> 1) & 1, abort_flag, p.status)) { ok = false; break; }
+        if (!pwait(bars.s_full + x, static_cast<uint32_t>(t & 1), abort_flag, p.status)) { ok = false; break; }
         tc::fence_after_sync();
-        float s[128];
-        {
-          uint32_t r[4][32];
-#pragma unroll
-          for (int c = 0; c < 4; ++c) tc::ld_32x32b_x32(lane_addr + sb * 128 + c * 32, r[c]);
-          tc::wait_ld();
-#pragma unroll
-          for (int c = 0; c < 4; ++c)
-#pragma unroll
-            for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(r[c][i]);
-        }
-        // causal mask only on tiles that reach past some row's last visible key
         const int key0 = j * kKeys;
-        if (!__all_sync(0xffffffffu, key0 + kKeys - 1 <= limit)) {
-#pragma unroll
-          for (int c = 0; c < 128; ++c) s[c] = (key0 + c <= limit) ? s[c] : -INFINITY;
-        }
+        const bool need_mask = !__all_sync(0xffffffffu, key0 + kKeys - 1 <= limit);
+        // pass 1: row max of the (masked) raw scores
         float mxp[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) mxp[i] = s[i];
+        for (int i = 0; i < 8; ++i) mxp[i] = -INFINITY;
 #pragma unroll
-        for (int c = 8; c < 128; ++c) mxp[c & 7] = fmaxf(mxp[c & 7], s[c]);
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r[32];
+          tc::ld_32x32b_x32(s_addr + c * 32, r);
+          tc::wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            float v = __uint_as_float(r[i]);
+            if (need_mask && key0 + c * 32 + i > limit) v = -INFINITY;
+            mxp[i & 7] = fmaxf(mxp[i & 7], v);
+          }
+        }
         float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
                          fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
         mx *= sl2;  // scale > 0: max of scaled = scaled max
@@ -401,24 +431,9 @@ __global__ void __launch_bounds__(192, 1)
           factor = ex2(m_run - m_new);  // 0 when m_run == -inf
         }
         const float neg_m = (m_new == -INFINITY) ? 0.f : -m_new;  // fully masked row: all p = 0
-        float rsp[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        uint32_t pk[64];
-#pragma unroll
-        for (int c = 0; c < 64; ++c) {
-          const float x0 = fmaf(s[2 * c], sl2, neg_m);
-          const float x1 = fmaf(s[2 * c + 1], sl2, neg_m);
-          const float p0 = ((2 * c) % 8 < PS_PREFILL_EMU_PER8) ? exp2_fma(x0) : ex2(x0);
-          const float p1 = ((2 * c + 1) % 8 < PS_PREFILL_EMU_PER8) ? exp2_fma(x1) : ex2(x1);
-          rsp[c & 7] += p0 + p1;
-          pk[c] = pack2<kBF16>(p0, p1);
-        }
-        const float rs = ((rsp[0] + rsp[1]) + (rsp[2] + rsp[3])) + ((rsp[4] + rsp[5]) + (rsp[6] + rsp[7]));
-        l_run = l_run * factor + rs;
-        m_run = m_new;
-        // O lives in TMEM: rescaling it needs PV of the previous tile done.  The
-        // running max moves rarely (threshold 2^8), so most tiles skip this.
+        // O lives in TMEM: rescaling it needs the previous PV of this tile done.
         if (j > 0 && __any_sync(0xffffffffu, factor != 1.f)) {
-          if (!pwait(bars.pv_done, static_cast<uint32_t>((t - 1) & 1), abort_flag, p.status)) {
+          if (!pwait(bars.pv_done + x, static_cast<uint32_t>((t - 1) & 1), abort_flag, p.status)) {
             ok = false;
             break;
           }
@@ -426,27 +441,44 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
             uint32_t r[32];
-            tc::ld_32x32b_x32(lane_addr + 256 + c * 32, r);
+            tc::ld_32x32b_x32(o_addr + c * 32, r);
             tc::wait_ld();
 #pragma unroll
             for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * factor);
-            tc::st_32x32b_x32(lane_addr + 256 + c * 32, r);
+            tc::st_32x32b_x32(o_addr + c * 32, r);
           }
         }
-        // P row -> TMEM over the S columns just read (the PV A operand)
-        {
-          uint32_t r0[32], r1[32];
+        // pass 2: p = exp2(s * scale - m), packed to 16 bit, written over the S
+        // columns already read (chunk c's P lands in columns [16c, 16c + 16))
+        float rsp[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r[32];
+          tc::ld_32x32b_x32(s_addr + c * 32, r);
+          tc::wait_ld();
+          uint32_t pk[16];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            r0[i] = pk[i];
-            r1[i] = pk[32 + i];
+          for (int i = 0; i < 16; ++i) {
+            float s0 = __uint_as_float(r[2 * i]), s1 = __uint_as_float(r[2 * i + 1]);
+            if (need_mask) {
+              if (key0 + c * 32 + 2 * i > limit) s0 = -INFINITY;
+              if (key0 + c * 32 + 2 * i + 1 > limit) s1 = -INFINITY;
+            }
+            const float x0 = fmaf(s0, sl2, neg_m), x1 = fmaf(s1, sl2, neg_m);
+            const float p0 = ((2 * i) % 8 < PS_PREFILL_EMU_PER8) ? exp2_fma(x0) : ex2(x0);
+            const float p1 = ((2 * i + 1) % 8 < PS_PREFILL_EMU_PER8) ? exp2_fma(x1) : ex2(x1);
+            rsp[i & 7] += p0 + p1;
+            pk[i] = pack2<kBF16>(p0, p1);
           }
-          tc::st_32x32b_x32(lane_addr + sb * 128, r0);
-          tc::st_32x32b_x32(lane_addr + sb * 128 + 32, r1);
+          tmem_st_x16(s_addr + c * 16, pk);
         }
+        const float rs = ((rsp[0] + rsp[1]) + (rsp[2] + rsp[3])) + ((rsp[4] + rsp[5]) + (rsp[6] + rsp[7]));
+        l_run = l_run * factor + rs;
+        m_run = m_new;
         tc::wait_st();
         // last tile of the unit: V rows at or past kv_end must be finite (zero)
-        if (j == ui.ntiles - 1) {
+        // before PV_A reads them (group A does it; PV_B is issued after PV_A)
+        if (x == 0 && j == ui.ntiles - 1) {
           const int z0 = ui.kv_end - key0;
           if (z0 < kKeys) {
             const int s = t % kKvStages;
@@ -462,16 +494,16 @@ __global__ void __launch_bounds__(192, 1)
               *reinterpret_cast<uint4*>(vd + region * kRegionBytes + rr * 128 + (i & 7) * 16) =
                   make_uint4(0u, 0u, 0u, 0u);
             }
+            fence_proxy_async_smem();  // generic writes before the tensor core reads V
           }
         }
-        fence_proxy_async_smem();  // V tail zeroing (generic) before the MMA reads it
         tc::fence_before_sync();
         __syncwarp();
-        if (lane == 0) mbar_arrive(bars.p_full);
+        if (lane == 0) mbar_arrive(bars.p_full + x);
       }
       if (!ok) break;
       // ---- epilogue: O / l -> global ----
-      if (!pwait(bars.pv_done, static_cast<uint32_t>((t - 1) & 1), abort_flag, p.status)) break;
+      if (!pwait(bars.pv_done + x, static_cast<uint32_t>((t - 1) & 1), abort_flag, p.status)) break;
       tc::fence_after_sync();
       const bool zero = (l_run == 0.f) || (l_run != l_run);
       const float inv = zero ? 0.f : 1.f / l_run;
@@ -480,7 +512,7 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t r[32];
-        tc::ld_32x32b_x32(lane_addr + 256 + c * 32, r);
+        tc::ld_32x32b_x32(o_addr + c * 32, r);
         tc::wait_ld();
         if (row_valid) {
           uint8_t* dst = reinterpret_cast<uint8_t*>(p.out) +
@@ -526,7 +558,7 @@ static int launch_prefill_t(const PrefillParams& p, const CUtensorMap& qmap, con
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(192);
+  cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
