@@ -179,7 +179,12 @@ def run_ours(args):
     B = batch.num_seqs
     hq = batch.q.shape[1]
     hkv = batch.kv_cache.shape[3]
-    ws = ops.DecodeWorkspace(B, hq, hkv, 128, dev)
+    # GRPO groups share prompt pages: the cascade decode reads each prefix once
+    # per 16-column pass (opt-in: on B200 it is not faster than the plain
+    # decode, whose repeated prefix reads mostly hit L2)
+    cascade = cfg == 3 and args.cascade
+    ws = ops.DecodeWorkspace(B, hq, hkv, 128, dev, cascade=cascade)
+    plan = ops.CascadePlan(B, dev) if cascade else None
     out = torch.empty_like(batch.q)
     lse = torch.empty(hq, B, dtype=torch.float32, device=dev)
     kc, vc = batch.kv_cache[0], batch.kv_cache[1]
@@ -197,6 +202,9 @@ def run_ours(args):
             ops.kv_append(batch.key, batch.value, kc, vc, batch.slot_mapping)
         elif mixed:  # prefill tokens still go through the append kernel
             ops.kv_append(batch.key[nd:], batch.value[nd:], kc, vc, batch.slot_mapping[nd:])
+        if cascade:  # the per-step plan (a serving engine builds it once per step for all layers)
+            ops.cascade_plan(batch.block_table, batch.seq_lens, hq, hkv, 16,
+                             query_start_loc=batch.query_start_loc, plan=plan)
 
     if mixed:
         qlens = (batch.query_start_loc[1:] - batch.query_start_loc[:-1]).tolist()
@@ -210,7 +218,8 @@ def run_ours(args):
         if not mixed:
             ops.paged_decode(batch.q, kc, vc, batch.block_table, batch.seq_lens,
                              batch.softmax_scale, out, lse=lse,
-                             query_start_loc=batch.query_start_loc, workspace=ws, **fkw)
+                             query_start_loc=batch.query_start_loc, workspace=ws, cascade=plan,
+                             **fkw)
             return
         ops.paged_decode(batch.q[:nd], kc, vc, batch.block_table[:nd], batch.seq_lens[:nd],
                          batch.softmax_scale, out[:nd], workspace=ws, **fkw)
@@ -237,7 +246,7 @@ def run_ours(args):
             prefill()
             stream.synchronize()
         if use_graph:
-            fns = ([("append", append)] if (not fused or mixed) else []) + [("decode", decode)] + (
+            fns = ([("append", append)] if (not fused or mixed or cascade) else []) + [("decode", decode)] + (
                 [("prefill", prefill)] if mixed else [])
             for name, fn in fns:
                 g = torch.cuda.CUDAGraph()
@@ -317,7 +326,8 @@ def run_ours(args):
     # ---- end to end through the public API: host inputs in, host output back ----
     e2e = None if args.quick else run_e2e(batch, ws, dev, args.steps, world,
                                           nd=nd if mixed else None,
-                                          replicas=1 if sharded else world, fused=fused)
+                                          replicas=1 if sharded else world, fused=fused,
+                                          cascade=cascade)
 
     ms = elapsed_ms / args.steps
     tokens_per_step = batch.num_tokens  # every rank produces all tokens (its heads when sharded)
@@ -355,8 +365,13 @@ def run_ours(args):
         },
         "hbm_gbs_step": round(step_bytes / (ms / 1e3) / 1e9, 1),
         "hbm_frac_of_8tbs_step": round(step_bytes / (ms / 1e3) / 1e9 / NOMINAL_HBM_GBS, 4),
-        "gpu_launches": ((3 if mixed else 2) - (1 if fused and not mixed else 0)) * args.steps,
+        "gpu_launches": ((3 if mixed else 2) - (1 if fused and not mixed else 0)
+                         + (1 if cascade else 0)) * args.steps,
         "append_fused_into_decode": fused,
+        "cascade": (None if not cascade else {
+            "groups": int(plan.views()["num_groups"].item()),
+            "note": "shared prompt pages read once per 16-column pass; plan built every step "
+                    "(timed in append_ms); roofline bytes count each shared page once"}),
         "roofline": {"kernel": "paged_decode", "bound": "hbm", "achieved": round(achieved, 1),
                      "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
                      "frac": round(achieved / peak, 4),
@@ -385,7 +400,7 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
-def run_e2e(batch, ws, dev, steps, world, nd=None, replicas=1, fused=True):
+def run_e2e(batch, ws, dev, steps, world, nd=None, replicas=1, fused=True, cascade=False):
     """Same step through the public ops with per-step host->device inputs
     (pinned) and the device->host read of the attention output.  ``nd``:
     number of leading decode sequences of a mixed batch (the rest prefill)."""
@@ -401,6 +416,7 @@ def run_e2e(batch, ws, dev, steps, world, nd=None, replicas=1, fused=True):
     h2d = sum(v.numel() * v.element_size() for v in host.values())
     d2h = out.numel() * out.element_size()
     kc, vc = batch.kv_cache[0], batch.kv_cache[1]
+    plan = ops.CascadePlan(B, dev) if cascade else None
 
     def one():
         for k, v in host.items():
@@ -412,9 +428,13 @@ def run_e2e(batch, ws, dev, steps, world, nd=None, replicas=1, fused=True):
         elif nd is not None:
             ops.kv_append(dev_in["key"][nd:], dev_in["value"][nd:], kc, vc, dev_in["slot_mapping"][nd:])
         if nd is None:
+            if cascade:
+                ops.cascade_plan(dev_in["block_table"], dev_in["seq_lens"], hq,
+                                 kc.shape[2], kc.shape[1], query_start_loc=dev_in["query_start_loc"],
+                                 plan=plan)
             ops.paged_decode(dev_in["q"], kc, vc, dev_in["block_table"], dev_in["seq_lens"],
                              batch.softmax_scale, out, query_start_loc=dev_in["query_start_loc"],
-                             workspace=ws, **fkw)
+                             workspace=ws, cascade=plan, **fkw)
         else:
             ops.paged_decode(dev_in["q"][:nd], kc, vc, dev_in["block_table"][:nd],
                              dev_in["seq_lens"][:nd], batch.softmax_scale, out[:nd], workspace=ws,
@@ -559,6 +579,8 @@ def main():
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--unfused", action="store_true",
                     help="separate append launch instead of the append fused into decode")
+    ap.add_argument("--cascade", action="store_true",
+                    help="config 3: shared-prefix (cascade) decode with a per-step plan")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--quick", action="store_true",
                     help="timed steps only: no end-to-end, CPU baseline or clock sampling")

@@ -133,6 +133,7 @@ typedef struct {
  * buffer sized for max_num_seqs serves every step and every CUDA-graph
  * replay.  The buffer must be zeroed once before first use (the kernel keeps
  * its counters at zero between calls); its first int32 is the status word.
+ * After PS_DEV_WAIT_TIMEOUT the buffer must be zeroed again.
  */
 int64_t ps_paged_decode_workspace_size(int32_t num_seqs, int32_t num_q_heads,
                                        int32_t num_kv_heads, int32_t head_size);
@@ -161,7 +162,7 @@ int ps_paged_decode(const ps_paged_problem* problem, void* workspace, int64_t wo
  * live in a 16 MiB array inside the library, of which every GPU that loads it
  * holds one copy until the process exits.  Problems whose
  * ps_paged_decode_workspace_size exceeds 16 MiB are rejected with
- * PS_ERR_WORKSPACE (with 8 KV heads, GQA group <= 8 and 148 SMs: at most 356
+ * PS_ERR_WORKSPACE (with 8 KV heads, GQA group <= 8 and 148 SMs: at most 352
  * sequences per call).  Allocates nothing (no cudaMalloc / cudaFree).  The
  * first call on a device looks up the array's device address for that device;
  * make that first call before any stream capture.  All calls share the one
@@ -170,6 +171,44 @@ int ps_paged_decode(const ps_paged_problem* problem, void* workspace, int64_t wo
  * receives this call's PS_DEV_* bits.
  */
 int ps_paged_decode_static_scratch(const ps_paged_problem* problem, void* stream);
+
+/*
+ * Shared-prefix ("cascade") decode.  vLLM's FlashAttention backend runs
+ * cascade attention only when every request of the batch shares one prefix
+ * (flash_attn.py:1088-1130 use_cascade_attention, :1132-1223
+ * cascade_attention + merge_attn_states); GRPO rollouts instead share one
+ * prompt per group of samples.  These three calls generalise it to per-group
+ * prefixes; they have no single counterpart in the reference.
+ *
+ * ps_cascade_plan_build finds groups of adjacent decode sequences whose
+ * leading block-table entries are identical (what prefix caching produces
+ * for samples of one prompt) and writes them to `plan`, a device buffer of
+ * ps_cascade_plan_bytes(num_seqs) bytes, zeroed once before its first use.
+ * Only pages that are complete in every member count as shared; a group
+ * needs >= 2 members and >= min_shared_pages shared 16-token pages.  The
+ * plan is a function of block_table, seq_lens and query_start_loc: build it
+ * once per step and reuse it for every layer.  Plan layout (int32 words, B =
+ * num_seqs, Gm = max(1, B / 2)): [0] number of groups, [1] internal,
+ * [32, 32 + B) group of each sequence (-1: none), then first sequence, member
+ * count and shared pages of each group (Gm words each), then the pages each
+ * sequence shares with its predecessor (B words).
+ *
+ * ps_paged_decode_cascade computes exactly what ps_paged_decode computes
+ * (same outputs, LSE and fused append) for the problem the plan was built
+ * from: each group's shared pages are read once per 16 query columns
+ * (members x GQA heads) instead of once per member, and the prefix result is
+ * merged into each member's split combine.  num_seqs <= 2048 and GQA group <=
+ * 8.  A plan inconsistent with the problem sets PS_DEV_BAD_METADATA and the
+ * call runs as a plain decode.  The workspace (zeroed once) may be shared
+ * with ps_paged_decode if it has the larger of the two sizes.
+ */
+int64_t ps_cascade_plan_bytes(int32_t num_seqs);
+int ps_cascade_plan_build(const ps_paged_problem* problem, int32_t min_shared_pages, void* plan,
+                          int64_t plan_bytes, void* stream);
+int64_t ps_paged_decode_cascade_workspace_size(int32_t num_seqs, int32_t num_q_heads,
+                                               int32_t num_kv_heads, int32_t head_size);
+int ps_paged_decode_cascade(const ps_paged_problem* problem, const void* plan, int64_t plan_bytes,
+                            void* workspace, int64_t workspace_bytes, void* stream);
 
 /*
  * Chunked prefill: any q_len >= 1 per sequence, causal bottom-right, over the

@@ -224,3 +224,111 @@ def decode_slots(block_table, seq_lens, block_size):
     L = np.asarray(seq_lens, dtype=np.int64)
     pos = L - 1
     return bt[np.arange(len(L)), pos // block_size] * block_size + pos % block_size
+
+
+# --------------------------------------------------------------------------
+# Shared-prefix (cascade) plan and cascade attention
+# --------------------------------------------------------------------------
+def cascade_plan(block_table, seq_lens, query_start_loc=None, block_size=16,
+                 min_shared_pages=8, enabled=True):
+    """Groups of adjacent decode sequences with identical leading pages.
+
+    The batch-wide rule vLLM applies (``flash_attn.py:1088-1130``,
+    ``use_cascade_attention``: one prefix common to every request) made per
+    group, read off the block table the way prefix caching lays it out
+    (shared prompt blocks have one physical id):
+
+    * ``full(b) = (seq_len - 1) // 16`` complete 16-token pages before the page
+      of the last token (0 unless sequence b has exactly one query row);
+    * ``shared(b)``: leading pages whose block entries equal row ``b-1``'s,
+      capped at ``min(full(b), full(b-1))``; ``shared(0) = 0``;
+    * ``b`` starts a group if ``b == 0``, ``shared(b) < min_shared_pages`` or
+      ``shared(b) < shared(b+1)``;
+    * a group's pages = min of ``shared`` over its members after the first;
+      groups of >= 2 members are listed in order.
+
+    Returns a dict with the plan's arrays (int lists).
+    """
+    bt = np.asarray(block_table)
+    L = np.asarray(seq_lens, dtype=np.int64)
+    B = len(L)
+    sub = block_size // 16
+    maxp = bt.shape[1] * sub if bt.ndim == 2 else 0
+    qlen = (np.diff(np.asarray(query_start_loc, dtype=np.int64)) if query_start_loc is not None
+            else np.ones(B, dtype=np.int64))
+
+    def full(b):
+        if qlen[b] != 1 or L[b] < 1:
+            return 0
+        return int(min((L[b] - 1) // 16, maxp))
+
+    shared = [0] * B
+    if enabled:
+        for b in range(1, B):
+            F = min(full(b), full(b - 1))
+            E = (F + sub - 1) // sub
+            m = 0
+            while m < E and bt[b, m] == bt[b - 1, m]:
+                m += 1
+            shared[b] = min(m * sub, F)
+
+    def starts(b):
+        return b == 0 or shared[b] < min_shared_pages or (b + 1 < B and shared[b] < shared[b + 1])
+
+    groups = []  # [first, size, pages]
+    for b in range(B):
+        if starts(b):
+            groups.append([b, 1, None])
+        else:
+            grp = groups[-1]
+            grp[1] += 1
+            grp[2] = shared[b] if grp[2] is None else min(grp[2], shared[b])
+    seq_group = [-1] * B
+    listed = []
+    for first, size, pages in groups:
+        if size >= 2:
+            for b in range(first, first + size):
+                seq_group[b] = len(listed)
+            listed.append((first, size, pages))
+    return {
+        "num_groups": len(listed),
+        "seq_group": seq_group,
+        "group_first": [g[0] for g in listed],
+        "group_size": [g[1] for g in listed],
+        "group_pages": [g[2] for g in listed],
+        "shared_pages": shared,
+    }
+
+
+def cascade_decode(q, key_cache, value_cache, block_table, seq_lens, plan, softmax_scale):
+    """Decode attention evaluated the cascade way, for one query row per sequence.
+
+    For a grouped sequence: attention over the group's shared pages (read
+    from the first member's table) and over its own remaining pages, merged
+    with :func:`combine` -- what ``cascade_attention`` + ``merge_attn_states``
+    compute (``flash_attn.py:1132-1223``).  It equals
+    :func:`paged_attention` up to fp32 rounding; the tests use it to show the
+    prefix/suffix split is exact.
+    """
+    q = np.asarray(q, dtype=np.float32)
+    B = len(seq_lens)
+    Hq = q.shape[1]
+    out = np.zeros_like(q)
+    lse = np.full((Hq, B), -np.inf, dtype=np.float32)
+    for b in range(B):
+        Lb = int(seq_lens[b])
+        k = gather_pages(key_cache, block_table[b], Lb)
+        v = gather_pages(value_cache, block_table[b], Lb)
+        g = plan["seq_group"][b]
+        cut = 16 * plan["group_pages"][g] if g >= 0 else 0
+        parts = [(0, cut), (cut, Lb)] if cut > 0 else [(0, Lb)]
+        os_, ls_ = [], []
+        for lo, hi in parts:
+            o, l = attention_ref(q[b:b + 1], k[lo:hi], v[lo:hi], causal=False,
+                                 softmax_scale=softmax_scale)
+            os_.append(o[0])
+            ls_.append(l[:, 0])
+        o, l = combine(np.stack(os_), np.stack(ls_))
+        out[b] = o
+        lse[:, b] = l
+    return out, lse

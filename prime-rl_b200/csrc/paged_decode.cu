@@ -17,6 +17,17 @@
 //   the counter to the split count merges all partials (no waiting, so no
 //   spin).  A segment that fits in one warp's range writes the output directly.
 //
+// Shared-prefix ("cascade") mode: with a plan of groups of adjacent sequences
+//   whose leading block-table entries are identical (GRPO samples of one
+//   prompt), the page-head list starts with prefix segments: (group, kv head,
+//   pass) streams the group's shared pages once for up to 16 query columns
+//   (members x GQA heads) instead of once per member.  Each member's own
+//   segment starts after the prefix.  The prefix result enters every member's
+//   combine as one more split, so the output is the same softmax over the same
+//   keys (vLLM's cascade_attention + merge_attn_states,
+//   vllm/v1/attention/backends/flash_attn.py:1132-1223, generalised from one
+//   batch-wide prefix to per-group prefixes).
+//
 // Per warp: a private ring of kDecodeStages page buffers in shared memory, each
 // filled by four TMA tensor loads (K lo/hi 64 dims, V lo/hi) of a 16-token
 // page, 128-byte swizzled, completion on an mbarrier.  The first page of a
@@ -41,54 +52,154 @@ constexpr int kHeadDim = 128;
 constexpr int kBoxBytes = kPageTokens * 64 * 2;  // 2 KB: 16 rows x 128 bytes
 constexpr int kStageBytes = 4 * kBoxBytes;       // K lo, K hi, V lo, V hi
 constexpr int kQRowBytes = kHeadDim * 2 + 16;    // padded query row (conflict-free ldmatrix)
+constexpr int kPrefixNT = 2;                     // prefix segments: 16 query columns
+#ifndef PS_CASCADE_PREFIX_COST16
+#define PS_CASCADE_PREFIX_COST16 26
+#endif
+// Streaming time of a prefix page-head (16 query columns) relative to an own
+// page-head, in sixteenths: the stream-K cut weights the two kinds by it.
+constexpr int kCascadePrefixCost16 = PS_CASCADE_PREFIX_COST16;
 
-// Split-slot record: kG output rows of 128 fp32, then kG fp32 LSEs.
-template <int kG>
+enum { kPlain = 0, kCasPrefix = 1, kCasSuffix = 2 };
+
+// Split-slot record: kRec output rows of 128 fp32, then kRec fp32 LSEs.
+template <int kRec>
 __device__ __forceinline__ float* slot_o(const DecodeParams& p, int64_t slot, int row) {
-  return p.part + slot * (kG * (kHeadDim + 1)) + row * kHeadDim;
+  return p.part + slot * (kRec * (kHeadDim + 1)) + row * kHeadDim;
 }
-template <int kG>
+template <int kRec>
 __device__ __forceinline__ float* slot_lse(const DecodeParams& p, int64_t slot, int row) {
-  return p.part + slot * (kG * (kHeadDim + 1)) + kG * kHeadDim + row;
+  return p.part + slot * (kRec * (kHeadDim + 1)) + kRec * kHeadDim + row;
 }
 
+// Shared-memory tables built by the prologue.
+struct Tables {
+  const int* prefix;  // [B+1] exclusive scan of each sequence's own pages
+  const int* soff;    // [B]   cascade: pages of the sequence covered by its group prefix
+  const int* gph;     // [G+1] cascade: exclusive scan of pages * passes per group
+  const int* gu;      // [G+1] cascade: exclusive scan of passes per group
+  int G;
+  int mpp;            // cascade: group members per 16-column pass
+  int64_t pre_total;  // page-heads in the prefix region (Hkv * gph[G])
+  int64_t pre_units;  // prefix segments (Hkv * gu[G])
+  // Cost-weighted partition: a prefix page-head costs wp, an own one wo, and
+  // warp w streams the list positions whose cost offset lies in [w*Qc,
+  // (w+1)*Qc).  Qc >= max(wp, wo), so the non-empty ranges are exactly those
+  // of the first warps: a segment's split count is the number of warps its
+  // pages span.
+  int wp, wo;
+  int64_t Qc;
+};
+
+// Cost offset of list position i, and the warp that streams it.
+__device__ __forceinline__ int64_t list_cost(const Tables& tb, int64_t i) {
+  return i < tb.pre_total ? i * tb.wp : tb.pre_total * tb.wp + (i - tb.pre_total) * tb.wo;
+}
+__device__ __forceinline__ int64_t warp_of(const Tables& tb, int64_t i) {
+  return list_cost(tb, i) / tb.Qc;
+}
+// First list position whose cost offset is >= X.
+__device__ __forceinline__ int64_t list_at_cost(const Tables& tb, int64_t X) {
+  const int64_t xp = tb.pre_total * tb.wp;
+  if (X <= xp) return (X + tb.wp - 1) / tb.wp;
+  return tb.pre_total + (X - xp + tb.wo - 1) / tb.wo;
+}
+
+// Position in the page-head list.  Own segments: (b, h, page p of P, first page
+// `off`).  Prefix segments: b = first member, g = group, pass of `passes`,
+// `ncols` query columns, P = shared pages.
 struct Cursor {
-  int b, h, p, P;  // sequence, kv head, page within sequence, pages of sequence
+  int b, h, p, P, off;
+  int g, pass, passes, ncols;
 };
 
 __device__ __forceinline__ int seq_pages(const int* prefix, int b) {
   return prefix[b + 1] - prefix[b];
 }
 
-// Advance to the next page-head in (sequence, kv head, page) order.
-__device__ __forceinline__ void cursor_next(Cursor& c, const int* prefix, int num_kv_heads) {
-  if (++c.p < c.P) return;
-  c.p = 0;
-  if (++c.h < num_kv_heads) return;
-  c.h = 0;
-  do {
-    ++c.b;
-    c.P = seq_pages(prefix, c.b);
-  } while (c.P == 0);
+template <int kMode>
+__device__ __forceinline__ void load_group(Cursor& c, const DecodeParams& p, const Tables& tb) {
+  c.b = __ldg(p.cas_group_first + c.g);
+  const int size = __ldg(p.cas_group_size + c.g);
+  c.P = __ldg(p.cas_group_pages + c.g);
+  c.passes = (size + tb.mpp - 1) / tb.mpp;
+  c.ncols = min(tb.mpp, size - c.pass * tb.mpp) * p.group;
 }
 
-// Locate page-head gi; requires gi < total.
-__device__ __forceinline__ Cursor cursor_at(int64_t gi, const int* prefix, int num_seqs,
+// Advance to the next page-head in list order.
+template <int kMode>
+__device__ __forceinline__ void cursor_next(Cursor& c, const DecodeParams& p, const Tables& tb,
                                             int num_kv_heads) {
-  int lo = 0, hi = num_seqs - 1;  // largest b with prefix[b]*Hkv <= gi
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (static_cast<int64_t>(prefix[mid]) * num_kv_heads <= gi)
-      lo = mid;
-    else
-      hi = mid - 1;
+  if (++c.p < c.P) return;
+  c.p = 0;
+  if constexpr (kMode == kCasPrefix) {
+    if (++c.pass < c.passes) {
+      const int size = __ldg(p.cas_group_size + c.g);
+      c.ncols = min(tb.mpp, size - c.pass * tb.mpp) * p.group;
+      return;
+    }
+    c.pass = 0;
+    if (++c.h < num_kv_heads) {
+      c.ncols = min(tb.mpp, __ldg(p.cas_group_size + c.g)) * p.group;
+      return;
+    }
+    c.h = 0;
+    ++c.g;  // the caller never advances past the region's last page-head
+    load_group<kMode>(c, p, tb);
+  } else {
+    if (++c.h < num_kv_heads) return;
+    c.h = 0;
+    do {
+      ++c.b;
+      c.P = seq_pages(tb.prefix, c.b);
+    } while (c.P == 0);
+    if constexpr (kMode == kCasSuffix) c.off = tb.soff[c.b];
   }
+}
+
+// Locate page-head gi of the region; requires gi < the region's size.
+template <int kMode>
+__device__ __forceinline__ Cursor cursor_at(int64_t gi, const DecodeParams& p, const Tables& tb,
+                                            int num_kv_heads) {
   Cursor c;
-  c.b = lo;
-  c.P = seq_pages(prefix, lo);
-  const int64_t r = gi - static_cast<int64_t>(prefix[lo]) * num_kv_heads;
-  c.h = static_cast<int>(r / c.P);
-  c.p = static_cast<int>(r - static_cast<int64_t>(c.h) * c.P);
+  c.off = 0;
+  c.g = c.pass = c.passes = c.ncols = 0;
+  if constexpr (kMode == kCasPrefix) {
+    int lo = 0, hi = tb.G - 1;  // largest g with gph[g]*Hkv <= gi
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (static_cast<int64_t>(tb.gph[mid]) * num_kv_heads <= gi)
+        lo = mid;
+      else
+        hi = mid - 1;
+    }
+    c.g = lo;
+    c.pass = 0;
+    load_group<kMode>(c, p, tb);
+    const int64_t r = gi - static_cast<int64_t>(tb.gph[lo]) * num_kv_heads;
+    const int64_t per = static_cast<int64_t>(c.passes) * c.P;
+    c.h = static_cast<int>(r / per);
+    const int64_t rem = r - static_cast<int64_t>(c.h) * per;
+    c.pass = static_cast<int>(rem / c.P);
+    c.p = static_cast<int>(rem - static_cast<int64_t>(c.pass) * c.P);
+    const int size = __ldg(p.cas_group_size + c.g);
+    c.ncols = min(tb.mpp, size - c.pass * tb.mpp) * p.group;
+  } else {
+    int lo = 0, hi = p.num_seqs - 1;  // largest b with prefix[b]*Hkv <= gi
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (static_cast<int64_t>(tb.prefix[mid]) * num_kv_heads <= gi)
+        lo = mid;
+      else
+        hi = mid - 1;
+    }
+    c.b = lo;
+    c.P = seq_pages(tb.prefix, lo);
+    const int64_t r = gi - static_cast<int64_t>(tb.prefix[lo]) * num_kv_heads;
+    c.h = static_cast<int>(r / c.P);
+    c.p = static_cast<int>(r - static_cast<int64_t>(c.h) * c.P);
+    if constexpr (kMode == kCasSuffix) c.off = tb.soff[lo];
+  }
   return c;
 }
 
@@ -122,32 +233,61 @@ __device__ __forceinline__ int atomic_add_release_gpu(int* addr, int v) {
   return old;
 }
 
-// Merge the n partials of segment (b, h) held in slots [slot0, slot0 + n).
-// FA4 combine: lse_max over splits (0 if all -inf), scale_s =
-// exp2((lse_s - lse_max_cur) * log2e), lse = log(sum) + lse_max, inv = 0 for a
-// zero/NaN sum, O = sum_s scale_s * inv * O_s over splits with scale > 0.
-template <bool kBF16, int NT>
-__device__ __noinline__ void combine_segment(const DecodeParams& p, int b, int h, int64_t slot0,
-                                             int n,
-                                int lane) {
-  constexpr int kG = 8 * NT;
+// Merge partial records.  Sources: slots [slot0, slot0 + n) rows [0, nrows)
+// and, when xslot >= 0, slot xslot rows [xrow0, xrow0 + nrows).  FA4 combine:
+// lse_max over sources (0 if all -inf), scale_s = exp2((lse_s - lse_max_cur) *
+// log2e), lse = log(sum) + lse_max, inv = 0 for a zero/NaN sum, O = sum_s
+// scale_s * inv * O_s over sources with scale > 0.
+// kToRecord: row j goes to record dst_slot row j (fp32; dst_slot may be slot0:
+// every read of a row precedes its write), else to out/lse of sequence b,
+// query heads h * group + j.
+template <bool kBF16, int kRec, bool kToRecord>
+__device__ __noinline__ void combine_rows(const DecodeParams& p, int64_t slot0, int n,
+                                          int64_t xslot, int xrow0, int nrows, int b, int h,
+                                          int64_t dst_slot, int lane) {
   const int group = p.group;
-  const int qrow = p.qsl ? __ldg(p.qsl + b) : b;
+  const int ntot = n + (xslot >= 0 ? 1 : 0);
+  const int qrow = kToRecord ? 0 : (p.qsl ? __ldg(p.qsl + b) : b);
   const float kLog2e = 1.4426950408889634f;
-  if (n <= 32) {
-    // fast path: lane k owns split k; the loads of a phase are independent.
-    // Heads in chunks of 4 keep the register footprint small.
-    for (int j0 = 0; j0 < group; j0 += 4) {
+  auto src_slot = [&](int k) { return k < n ? slot0 + k : xslot; };
+  auto src_row = [&](int k, int j) { return k < n ? j : xrow0 + j; };
+  auto emit = [&](int j, float4 acc, float lse) {
+    if constexpr (kToRecord) {
+      reinterpret_cast<float4*>(slot_o<kRec>(p, dst_slot, j))[lane] = acc;
+      if (lane == 0) *slot_lse<kRec>(p, dst_slot, j) = lse;
+    } else {
+      const int qh = h * group + j;
+      const int64_t obase = qrow * p.o_st + qh * p.o_sh + lane * 4;
+      uint2 packed;
+      packed.x = pack2<kBF16>(acc.x, acc.y);
+      packed.y = pack2<kBF16>(acc.z, acc.w);
+      if constexpr (kBF16)
+        *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(p.out) + obase) = packed;
+      else
+        *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(p.out) + obase) = packed;
+      if (lane == 0 && p.lse != nullptr) p.lse[qh * p.lse_sh + qrow * p.lse_st] = lse;
+    }
+  };
+  if (ntot <= 32) {
+    // fast path: lane k owns source k; one LSE load per lane and row, and the
+    // O loads of a phase are independent of one another and of the weights
+    // (an empty source has weight 0 and an all-zero partial, so every source
+    // is accumulated unconditionally).  Rows in chunks of 4 keep the register
+    // footprint small.
+    const int64_t my_slot = src_slot(min(lane, ntot - 1));
+    for (int j0 = 0; j0 < nrows; j0 += 4) {
       float w[4], lse_out[4];
 #pragma unroll
       for (int jj = 0; jj < 4; ++jj) {
         const int j = j0 + jj;
-        const float ls = (lane < n && j < group) ? __ldcg(slot_lse<kG>(p, slot0 + lane, j)) : -INFINITY;
+        const float ls = (lane < ntot && j < nrows)
+                             ? __ldcg(slot_lse<kRec>(p, my_slot, src_row(lane, j)))
+                             : -INFINITY;
         float mx = ls;
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
         const float mx_cur = (mx == -INFINITY) ? 0.f : mx;
-        const float e = (lane < n) ? ex2(ls * kLog2e - mx_cur * kLog2e) : 0.f;
+        const float e = (lane < ntot) ? ex2(ls * kLog2e - mx_cur * kLog2e) : 0.f;
         float sum = e;
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
@@ -158,16 +298,14 @@ __device__ __noinline__ void combine_segment(const DecodeParams& p, int b, int h
       float4 acc[4];
 #pragma unroll
       for (int jj = 0; jj < 4; ++jj) acc[jj] = make_float4(0.f, 0.f, 0.f, 0.f);
-      // An empty split has weight 0 and an all-zero partial, so every split
-      // can be accumulated unconditionally; the loads then do not wait for
-      // the weights.
-      for (int k = 0; k < n; ++k) {
+      for (int k = 0; k < ntot; ++k) {
+        const int64_t sk = src_slot(k);
 #pragma unroll
         for (int jj = 0; jj < 4; ++jj) {
           const float wk = __shfl_sync(0xffffffffu, w[jj], k);
-          if (j0 + jj < group) {
+          if (j0 + jj < nrows) {
             const float4 o =
-                __ldcg(reinterpret_cast<const float4*>(slot_o<kG>(p, slot0 + k, j0 + jj)) + lane);
+                __ldcg(reinterpret_cast<const float4*>(slot_o<kRec>(p, sk, src_row(k, j0 + jj))) + lane);
             acc[jj].x += wk * o.x;
             acc[jj].y += wk * o.y;
             acc[jj].z += wk * o.z;
@@ -175,60 +313,77 @@ __device__ __noinline__ void combine_segment(const DecodeParams& p, int b, int h
           }
         }
       }
+      __syncwarp();  // every lane's reads of these rows precede the writes
 #pragma unroll
-      for (int jj = 0; jj < 4; ++jj) {
-        const int j = j0 + jj;
-        if (j < group) {
-          const int qh = h * group + j;
-          const int64_t obase = qrow * p.o_st + qh * p.o_sh + lane * 4;
-          uint2 packed;
-          packed.x = pack2<kBF16>(acc[jj].x, acc[jj].y);
-          packed.y = pack2<kBF16>(acc[jj].z, acc[jj].w);
-          if constexpr (kBF16)
-            *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(p.out) + obase) = packed;
-          else
-            *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(p.out) + obase) = packed;
-          if (lane == 0 && p.lse != nullptr) p.lse[qh * p.lse_sh + qrow * p.lse_st] = lse_out[jj];
-        }
-      }
+      for (int jj = 0; jj < 4; ++jj)
+        if (j0 + jj < nrows) emit(j0 + jj, acc[jj], lse_out[jj]);
     }
     return;
   }
-  // general path: any number of splits
-  for (int j = 0; j < group; ++j) {
-    float mx = -INFINITY;
-    for (int k = lane; k < n; k += 32) mx = fmaxf(mx, __ldcg(slot_lse<kG>(p, slot0 + k, j)));
+  // many sources: lane k owns sources k, k + 32, ...; still no load waits on
+  // another's result within a phase.
+  // Lane k owns sources k, k + 32, ...; every load of a phase is independent
+  // of the others (an empty source has weight 0 and an all-zero partial, so
+  // all sources are accumulated unconditionally).  Rows in chunks of 4 keep
+  // the register footprint small.
+  for (int j0 = 0; j0 < nrows; j0 += 4) {
+    float w[4], lse_out[4];
+    float mx_cur[4], inv[4];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    const float mx_cur = (mx == -INFINITY) ? 0.f : mx;
-    float sum = 0.f;
-    for (int k = lane; k < n; k += 32)
-      sum += ex2(__ldcg(slot_lse<kG>(p, slot0 + k, j)) * kLog2e - mx_cur * kLog2e);
+    for (int jj = 0; jj < 4; ++jj) {
+      const int j = j0 + jj;
+      float mx = -INFINITY;
+      if (j < nrows)
+        for (int k = lane; k < ntot; k += 32)
+          mx = fmaxf(mx, __ldcg(slot_lse<kRec>(p, src_slot(k), src_row(k, j))));
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    const float lse = __logf(sum) + mx;
-    const float inv = (sum == 0.f || sum != sum) ? 0.f : 1.f / sum;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int k = 0; k < n; ++k) {
-      const float w = ex2(__ldcg(slot_lse<kG>(p, slot0 + k, j)) * kLog2e - mx_cur * kLog2e) * inv;
-      if (w > 0.f) {
-        const float4 o = __ldcg(reinterpret_cast<const float4*>(slot_o<kG>(p, slot0 + k, j)) + lane);
-        acc.x += w * o.x;
-        acc.y += w * o.y;
-        acc.z += w * o.z;
-        acc.w += w * o.w;
+      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      mx_cur[jj] = (mx == -INFINITY) ? 0.f : mx;
+      float sum = 0.f;
+      if (j < nrows)
+        for (int k = lane; k < ntot; k += 32)
+          sum += ex2(__ldcg(slot_lse<kRec>(p, src_slot(k), src_row(k, j))) * kLog2e -
+                     mx_cur[jj] * kLog2e);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      lse_out[jj] = __logf(sum) + mx;
+      inv[jj] = (sum == 0.f || sum != sum) ? 0.f : 1.f / sum;
+    }
+    float4 acc[4];
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) acc[jj] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int k0 = 0; k0 < ntot; k0 += 32) {
+      // weights of sources k0 .. k0 + 31, one per lane
+      const int kl = k0 + lane;
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) {
+        const int j = j0 + jj;
+        w[jj] = (kl < ntot && j < nrows)
+                    ? ex2(__ldcg(slot_lse<kRec>(p, src_slot(kl), src_row(kl, j))) * kLog2e -
+                          mx_cur[jj] * kLog2e) * inv[jj]
+                    : 0.f;
+      }
+      const int kn = min(32, ntot - k0);
+      for (int kk = 0; kk < kn; ++kk) {
+        const int64_t sk = src_slot(k0 + kk);
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          const float wk = __shfl_sync(0xffffffffu, w[jj], kk);
+          if (j0 + jj < nrows) {
+            const float4 o = __ldcg(
+                reinterpret_cast<const float4*>(slot_o<kRec>(p, sk, src_row(k0 + kk, j0 + jj))) + lane);
+            acc[jj].x += wk * o.x;
+            acc[jj].y += wk * o.y;
+            acc[jj].z += wk * o.z;
+            acc[jj].w += wk * o.w;
+          }
+        }
       }
     }
-    const int qh = h * group + j;
-    const int64_t obase = qrow * p.o_st + qh * p.o_sh + lane * 4;
-    uint2 packed;
-    packed.x = pack2<kBF16>(acc.x, acc.y);
-    packed.y = pack2<kBF16>(acc.z, acc.w);
-    if constexpr (kBF16)
-      *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(p.out) + obase) = packed;
-    else
-      *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(p.out) + obase) = packed;
-    if (lane == 0 && p.lse != nullptr) p.lse[qh * p.lse_sh + qrow * p.lse_st] = lse;
+    __syncwarp();  // every lane's reads of these rows precede the writes
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj)
+      if (j0 + jj < nrows) emit(j0 + jj, acc[jj], lse_out[jj]);
   }
 }
 
@@ -237,131 +392,67 @@ __host__ __device__ constexpr int decode_qslot_bytes() {
   return 8 * NT * kQRowBytes;
 }
 
-template <int NT>
+template <int kQNT>
 __host__ __device__ constexpr int decode_smem_bytes_before_table() {
   // stages | per-warp query slots | mbarriers
   return kDecodeWarps * kDecodeStages * kStageBytes +
-         kDecodeWarps * kDecodeStages * decode_qslot_bytes<NT>() + kDecodeWarps * kDecodeStages * 8;
+         kDecodeWarps * kDecodeStages * decode_qslot_bytes<kQNT>() + kDecodeWarps * kDecodeStages * 8;
 }
 
-template <bool kBF16, int NT>
-__global__ void __launch_bounds__(kDecodeWarps * 32, kDecodeCtasPerSm)
-    paged_decode_kernel(const __grid_constant__ DecodeParams p,
-                        const __grid_constant__ CUtensorMap kmap,
-                        const __grid_constant__ CUtensorMap vmap) {
-  constexpr int D = kDecodeStages;
-  constexpr int kG = 8 * NT;
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  // 1024-byte alignment for the 128B-swizzled TMA destinations.
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~static_cast<uintptr_t>(1023));
-  uint8_t* qslots = smem + kDecodeWarps * D * kStageBytes;
-  uint64_t* bars =
-      reinterpret_cast<uint64_t*>(qslots + kDecodeWarps * D * decode_qslot_bytes<NT>());
-  int* prefix = reinterpret_cast<int*>(bars + kDecodeWarps * D);
-  __shared__ int s_warp_tot[kDecodeWarps];
+// Own segment of sequence b (cascade modes): its split geometry in the list.
+struct OwnSeg {
+  int64_t slot0;  // slot of its first split
+  int nsplit;
+};
+__device__ __forceinline__ OwnSeg own_segment(const Tables& tb, int b, int h, int Hkv) {
+  const int P = seq_pages(tb.prefix, b);
+  const int64_t seg0 = tb.pre_total + static_cast<int64_t>(tb.prefix[b]) * Hkv + static_cast<int64_t>(h) * P;
+  const int64_t fw = warp_of(tb, seg0), lw = warp_of(tb, seg0 + P - 1);
+  OwnSeg s;
+  s.slot0 = fw + tb.pre_units + static_cast<int64_t>(b) * Hkv + h;
+  s.nsplit = static_cast<int>(lw - fw + 1);
+  return s;
+}
 
-  const int tid = threadIdx.x;
-  const int warp = tid >> 5;
-  const int lane = tid & 31;
-  const int B = p.num_seqs;
+// Slot holding the merged prefix result of member b of group g for kv head h,
+// and the record row of its first query head.
+__device__ __forceinline__ void prefix_result(const DecodeParams& p, const Tables& tb, int g, int b,
+                                              int h, int Hkv, int64_t& slot, int& row0) {
+  const int first = __ldg(p.cas_group_first + g);
+  const int size = __ldg(p.cas_group_size + g);
+  const int pages = __ldg(p.cas_group_pages + g);
+  const int passes = (size + tb.mpp - 1) / tb.mpp;
+  const int m = b - first;
+  const int pass = m / tb.mpp;
+  const int64_t seg0 = static_cast<int64_t>(tb.gph[g]) * Hkv + (static_cast<int64_t>(h) * passes + pass) * pages;
+  const int64_t unit = static_cast<int64_t>(tb.gu[g]) * Hkv + static_cast<int64_t>(h) * passes + pass;
+  slot = warp_of(tb, seg0) + unit;
+  row0 = (m - pass * tb.mpp) * p.group;
+}
+
+// One warp streams page-heads [start, end) of one region of the list (plain
+// list, cascade prefix region, or cascade own-segment region; indices are
+// global list positions).  k0: ring uses so far by this warp.  Returns the ring
+// uses after the range, or -1 after a wait timeout.
+template <bool kBF16, int NT, int kRec, int kQNT, int kMode>
+__device__ __forceinline__ int stream_range(const DecodeParams& p, const CUtensorMap* kmap,
+                                            const CUtensorMap* vmap, const Tables& tb,
+                                            int64_t start, int64_t end, int64_t gw,
+                                            uint8_t* wsm, uint8_t* wq, uint64_t* wbar, int k0,
+                                            int lane) {
+  constexpr int D = kDecodeStages;
   const int Hkv = p.num_kv_heads;
   const int sub_per_block = p.block_size / kPageTokens;
-
-  if (tid == 0) {
-    tma_prefetch_desc(&kmap);
-    tma_prefetch_desc(&vmap);
-  }
-  if (lane == 0) {
-    for (int s = 0; s < D; ++s) mbar_init(&bars[warp * D + s], 1);
-    fence_mbar_init();
-  }
-  // Programmatic dependent launch: everything above overlaps the previous
-  // kernel in the stream; global memory is read only after it completes.
-  asm volatile("griddepcontrol.wait;" ::: "memory");
-
-  // ---- prologue: pages per sequence and their exclusive prefix sum ----------
-  const int per = (B + blockDim.x - 1) / blockDim.x;
-  const int b_lo = min(B, tid * per), b_hi = min(B, b_lo + per);
-  int local = 0;
-  int bad = 0;
-  for (int b = b_lo; b < b_hi; ++b) {
-    int L = __ldg(p.seq_lens + b);
-    int qlen = 1;
-    if (p.qsl) qlen = __ldg(p.qsl + b + 1) - __ldg(p.qsl + b);
-    int P = 0;
-    if (qlen == 1) {
-      if (L < 0) {
-        L = 0;
-        bad = 1;
-      }
-      P = (L + kPageTokens - 1) / kPageTokens;
-      const int maxP = p.max_blocks_per_seq * sub_per_block;
-      if (P > maxP) {
-        P = maxP;
-        bad = 1;
-      }
-    } else if (qlen != 0) {
-      bad = 1;  // multi-token queries belong to the prefill kernel
-    }
-    local += P;
-  }
-  // block exclusive scan of `local`
-  int incl = local;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int v = __shfl_up_sync(0xffffffffu, incl, o);
-    if (lane >= o) incl += v;
-  }
-  if (lane == 31) s_warp_tot[warp] = incl;
-  const int any_bad = __syncthreads_or(bad);
-  int warp_off = 0;
-  for (int w = 0; w < warp; ++w) warp_off += s_warp_tot[w];
-  int run = warp_off + incl - local;
-  for (int b = b_lo; b < b_hi; ++b) {
-    prefix[b] = run;
-    const int L = __ldg(p.seq_lens + b);
-    int qlen = 1;
-    if (p.qsl) qlen = __ldg(p.qsl + b + 1) - __ldg(p.qsl + b);
-    int P = 0;
-    if (qlen == 1) {
-      P = (max(L, 0) + kPageTokens - 1) / kPageTokens;
-      P = min(P, p.max_blocks_per_seq * sub_per_block);
-    }
-    run += P;
-  }
-  if (tid == blockDim.x - 1) prefix[B] = warp_off + incl;  // last thread owns the tail
-  __syncthreads();
-  if (tid == 0 && any_bad) set_status(p.status, PS_DEV_BAD_METADATA);
-
-  const int total_pages = prefix[B];
-  const int64_t total = static_cast<int64_t>(total_pages) * Hkv;
-  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kDecodeWarps;
-  const int64_t Q = total > 0 ? (total + nwarps - 1) / nwarps : 1;
-
-  // ---- empty sequences (q_len 1, seq_len 0): zero output, LSE -inf ----------
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + tid;
-       i < static_cast<int64_t>(B) * p.num_q_heads; i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int b = static_cast<int>(i / p.num_q_heads);
-    const int qh = static_cast<int>(i - static_cast<int64_t>(b) * p.num_q_heads);
-    int qlen = 1;
-    if (p.qsl) qlen = __ldg(p.qsl + b + 1) - __ldg(p.qsl + b);
-    if (qlen != 1 || prefix[b + 1] != prefix[b]) continue;
-    const int qrow = p.qsl ? __ldg(p.qsl + b) : b;
-    for (int d = 0; d < kHeadDim; ++d) store_out2<kBF16>(p.out, qrow * p.o_st + qh * p.o_sh + d, 0.f);
-    if (p.lse) p.lse[qh * p.lse_sh + qrow * p.lse_st] = -INFINITY;
-  }
-
-  const int64_t gw = static_cast<int64_t>(blockIdx.x) * kDecodeWarps + warp;
-  const int64_t start = gw * Q;
-  const int64_t end = min(total, start + Q);
-  if (start >= end) return;
-  const int cnt = static_cast<int>(end - start);
-
-  uint8_t* wsm = smem + warp * D * kStageBytes;
-  uint8_t* wq = qslots + warp * D * decode_qslot_bytes<NT>();
-  uint64_t* wbar = bars + warp * D;
   const int group = p.group;
+  const int cnt = static_cast<int>(end - start);
+  const int64_t base = (kMode == kCasSuffix) ? tb.pre_total : 0;
+
+  if (k0 > 0) {
+    // the ring and query slots were last read by this warp's generic-proxy
+    // loads; order them before the async-proxy refills
+    fence_proxy_async_smem();
+    __syncwarp();
+  }
 
   // ---- producer state: block-table entries cached 32 at a time --------------
   int bt_b = -1, bt_e0 = 0, bt_reg = 0;
@@ -370,7 +461,8 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, kDecodeCtasPerSm)
   // Issue the TMA loads of page-head c into `stage` (warp-collective).
   // `seg_start`: c begins a segment for this warp -> also bring its query rows.
   auto issue = [&](int stage, const Cursor& c, bool seg_start) {
-    const int e = c.p / sub_per_block;
+    const int pg = c.p + c.off;
+    const int e = pg / sub_per_block;
     if (c.b != bt_b || e < bt_e0 || e >= bt_e0 + 32) {
       bt_b = c.b;
       bt_e0 = e;
@@ -378,10 +470,11 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, kDecodeCtasPerSm)
       bt_reg = idx < p.max_blocks_per_seq ? __ldg(p.block_table + c.b * p.bt_stride + idx) : 0;
     }
     int blk = __shfl_sync(0xffffffffu, bt_reg, e - bt_e0);
-    const int sub = c.p - e * sub_per_block;
+    const int sub = pg - e * sub_per_block;
     uint8_t* dst = wsm + stage * kStageBytes;
     uint64_t* bar = wbar + stage;
-    const uint32_t qbytes = seg_start ? static_cast<uint32_t>(group) * (kHeadDim * 2) : 0u;
+    const int nrows = (kMode == kCasPrefix) ? c.ncols : group;
+    const uint32_t qbytes = seg_start ? static_cast<uint32_t>(nrows) * (kHeadDim * 2) : 0u;
     if (lane == 0) {
       if (blk < 0 || blk >= p.num_blocks) {
         set_status(p.status, PS_DEV_BLOCK_OUT_OF_RANGE);
@@ -389,38 +482,43 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, kDecodeCtasPerSm)
       }
       mbar_arrive_expect_tx(bar, kStageBytes + qbytes);
       const int tok = sub * kPageTokens;
-      tma_load_4d(dst + 0 * kBoxBytes, &kmap, bar, 0, c.h, tok, blk);
-      tma_load_4d(dst + 1 * kBoxBytes, &kmap, bar, 64, c.h, tok, blk);
-      tma_load_4d(dst + 2 * kBoxBytes, &vmap, bar, 0, c.h, tok, blk);
-      tma_load_4d(dst + 3 * kBoxBytes, &vmap, bar, 64, c.h, tok, blk);
+      tma_load_4d(dst + 0 * kBoxBytes, kmap, bar, 0, c.h, tok, blk);
+      tma_load_4d(dst + 1 * kBoxBytes, kmap, bar, 64, c.h, tok, blk);
+      tma_load_4d(dst + 2 * kBoxBytes, vmap, bar, 0, c.h, tok, blk);
+      tma_load_4d(dst + 3 * kBoxBytes, vmap, bar, 64, c.h, tok, blk);
     }
     if (seg_start) {
       __syncwarp();  // expect_tx is armed before the row copies complete_tx
-      if (lane < group) {
-        const int qrow = p.qsl ? __ldg(p.qsl + c.b) : c.b;
-        const uint16_t* src = reinterpret_cast<const uint16_t*>(p.q) + qrow * p.q_st +
-                              (c.h * group + lane) * p.q_sh;
-        bulk_load(wq + (pseg % D) * decode_qslot_bytes<NT>() + lane * kQRowBytes, src,
+      if (lane < nrows) {
+        int seq = c.b, qh = c.h * group + lane;
+        if constexpr (kMode == kCasPrefix) {
+          // column lane -> (member, query head) of this pass
+          const int mem = lane / group;
+          seq = c.b + c.pass * tb.mpp + mem;
+          qh = c.h * group + (lane - mem * group);
+        }
+        const int qrow = p.qsl ? __ldg(p.qsl + seq) : seq;
+        const uint16_t* src = reinterpret_cast<const uint16_t*>(p.q) + qrow * p.q_st + qh * p.q_sh;
+        bulk_load(wq + (pseg % D) * decode_qslot_bytes<kQNT>() + lane * kQRowBytes, src,
                   kHeadDim * 2, bar);
       }
       ++pseg;
     }
   };
 
-  const int* cprefix = prefix;
   // pc always names the most recently issued page-head; cc the one consumed next.
-  Cursor pc = cursor_at(start, cprefix, B, Hkv);
+  Cursor pc = cursor_at<kMode>(start - base, p, tb, Hkv);
   Cursor cc = pc;
   const int npre = min(cnt, D);
   for (int k = 0; k < npre; ++k) {
-    if (k > 0) cursor_next(pc, cprefix, Hkv);
-    issue(k, pc, k == 0 || pc.p == 0);
+    if (k > 0) cursor_next<kMode>(pc, p, tb, Hkv);
+    issue((k0 + k) % D, pc, k == 0 || pc.p == 0);
   }
   int issued = npre;
 
   const int g = lane >> 2;  // MMA row group
   const int t = lane & 3;   // MMA thread-in-group
-  // per-lane ldmatrix row/chunk offsets (see header comment)
+  // per-lane ldmatrix row/chunk offsets
   const int k_mi = lane >> 3;
   const int k_row = (lane & 7) + ((k_mi & 1) << 3);
   const int k_chk = k_mi >> 1;
@@ -431,28 +529,35 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, kDecodeCtasPerSm)
   float o[NT][8][4];
   float m[NT][2], l[NT][2];
   int L = 0;
+  int ncols = group;
   int cseg = 0;  // segments started on the consumer side
   // fused append: this lane's 16 bytes of the new key (lanes 0-15) or value
   // (lanes 16-31) row of the current segment's (sequence, kv head)
-  const bool fused = p.new_key != nullptr;
+  const bool fused = (kMode != kCasPrefix) && p.new_key != nullptr;
   uint4 new_row = make_uint4(0u, 0u, 0u, 0u);
   int64_t new_slot = -1;
 
   for (int k = 0; k < cnt; ++k) {
-    const int stage = k % D;
-    const uint32_t phase = static_cast<uint32_t>((k / D) & 1);
+    const int kr = k0 + k;
+    const int stage = kr % D;
+    const uint32_t phase = static_cast<uint32_t>((kr / D) & 1);
     uint8_t* st = wsm + stage * kStageBytes;
     if (!mbar_wait_bounded(wbar + stage, phase)) {
       if (lane == 0) set_status(p.status, PS_DEV_WAIT_TIMEOUT);
       // drain copies still in flight into this warp's ring, bounded
       for (int kk = k + 1; kk < issued; ++kk)
-        if (!mbar_wait_bounded(wbar + kk % D, static_cast<uint32_t>((kk / D) & 1))) break;
-      return;
+        if (!mbar_wait_bounded(wbar + (k0 + kk) % D, static_cast<uint32_t>(((k0 + kk) / D) & 1))) break;
+      return -1;
     }
 
     // ---- segment start: query fragments from the slot, reset state ------------
     if (k == 0 || cc.p == 0) {
-      L = __ldg(p.seq_lens + cc.b);
+      if constexpr (kMode == kCasPrefix) {
+        L = cc.P * kPageTokens;  // shared pages are complete for every member
+        ncols = cc.ncols;
+      } else {
+        L = __ldg(p.seq_lens + cc.b);
+      }
       if (fused) {
         // fetch the new token's row now; it is written when the segment's last
         // page comes through this warp (the warp that owns that page)
@@ -464,11 +569,11 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, kDecodeCtasPerSm)
             : reinterpret_cast<const uint16_t*>(p.new_value) + qrow * p.nv_st + cc.h * p.nv_sh;
         new_row = __ldg(reinterpret_cast<const uint4*>(src) + c);
       }
-      const uint32_t qbase = smem_u32(wq + (cseg % D) * decode_qslot_bytes<NT>());
+      const uint32_t qbase = smem_u32(wq + (cseg % D) * decode_qslot_bytes<kQNT>());
       ++cseg;
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
-        const bool ok = nt * 8 + g < group;
+        const bool ok = nt * 8 + g < ncols;
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
           // matrices: heads nt*8..+7 x dims 32i + 8*(lane/8) .. +7
@@ -489,7 +594,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, kDecodeCtasPerSm)
       }
     }
 
-    const int valid = min(kPageTokens, L - cc.p * kPageTokens);
+    const int valid = min(kPageTokens, L - (cc.p + cc.off) * kPageTokens);
 
     // ---- fused append: the sequence's last page carries the new token -----
     if (fused && cc.p == cc.P - 1 && new_slot >= 0) {
@@ -595,7 +700,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, kDecodeCtasPerSm)
     // ---- refill this stage with the page D ahead -------------------------------
     if (issued < cnt) {
       fence_proxy_async_smem();
-      cursor_next(pc, cprefix, Hkv);
+      cursor_next<kMode>(pc, p, tb, Hkv);
       issue(stage, pc, pc.p == 0);
       ++issued;
     }
@@ -604,11 +709,23 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, kDecodeCtasPerSm)
     const bool seg_end = (cc.p == cc.P - 1) || (k == cnt - 1);
     if (seg_end) {
       const int b = cc.b, h = cc.h;
-      const int64_t seg0 = (static_cast<int64_t>(cprefix[b]) * Hkv + static_cast<int64_t>(h) * cc.P);
-      const int64_t first_w = seg0 / Q;
-      const int64_t last_w = (seg0 + cc.P - 1) / Q;
+      // list position of the segment's first page-head and its unit index
+      int64_t seg0, unit;
+      if constexpr (kMode == kCasPrefix) {
+        seg0 = static_cast<int64_t>(tb.gph[cc.g]) * Hkv +
+               (static_cast<int64_t>(h) * cc.passes + cc.pass) * cc.P;
+        unit = static_cast<int64_t>(tb.gu[cc.g]) * Hkv + static_cast<int64_t>(h) * cc.passes + cc.pass;
+      } else {
+        seg0 = base + static_cast<int64_t>(tb.prefix[b]) * Hkv + static_cast<int64_t>(h) * cc.P;
+        unit = tb.pre_units + static_cast<int64_t>(b) * Hkv + h;
+      }
+      // (plain list: every page-head costs 1, so the warp is position / quota)
+      const int64_t first_w = kMode == kPlain ? seg0 / tb.Qc : warp_of(tb, seg0);
+      const int64_t last_w = kMode == kPlain ? (seg0 + cc.P - 1) / tb.Qc : warp_of(tb, seg0 + cc.P - 1);
       const int nsplit = static_cast<int>(last_w - first_w + 1);
-      const int qrow = p.qsl ? __ldg(p.qsl + b) : b;
+      // cascade: an own segment whose sequence has a group prefix always
+      // writes a partial; the prefix arrives as one more split
+      const bool member = (kMode == kCasSuffix) && cc.off > 0;
       float inv[NT][2], lse[NT][2];
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
@@ -619,7 +736,8 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, kDecodeCtasPerSm)
           inv[nt][j] = zero ? 0.f : 1.f / lt;
           lse[nt][j] = zero ? -INFINITY : (m[nt][j] + __log2f(lt)) * 0.6931471805599453f;
         }
-      if (nsplit == 1) {
+      if (kMode != kCasPrefix && nsplit == 1 && !member) {
+        const int qrow = p.qsl ? __ldg(p.qsl + b) : b;
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -637,51 +755,349 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, kDecodeCtasPerSm)
             }
           }
       } else {
-        const int64_t slot = gw + static_cast<int64_t>(b) * Hkv + h;
+        const int64_t slot = gw + unit;
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
           for (int j = 0; j < 2; ++j) {
             const int col = nt * 8 + 2 * t + j;
-            float* po = slot_o<kG>(p, slot, col);
+            if (col < kRec) {
+              float* po = slot_o<kRec>(p, slot, col);
 #pragma unroll
-            for (int mi = 0; mi < 8; ++mi) {
-              po[mi * 16 + g] = o[nt][mi][j] * inv[nt][j];
-              po[mi * 16 + g + 8] = o[nt][mi][j + 2] * inv[nt][j];
+              for (int mi = 0; mi < 8; ++mi) {
+                po[mi * 16 + g] = o[nt][mi][j] * inv[nt][j];
+                po[mi * 16 + g + 8] = o[nt][mi][j + 2] * inv[nt][j];
+              }
+              if (g == 0) *slot_lse<kRec>(p, slot, col) = lse[nt][j];
             }
-            if (g == 0) *slot_lse<kG>(p, slot, col) = lse[nt][j];
           }
         // release: the warp's partial is visible (gpu scope) before the count
         __syncwarp();
-        int last = 0;
-        if (lane == 0) {
-          const int old = atomic_add_release_gpu(p.counters + b * Hkv + h, 1);
-          last = (old == nsplit - 1);
-          if (last) fence_acq_rel_gpu();  // acquire the other splits' partials
-        }
-        last = __shfl_sync(0xffffffffu, last, 0);
-        if (last) {
-          combine_segment<kBF16, NT>(p, b, h, first_w + static_cast<int64_t>(b) * Hkv + h, nsplit, lane);
-          if (lane == 0) p.counters[b * Hkv + h] = 0;
+        if constexpr (kMode == kCasPrefix) {
+          bool done = nsplit == 1;
+          if (!done) {
+            int last = 0;
+            if (lane == 0) {
+              const int old = atomic_add_release_gpu(p.pre_counters + unit, 1);
+              last = (old == nsplit - 1);
+              if (last) fence_acq_rel_gpu();
+            }
+            done = __shfl_sync(0xffffffffu, last, 0) != 0;
+            __syncwarp();  // lane 0's acquire orders the whole warp's reads
+            if (done) {
+              // merge the prefix splits in place into the first split's record
+              const int64_t s0 = first_w + unit;
+              combine_rows<kBF16, kRec, true>(p, s0, nsplit, -1, 0, ncols, 0, 0, s0, lane);
+              if (lane == 0) p.pre_counters[unit] = 0;
+              __syncwarp();
+            }
+          }
+          if (done) {
+            // the prefix result is complete: count it into every member's
+            // combine; the member whose count completes is merged here
+            const int nmem = ncols / group;
+            int lastm = 0;
+            if (lane < nmem) {
+              const int bm = b + cc.pass * tb.mpp + lane;
+              const OwnSeg os = own_segment(tb, bm, h, Hkv);
+              const int old = atomic_add_release_gpu(p.counters + bm * Hkv + h, 1);
+              lastm = (old == os.nsplit);  // own splits + this prefix
+              if (lastm) fence_acq_rel_gpu();
+            }
+            unsigned todo = __ballot_sync(0xffffffffu, lastm);
+            __syncwarp();
+            while (todo) {
+              const int mm = __ffs(todo) - 1;
+              todo &= todo - 1;
+              const int bm = b + cc.pass * tb.mpp + mm;
+              const OwnSeg os = own_segment(tb, bm, h, Hkv);
+              combine_rows<kBF16, kRec, false>(p, os.slot0, os.nsplit, first_w + unit, mm * group,
+                                               group, bm, h, 0, lane);
+              if (lane == 0) p.counters[bm * Hkv + h] = 0;
+            }
+          }
+        } else {
+          const int total = nsplit + (member ? 1 : 0);
+          int last = 0;
+          if (lane == 0) {
+            const int old = atomic_add_release_gpu(p.counters + b * Hkv + h, 1);
+            last = (old == total - 1);
+            if (last) fence_acq_rel_gpu();  // acquire the other splits' partials
+          }
+          last = __shfl_sync(0xffffffffu, last, 0);
+          __syncwarp();  // lane 0's acquire orders the whole warp's reads
+          if (last) {
+            int64_t xslot = -1;
+            int xrow0 = 0;
+            if (member) prefix_result(p, tb, __ldg(p.cas_seq_group + b), b, h, Hkv, xslot, xrow0);
+            combine_rows<kBF16, kRec, false>(p, first_w + unit, nsplit, xslot, xrow0, group, b, h, 0,
+                                             lane);
+            if (lane == 0) p.counters[b * Hkv + h] = 0;
+          }
         }
       }
     }
-    if (k + 1 < cnt) cursor_next(cc, cprefix, Hkv);
+    if (k + 1 < cnt) cursor_next<kMode>(cc, p, tb, Hkv);
+  }
+  return k0 + cnt;
+}
+
+// Exclusive scan over the block of one int per thread; *total gets the sum.
+// s_warp: kDecodeWarps ints of shared memory.  Contains __syncthreads.
+__device__ __forceinline__ int block_exclusive_scan(int v, int* s_warp, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int u = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += u;
+  }
+  if (lane == 31) s_warp[warp] = incl;
+  __syncthreads();
+  int off = 0, tot = 0;
+  for (int w = 0; w < kDecodeWarps; ++w) {
+    const int x = s_warp[w];
+    if (w < warp) off += x;
+    tot += x;
+  }
+  __syncthreads();
+  *total = tot;
+  return off + incl - v;
+}
+
+__device__ __forceinline__ int own_pages_of(const DecodeParams& p, int b, int sub_per_block) {
+  int qlen = 1;
+  if (p.qsl) qlen = __ldg(p.qsl + b + 1) - __ldg(p.qsl + b);
+  if (qlen != 1) return 0;
+  const int L = __ldg(p.seq_lens + b);
+  const int P = (max(L, 0) + kPageTokens - 1) / kPageTokens;
+  return min(P, p.max_blocks_per_seq * sub_per_block);
+}
+
+template <bool kBF16, int NT, bool kCascade>
+__global__ void __launch_bounds__(kDecodeWarps * 32, kDecodeCtasPerSm)
+    paged_decode_kernel(const __grid_constant__ DecodeParams p,
+                        const __grid_constant__ CUtensorMap kmap,
+                        const __grid_constant__ CUtensorMap vmap) {
+  constexpr int D = kDecodeStages;
+  constexpr int kQNT = kCascade ? kPrefixNT : NT;
+  constexpr int kRec = kCascade ? 8 * kPrefixNT : 8 * NT;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // 1024-byte alignment for the 128B-swizzled TMA destinations.
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* qslots = smem + kDecodeWarps * D * kStageBytes;
+  uint64_t* bars =
+      reinterpret_cast<uint64_t*>(qslots + kDecodeWarps * D * decode_qslot_bytes<kQNT>());
+  int* prefix = reinterpret_cast<int*>(bars + kDecodeWarps * D);
+  __shared__ int s_warp_tot[kDecodeWarps];
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int B = p.num_seqs;
+  const int Hkv = p.num_kv_heads;
+  const int sub_per_block = p.block_size / kPageTokens;
+
+  if (tid == 0) {
+    tma_prefetch_desc(&kmap);
+    tma_prefetch_desc(&vmap);
+  }
+  if (lane == 0) {
+    for (int s = 0; s < D; ++s) mbar_init(&bars[warp * D + s], 1);
+    fence_mbar_init();
+  }
+  // Programmatic dependent launch: everything above overlaps the previous
+  // kernel in the stream; global memory is read only after it completes.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+
+  Tables tb;
+  tb.prefix = prefix;
+  tb.soff = nullptr;
+  tb.gph = nullptr;
+  tb.gu = nullptr;
+  tb.G = 0;
+  tb.mpp = 1;
+  tb.pre_total = 0;
+  tb.pre_units = 0;
+  tb.wp = 1;
+  tb.wo = 1;
+  tb.Qc = 1;
+
+  // ---- prologue: pages per sequence and their exclusive prefix sum ----------
+  const int per = (B + blockDim.x - 1) / blockDim.x;
+  const int b_lo = min(B, tid * per), b_hi = min(B, b_lo + per);
+  int bad = 0;
+  for (int b = b_lo; b < b_hi; ++b) {
+    const int L = __ldg(p.seq_lens + b);
+    int qlen = 1;
+    if (p.qsl) qlen = __ldg(p.qsl + b + 1) - __ldg(p.qsl + b);
+    if (qlen == 1) {
+      if (L < 0) bad = 1;
+      if ((max(L, 0) + kPageTokens - 1) / kPageTokens > p.max_blocks_per_seq * sub_per_block) bad = 1;
+    } else if (qlen != 0) {
+      bad = 1;  // multi-token queries belong to the prefill kernel
+    }
+  }
+
+  int* soff = nullptr;
+  int G = 0;
+  if constexpr (kCascade) {
+    // plan tables follow the sequence scan: soff[B], gph[Gmax+1], gu[Gmax+1]
+    soff = prefix + B + 1;
+    int* gph = soff + B;
+    int* gu = gph + p.cas_max_groups + 1;
+    G = min(max(__ldg(p.cas_num_groups), 0), p.cas_max_groups);
+    tb.mpp = max(1, 16 / p.group);
+    tb.wp = kCascadePrefixCost16;  // 16-column prefix pages cost more than own pages
+    tb.wo = 16;
+    // validate the plan; an invalid plan runs as a plain decode
+    int bad_plan = tb.mpp < 2 && G > 0;
+    for (int gi = tid; gi < G && !bad_plan; gi += blockDim.x) {
+      const int f = __ldg(p.cas_group_first + gi), s = __ldg(p.cas_group_size + gi);
+      const int pg = __ldg(p.cas_group_pages + gi);
+      if (s < 2 || s > B || f < 0 || f > B - s || pg < 1 ||
+          (gi > 0 && f < __ldg(p.cas_group_first + gi - 1) + __ldg(p.cas_group_size + gi - 1))) {
+        bad_plan = 1;
+        break;
+      }
+      for (int mm = 0; mm < s; ++mm) {
+        const int b = f + mm;
+        if (__ldg(p.cas_seq_group + b) != gi || own_pages_of(p, b, sub_per_block) - 1 < pg) {
+          bad_plan = 1;
+          break;
+        }
+      }
+    }
+    for (int b = b_lo; b < b_hi && !bad_plan; ++b) {
+      const int gsb = __ldg(p.cas_seq_group + b);
+      if (gsb >= G) bad_plan = 1;
+      else if (gsb >= 0) {
+        const int f = __ldg(p.cas_group_first + gsb);
+        if (b < f || b >= f + __ldg(p.cas_group_size + gsb)) bad_plan = 1;
+      }
+    }
+    if (__syncthreads_or(bad_plan)) {
+      G = 0;
+      bad = 1;
+    }
+    tb.soff = soff;
+    tb.gph = gph;
+    tb.gu = gu;
+    tb.G = G;
+    // group scans: pages * passes and passes
+    const int gper = (G + blockDim.x - 1) / blockDim.x;
+    const int g_lo = min(G, tid * gper), g_hi = min(G, g_lo + gper);
+    int lph = 0, lu = 0;
+    for (int gi = g_lo; gi < g_hi; ++gi) {
+      const int passes = (__ldg(p.cas_group_size + gi) + tb.mpp - 1) / tb.mpp;
+      lph += passes * __ldg(p.cas_group_pages + gi);
+      lu += passes;
+    }
+    int tot_ph, tot_u;
+    int run_ph = block_exclusive_scan(lph, s_warp_tot, &tot_ph);
+    int run_u = block_exclusive_scan(lu, s_warp_tot, &tot_u);
+    for (int gi = g_lo; gi < g_hi; ++gi) {
+      gph[gi] = run_ph;
+      gu[gi] = run_u;
+      const int passes = (__ldg(p.cas_group_size + gi) + tb.mpp - 1) / tb.mpp;
+      run_ph += passes * __ldg(p.cas_group_pages + gi);
+      run_u += passes;
+    }
+    if (tid == 0) {
+      gph[G] = tot_ph;
+      gu[G] = tot_u;
+    }
+    tb.pre_total = static_cast<int64_t>(tot_ph) * Hkv;
+    tb.pre_units = static_cast<int64_t>(tot_u) * Hkv;
+  }
+
+  // own pages per sequence (after the group prefix in cascade mode)
+  int local = 0;
+  for (int b = b_lo; b < b_hi; ++b) {
+    int P = own_pages_of(p, b, sub_per_block);
+    if constexpr (kCascade) {
+      const int gsb = G > 0 ? __ldg(p.cas_seq_group + b) : -1;
+      const int off = gsb >= 0 ? __ldg(p.cas_group_pages + gsb) : 0;
+      soff[b] = off;
+      P -= off;
+    }
+    local += P;
+  }
+  int total_own;
+  int run = block_exclusive_scan(local, s_warp_tot, &total_own);
+  for (int b = b_lo; b < b_hi; ++b) {
+    prefix[b] = run;
+    int P = own_pages_of(p, b, sub_per_block);
+    if constexpr (kCascade) P -= soff[b];
+    run += P;
+  }
+  if (tid == 0) prefix[B] = total_own;
+  const int any_bad = __syncthreads_or(bad);
+  if (tid == 0 && any_bad) set_status(p.status, PS_DEV_BAD_METADATA);
+
+  const int64_t total = tb.pre_total + static_cast<int64_t>(total_own) * Hkv;
+  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kDecodeWarps;
+  const int64_t total_cost = list_cost(tb, total);
+  tb.Qc = max(static_cast<int64_t>(max(tb.wp, tb.wo)),
+              total_cost > 0 ? (total_cost + nwarps - 1) / nwarps : 1);
+
+  // ---- empty sequences (q_len 1, seq_len 0): zero output, LSE -inf ----------
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + tid;
+       i < static_cast<int64_t>(B) * p.num_q_heads; i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int b = static_cast<int>(i / p.num_q_heads);
+    const int qh = static_cast<int>(i - static_cast<int64_t>(b) * p.num_q_heads);
+    int qlen = 1;
+    if (p.qsl) qlen = __ldg(p.qsl + b + 1) - __ldg(p.qsl + b);
+    if (qlen != 1 || prefix[b + 1] != prefix[b]) continue;
+    const int qrow = p.qsl ? __ldg(p.qsl + b) : b;
+    for (int d = 0; d < kHeadDim; ++d) store_out2<kBF16>(p.out, qrow * p.o_st + qh * p.o_sh + d, 0.f);
+    if (p.lse) p.lse[qh * p.lse_sh + qrow * p.lse_st] = -INFINITY;
+  }
+
+  const int64_t gw = static_cast<int64_t>(blockIdx.x) * kDecodeWarps + warp;
+  const int64_t start = min(total, list_at_cost(tb, gw * tb.Qc));
+  const int64_t end = min(total, list_at_cost(tb, (gw + 1) * tb.Qc));
+  if (start >= end) return;
+
+  uint8_t* wsm = smem + warp * D * kStageBytes;
+  uint8_t* wq = qslots + warp * D * decode_qslot_bytes<kQNT>();
+  uint64_t* wbar = bars + warp * D;
+
+  if constexpr (kCascade) {
+    int k = 0;
+    if (start < tb.pre_total)
+      k = stream_range<kBF16, kPrefixNT, kRec, kQNT, kCasPrefix>(
+          p, &kmap, &vmap, tb, start, min(end, tb.pre_total), gw, wsm, wq, wbar, 0, lane);
+    if (k >= 0 && end > tb.pre_total)
+      stream_range<kBF16, NT, kRec, kQNT, kCasSuffix>(p, &kmap, &vmap, tb, max(start, tb.pre_total),
+                                                      end, gw, wsm, wq, wbar, k, lane);
+  } else {
+    stream_range<kBF16, NT, kRec, kQNT, kPlain>(p, &kmap, &vmap, tb, start, end, gw, wsm, wq,
+                                                wbar, 0, lane);
   }
 }
 
-template <bool kBF16, int NT>
+template <bool kBF16, int NT, bool kCascade>
 static int launch_t(const DecodeParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap,
                     int sm_count, cudaStream_t stream) {
-  const size_t smem = 1024 + decode_smem_bytes_before_table<NT>() + static_cast<size_t>(p.num_seqs + 1) * 4;
+  constexpr int kQNT = kCascade ? kPrefixNT : NT;
+  const int max_seqs = kCascade ? kCascadeMaxSeqs : kDecodeMaxSeqs;
+  // sequence scan [B+1]; cascade adds soff[B] and two group scans [Gmax+1]
+  auto table_ints = [](int B, int gmax) {
+    return kCascade ? (2 * B + 1) + 2 * (gmax + 1) : B + 1;
+  };
+  const size_t smem = 1024 + decode_smem_bytes_before_table<kQNT>() +
+                      static_cast<size_t>(table_ints(p.num_seqs, p.cas_max_groups)) * 4;
   // the attribute is per function and per device
   static bool configured[64] = {false};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev >= 64) return static_cast<int>(cudaErrorInvalidDevice);
   if (!configured[dev]) {
     const cudaError_t e = cudaFuncSetAttribute(
-        paged_decode_kernel<kBF16, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-        static_cast<int>(1024 + decode_smem_bytes_before_table<NT>() + (kDecodeMaxSeqs + 1) * 4));
+        paged_decode_kernel<kBF16, NT, kCascade>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        static_cast<int>(1024 + decode_smem_bytes_before_table<kQNT>() +
+                         static_cast<size_t>(table_ints(max_seqs, max_seqs / 2)) * 4));
     if (e != cudaSuccess) return static_cast<int>(e);
     configured[dev] = true;
   }
@@ -695,26 +1111,31 @@ static int launch_t(const DecodeParams& p, const CUtensorMap& kmap, const CUtens
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, paged_decode_kernel<kBF16, NT>, p, kmap, vmap);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, paged_decode_kernel<kBF16, NT, kCascade>, p, kmap, vmap);
   return static_cast<int>(e != cudaSuccess ? e : cudaGetLastError());
 }
 
 }  // namespace ps
 
-int64_t ps_decode_partial_slots(int num_seqs, int num_kv_heads, int sm_count) {
-  // slot = global warp index + (sequence * kv heads + kv head)
-  return static_cast<int64_t>(sm_count) * ps::kDecodeCtasPerSm * ps::kDecodeWarps +
-         static_cast<int64_t>(num_seqs) * num_kv_heads;
+int64_t ps_decode_partial_slots(int num_seqs, int num_kv_heads, int sm_count, int cascade) {
+  // slot = global warp index + unit index; units: (sequence, kv head) and, in
+  // cascade mode, at most one prefix segment per (sequence, kv head) more
+  const int64_t units = static_cast<int64_t>(num_seqs) * num_kv_heads * (cascade ? 2 : 1);
+  return static_cast<int64_t>(sm_count) * ps::kDecodeCtasPerSm * ps::kDecodeWarps + units;
 }
 
 int ps_launch_paged_decode(const ps::DecodeParams& p, const CUtensorMap& kmap,
                            const CUtensorMap& vmap, int dtype_bf16, int sm_count,
                            cudaStream_t stream) {
   const int nt = p.group <= 8 ? 1 : 2;
-  if (dtype_bf16) {
-    return nt == 1 ? ps::launch_t<true, 1>(p, kmap, vmap, sm_count, stream)
-                   : ps::launch_t<true, 2>(p, kmap, vmap, sm_count, stream);
+  if (p.cas_num_groups != nullptr) {  // cascade: group <= 8 (checked by the caller)
+    return dtype_bf16 ? ps::launch_t<true, 1, true>(p, kmap, vmap, sm_count, stream)
+                      : ps::launch_t<false, 1, true>(p, kmap, vmap, sm_count, stream);
   }
-  return nt == 1 ? ps::launch_t<false, 1>(p, kmap, vmap, sm_count, stream)
-                 : ps::launch_t<false, 2>(p, kmap, vmap, sm_count, stream);
+  if (dtype_bf16) {
+    return nt == 1 ? ps::launch_t<true, 1, false>(p, kmap, vmap, sm_count, stream)
+                   : ps::launch_t<true, 2, false>(p, kmap, vmap, sm_count, stream);
+  }
+  return nt == 1 ? ps::launch_t<false, 1, false>(p, kmap, vmap, sm_count, stream)
+                 : ps::launch_t<false, 2, false>(p, kmap, vmap, sm_count, stream);
 }

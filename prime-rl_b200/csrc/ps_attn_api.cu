@@ -109,23 +109,30 @@ bool aligned(const void* p, int bytes) {
 int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
 
 // Decode workspace layout.  Every offset is independent of the call's
-// num_seqs, so one buffer serves calls with any batch size up to the one it
-// was sized for without regions of different calls overlapping:
+// num_seqs, and the plain and cascade layouts agree on everything but the
+// record size, so one buffer (sized for the larger use) serves calls of either
+// kind with any batch size up to the one it was sized for:
 //   [0, 256)                 status word (+ reserved)
 //   [256, 256 + C)           counters, kDecodeMaxSeqs * num_kv_heads int32
-//   [256 + C, ...)           partial records, one per split slot:
+//   [.., + C)                prefix-segment counters (cascade)
+//   [..., ...)               partial records, one per split slot:
 //                            kg * 128 fp32 output rows, then kg fp32 LSEs
+//                            (kg = 8 or 16 by GQA group; 16 in cascade mode)
+// The counters must be zero before the first call; every call leaves them zero.
 struct DecodeWorkspaceLayout {
-  int64_t counters_off, part_off, record_bytes, total;
+  int64_t counters_off, pre_counters_off, part_off, record_bytes, total;
 };
 
-DecodeWorkspaceLayout decode_layout(int num_seqs, int num_q_heads, int num_kv_heads, int sm_count) {
+DecodeWorkspaceLayout decode_layout(int num_seqs, int num_q_heads, int num_kv_heads, int sm_count,
+                                    bool cascade) {
   const int group = num_q_heads / num_kv_heads;
-  const int kg = group <= 8 ? 8 : 16;
-  const int64_t slots = ps_decode_partial_slots(num_seqs, num_kv_heads, sm_count);
+  const int kg = (group <= 8 && !cascade) ? 8 : 16;
+  const int64_t slots = ps_decode_partial_slots(num_seqs, num_kv_heads, sm_count, cascade ? 1 : 0);
+  const int64_t counter_bytes = static_cast<int64_t>(ps::kDecodeMaxSeqs) * num_kv_heads * 4;
   DecodeWorkspaceLayout l;
   l.counters_off = 256;
-  l.part_off = round_up(l.counters_off + static_cast<int64_t>(ps::kDecodeMaxSeqs) * num_kv_heads * 4, 256);
+  l.pre_counters_off = round_up(l.counters_off + counter_bytes, 256);
+  l.part_off = round_up(l.pre_counters_off + counter_bytes, 256);
   l.record_bytes = static_cast<int64_t>(kg) * 129 * 4;
   l.total = round_up(l.part_off + slots * l.record_bytes, 256);
   return l;
@@ -167,6 +174,106 @@ int validate_problem(const ps_paged_problem* pr, bool decode) {
     return fail(PS_ERR_INVALID_ARGUMENT, "out base/strides must be 16-byte aligned");
   if (!(pr->softmax_scale > 0.f))
     return fail(PS_ERR_INVALID_ARGUMENT, "softmax_scale must be positive");
+  return PS_OK;
+}
+
+int decode_impl(const ps_paged_problem* pr, const void* plan, int64_t plan_bytes, void* workspace,
+                int64_t workspace_bytes, void* stream, bool cascade) {
+  int rc = validate_problem(pr, true);
+  if (rc != PS_OK) return rc;
+  if (pr->num_seqs == 0) return PS_OK;
+  if (pr->num_seqs > ps::kDecodeMaxSeqs)
+    return fail(PS_ERR_UNSUPPORTED, "num_seqs %d > %d per decode launch", pr->num_seqs,
+                ps::kDecodeMaxSeqs);
+  int dev = 0;
+  const int sms = sm_count_current(&dev);
+  if (sms <= 0) return fail(PS_ERR_CUDA, "no CUDA device");
+  if (cascade) {
+    if (pr->num_seqs > ps::kCascadeMaxSeqs)
+      return fail(PS_ERR_UNSUPPORTED, "num_seqs %d > %d per cascade decode launch", pr->num_seqs,
+                  ps::kCascadeMaxSeqs);
+    if (pr->num_q_heads / pr->num_kv_heads > 8)
+      return fail(PS_ERR_UNSUPPORTED, "cascade decode needs a GQA group <= 8");
+    if (!plan || !aligned(plan, 16) ||
+        plan_bytes < ps_cascade_plan_words(pr->num_seqs) * static_cast<int64_t>(sizeof(int32_t)))
+      return fail(PS_ERR_INVALID_ARGUMENT, "cascade plan must be >= %lld bytes, 16-byte aligned",
+                  static_cast<long long>(ps_cascade_plan_words(pr->num_seqs) * 4));
+  }
+  const DecodeWorkspaceLayout lay =
+      decode_layout(pr->num_seqs, pr->num_q_heads, pr->num_kv_heads, sms, cascade);
+  if (!workspace || workspace_bytes < lay.total || !aligned(workspace, 256))
+    return fail(PS_ERR_WORKSPACE, "decode workspace must be >= %lld bytes, 256-byte aligned",
+                static_cast<long long>(lay.total));
+  CUtensorMap kmap, vmap;
+  rc = make_page_map(&kmap, pr->key_cache, pr->num_blocks, pr->block_size, pr->num_kv_heads,
+                     pr->cache_stride_block, pr->cache_stride_slot, pr->cache_stride_head);
+  if (rc != PS_OK) return rc;
+  rc = make_page_map(&vmap, pr->value_cache, pr->num_blocks, pr->block_size, pr->num_kv_heads,
+                     pr->cache_stride_block, pr->cache_stride_slot, pr->cache_stride_head);
+  if (rc != PS_OK) return rc;
+  char* ws = static_cast<char*>(workspace);
+  ps::DecodeParams p;
+  p.q = pr->q;
+  p.q_st = pr->q_stride_token;
+  p.q_sh = pr->q_stride_head;
+  p.block_table = pr->block_table;
+  p.bt_stride = pr->block_table_stride;
+  p.max_blocks_per_seq = pr->max_blocks_per_seq;
+  p.seq_lens = pr->seq_lens;
+  p.qsl = pr->query_start_loc;
+  p.num_seqs = pr->num_seqs;
+  p.out = pr->out;
+  p.o_st = pr->out_stride_token;
+  p.o_sh = pr->out_stride_head;
+  p.lse = pr->lse;
+  p.lse_sh = pr->lse_stride_head;
+  p.lse_st = pr->lse_stride_token;
+  p.num_q_heads = pr->num_q_heads;
+  p.num_kv_heads = pr->num_kv_heads;
+  p.group = pr->num_q_heads / pr->num_kv_heads;
+  p.block_size = pr->block_size;
+  p.num_blocks = pr->num_blocks;
+  p.scale_log2 = pr->softmax_scale * 1.4426950408889634f;
+  p.status = reinterpret_cast<int32_t*>(ws);
+  p.counters = reinterpret_cast<int32_t*>(ws + lay.counters_off);
+  p.part = reinterpret_cast<float*>(ws + lay.part_off);
+  p.num_part_slots = ps_decode_partial_slots(pr->num_seqs, pr->num_kv_heads, sms, cascade ? 1 : 0);
+  p.pre_counters = reinterpret_cast<int32_t*>(ws + lay.pre_counters_off);
+  p.cas_num_groups = nullptr;
+  p.cas_seq_group = p.cas_group_first = p.cas_group_size = p.cas_group_pages = nullptr;
+  p.cas_max_groups = 0;
+  if (cascade) {
+    const int32_t* w = static_cast<const int32_t*>(plan);
+    const int gm = pr->num_seqs / 2 > 1 ? pr->num_seqs / 2 : 1;
+    p.cas_num_groups = w;
+    p.cas_seq_group = w + 32;
+    p.cas_group_first = p.cas_seq_group + pr->num_seqs;
+    p.cas_group_size = p.cas_group_first + gm;
+    p.cas_group_pages = p.cas_group_size + gm;
+    p.cas_max_groups = gm;
+  }
+  p.new_key = pr->new_key;
+  p.new_value = pr->new_value;
+  p.nk_st = pr->new_key_stride_token;
+  p.nk_sh = pr->new_key_stride_head;
+  p.nv_st = pr->new_value_stride_token;
+  p.nv_sh = pr->new_value_stride_head;
+  p.slot_mapping = pr->slot_mapping;
+  p.key_cache = const_cast<void*>(pr->key_cache);
+  p.value_cache = const_cast<void*>(pr->value_cache);
+  p.c_sblock = pr->cache_stride_block;
+  p.c_sslot = pr->cache_stride_slot;
+  p.c_shead = pr->cache_stride_head;
+  if (pr->new_key != nullptr) {
+    if (!pr->new_value || !pr->slot_mapping)
+      return fail(PS_ERR_INVALID_ARGUMENT, "fused append needs new_key, new_value and slot_mapping");
+    if (!aligned(pr->new_key, 16) || !aligned(pr->new_value, 16) || pr->new_key_stride_token % 8 ||
+        pr->new_key_stride_head % 8 || pr->new_value_stride_token % 8 || pr->new_value_stride_head % 8)
+      return fail(PS_ERR_INVALID_ARGUMENT, "new key/value rows must be 16-byte aligned");
+  }
+  const int e = ps_launch_paged_decode(p, kmap, vmap, pr->dtype == PS_DTYPE_BF16, sms,
+                                       static_cast<cudaStream_t>(stream));
+  if (e != 0) return cuda_fail(static_cast<cudaError_t>(e), "paged_decode launch");
   return PS_OK;
 }
 
@@ -248,81 +355,82 @@ int64_t ps_paged_decode_workspace_size(int32_t num_seqs, int32_t num_q_heads,
     fail(PS_ERR_CUDA, "no CUDA device");
     return -1;
   }
-  return decode_layout(num_seqs, num_q_heads, num_kv_heads, sms).total;
+  return decode_layout(num_seqs, num_q_heads, num_kv_heads, sms, false).total;
 }
 
 int ps_paged_decode(const ps_paged_problem* pr, void* workspace, int64_t workspace_bytes,
                     void* stream) {
-  int rc = validate_problem(pr, true);
-  if (rc != PS_OK) return rc;
-  if (pr->num_seqs == 0) return PS_OK;
-  if (pr->num_seqs > ps::kDecodeMaxSeqs)
-    return fail(PS_ERR_UNSUPPORTED, "num_seqs %d > %d per decode launch", pr->num_seqs,
-                ps::kDecodeMaxSeqs);
-  int dev = 0;
-  const int sms = sm_count_current(&dev);
-  if (sms <= 0) return fail(PS_ERR_CUDA, "no CUDA device");
-  const DecodeWorkspaceLayout lay = decode_layout(pr->num_seqs, pr->num_q_heads, pr->num_kv_heads, sms);
-  if (!workspace || workspace_bytes < lay.total || !aligned(workspace, 256))
-    return fail(PS_ERR_WORKSPACE, "decode workspace must be >= %lld bytes, 256-byte aligned",
-                static_cast<long long>(lay.total));
-  CUtensorMap kmap, vmap;
-  rc = make_page_map(&kmap, pr->key_cache, pr->num_blocks, pr->block_size, pr->num_kv_heads,
-                     pr->cache_stride_block, pr->cache_stride_slot, pr->cache_stride_head);
-  if (rc != PS_OK) return rc;
-  rc = make_page_map(&vmap, pr->value_cache, pr->num_blocks, pr->block_size, pr->num_kv_heads,
-                     pr->cache_stride_block, pr->cache_stride_slot, pr->cache_stride_head);
-  if (rc != PS_OK) return rc;
-  char* ws = static_cast<char*>(workspace);
-  ps::DecodeParams p;
-  p.q = pr->q;
-  p.q_st = pr->q_stride_token;
-  p.q_sh = pr->q_stride_head;
-  p.block_table = pr->block_table;
-  p.bt_stride = pr->block_table_stride;
-  p.max_blocks_per_seq = pr->max_blocks_per_seq;
-  p.seq_lens = pr->seq_lens;
-  p.qsl = pr->query_start_loc;
-  p.num_seqs = pr->num_seqs;
-  p.out = pr->out;
-  p.o_st = pr->out_stride_token;
-  p.o_sh = pr->out_stride_head;
-  p.lse = pr->lse;
-  p.lse_sh = pr->lse_stride_head;
-  p.lse_st = pr->lse_stride_token;
-  p.num_q_heads = pr->num_q_heads;
-  p.num_kv_heads = pr->num_kv_heads;
-  p.group = pr->num_q_heads / pr->num_kv_heads;
-  p.block_size = pr->block_size;
-  p.num_blocks = pr->num_blocks;
-  p.scale_log2 = pr->softmax_scale * 1.4426950408889634f;
-  p.status = reinterpret_cast<int32_t*>(ws);
-  p.counters = reinterpret_cast<int32_t*>(ws + lay.counters_off);
-  p.part = reinterpret_cast<float*>(ws + lay.part_off);
-  p.num_part_slots = ps_decode_partial_slots(pr->num_seqs, pr->num_kv_heads, sms);
-  p.new_key = pr->new_key;
-  p.new_value = pr->new_value;
-  p.nk_st = pr->new_key_stride_token;
-  p.nk_sh = pr->new_key_stride_head;
-  p.nv_st = pr->new_value_stride_token;
-  p.nv_sh = pr->new_value_stride_head;
-  p.slot_mapping = pr->slot_mapping;
-  p.key_cache = const_cast<void*>(pr->key_cache);
-  p.value_cache = const_cast<void*>(pr->value_cache);
-  p.c_sblock = pr->cache_stride_block;
-  p.c_sslot = pr->cache_stride_slot;
-  p.c_shead = pr->cache_stride_head;
-  if (pr->new_key != nullptr) {
-    if (!pr->new_value || !pr->slot_mapping)
-      return fail(PS_ERR_INVALID_ARGUMENT, "fused append needs new_key, new_value and slot_mapping");
-    if (!aligned(pr->new_key, 16) || !aligned(pr->new_value, 16) || pr->new_key_stride_token % 8 ||
-        pr->new_key_stride_head % 8 || pr->new_value_stride_token % 8 || pr->new_value_stride_head % 8)
-      return fail(PS_ERR_INVALID_ARGUMENT, "new key/value rows must be 16-byte aligned");
+  return decode_impl(pr, nullptr, 0, workspace, workspace_bytes, stream, false);
+}
+
+int64_t ps_cascade_plan_bytes(int32_t num_seqs) {
+  if (num_seqs < 0 || num_seqs > ps::kCascadeMaxSeqs) {
+    fail(PS_ERR_INVALID_ARGUMENT, "cascade plan: num_seqs %d outside [0, %d]", num_seqs,
+         ps::kCascadeMaxSeqs);
+    return -1;
   }
-  const int e = ps_launch_paged_decode(p, kmap, vmap, pr->dtype == PS_DTYPE_BF16, sms,
-                                       static_cast<cudaStream_t>(stream));
-  if (e != 0) return cuda_fail(static_cast<cudaError_t>(e), "paged_decode launch");
+  return ps_cascade_plan_words(num_seqs) * static_cast<int64_t>(sizeof(int32_t));
+}
+
+int ps_cascade_plan_build(const ps_paged_problem* pr, int32_t min_shared_pages, void* plan,
+                          int64_t plan_bytes, void* stream) {
+  if (!pr || !plan) return fail(PS_ERR_INVALID_ARGUMENT, "problem or plan is NULL");
+  if (pr->num_seqs < 0 || pr->num_seqs > ps::kCascadeMaxSeqs)
+    return fail(PS_ERR_UNSUPPORTED, "cascade plan: num_seqs %d outside [0, %d]", pr->num_seqs,
+                ps::kCascadeMaxSeqs);
+  if (!aligned(plan, 16) ||
+      plan_bytes < ps_cascade_plan_words(pr->num_seqs) * static_cast<int64_t>(sizeof(int32_t)))
+    return fail(PS_ERR_INVALID_ARGUMENT, "cascade plan must be >= %lld bytes, 16-byte aligned",
+                static_cast<long long>(ps_cascade_plan_words(pr->num_seqs) * 4));
+  if (min_shared_pages < 1) return fail(PS_ERR_INVALID_ARGUMENT, "min_shared_pages must be >= 1");
+  if (pr->num_seqs == 0) {
+    const cudaError_t e = cudaMemsetAsync(plan, 0, 4, static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? PS_OK : cuda_fail(e, "cascade plan");
+  }
+  if (!pr->block_table || !pr->seq_lens) return fail(PS_ERR_INVALID_ARGUMENT, "a required pointer is NULL");
+  if (pr->block_size <= 0 || pr->block_size % 16 != 0 || pr->block_size > 256)
+    return fail(PS_ERR_INVALID_ARGUMENT, "block_size %d must be a multiple of 16 in [16, 256]",
+                pr->block_size);
+  if (pr->num_kv_heads <= 0 || pr->num_q_heads <= 0 || pr->num_q_heads % pr->num_kv_heads != 0)
+    return fail(PS_ERR_INVALID_ARGUMENT, "num_q_heads %d must be a positive multiple of num_kv_heads %d",
+                pr->num_q_heads, pr->num_kv_heads);
+  if (pr->max_blocks_per_seq < 0 || pr->block_table_stride < pr->max_blocks_per_seq)
+    return fail(PS_ERR_INVALID_ARGUMENT, "block_table_stride < max_blocks_per_seq");
+  ps::PlanArgs a;
+  a.block_table = pr->block_table;
+  a.bt_stride = pr->block_table_stride;
+  a.max_blocks_per_seq = pr->max_blocks_per_seq;
+  a.seq_lens = pr->seq_lens;
+  a.qsl = pr->query_start_loc;
+  a.num_seqs = pr->num_seqs;
+  a.block_size = pr->block_size;
+  a.min_shared_pages = min_shared_pages;
+  // a 16-column prefix pass must hold two members
+  a.enabled = (pr->num_q_heads / pr->num_kv_heads) <= 8;
+  a.plan = static_cast<int32_t*>(plan);
+  const int e = ps_launch_cascade_plan(a, static_cast<cudaStream_t>(stream));
+  if (e != 0) return cuda_fail(static_cast<cudaError_t>(e), "cascade plan launch");
   return PS_OK;
+}
+
+int64_t ps_paged_decode_cascade_workspace_size(int32_t num_seqs, int32_t num_q_heads,
+                                               int32_t num_kv_heads, int32_t head_size) {
+  if (num_seqs < 0 || num_seqs > ps::kCascadeMaxSeqs || num_kv_heads <= 0 || num_q_heads <= 0 ||
+      head_size != 128) {
+    fail(PS_ERR_INVALID_ARGUMENT, "workspace size: bad shape");
+    return -1;
+  }
+  const int sms = sm_count_current(nullptr);
+  if (sms <= 0) {
+    fail(PS_ERR_CUDA, "no CUDA device");
+    return -1;
+  }
+  return decode_layout(num_seqs, num_q_heads, num_kv_heads, sms, true).total;
+}
+
+int ps_paged_decode_cascade(const ps_paged_problem* pr, const void* plan, int64_t plan_bytes,
+                            void* workspace, int64_t workspace_bytes, void* stream) {
+  return decode_impl(pr, plan, plan_bytes, workspace, workspace_bytes, stream, true);
 }
 
 int ps_chunked_prefill(const ps_paged_problem* pr, void* stream) {

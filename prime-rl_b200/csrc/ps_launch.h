@@ -56,6 +56,14 @@ struct DecodeParams {
   void* key_cache;
   void* value_cache;
   int64_t c_sblock, c_sslot, c_shead;
+  // shared-prefix (cascade) plan (cas_num_groups == nullptr: off)
+  const int32_t* cas_num_groups;   // [1]
+  const int32_t* cas_seq_group;    // [num_seqs] group of each sequence, -1 none
+  const int32_t* cas_group_first;  // [cas_max_groups]
+  const int32_t* cas_group_size;   // [cas_max_groups]
+  const int32_t* cas_group_pages;  // [cas_max_groups] shared 16-token pages
+  int32_t cas_max_groups;
+  int32_t* pre_counters;           // [num_seqs * num_kv_heads] prefix-segment split counters
 };
 
 // Static sizing of the decode kernel, shared by the workspace-size query.
@@ -73,6 +81,7 @@ constexpr int kDecodeWarps = PS_DECODE_WARPS;           // warps per CTA
 constexpr int kDecodeStages = PS_DECODE_STAGES;         // pages in flight per warp
 constexpr int kDecodeCtasPerSm = PS_DECODE_CTAS_PER_SM; // persistent CTAs per SM
 constexpr int kDecodeMaxSeqs = 4096;                    // sequences per launch (prefix table in smem)
+constexpr int kCascadeMaxSeqs = 2048;                   // per cascade launch (plan tables in smem)
 
 }  // namespace ps
 
@@ -109,7 +118,30 @@ int ps_launch_paged_decode(const ps::DecodeParams& p, const CUtensorMap& kmap,
                            const CUtensorMap& vmap, int dtype_bf16, int sm_count,
                            cudaStream_t stream);
 
-int64_t ps_decode_partial_slots(int num_seqs, int num_kv_heads, int sm_count);
+int64_t ps_decode_partial_slots(int num_seqs, int num_kv_heads, int sm_count, int cascade);
+
+// Shared-prefix plan (cascade_plan.cu).  Plan buffer layout in int32 words,
+// Gm = max(1, num_seqs / 2):
+//   [0] num_groups  [1] CTA arrival counter  [2, 32) reserved
+//   [32, 32 + B) seq_group  then group_first[Gm], group_size[Gm],
+//   group_pages[Gm], shared_pages[B] (pages each sequence shares with its
+//   predecessor)
+namespace ps {
+struct PlanArgs {
+  const int32_t* block_table;
+  int64_t bt_stride;
+  int32_t max_blocks_per_seq;
+  const int32_t* seq_lens;
+  const int32_t* qsl;
+  int32_t num_seqs;
+  int32_t block_size;
+  int32_t min_shared_pages;
+  int32_t enabled;  // 0: write an empty plan
+  int32_t* plan;
+};
+}  // namespace ps
+int64_t ps_cascade_plan_words(int num_seqs);
+int ps_launch_cascade_plan(const ps::PlanArgs& a, cudaStream_t stream);
 
 int ps_launch_chunked_prefill(const ps::PrefillParams& p, const CUtensorMap& qmap,
                               const CUtensorMap& kmap, const CUtensorMap& vmap, int dtype_bf16,

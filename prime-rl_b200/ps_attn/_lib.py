@@ -39,6 +39,10 @@ EXPORTED_SYMBOLS = (
     "ps_paged_decode",
     "ps_chunked_prefill",
     "ps_paged_decode_static_scratch",
+    "ps_cascade_plan_bytes",
+    "ps_cascade_plan_build",
+    "ps_paged_decode_cascade_workspace_size",
+    "ps_paged_decode_cascade",
 )
 
 
@@ -123,6 +127,16 @@ def _declare(lib):
     lib.ps_chunked_prefill.argtypes = [c.POINTER(PagedProblem), c.c_void_p]
     lib.ps_paged_decode_static_scratch.restype = c.c_int
     lib.ps_paged_decode_static_scratch.argtypes = [c.POINTER(PagedProblem), c.c_void_p]
+    lib.ps_cascade_plan_bytes.restype = c.c_int64
+    lib.ps_cascade_plan_bytes.argtypes = [c.c_int32]
+    lib.ps_cascade_plan_build.restype = c.c_int
+    lib.ps_cascade_plan_build.argtypes = [c.POINTER(PagedProblem), c.c_int32, c.c_void_p, c.c_int64,
+                                          c.c_void_p]
+    lib.ps_paged_decode_cascade_workspace_size.restype = c.c_int64
+    lib.ps_paged_decode_cascade_workspace_size.argtypes = [c.c_int32] * 4
+    lib.ps_paged_decode_cascade.restype = c.c_int
+    lib.ps_paged_decode_cascade.argtypes = [c.POINTER(PagedProblem), c.c_void_p, c.c_int64,
+                                            c.c_void_p, c.c_int64, c.c_void_p]
 
 
 def load(build_if_stale: bool = True):

@@ -88,15 +88,20 @@ class DecodeWorkspace:
     """
 
     def __init__(self, max_num_seqs: int, num_q_heads: int, num_kv_heads: int,
-                 head_size: int, device: torch.device | str | int | None = None):
+                 head_size: int, device: torch.device | str | int | None = None,
+                 cascade: bool = False):
         lib = _lib.load()
         dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
         if dev.type != "cuda":
             raise ValueError("DecodeWorkspace lives on a CUDA device")
         with torch.cuda.device(dev):
             nbytes = lib.ps_paged_decode_workspace_size(max_num_seqs, num_q_heads, num_kv_heads, head_size)
+            if cascade:  # serves both kinds of call: the larger size
+                nbytes = max(nbytes, lib.ps_paged_decode_cascade_workspace_size(
+                    max_num_seqs, num_q_heads, num_kv_heads, head_size))
         if nbytes < 0:
             _lib.check(_lib.PS_ERR_INVALID_ARGUMENT)
+        self.cascade = cascade
         self.max_num_seqs = max_num_seqs
         self.num_q_heads = num_q_heads
         self.num_kv_heads = num_kv_heads
@@ -114,15 +119,96 @@ _WS_CACHE: dict = {}
 
 
 def get_workspace(num_seqs: int, num_q_heads: int, num_kv_heads: int, head_size: int,
-                  device: torch.device) -> DecodeWorkspace:
-    """Process-wide workspace per (device, heads), grown to the largest batch seen."""
-    key = (device.index, num_q_heads, num_kv_heads, head_size)
+                  device: torch.device, cascade: bool = False) -> DecodeWorkspace:
+    """Process-wide workspace per (device, heads, kind), grown to the largest batch seen."""
+    key = (device.index, num_q_heads, num_kv_heads, head_size, cascade)
     ws = _WS_CACHE.get(key)
     if ws is None or ws.max_num_seqs < num_seqs:
         cap = max(num_seqs, 256 if ws is None else 2 * ws.max_num_seqs)
-        ws = DecodeWorkspace(cap, num_q_heads, num_kv_heads, head_size, device)
+        if cascade:
+            cap = min(cap, CASCADE_MAX_SEQS)
+        ws = DecodeWorkspace(cap, num_q_heads, num_kv_heads, head_size, device, cascade=cascade)
         _WS_CACHE[key] = ws
     return ws
+
+
+CASCADE_MAX_SEQS = 2048
+PLAN_HEADER_WORDS = 32
+
+
+class CascadePlan:
+    """Device buffer of a shared-prefix plan (``ps_cascade_plan_build``).
+
+    Sized for up to ``max_num_seqs`` sequences and zeroed once; rebuilt in
+    place by :func:`cascade_plan` for each batch (once per step, shared by all
+    layers).  ``num_seqs`` is the batch the current contents describe.
+    """
+
+    def __init__(self, max_num_seqs: int, device: torch.device | str | int | None = None):
+        lib = _lib.load()
+        if not 0 <= max_num_seqs <= CASCADE_MAX_SEQS:
+            raise ValueError(f"cascade plans hold at most {CASCADE_MAX_SEQS} sequences")
+        dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        nbytes = lib.ps_cascade_plan_bytes(max(max_num_seqs, 1))
+        if nbytes < 0:
+            _lib.check(_lib.PS_ERR_INVALID_ARGUMENT)
+        self.max_num_seqs = max_num_seqs
+        self.nbytes = int(nbytes)
+        self.buffer = torch.zeros(self.nbytes // 4, dtype=torch.int32, device=dev)
+        self.num_seqs = 0
+
+    def views(self) -> dict:
+        """The plan's arrays for the batch it was last built for (device tensors)."""
+        B = self.num_seqs
+        gm = max(1, B // 2)
+        w = self.buffer
+        o = PLAN_HEADER_WORDS
+        return {
+            "num_groups": w[0:1],
+            "seq_group": w[o:o + B],
+            "group_first": w[o + B:o + B + gm],
+            "group_size": w[o + B + gm:o + B + 2 * gm],
+            "group_pages": w[o + B + 2 * gm:o + B + 3 * gm],
+            "shared_pages": w[o + B + 3 * gm:o + 2 * B + 3 * gm],
+        }
+
+
+def cascade_plan(block_table: torch.Tensor, seq_lens: torch.Tensor, num_q_heads: int,
+                 num_kv_heads: int, block_size: int, query_start_loc: torch.Tensor | None = None,
+                 min_shared_pages: int = 8, plan: CascadePlan | None = None) -> CascadePlan:
+    """Find groups of adjacent decode sequences with identical leading pages.
+
+    Enqueued on the current stream (no host synchronisation).  The result is
+    valid for any later :func:`paged_decode` call on the same block_table,
+    seq_lens and query_start_loc; pass it as ``cascade=``.
+    """
+    lib = _lib.load()
+    _require_cuda(block_table, seq_lens, query_start_loc)
+    if block_table.dtype != torch.int32 or seq_lens.dtype != torch.int32:
+        raise ValueError("block_table and seq_lens must be int32")
+    if block_table.stride(-1) != 1 or not seq_lens.is_contiguous():
+        raise ValueError("block_table rows and seq_lens must be contiguous")
+    B = seq_lens.shape[0]
+    if plan is None:
+        plan = CascadePlan(B, seq_lens.device)
+    elif plan.max_num_seqs < B:
+        raise ValueError(f"plan sized for {plan.max_num_seqs} sequences < {B}")
+    pr = _lib.PagedProblem()
+    pr.block_table = block_table.data_ptr()
+    pr.block_table_stride = block_table.stride(0)
+    pr.max_blocks_per_seq = block_table.shape[1]
+    pr.seq_lens = seq_lens.data_ptr()
+    pr.query_start_loc = query_start_loc.data_ptr() if query_start_loc is not None else None
+    pr.num_seqs = B
+    pr.num_q_heads = num_q_heads
+    pr.num_kv_heads = num_kv_heads
+    pr.head_size = 128
+    pr.block_size = block_size
+    _lib.check(lib.ps_cascade_plan_build(ctypes.byref(pr), int(min_shared_pages),
+                                         plan.buffer.data_ptr(), plan.nbytes,
+                                         _stream_ptr(seq_lens.device)))
+    plan.num_seqs = B
+    return plan
 
 
 def _problem(q, key_cache, value_cache, block_table, seq_lens, query_start_loc,
@@ -186,7 +272,8 @@ def paged_decode(q: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Te
                  query_start_loc: torch.Tensor | None = None,
                  workspace: DecodeWorkspace | None = None,
                  new_key: torch.Tensor | None = None, new_value: torch.Tensor | None = None,
-                 slot_mapping: torch.Tensor | None = None) -> torch.Tensor:
+                 slot_mapping: torch.Tensor | None = None,
+                 cascade: CascadePlan | None = None) -> torch.Tensor:
     """Decode attention, one query row per sequence, written into ``out``.
 
     q/out: [T, Hq, D]; caches [num_blocks, block_size, Hkv, D]; block_table
@@ -197,13 +284,20 @@ def paged_decode(q: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Te
     ``new_key``/``new_value`` [T, Hkv, D] + ``slot_mapping`` int64 [T] fuse the
     KV append of the decode tokens into the same launch (same result as
     :func:`kv_append` followed by this call without them).
+
+    ``cascade``: a :class:`CascadePlan` built by :func:`cascade_plan` for this
+    batch; shared prefixes are then read once per group pass (same outputs).
+    The workspace must then be a cascade workspace.
     """
     lib = _lib.load()
     B = seq_lens.shape[0]
     if workspace is None:
-        workspace = get_workspace(B, q.shape[1], key_cache.shape[2], key_cache.shape[3], q.device)
+        workspace = get_workspace(B, q.shape[1], key_cache.shape[2], key_cache.shape[3], q.device,
+                                  cascade=cascade is not None)
     elif workspace.max_num_seqs < B:
         raise ValueError(f"workspace sized for {workspace.max_num_seqs} sequences < {B}")
+    if cascade is not None and cascade.num_seqs != B:
+        raise ValueError(f"cascade plan built for {cascade.num_seqs} sequences, call has {B}")
     pr = _problem(q, key_cache, value_cache, block_table, seq_lens, query_start_loc,
                   softmax_scale, out, lse)
     if new_key is not None:
@@ -226,8 +320,13 @@ def paged_decode(q: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Te
         pr.new_value = new_value.data_ptr()
         pr.new_value_stride_token, pr.new_value_stride_head = new_value.stride(0), new_value.stride(1)
         pr.slot_mapping = slot_mapping.data_ptr()
-    _lib.check(lib.ps_paged_decode(ctypes.byref(pr), workspace.buffer.data_ptr(),
-                                   workspace.nbytes, _stream_ptr(q.device)))
+    if cascade is not None:
+        _lib.check(lib.ps_paged_decode_cascade(ctypes.byref(pr), cascade.buffer.data_ptr(),
+                                               cascade.nbytes, workspace.buffer.data_ptr(),
+                                               workspace.nbytes, _stream_ptr(q.device)))
+    else:
+        _lib.check(lib.ps_paged_decode(ctypes.byref(pr), workspace.buffer.data_ptr(),
+                                       workspace.nbytes, _stream_ptr(q.device)))
     return out
 
 

@@ -89,3 +89,24 @@ def test_ops_refuse_cpu_tensors():
         ops.kv_append(k, k, torch.zeros(1, 16, 1, 128, dtype=torch.bfloat16),
                       torch.zeros(1, 16, 1, 128, dtype=torch.bfloat16),
                       torch.zeros(2, dtype=torch.int64))
+
+
+def test_cascade_entry_points_validate_on_the_host():
+    lib = _lib.load()
+    assert lib.ps_cascade_plan_bytes(-1) == -1
+    assert lib.ps_cascade_plan_bytes(4096) == -1  # over the per-launch limit
+    # header (32 words) + seq_group + shared_pages (B each) + 3 group arrays (B/2)
+    assert lib.ps_cascade_plan_bytes(8) == (32 + 2 * 8 + 3 * 4) * 4
+    assert lib.ps_cascade_plan_bytes(1) == (32 + 2 + 3) * 4
+    assert lib.ps_cascade_plan_build(None, 8, None, 0, None) == _lib.PS_ERR_INVALID_ARGUMENT
+    rc = lib.ps_paged_decode_cascade(None, None, 0, None, 0, None)
+    assert rc == _lib.PS_ERR_INVALID_ARGUMENT
+    pr = _lib.PagedProblem()
+    pr.num_seqs = 3000
+    rc = lib.ps_cascade_plan_build(ctypes.byref(pr), 8, ctypes.c_void_p(16), 1 << 20, None)
+    assert rc == _lib.PS_ERR_UNSUPPORTED and b"2048" in lib.ps_last_error()
+    pr.num_seqs = 4
+    rc = lib.ps_cascade_plan_build(ctypes.byref(pr), 0, ctypes.c_void_p(16), 1 << 20, None)
+    assert rc == _lib.PS_ERR_INVALID_ARGUMENT
+    rc = lib.ps_cascade_plan_build(ctypes.byref(pr), 8, ctypes.c_void_p(16), 8, None)
+    assert rc == _lib.PS_ERR_INVALID_ARGUMENT  # buffer too small

@@ -278,3 +278,4 @@ def test_fused_append_padding_and_slot_mismatch(cuda_device):
                      new_value=batch.value, slot_mapping=slots2)
     torch.cuda.synchronize()
     assert ws.status() & _lib.PS_DEV_BAD_METADATA
+

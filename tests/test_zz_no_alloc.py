@@ -62,3 +62,21 @@ def test_static_scratch_rejects_oversized_problem(cuda_device):
     rc = lib.ps_paged_decode_static_scratch(ctypes.byref(pr), None)
     assert rc == _lib.PS_ERR_WORKSPACE
     assert b"16 MiB" in lib.ps_last_error()
+
+
+def test_static_scratch_size_limit(cuda_device):
+    """The static scratch takes every problem whose decode workspace fits in
+    16 MiB: 352 sequences at 8 KV heads on 148 SMs."""
+    lib = _lib.load()
+    nwarps = torch.cuda.get_device_properties(cuda_device).multi_processor_count * 8
+    part_off = 256 + 2 * 4096 * 8 * 4
+    limit = ((16 << 20) - part_off) // (8 * 129 * 4) - nwarps
+    max_seqs = limit // 8
+    for n, ok in ((max_seqs, True), (max_seqs + 1, False)):
+        batch = workloads.make_batch([1] * n, [40] * n, 16, 8, seed=2, pool_slack=0).to(cuda_device)
+        out = torch.empty_like(batch.q)
+        pr = ops._problem(batch.q, batch.kv_cache[0], batch.kv_cache[1], batch.block_table,
+                          batch.seq_lens, batch.query_start_loc, batch.softmax_scale, out, None)
+        rc = lib.ps_paged_decode_static_scratch(ctypes.byref(pr), None)
+        torch.cuda.synchronize()
+        assert rc == (_lib.PS_OK if ok else _lib.PS_ERR_WORKSPACE), (n, rc)
