@@ -25,11 +25,17 @@ or as an override of FLASH_ATTN::
 
 Batches are reordered decode-first (``reorder_batch_threshold = 1``); decode
 requests run the split-KV decode kernel, the rest the chunked-prefill kernel.
+With ``PS_ATTN_CASCADE=1`` the metadata builder also finds groups of decode
+requests that share their leading KV pages (GRPO samples of one prompt; vLLM
+itself only uses cascade attention when every request shares one prefix,
+``flash_attn.py:1088-1130``) once per step, and the decode reads each shared
+prefix once per group pass.
 Unsupported options (ALiBi, sliding window, soft-cap, sinks, fp8 KV cache,
 encoder attention) raise ``NotImplementedError`` at construction.
 """
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass
 from typing import ClassVar
 
@@ -115,6 +121,7 @@ class PSAttentionMetadata:
     num_prefills: int
     workspace: ops.DecodeWorkspace
     causal: bool = True
+    cascade_plan: ops.CascadePlan | None = None  # shared-prefix plan of the decode rows
 
 
 class PSAttentionMetadataBuilder(AttentionMetadataBuilder[PSAttentionMetadata]):
@@ -132,8 +139,12 @@ class PSAttentionMetadataBuilder(AttentionMetadataBuilder[PSAttentionMetadata]):
         self.head_size = mc.get_head_size()
         max_seqs = max(vllm_config.scheduler_config.max_num_seqs,
                        vllm_config.compilation_config.max_cudagraph_capture_size or 0)
+        self.block_size = kv_cache_spec.block_size
+        self.cascade = (cascade_enabled() and max_seqs <= ops.CASCADE_MAX_SEQS
+                        and self.num_heads_q // self.num_heads_kv <= 8)
         self.workspace = ops.DecodeWorkspace(max_seqs, self.num_heads_q, self.num_heads_kv,
-                                             self.head_size, device)
+                                             self.head_size, device, cascade=self.cascade)
+        self.plan = ops.CascadePlan(max_seqs, device) if self.cascade else None
 
     def build(self, common_prefix_len: int, common_attn_metadata: CommonAttentionMetadata,
               fast_build: bool = False) -> PSAttentionMetadata:
@@ -143,11 +154,18 @@ class PSAttentionMetadataBuilder(AttentionMetadataBuilder[PSAttentionMetadata]):
         if not m.causal:
             raise NotImplementedError("the PS backend is causal-only")
         nd, npf, ndt, _ = split_decodes_and_prefills(m, decode_threshold=1)
+        plan = None
+        if getattr(self, "cascade", False) and nd > 0:
+            # once per step, from exactly the arrays forward() hands the decode
+            plan = ops.cascade_plan(m.block_table_tensor[:nd], m.seq_lens[:nd], self.num_heads_q,
+                                    self.num_heads_kv, self.block_size,
+                                    query_start_loc=m.query_start_loc[:nd + 1], plan=self.plan)
         return PSAttentionMetadata(
             num_actual_tokens=m.num_actual_tokens, max_query_len=m.max_query_len,
             query_start_loc=m.query_start_loc, max_seq_len=m.max_seq_len, seq_lens=m.seq_lens,
             block_table=m.block_table_tensor, slot_mapping=m.slot_mapping, num_decodes=nd,
-            num_decode_tokens=ndt, num_prefills=npf, workspace=self.workspace, causal=True)
+            num_decode_tokens=ndt, num_prefills=npf, workspace=self.workspace, causal=True,
+            cascade_plan=plan)
 
     def update_block_table(self, metadata: PSAttentionMetadata, blk_table: torch.Tensor,
                            slot_mapping: torch.Tensor) -> PSAttentionMetadata:
@@ -220,11 +238,16 @@ class PSAttentionImpl(AttentionImpl):
             ops.paged_decode(query[:ndt], key_cache, value_cache, m.block_table[:nd],
                              m.seq_lens[:nd], self.scale, output[:ndt],
                              query_start_loc=m.query_start_loc[:nd + 1], workspace=m.workspace,
-                             **fused)
+                             cascade=m.cascade_plan, **fused)
         if m.num_prefills > 0:
             ops.chunked_prefill(query[:T], key_cache, value_cache, m.block_table[nd:],
                                 m.seq_lens[nd:], m.query_start_loc[nd:], self.scale, output[:T])
         return output
+
+
+def cascade_enabled() -> bool:
+    """Shared-prefix decode is opt-in (``PS_ATTN_CASCADE=1``)."""
+    return os.environ.get("PS_ATTN_CASCADE", "0") == "1"
 
 
 def register(override_flash: bool = False) -> None:

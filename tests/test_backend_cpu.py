@@ -132,3 +132,28 @@ def test_kv_update_unbinds_cache(monkeypatch):
     impl.do_kv_cache_update(None, torch.zeros(3, 8, 128), torch.zeros(3, 8, 128), kv,
                             torch.arange(3))
     assert seen["kc"].data_ptr() == kv[0].data_ptr() and seen["vc"].data_ptr() == kv[1].data_ptr()
+
+
+def test_cascade_opt_in_builds_one_plan_per_step(monkeypatch):
+    """With PS_ATTN_CASCADE=1 the builder builds the shared-prefix plan for the
+    decode rows (the same slices forward() passes) and forward hands it on."""
+    built, calls = [], []
+    monkeypatch.setattr(psb.ops, "cascade_plan",
+                        lambda bt, sl, hq, hkv, bs, query_start_loc=None, plan=None:
+                        built.append((bt.shape[0], sl.tolist(), query_start_loc.tolist(), bs)) or "PLAN")
+    monkeypatch.setattr(psb.ops, "paged_decode", lambda *a, **k: calls.append(k))
+    monkeypatch.setattr(psb.ops, "chunked_prefill", lambda *a, **k: None)
+    b = _builder()
+    b.cascade, b.plan, b.block_size = True, None, 16
+    b.num_heads_q, b.num_heads_kv = 16, 8
+    md = b.build(0, _common([1, 1, 1, 7], [10, 20, 30, 40]))
+    assert built == [(3, [10, 20, 30], [0, 1, 2, 3], 16)] and md.cascade_plan == "PLAN"
+    impl = psb.PSAttentionImpl(16, 128, 0.088, 8, None, None, "auto")
+    impl.forward(None, torch.zeros(10, 16, 128), None, None, torch.zeros(2, 4, 16, 8, 128), md,
+                 torch.zeros(10, 16, 128))
+    assert calls[0]["cascade"] == "PLAN"
+    # off by default
+    monkeypatch.delenv("PS_ATTN_CASCADE", raising=False)
+    assert not psb.cascade_enabled()
+    monkeypatch.setenv("PS_ATTN_CASCADE", "1")
+    assert psb.cascade_enabled()

@@ -268,3 +268,29 @@ def test_full_config3_cascade_properties(cuda_device):
         ro, rl = ps_oracle.attention_ref(to_np32(batch.q[r:r + 1]), kb, vb,
                                          softmax_scale=1 / math.sqrt(128))
         assert_attn_close(to_np32(out_c[r:r + 1]), ro, to_np32(lse_c[:, r:r + 1]), rl)
+
+
+def test_vllm_impl_forward_with_cascade_plan(cuda_device):
+    """PSAttentionImpl.forward (append fused into the decode) with a
+    shared-prefix plan in the metadata, as the builder makes it when
+    PS_ATTN_CASCADE=1."""
+    pytest.importorskip("vllm.v1.attention.backend")
+    from ps_attn import backend as psb
+
+    batch = grouped_batch(16, 8, seed=70)
+    _, (rout, _) = oracle_step(batch)
+    g = batch.to(cuda_device)
+    B = batch.num_seqs
+    impl = psb.PSAttentionImpl(16, 128, g.softmax_scale, 8, None, None, "auto")
+    ws = ops.DecodeWorkspace(B, 16, 8, 128, cuda_device, cascade=True)
+    plan = gpu_plan(g)
+    md = psb.PSAttentionMetadata(
+        num_actual_tokens=B, max_query_len=1, query_start_loc=g.query_start_loc,
+        max_seq_len=int(batch.seq_lens.max()), seq_lens=g.seq_lens, block_table=g.block_table,
+        slot_mapping=g.slot_mapping, num_decodes=B, num_decode_tokens=B, num_prefills=0,
+        workspace=ws, cascade_plan=plan)
+    out = torch.empty_like(g.q)
+    impl.forward(None, g.q, g.key, g.value, g.kv_cache, md, out)
+    torch.cuda.synchronize()
+    assert ws.status() == 0 and plan.views()["num_groups"].item() == 4
+    assert_attn_close(to_np32(out), rout)
