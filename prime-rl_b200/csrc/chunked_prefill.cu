@@ -68,6 +68,33 @@ __device__ __forceinline__ float exp2_fma(float x) {
   return x < -126.f ? 0.f : r;
 }
 
+// Packed fp32 pairs (sm_100 f32x2 instructions): one instruction updates two
+// softmax elements.  Results equal two scalar fmaf / additions.
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+// Three-input maximum (sm_100); like fmaxf, a NaN input is ignored.
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 struct PrefillSmem {
   // all tiles 1024-byte aligned (offsets from the aligned base)
   static constexpr int q_off = 0;  // Q_A then Q_B
@@ -415,15 +442,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t r[32];
           tc::ld_32x32b_x32(s_addr + c * 32, r);
           tc::wait_ld();
+          if (need_mask) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            float v = __uint_as_float(r[i]);
-            if (need_mask && key0 + c * 32 + i > limit) v = -INFINITY;
-            mxp[i & 7] = fmaxf(mxp[i & 7], v);
+            for (int i = 0; i < 32; ++i)
+              if (key0 + c * 32 + i > limit) r[i] = __float_as_uint(-INFINITY);
           }
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            mxp[i & 7] = max3(mxp[i & 7], __uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
         }
-        float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
-                         fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
+        float mx = fmaxf(max3(mxp[0], mxp[1], mxp[2]), max3(mxp[3], mxp[4], max3(mxp[5], mxp[6], mxp[7])));
         mx *= sl2;  // scale > 0: max of scaled = scaled max
         float m_new = m_run, factor = 1.f;
         if (mx > m_run + kRescaleThreshold || (m_run == -INFINITY && mx > -INFINITY)) {
@@ -450,29 +478,40 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         // pass 2: p = exp2(s * scale - m), packed to 16 bit, written over the S
         // columns already read (chunk c's P lands in columns [16c, 16c + 16))
-        float rsp[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        // (pairs of elements go through the packed f32x2 FMA and add)
+        uint64_t rsp[4] = {0ull, 0ull, 0ull, 0ull};
+        const uint64_t sl2x2 = f2_pack(sl2, sl2), negm_x2 = f2_pack(neg_m, neg_m);
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           uint32_t r[32];
           tc::ld_32x32b_x32(s_addr + c * 32, r);
           tc::wait_ld();
+          if (need_mask) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (key0 + c * 32 + i > limit) r[i] = __float_as_uint(-INFINITY);
+          }
           uint32_t pk[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            float s0 = __uint_as_float(r[2 * i]), s1 = __uint_as_float(r[2 * i + 1]);
-            if (need_mask) {
-              if (key0 + c * 32 + 2 * i > limit) s0 = -INFINITY;
-              if (key0 + c * 32 + 2 * i + 1 > limit) s1 = -INFINITY;
-            }
-            const float x0 = fmaf(s0, sl2, neg_m), x1 = fmaf(s1, sl2, neg_m);
+            float x0, x1;
+            f2_unpack(f2_fma(f2_pack(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])), sl2x2,
+                             negm_x2),
+                      x0, x1);
             const float p0 = ((2 * i) % 8 < PS_PREFILL_EMU_PER8) ? exp2_fma(x0) : ex2(x0);
             const float p1 = ((2 * i + 1) % 8 < PS_PREFILL_EMU_PER8) ? exp2_fma(x1) : ex2(x1);
-            rsp[i & 7] += p0 + p1;
+            rsp[i & 3] = f2_add(rsp[i & 3], f2_pack(p0, p1));
             pk[i] = pack2<kBF16>(p0, p1);
           }
           tmem_st_x16(s_addr + c * 16, pk);
         }
-        const float rs = ((rsp[0] + rsp[1]) + (rsp[2] + rsp[3])) + ((rsp[4] + rsp[5]) + (rsp[6] + rsp[7]));
+        float rs;
+        {
+          float a0, a1, b0, b1;
+          f2_unpack(f2_add(rsp[0], rsp[1]), a0, a1);
+          f2_unpack(f2_add(rsp[2], rsp[3]), b0, b1);
+          rs = (a0 + b0) + (a1 + b1);
+        }
         l_run = l_run * factor + rs;
         m_run = m_new;
         tc::wait_st();
