@@ -47,9 +47,11 @@ constexpr int kThreads = 384;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 // Of every 8 exponentials in a softmax row, this many are evaluated on the FMA
-// pipe (exp2_fma) instead of the MUFU unit.  The macro exists for sweeps.
+// pipe (exp2_fma) instead of the MUFU unit, which the softmax otherwise keeps
+// ~45 % busy next to a ~45 % busy tensor pipe (measured on config 4: 0/8 865,
+// 1/8 891, 2/8 875 TFLOP/s).  The macro exists for sweeps.
 #ifndef PS_PREFILL_EMU_PER8
-#define PS_PREFILL_EMU_PER8 0
+#define PS_PREFILL_EMU_PER8 1
 #endif
 
 // 2^x on the FMA/ALU pipes: 2^x = 2^n * 2^f with n = round(x) and
