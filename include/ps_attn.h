@@ -211,6 +211,55 @@ int ps_paged_decode_cascade(const ps_paged_problem* problem, const void* plan, i
                             void* workspace, int64_t workspace_bytes, void* stream);
 
 /*
+ * Fused rotary embedding + KV append.  Replaces the custom op
+ * fused_rope_and_unified_kv_cache_update
+ * (vllm/compilation/passes/fusion/rope_kvcache_fusion.py:40-73), i.e.
+ * AttentionImpl.do_rope_and_kv_cache_update (vllm/v1/attention/backend.py:
+ * 815-841), which vLLM's fusion pass substitutes for rotary_embedding followed
+ * by the KV update:
+ *
+ *   query[t, h, :], key[t, h, :] <- RoPE(., positions[t])       (in place)
+ *   key_cache / value_cache at slot_mapping[t] <- rotated key, value
+ *                                   (ps_kv_append's contract; slot < 0 skipped)
+ *
+ * RoPE as vLLM's torch-native rotary embedding
+ * (rotary_embedding/base.py:140-181): cos_sin_cache rows are [cos | sin] of
+ * rotary_dim / 2 entries each, cast to the model dtype; neox style pairs
+ * element i with i + rotary_dim / 2, GPT-J style 2i with 2i + 1; every
+ * product and sum is rounded to the model dtype (bit-identical to the
+ * reference); dims past rotary_dim pass through.  Positions outside
+ * [0, max_position) set PS_DEV_BAD_METADATA and leave that token untouched.
+ * Strides in elements; the last dimension of every tensor is contiguous.
+ */
+typedef struct {
+  void* query;        /* [num_tokens, num_q_heads, head_size] */
+  int64_t query_stride_token, query_stride_head;
+  void* key;          /* [num_tokens, num_kv_heads, head_size] */
+  int64_t key_stride_token, key_stride_head;
+  const void* value;  /* [num_tokens, num_kv_heads, head_size] */
+  int64_t value_stride_token, value_stride_head;
+  void* key_cache;
+  void* value_cache;  /* [num_blocks, block_size, num_kv_heads, head_size] */
+  int64_t cache_stride_block, cache_stride_slot, cache_stride_head;
+  int64_t num_blocks;
+  int32_t block_size;
+  const int64_t* slot_mapping; /* [num_tokens] */
+  const int64_t* positions;    /* [num_tokens] */
+  const void* cos_sin_cache;   /* [max_position, rotary_dim] */
+  int64_t cos_sin_stride;      /* elements between rows */
+  int64_t max_position;
+  int32_t cos_sin_dtype;       /* PS_DTYPE_FP32 or the model dtype */
+  int32_t rotary_dim;          /* even, <= head_size */
+  int32_t is_neox;
+  int64_t num_tokens;
+  int32_t num_q_heads, num_kv_heads, head_size;
+  int32_t dtype;               /* PS_DTYPE_BF16 or PS_DTYPE_FP16 */
+  int32_t* status;             /* nullable, PS_DEV_* bits */
+} ps_rope_append_problem;
+
+int ps_rope_kv_append(const ps_rope_append_problem* problem, void* stream);
+
+/*
  * Chunked prefill: any q_len >= 1 per sequence, causal bottom-right, over the
  * same paged cache.  Replaces flash_attn_varlen_func for max_seqlen_q > 1
  * (flash_attn.py:796-817 -> cute/flash_fwd_sm100.py).  Tensor-core path:

@@ -332,3 +332,53 @@ def cascade_decode(q, key_cache, value_cache, block_table, seq_lens, plan, softm
         out[b] = o
         lse[:, b] = l
     return out, lse
+
+
+# --------------------------------------------------------------------------
+# Rotary embedding (fused RoPE + KV append)
+# --------------------------------------------------------------------------
+def round_to(x, dtype):
+    """Round float32 values to ``dtype`` ("bf16", "fp16" or "fp32") and back,
+    round-to-nearest-even (what torch does after every bf16/fp16 operation)."""
+    x = np.asarray(x, dtype=np.float32)
+    if dtype == "fp32":
+        return x
+    if dtype == "fp16":
+        return x.astype(np.float16).astype(np.float32)
+    bits = x.view(np.uint32).astype(np.uint64)
+    nan = np.isnan(x)
+    rounded = ((bits + 0x7FFF + ((bits >> 16) & 1)) >> 16) << 16
+    out = (rounded & 0xFFFFFFFF).astype(np.uint32).view(np.float32)
+    return np.where(nan, x, out).astype(np.float32)
+
+
+def rope(x, positions, cos_sin_rows, rotary_dim, is_neox, dtype):
+    """Rotary embedding of ``x`` [T, H, D] (float32 holding ``dtype`` values).
+
+    Restates ``RotaryEmbedding.forward_static`` /
+    ``ApplyRotaryEmb.forward_static``
+    (``vllm/model_executor/layers/rotary_embedding/base.py:140-181``,
+    ``common.py:144-180``): ``cos, sin = cos_sin_cache[positions].chunk(2)``
+    cast to the model dtype; neox style pairs element ``i`` with ``i + rot/2``,
+    GPT-J style ``2i`` with ``2i + 1``; ``o1 = x1*cos - x2*sin``, ``o2 =
+    x2*cos + x1*sin`` with every product and sum rounded to the model dtype
+    (torch's bf16/fp16 tensor arithmetic); dims past ``rotary_dim`` pass
+    through.  ``cos_sin_rows`` [T, rot] are the cache rows at ``positions``.
+    """
+    x = np.asarray(x, dtype=np.float32)
+    out = x.copy()
+    half = rotary_dim // 2
+    cs = round_to(np.asarray(cos_sin_rows, dtype=np.float32), dtype)
+    cos = cs[:, None, :half]
+    sin = cs[:, None, half:rotary_dim]
+    if is_neox:
+        x1, x2 = x[..., :half], x[..., half:rotary_dim]
+    else:
+        x1, x2 = x[..., 0:rotary_dim:2], x[..., 1:rotary_dim:2]
+    o1 = round_to(round_to(x1 * cos, dtype) - round_to(x2 * sin, dtype), dtype)
+    o2 = round_to(round_to(x2 * cos, dtype) + round_to(x1 * sin, dtype), dtype)
+    if is_neox:
+        out[..., :half], out[..., half:rotary_dim] = o1, o2
+    else:
+        out[..., 0:rotary_dim:2], out[..., 1:rotary_dim:2] = o1, o2
+    return out

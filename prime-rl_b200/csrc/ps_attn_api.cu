@@ -433,6 +433,72 @@ int ps_paged_decode_cascade(const ps_paged_problem* pr, const void* plan, int64_
   return decode_impl(pr, plan, plan_bytes, workspace, workspace_bytes, stream, true);
 }
 
+int ps_rope_kv_append(const ps_rope_append_problem* pr, void* stream) {
+  if (!pr) return fail(PS_ERR_INVALID_ARGUMENT, "problem is NULL");
+  if (pr->num_tokens < 0) return fail(PS_ERR_INVALID_ARGUMENT, "num_tokens < 0");
+  if (pr->num_tokens == 0) return PS_OK;
+  if (!pr->query || !pr->key || !pr->value || !pr->key_cache || !pr->value_cache ||
+      !pr->slot_mapping || !pr->positions || !pr->cos_sin_cache)
+    return fail(PS_ERR_INVALID_ARGUMENT, "a required pointer is NULL");
+  if (pr->dtype != PS_DTYPE_BF16 && pr->dtype != PS_DTYPE_FP16)
+    return fail(PS_ERR_UNSUPPORTED, "rope_kv_append supports fp16 and bf16 (dtype %d)", pr->dtype);
+  if (pr->cos_sin_dtype != PS_DTYPE_FP32 && pr->cos_sin_dtype != pr->dtype)
+    return fail(PS_ERR_UNSUPPORTED, "cos_sin_cache must be fp32 or the model dtype");
+  if (pr->head_size <= 0 || pr->rotary_dim <= 0 || pr->rotary_dim % 2 || pr->rotary_dim > pr->head_size)
+    return fail(PS_ERR_INVALID_ARGUMENT, "rotary_dim %d must be even and <= head_size %d",
+                pr->rotary_dim, pr->head_size);
+  if (pr->num_q_heads <= 0 || pr->num_kv_heads <= 0 || pr->block_size <= 0 || pr->num_blocks <= 0 ||
+      pr->max_position <= 0 || pr->cos_sin_stride < pr->rotary_dim)
+    return fail(PS_ERR_INVALID_ARGUMENT, "non-positive shape or cos_sin_stride < rotary_dim");
+  int dev = 0;
+  const int sms = sm_count_current(&dev);
+  if (sms <= 0) return fail(PS_ERR_CUDA, "no CUDA device");
+  const int es = 2;
+  ps::RopeArgs a;
+  a.q = static_cast<char*>(pr->query);
+  a.q_st = pr->query_stride_token * es;
+  a.q_sh = pr->query_stride_head * es;
+  a.k = static_cast<char*>(pr->key);
+  a.k_st = pr->key_stride_token * es;
+  a.k_sh = pr->key_stride_head * es;
+  a.v = static_cast<const char*>(pr->value);
+  a.v_st = pr->value_stride_token * es;
+  a.v_sh = pr->value_stride_head * es;
+  a.key_cache = static_cast<char*>(pr->key_cache);
+  a.value_cache = static_cast<char*>(pr->value_cache);
+  a.c_sblock = pr->cache_stride_block * es;
+  a.c_sslot = pr->cache_stride_slot * es;
+  a.c_shead = pr->cache_stride_head * es;
+  a.num_slots = pr->num_blocks * pr->block_size;
+  a.block_size = pr->block_size;
+  a.slot_mapping = pr->slot_mapping;
+  a.positions = pr->positions;
+  a.cos_sin = static_cast<const char*>(pr->cos_sin_cache);
+  a.cs_fp32 = pr->cos_sin_dtype == PS_DTYPE_FP32;
+  a.cs_stride_bytes = pr->cos_sin_stride * (a.cs_fp32 ? 4 : 2);
+  a.max_position = pr->max_position;
+  a.rotary_dim = pr->rotary_dim;
+  a.neox = pr->is_neox != 0;
+  a.num_tokens = pr->num_tokens;
+  a.num_q_heads = pr->num_q_heads;
+  a.num_kv_heads = pr->num_kv_heads;
+  a.head_size = pr->head_size;
+  a.bf16 = pr->dtype == PS_DTYPE_BF16;
+  a.status = pr->status;
+  // the 16-byte path needs every row and cos/sin row 16-byte aligned
+  const int64_t cs_es = a.cs_fp32 ? 4 : 2;
+  const bool vec = pr->head_size % 8 == 0 && pr->rotary_dim % 16 == 0 && aligned(pr->query, 16) &&
+                   aligned(pr->key, 16) && aligned(pr->value, 16) && aligned(pr->key_cache, 16) &&
+                   aligned(pr->value_cache, 16) && aligned(pr->cos_sin_cache, 16) &&
+                   a.q_st % 16 == 0 && a.q_sh % 16 == 0 && a.k_st % 16 == 0 && a.k_sh % 16 == 0 &&
+                   a.v_st % 16 == 0 && a.v_sh % 16 == 0 && a.c_sblock % 16 == 0 &&
+                   a.c_sslot % 16 == 0 && a.c_shead % 16 == 0 && (pr->cos_sin_stride * cs_es) % 16 == 0 &&
+                   (static_cast<const char*>(pr->value_cache) - static_cast<const char*>(pr->key_cache)) % 16 == 0;
+  const int e = ps_launch_rope_kv_append(a, sms, vec ? 1 : 0, static_cast<cudaStream_t>(stream));
+  if (e != 0) return cuda_fail(static_cast<cudaError_t>(e), "rope_kv_append launch");
+  return PS_OK;
+}
+
 int ps_chunked_prefill(const ps_paged_problem* pr, void* stream) {
   int rc = validate_problem(pr, false);
   if (rc != PS_OK) return rc;

@@ -140,6 +140,37 @@ struct PlanArgs {
   int32_t* plan;
 };
 }  // namespace ps
+namespace ps {
+// Fused rotary embedding + KV append.  Strides in bytes.
+struct RopeArgs {
+  char* q;
+  int64_t q_st, q_sh;
+  char* k;
+  int64_t k_st, k_sh;
+  const char* v;
+  int64_t v_st, v_sh;
+  char* key_cache;
+  char* value_cache;
+  int64_t c_sblock, c_sslot, c_shead;
+  int64_t num_slots;  // num_blocks * block_size
+  int32_t block_size;
+  const int64_t* slot_mapping;
+  const int64_t* positions;
+  const char* cos_sin;  // [max_position, rotary_dim]: cos then sin halves
+  int64_t cs_stride_bytes;
+  int64_t max_position;
+  int32_t cs_fp32;  // cache in fp32 (else the model dtype)
+  int32_t rotary_dim, neox;
+  int64_t num_tokens;
+  int32_t num_q_heads, num_kv_heads, head_size;
+  int32_t bf16;
+  int32_t* status;
+};
+}  // namespace ps
+// vec: the 16-byte path (rows, strides and cos/sin rows 16-byte aligned,
+// head_size % 8 == 0, rotary_dim % 16 == 0)
+int ps_launch_rope_kv_append(const ps::RopeArgs& a, int sm_count, int vec, cudaStream_t stream);
+
 int64_t ps_cascade_plan_words(int num_seqs);
 int ps_launch_cascade_plan(const ps::PlanArgs& a, cudaStream_t stream);
 

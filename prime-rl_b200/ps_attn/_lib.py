@@ -43,6 +43,7 @@ EXPORTED_SYMBOLS = (
     "ps_cascade_plan_build",
     "ps_paged_decode_cascade_workspace_size",
     "ps_paged_decode_cascade",
+    "ps_rope_kv_append",
 )
 
 
@@ -97,6 +98,43 @@ class PagedProblem(ctypes.Structure):
     ]
 
 
+class RopeAppendProblem(ctypes.Structure):
+    """Mirror of ``ps_rope_append_problem`` in include/ps_attn.h (same field order)."""
+
+    _fields_ = [
+        ("query", ctypes.c_void_p),
+        ("query_stride_token", ctypes.c_int64),
+        ("query_stride_head", ctypes.c_int64),
+        ("key", ctypes.c_void_p),
+        ("key_stride_token", ctypes.c_int64),
+        ("key_stride_head", ctypes.c_int64),
+        ("value", ctypes.c_void_p),
+        ("value_stride_token", ctypes.c_int64),
+        ("value_stride_head", ctypes.c_int64),
+        ("key_cache", ctypes.c_void_p),
+        ("value_cache", ctypes.c_void_p),
+        ("cache_stride_block", ctypes.c_int64),
+        ("cache_stride_slot", ctypes.c_int64),
+        ("cache_stride_head", ctypes.c_int64),
+        ("num_blocks", ctypes.c_int64),
+        ("block_size", ctypes.c_int32),
+        ("slot_mapping", ctypes.c_void_p),
+        ("positions", ctypes.c_void_p),
+        ("cos_sin_cache", ctypes.c_void_p),
+        ("cos_sin_stride", ctypes.c_int64),
+        ("max_position", ctypes.c_int64),
+        ("cos_sin_dtype", ctypes.c_int32),
+        ("rotary_dim", ctypes.c_int32),
+        ("is_neox", ctypes.c_int32),
+        ("num_tokens", ctypes.c_int64),
+        ("num_q_heads", ctypes.c_int32),
+        ("num_kv_heads", ctypes.c_int32),
+        ("head_size", ctypes.c_int32),
+        ("dtype", ctypes.c_int32),
+        ("status", ctypes.c_void_p),
+    ]
+
+
 def lib_path() -> Path:
     """The in-tree library, or a tuning variant named by ``PS_ATTN_LIB``."""
     override = os.environ.get("PS_ATTN_LIB")
@@ -127,6 +165,8 @@ def _declare(lib):
     lib.ps_chunked_prefill.argtypes = [c.POINTER(PagedProblem), c.c_void_p]
     lib.ps_paged_decode_static_scratch.restype = c.c_int
     lib.ps_paged_decode_static_scratch.argtypes = [c.POINTER(PagedProblem), c.c_void_p]
+    lib.ps_rope_kv_append.restype = c.c_int
+    lib.ps_rope_kv_append.argtypes = [c.POINTER(RopeAppendProblem), c.c_void_p]
     lib.ps_cascade_plan_bytes.restype = c.c_int64
     lib.ps_cascade_plan_bytes.argtypes = [c.c_int32]
     lib.ps_cascade_plan_build.restype = c.c_int

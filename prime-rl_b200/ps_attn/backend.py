@@ -22,6 +22,15 @@ or as an override of FLASH_ATTN::
     from ps_attn.backend import register
     register()                      # CUSTOM
     register(override_flash=True)   # FLASH_ATTN -> PS
+    register(rope_fusion=True)      # variant with the fused RoPE + KV append
+
+The ``rope_fusion`` variant (:class:`PSRopeAttentionBackend`) keeps
+FlashAttention's ``forward_includes_kv_cache_update = False``, so vLLM issues
+the KV update itself and its RoPE + KV-cache fusion pass
+(``vllm/compilation/passes/fusion/rope_kvcache_fusion.py``) can replace
+``rotary_embedding`` + ``unified_kv_cache_update`` by
+:meth:`PSRopeAttentionImpl.do_rope_and_kv_cache_update` (``ps_rope_kv_append``);
+its forward does not append.
 
 Batches are reordered decode-first (``reorder_batch_threshold = 1``); decode
 requests run the split-KV decode kernel, the rest the chunked-prefill kernel.
@@ -182,6 +191,9 @@ class PSAttentionMetadataBuilder(AttentionMetadataBuilder[PSAttentionMetadata]):
 
 class PSAttentionImpl(AttentionImpl):
     can_return_lse_for_decode: bool = True
+    # forward appends the step's keys and values (the backend declares
+    # forward_includes_kv_cache_update = True)
+    appends_in_forward: bool = True
 
     def __init__(self, num_heads: int, head_size: int, scale: float, num_kv_heads: int,
                  alibi_slopes: list[float] | None, sliding_window: int | None,
@@ -230,7 +242,8 @@ class PSAttentionImpl(AttentionImpl):
         nd, ndt = m.num_decodes, m.num_decode_tokens
         T = m.num_actual_tokens
         # key/value are None when this layer shares another layer's cache
-        append = key is not None and value is not None and self.kv_sharing_target_layer_name is None
+        append = (self.appends_in_forward and key is not None and value is not None
+                  and self.kv_sharing_target_layer_name is None)
         if append and T > ndt:  # prefill tokens: into the cache before their attention
             ops.kv_append(key[ndt:T], value[ndt:T], key_cache, value_cache, m.slot_mapping[ndt:T])
         if nd > 0:
@@ -245,14 +258,45 @@ class PSAttentionImpl(AttentionImpl):
         return output
 
 
+class PSRopeAttentionImpl(PSAttentionImpl):
+    """Impl for :class:`PSRopeAttentionBackend`: vLLM performs the KV update
+    before ``forward`` (``do_kv_cache_update``, or the fused RoPE + update)."""
+
+    appends_in_forward: bool = False
+
+    def fused_rope_kvcache_supported(self) -> bool:
+        return True
+
+    def do_rope_and_kv_cache_update(self, layer, query: torch.Tensor, key: torch.Tensor,
+                                    value: torch.Tensor, positions: torch.Tensor,
+                                    cos_sin_cache: torch.Tensor, is_neox: bool,
+                                    kv_cache: torch.Tensor,
+                                    layer_slot_mapping: torch.Tensor) -> None:
+        """``vllm/v1/attention/backend.py:823-841``: RoPE of query and key in
+        place, then the KV append of the rotated key (one launch)."""
+        key_cache, value_cache = kv_cache.unbind(0)
+        ops.rope_kv_append(query, key, value, positions.flatten(), cos_sin_cache, is_neox,
+                           key_cache, value_cache, layer_slot_mapping)
+
+
+class PSRopeAttentionBackend(PSAttentionBackend):
+    forward_includes_kv_cache_update: bool = False
+
+    @staticmethod
+    def get_impl_cls() -> type["PSRopeAttentionImpl"]:
+        return PSRopeAttentionImpl
+
+
 def cascade_enabled() -> bool:
     """Shared-prefix decode is opt-in (``PS_ATTN_CASCADE=1``)."""
     return os.environ.get("PS_ATTN_CASCADE", "0") == "1"
 
 
-def register(override_flash: bool = False) -> None:
-    """Register the PS backend with vLLM's backend registry."""
+def register(override_flash: bool = False, rope_fusion: bool = False) -> None:
+    """Register the PS backend with vLLM's backend registry (``rope_fusion``:
+    the variant whose KV update vLLM issues, fusable with RoPE)."""
     from vllm.v1.attention.backends.registry import AttentionBackendEnum, register_backend
 
+    cls = PSRopeAttentionBackend if rope_fusion else PSAttentionBackend
     target = AttentionBackendEnum.FLASH_ATTN if override_flash else AttentionBackendEnum.CUSTOM
-    register_backend(target, f"{PSAttentionBackend.__module__}.{PSAttentionBackend.__qualname__}")
+    register_backend(target, f"{cls.__module__}.{cls.__qualname__}")

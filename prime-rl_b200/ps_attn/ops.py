@@ -78,6 +78,72 @@ def kv_append(key: torch.Tensor, value: torch.Tensor, key_cache: torch.Tensor,
         _stream_ptr(key.device)))
 
 
+def rope_kv_append(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
+                   positions: torch.Tensor, cos_sin_cache: torch.Tensor, is_neox: bool,
+                   key_cache: torch.Tensor, value_cache: torch.Tensor,
+                   slot_mapping: torch.Tensor, status: torch.Tensor | None = None) -> None:
+    """Rotary embedding of ``query``/``key`` in place, then the KV append of the
+    rotated key and ``value`` (``do_rope_and_kv_cache_update``'s contract).
+
+    query [T, Hq*D] or [T, Hq, D]; key, value [T, Hkv*D] or [T, Hkv, D];
+    positions int64 [T]; cos_sin_cache [max_position, rotary_dim] (fp32 or the
+    model dtype; cos half then sin half); caches [num_blocks, block_size, Hkv,
+    D]; slot_mapping int64 [T] (negative: no cache write).  Bit-identical to
+    vLLM's torch-native rotary embedding followed by ``kv_append``.
+    """
+    lib = _lib.load()
+    _require_cuda(query, key, value, positions, cos_sin_cache, key_cache, value_cache, slot_mapping)
+    nb, bs, hkv, d = key_cache.shape
+    T = slot_mapping.shape[0]
+    if positions.dtype != torch.int64 or slot_mapping.dtype != torch.int64:
+        raise ValueError("positions and slot_mapping must be int64")
+    if positions.numel() < T or not positions.is_contiguous() or not slot_mapping.is_contiguous():
+        raise ValueError("positions must hold a position per token; both contiguous")
+    q3 = query.view(query.shape[0], -1, d)
+    k3 = key.view(key.shape[0], -1, d)
+    v3 = value.view(value.shape[0], -1, d)
+    if k3.shape[1] != hkv or v3.shape[1] != hkv or q3.shape[0] < T or k3.shape[0] < T:
+        raise ValueError("query/key/value shapes do not match the cache")
+    dtype = query.dtype
+    if dtype not in (torch.bfloat16, torch.float16) or key.dtype != dtype or value.dtype != dtype \
+            or key_cache.dtype != dtype or value_cache.dtype != dtype:
+        raise ValueError("query, key, value and caches must share one fp16/bf16 dtype")
+    if cos_sin_cache.dtype not in (torch.float32, dtype) or cos_sin_cache.stride(-1) != 1:
+        raise ValueError("cos_sin_cache must be fp32 or the model dtype, rows contiguous")
+    if key_cache.stride() != value_cache.stride() or key_cache.stride(-1) != 1:
+        raise ValueError("key_cache and value_cache must share strides, last dim contiguous")
+    if q3.stride(-1) != 1 or k3.stride(-1) != 1 or v3.stride(-1) != 1:
+        raise ValueError("last dimension must be contiguous")
+    pr = _lib.RopeAppendProblem()
+    pr.query = q3.data_ptr()
+    pr.query_stride_token, pr.query_stride_head = q3.stride(0), q3.stride(1)
+    pr.key = k3.data_ptr()
+    pr.key_stride_token, pr.key_stride_head = k3.stride(0), k3.stride(1)
+    pr.value = v3.data_ptr()
+    pr.value_stride_token, pr.value_stride_head = v3.stride(0), v3.stride(1)
+    pr.key_cache = key_cache.data_ptr()
+    pr.value_cache = value_cache.data_ptr()
+    pr.cache_stride_block, pr.cache_stride_slot, pr.cache_stride_head = key_cache.stride()[:3]
+    pr.num_blocks = nb
+    pr.block_size = bs
+    pr.slot_mapping = slot_mapping.data_ptr()
+    pr.positions = positions.data_ptr()
+    pr.cos_sin_cache = cos_sin_cache.data_ptr()
+    pr.cos_sin_stride = cos_sin_cache.stride(0)
+    pr.max_position = cos_sin_cache.shape[0]
+    pr.cos_sin_dtype = _DTYPES[cos_sin_cache.dtype]
+    pr.rotary_dim = cos_sin_cache.shape[-1]
+    pr.is_neox = int(bool(is_neox))
+    pr.num_tokens = T
+    pr.num_q_heads = q3.shape[1]
+    pr.num_kv_heads = hkv
+    pr.head_size = d
+    pr.dtype = _DTYPES[dtype]
+    if status is not None:
+        pr.status = status.data_ptr()
+    _lib.check(lib.ps_rope_kv_append(ctypes.byref(pr), _stream_ptr(query.device)))
+
+
 class DecodeWorkspace:
     """Fixed-size device workspace for :func:`paged_decode`.
 

@@ -14,6 +14,15 @@ Run in a container where vLLM 0.22 is installed (not needed at test time):
   (``vllm/v1/attention/ops/triton_reshape_and_cache_flash.py:17-124``) run on CPU
   tensors under the Triton interpreter (``TRITON_INTERPRET=1``).
 
+* Rotary embedding (for the fused RoPE + KV append): vLLM's
+  ``RotaryEmbedding.forward_static``
+  (``vllm/model_executor/layers/rotary_embedding/base.py:140-181``, the
+  torch-native path ``forward_native`` takes) on CPU tensors, neox and GPT-J
+  styles, full and partial rotary dims, bf16 and fp16, with the cos/sin cache
+  in the model dtype or in fp32.  The inputs are stored with the outputs
+  (``rope_*.npz``); only the cos/sin rows at the tested positions are stored.
+  ``python tests/golden/make_golden.py --only rope`` regenerates just these.
+
 Inputs are regenerated at test time from the seeds recorded here by
 ``ps_attn.workloads.make_batch`` (CPU generator); a checksum of the inputs is
 stored so a generator change is detected instead of silently comparing
@@ -138,7 +147,54 @@ def append_golden(triton_mod, dtype, seed):
                 slot_mapping=slots.numpy(), key_cache_out=as_np(kc), value_cache_out=as_np(vc))
 
 
+ROPE_CASES = {
+    # name: (dtype, cache dtype, rotary_dim, is_neox, seed)
+    "bf16_neox": (torch.bfloat16, torch.bfloat16, 128, True, 31),
+    "bf16_gptj": (torch.bfloat16, torch.bfloat16, 128, False, 32),
+    "fp16_partial": (torch.float16, torch.float16, 64, True, 33),
+    "bf16_fp32cache": (torch.bfloat16, torch.float32, 128, True, 34),
+}
+ROPE_MAX_POS = 40960   # Qwen3 max_position_embeddings
+ROPE_THETA = 1.0e6     # Qwen3 rope_theta
+
+
+def rope_golden(dtype, cache_dtype, rot, neox, seed):
+    """vLLM's torch-native rotary embedding on random q/k rows."""
+    from vllm.model_executor.layers.rotary_embedding.base import RotaryEmbedding
+
+    g = torch.Generator().manual_seed(seed)
+    T, Hq, Hkv, D = 9, 4, 2, 128
+    positions = torch.tensor([0, 1, 7, 255, 1000, 4097, 20000, 40958, 40959], dtype=torch.int64)
+    # the cache as vLLM's RotaryEmbedding._compute_cos_sin_cache builds it
+    inv_freq = 1.0 / (ROPE_THETA ** (torch.arange(0, rot, 2, dtype=torch.float) / rot))
+    freqs = torch.einsum("i,j -> ij", positions.to(torch.float), inv_freq)
+    rows = torch.cat((freqs.cos(), freqs.sin()), dim=-1).to(cache_dtype)  # [T, rot]
+    q = torch.randn(T, Hq * D, generator=g).to(dtype)
+    k = torch.randn(T, Hkv * D, generator=g).to(dtype)
+    full = torch.zeros(ROPE_MAX_POS, rot, dtype=cache_dtype)
+    full[positions] = rows
+    qo, ko = RotaryEmbedding.forward_static(positions, q.clone(), k.clone(), D, rot, full, neox)
+    bits = (lambda t: t.view(torch.int16).numpy()) if dtype == torch.bfloat16 else (lambda t: t.numpy())
+    cbits = (lambda t: t.view(torch.int16).numpy()) if cache_dtype == torch.bfloat16 else (lambda t: t.numpy())
+    return dict(positions=positions.numpy(), cos_sin_rows=cbits(rows), q_in=bits(q), k_in=bits(k),
+                q_out=bits(qo), k_out=bits(ko), shape=np.array([T, Hq, Hkv, D, rot, int(neox)]))
+
+
+def main_rope(meta):
+    meta["rope"] = {}
+    for name, (dtype, cdtype, rot, neox, seed) in ROPE_CASES.items():
+        np.savez_compressed(HERE / f"rope_{name}.npz", **rope_golden(dtype, cdtype, rot, neox, seed))
+        meta["rope"][name] = {"dtype": str(dtype), "cache_dtype": str(cdtype), "rotary_dim": rot,
+                              "is_neox": neox, "seed": seed, "max_position": ROPE_MAX_POS}
+        print(f"rope_{name}: written")
+
+
 def main():
+    if "--only" in sys.argv and sys.argv[sys.argv.index("--only") + 1] == "rope":
+        meta = json.loads((HERE / "golden_meta.json").read_text())
+        main_rope(meta)
+        (HERE / "golden_meta.json").write_text(json.dumps(meta, indent=1, default=str) + "\n")
+        return
     attention_ref = load_attention_ref()
     meta = {"attention": {}, "append": {}}
     for name, spec in ATTN_CASES.items():
@@ -153,6 +209,7 @@ def main():
         np.savez_compressed(HERE / f"append_{name}.npz", **arrays)
         meta["append"][name] = {"dtype": str(dtype), "seed": seed}
         print(f"append_{name}: written")
+    main_rope(meta)
     (HERE / "golden_meta.json").write_text(json.dumps(meta, indent=1, default=str) + "\n")
 
 

@@ -110,3 +110,37 @@ def test_cascade_entry_points_validate_on_the_host():
     assert rc == _lib.PS_ERR_INVALID_ARGUMENT
     rc = lib.ps_cascade_plan_build(ctypes.byref(pr), 8, ctypes.c_void_p(16), 8, None)
     assert rc == _lib.PS_ERR_INVALID_ARGUMENT  # buffer too small
+
+
+def _struct_fields(name):
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    end = text.index("} " + name + ";")
+    start = text.rindex("typedef struct {", 0, end) + len("typedef struct {")
+    names = []
+    for decl in text[start:end].split(";"):
+        toks = decl.replace("*", " ").replace(",", " ").split()
+        for i, tok in enumerate(toks):
+            if tok not in ("const", "void", "int64_t", "int32_t", "float"):
+                names.extend(toks[i:])
+                break
+    return names
+
+
+def test_rope_struct_layout_and_validation():
+    assert _struct_fields("ps_rope_append_problem") == [f for f, _ in _lib.RopeAppendProblem._fields_]
+    assert _struct_fields("ps_paged_problem") == [f for f, _ in _lib.PagedProblem._fields_]
+    lib = _lib.load()
+    assert lib.ps_rope_kv_append(None, None) == _lib.PS_ERR_INVALID_ARGUMENT
+    pr = _lib.RopeAppendProblem()
+    pr.num_tokens = 0
+    assert lib.ps_rope_kv_append(ctypes.byref(pr), None) == _lib.PS_OK  # nothing to do
+    pr.num_tokens = 4
+    assert lib.ps_rope_kv_append(ctypes.byref(pr), None) == _lib.PS_ERR_INVALID_ARGUMENT
+    for name in ("query", "key", "value", "key_cache", "value_cache", "slot_mapping", "positions",
+                 "cos_sin_cache"):
+        setattr(pr, name, 16)
+    pr.dtype, pr.cos_sin_dtype = _lib.PS_DTYPE_FP32, _lib.PS_DTYPE_FP32
+    assert lib.ps_rope_kv_append(ctypes.byref(pr), None) == _lib.PS_ERR_UNSUPPORTED
+    pr.dtype, pr.head_size, pr.rotary_dim = _lib.PS_DTYPE_BF16, 128, 63
+    assert lib.ps_rope_kv_append(ctypes.byref(pr), None) == _lib.PS_ERR_INVALID_ARGUMENT
+    assert b"rotary_dim" in lib.ps_last_error()

@@ -157,3 +157,34 @@ def test_cascade_opt_in_builds_one_plan_per_step(monkeypatch):
     assert not psb.cascade_enabled()
     monkeypatch.setenv("PS_ATTN_CASCADE", "1")
     assert psb.cascade_enabled()
+
+
+def test_rope_fusion_variant(monkeypatch):
+    """The rope_fusion variant: vLLM issues the KV update (the backend says
+    forward does not include it), the fused RoPE hook unbinds the cache and
+    calls ps_rope_kv_append, and forward does not append."""
+    from vllm.v1.attention.backends.registry import AttentionBackendEnum
+
+    B = psb.PSRopeAttentionBackend
+    assert B.forward_includes_kv_cache_update is False and B.get_impl_cls() is psb.PSRopeAttentionImpl
+    psb.register(rope_fusion=True)
+    assert AttentionBackendEnum.CUSTOM.get_class() is B
+    AttentionBackendEnum.CUSTOM.clear_override()
+    seen, calls = {}, []
+    monkeypatch.setattr(psb.ops, "rope_kv_append", lambda *a: seen.update(args=a))
+    monkeypatch.setattr(psb.ops, "kv_append", lambda *a, **k: calls.append("append"))
+    monkeypatch.setattr(psb.ops, "paged_decode", lambda *a, **k: calls.append(("decode", k)))
+    monkeypatch.setattr(psb.ops, "chunked_prefill", lambda *a, **k: calls.append("prefill"))
+    impl = psb.PSRopeAttentionImpl(16, 128, 0.088, 8, None, None, "auto")
+    assert impl.fused_rope_kvcache_supported()
+    kv = torch.zeros(2, 4, 16, 8, 128)
+    q, k, v = torch.zeros(3, 16 * 128), torch.zeros(3, 8 * 128), torch.zeros(3, 8 * 128)
+    pos, cs, slots = torch.arange(3).view(1, 3), torch.zeros(10, 128), torch.arange(3)
+    impl.do_rope_and_kv_cache_update(None, q, k, v, pos, cs, True, kv, slots)
+    a = seen["args"]
+    assert a[0] is q and a[1] is k and a[3].shape == (3,) and a[5] is True
+    assert a[6].data_ptr() == kv[0].data_ptr() and a[7].data_ptr() == kv[1].data_ptr()
+    md = _builder().build(0, _common([1, 1, 5], [10, 20, 40]))
+    impl.forward(None, torch.zeros(8, 16, 128), torch.zeros(8, 8, 128), torch.zeros(8, 8, 128),
+                 kv, md, torch.zeros(8, 16, 128))
+    assert calls[0][0] == "decode" and "new_key" not in calls[0][1] and calls[1] == "prefill"
