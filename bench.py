@@ -226,7 +226,7 @@ def run_ours(args):
 
     def prefill():
         ops.chunked_prefill(batch.q, kc, vc, batch.block_table[nd:], batch.seq_lens[nd:],
-                            batch.query_start_loc[nd:], batch.softmax_scale, out)
+                            batch.query_start_loc[nd:], batch.softmax_scale, out, workspace=ws)
 
     def gather():
         import torch.distributed as dist
@@ -441,7 +441,7 @@ def run_e2e(batch, ws, dev, steps, world, nd=None, replicas=1, fused=True, casca
                              **fkw)
             ops.chunked_prefill(dev_in["q"], kc, vc, dev_in["block_table"][nd:],
                                 dev_in["seq_lens"][nd:], dev_in["query_start_loc"][nd:],
-                                batch.softmax_scale, out)
+                                batch.softmax_scale, out, workspace=ws)
         out_host.copy_(out, non_blocking=True)
 
     n = max(3, min(steps, 200))

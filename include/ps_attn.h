@@ -269,6 +269,20 @@ int ps_rope_kv_append(const ps_rope_append_problem* problem, void* stream);
  */
 int ps_chunked_prefill(const ps_paged_problem* problem, void* stream);
 
+/*
+ * ps_chunked_prefill with dynamic work distribution: the (sequence, kv head,
+ * pair of 128-row Q tiles) units are claimed by the CTAs through two int32
+ * counters at bytes 16..23 of `workspace` (>= 256 bytes, 256-byte aligned,
+ * zeroed once; a ps_paged_decode workspace serves, its counters are
+ * elsewhere) instead of the fixed round-robin of ps_chunked_prefill, so
+ * CTAs that finish early take the remaining units.  Same outputs.  Prefill
+ * calls that can overlap on the GPU must not share a workspace.  No
+ * counterpart in the reference (an implementation choice inside the
+ * flash_attn_varlen_func replacement).
+ */
+int ps_chunked_prefill_ws(const ps_paged_problem* problem, void* workspace,
+                          int64_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -33,6 +33,8 @@
 // Every mbarrier wait is bounded (~1 s); on timeout the kernel records
 // PS_DEV_WAIT_TIMEOUT, raises a CTA-wide abort flag that ends every role's
 // loop, and still frees its TMEM.
+#include <climits>
+
 #include "ps_common.cuh"
 #include "ps_launch.h"
 #include "tcgen05.cuh"
@@ -103,9 +105,9 @@ struct PrefillSmem {
   static constexpr int k_off = q_off + 2 * kTileBytes;
   static constexpr int v_off = k_off + kKvStages * kTileBytes;
   static constexpr int bar_off = v_off + kKvStages * kTileBytes;
-  static constexpr int n_bars = 2 /*q*/ + 3 * kKvStages /*kfull vfull kvempty*/ +
+  static constexpr int n_bars = 4 /*unit_full, unit_empty*/ + 2 /*q*/ + 3 * kKvStages /*kfull vfull kvempty*/ +
                                 2 /*s_full*/ + 2 /*p_full*/ + 2 /*pv_done*/;
-  static constexpr int misc_off = bar_off + n_bars * 8;  // tmem base, abort flag
+  static constexpr int misc_off = bar_off + n_bars * 8;  // tmem base, abort flag, next units[2]
   static constexpr int table_off = misc_off + 16;
   static constexpr int bytes_before_table = table_off;
 };
@@ -119,7 +121,13 @@ struct PBars {
   uint64_t* s_full;   // [2]: tile A, tile B
   uint64_t* p_full;   // [2]
   uint64_t* pv_done;  // [2]
+  uint64_t* unit_full;   // [2]: a claimed unit id is in s_unit[k]
+  uint64_t* unit_empty;  // [2]: every consumer has read s_unit[k]
 };
+
+// Consumers of the MMA warp (one thread) and the 8 softmax warps release a
+// published unit id.
+constexpr int kUnitConsumers = 1 + 8;
 
 struct UnitInfo {
   int b, h;         // sequence, kv head
@@ -189,6 +197,45 @@ __device__ __forceinline__ void tmem_st_x16(uint32_t taddr, const uint32_t (&r)[
       : "memory");
 }
 
+// Unit scheduling.  Static: CTA c takes units c, c + grid, ...  Dynamic
+// (p.sched): CTA c starts with unit c; when its TMA warp has issued every
+// load of its uit-th unit it claims the next id (grid + an atomic counter)
+// and publishes it in s_unit[(uit + 1) & 1] (use m = uit >> 1 of that slot);
+// the MMA thread and the softmax warps read it there.  Ids are claimed in unit
+// order (longest pair of each sequence first), so the CTAs that finish early
+// take the remaining units.
+__device__ __forceinline__ int claim_and_publish(const PrefillParams& p, const PBars& bars,
+                                                 volatile int* s_unit, int u, int uit,
+                                                 volatile int* abort_flag, int lane) {
+  if (p.sched == nullptr) return u + static_cast<int>(gridDim.x);
+  int nxt = 0;
+  if (lane == 0) {
+    nxt = static_cast<int>(gridDim.x) + atomicAdd(p.sched, 1);
+    const int k = (uit + 1) & 1, m = uit >> 1;
+    if (pwait(bars.unit_empty + k, static_cast<uint32_t>((m & 1) ^ 1), abort_flag, p.status)) {
+      s_unit[k] = nxt;
+      mbar_arrive(bars.unit_full + k);  // release: the id is visible with the phase
+    } else {
+      nxt = INT_MAX;
+    }
+  }
+  return __shfl_sync(0xffffffffu, nxt, 0);
+}
+
+// Next unit for a consumer (all lanes of a softmax warp, or the MMA thread
+// alone: `single`).  INT_MAX after an abort.
+__device__ __forceinline__ int next_unit(const PrefillParams& p, const PBars& bars,
+                                         volatile int* s_unit, int u, int uit,
+                                         volatile int* abort_flag, bool single, int lane) {
+  if (p.sched == nullptr) return u + static_cast<int>(gridDim.x);
+  const int k = (uit + 1) & 1, m = uit >> 1;
+  if (!pwait(bars.unit_full + k, static_cast<uint32_t>(m & 1), abort_flag, p.status)) return INT_MAX;
+  const int nxt = s_unit[k];
+  if (!single) __syncwarp();
+  if (single || lane == 0) mbar_arrive(bars.unit_empty + k);
+  return nxt;
+}
+
 template <bool kBF16>
 __global__ void __launch_bounds__(kThreads, 1)
     chunked_prefill_kernel(const __grid_constant__ PrefillParams p,
@@ -209,8 +256,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   bars.s_full = bar + 2 + 3 * kKvStages;
   bars.p_full = bar + 4 + 3 * kKvStages;
   bars.pv_done = bar + 6 + 3 * kKvStages;
+  bars.unit_full = bar + 8 + 3 * kKvStages;
+  bars.unit_empty = bar + 10 + 3 * kKvStages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::misc_off);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::misc_off + 4);
+  volatile int* s_unit = reinterpret_cast<volatile int*>(smem + L::misc_off + 8);
   int* prefix = reinterpret_cast<int*>(smem + L::table_off);
   __shared__ int s_warp_tot[kThreads / 32];
 
@@ -252,6 +302,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bars.s_full + x, 1);
       mbar_init(bars.p_full + x, 4);
       mbar_init(bars.pv_done + x, 1);
+      mbar_init(bars.unit_full + x, 1);
+      mbar_init(bars.unit_empty + x, kUnitConsumers);
     }
     fence_mbar_init();
     tma_prefetch_desc(&qmap);
@@ -290,7 +342,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // and handed out by shuffle; lane i issues page i of a KV tile.
     int t = 0, uit = 0;
     int bt_b = -1, bt_e0 = 0, bt_reg = 0;
-    for (int u = blockIdx.x; u < total_units && !*abort_flag; u += gridDim.x, ++uit) {
+    for (int u = blockIdx.x; u < total_units && !*abort_flag; ++uit) {
       const UnitInfo ui = unit_info(p, prefix, u);
       if (!pwait(bars.q_empty, (uit & 1) ^ 1, abort_flag, p.status)) break;
       if (lane == 0) {
@@ -342,6 +394,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (!ok) break;
+      u = claim_and_publish(p, bars, s_unit, u, uit, abort_flag, lane);
     }
   } else if (warp == 1) {
     // =========================== MMA issuer ===========================
@@ -380,7 +433,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       };
       int t = 0, uit = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x, ++uit) {
+      for (int u = blockIdx.x; u < total_units && ok; ++uit) {
         const UnitInfo ui = unit_info(p, prefix, u);
         if (!pwait(bars.q_full, static_cast<uint32_t>(uit & 1), abort_flag, p.status)) break;
         tc::fence_after_sync();
@@ -410,6 +463,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         t += ui.ntiles;
+        if (ok) u = next_unit(p, bars, s_unit, u, uit, abort_flag, true, lane);
       }
     }
   } else if (warp >= 4) {
@@ -421,8 +475,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t s_addr = lane_addr + x * 128;
     const uint32_t o_addr = lane_addr + 256 + x * 128;
     const float sl2 = p.scale_log2;
-    int t = 0;
-    for (int u = blockIdx.x; u < total_units; u += gridDim.x) {
+    int t = 0, uit = 0;
+    for (int u = blockIdx.x; u < total_units; ++uit) {
       const UnitInfo ui = unit_info(p, prefix, u);
       const int tok = ui.t0 + x * tpt + row / G;
       const int hin = row - (row / G) * G;
@@ -573,6 +627,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         p.lse[static_cast<int64_t>(qh) * p.lse_sh + orow * p.lse_st] =
             zero ? -INFINITY : (m_run + __log2f(l_run)) * 0.6931471805599453f;
       tc::fence_before_sync();
+      u = next_unit(p, bars, s_unit, u, uit, abort_flag, false, lane);
     }
   }
 
@@ -581,6 +636,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc::fence_after_sync();
   if (warp == 1) tc::tmem_dealloc(tmem, 512);
+  // the last CTA out resets the scheduler (every CTA made its last claim
+  // before its threads met above)
+  if (tid == 0 && p.sched != nullptr) {
+    __threadfence();
+    if (atomicAdd(p.sched + 1, 1) == static_cast<int>(gridDim.x) - 1) {
+      p.sched[0] = 0;
+      p.sched[1] = 0;
+    }
+  }
 }
 
 template <bool kBF16>

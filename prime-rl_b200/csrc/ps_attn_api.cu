@@ -112,7 +112,7 @@ int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
 // num_seqs, and the plain and cascade layouts agree on everything but the
 // record size, so one buffer (sized for the larger use) serves calls of either
 // kind with any batch size up to the one it was sized for:
-//   [0, 256)                 status word (+ reserved)
+//   [0, 256)                 status word; bytes 16..23: prefill unit scheduler
 //   [256, 256 + C)           counters, kDecodeMaxSeqs * num_kv_heads int32
 //   [.., + C)                prefix-segment counters (cascade)
 //   [..., ...)               partial records, one per split slot:
@@ -500,6 +500,13 @@ int ps_rope_kv_append(const ps_rope_append_problem* pr, void* stream) {
 }
 
 int ps_chunked_prefill(const ps_paged_problem* pr, void* stream) {
+  return ps_chunked_prefill_ws(pr, nullptr, 0, stream);
+}
+
+int ps_chunked_prefill_ws(const ps_paged_problem* pr, void* workspace, int64_t workspace_bytes,
+                          void* stream) {
+  if (workspace != nullptr && (workspace_bytes < 256 || !aligned(workspace, 256)))
+    return fail(PS_ERR_WORKSPACE, "prefill workspace must be >= 256 bytes, 256-byte aligned");
   int rc = validate_problem(pr, false);
   if (rc != PS_OK) return rc;
   if (pr->num_seqs == 0 || pr->num_tokens == 0) return PS_OK;
@@ -543,6 +550,9 @@ int ps_chunked_prefill(const ps_paged_problem* pr, void* stream) {
   p.num_blocks = pr->num_blocks;
   p.scale_log2 = pr->softmax_scale * 1.4426950408889634f;
   p.status = pr->status;
+  // dynamic unit scheduling: two counters in the workspace's reserved header
+  // (bytes 16..23; the decode uses bytes 0..3 of the same header)
+  p.sched = workspace != nullptr ? reinterpret_cast<int32_t*>(static_cast<char*>(workspace) + 16) : nullptr;
   const int e = ps_launch_chunked_prefill(p, qmap, kmap, vmap, pr->dtype == PS_DTYPE_BF16, sms,
                                           static_cast<cudaStream_t>(stream));
   if (e != 0) return cuda_fail(static_cast<cudaError_t>(e), "chunked_prefill launch");

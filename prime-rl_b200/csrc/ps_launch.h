@@ -104,6 +104,9 @@ struct PrefillParams {
   int64_t num_blocks;
   float scale_log2;
   int32_t* status;
+  // dynamic unit scheduling: [0] units claimed past the grid, [1] CTAs done
+  // (both zero between launches); nullptr: static round-robin
+  int32_t* sched;
 };
 constexpr int kPrefillMaxSeqs = 4096;
 }  // namespace ps

@@ -44,6 +44,7 @@ EXPORTED_SYMBOLS = (
     "ps_paged_decode_cascade_workspace_size",
     "ps_paged_decode_cascade",
     "ps_rope_kv_append",
+    "ps_chunked_prefill_ws",
 )
 
 
@@ -165,6 +166,8 @@ def _declare(lib):
     lib.ps_chunked_prefill.argtypes = [c.POINTER(PagedProblem), c.c_void_p]
     lib.ps_paged_decode_static_scratch.restype = c.c_int
     lib.ps_paged_decode_static_scratch.argtypes = [c.POINTER(PagedProblem), c.c_void_p]
+    lib.ps_chunked_prefill_ws.restype = c.c_int
+    lib.ps_chunked_prefill_ws.argtypes = [c.POINTER(PagedProblem), c.c_void_p, c.c_int64, c.c_void_p]
     lib.ps_rope_kv_append.restype = c.c_int
     lib.ps_rope_kv_append.argtypes = [c.POINTER(RopeAppendProblem), c.c_void_p]
     lib.ps_cascade_plan_bytes.restype = c.c_int64

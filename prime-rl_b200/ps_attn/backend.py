@@ -254,7 +254,8 @@ class PSAttentionImpl(AttentionImpl):
                              cascade=m.cascade_plan, **fused)
         if m.num_prefills > 0:
             ops.chunked_prefill(query[:T], key_cache, value_cache, m.block_table[nd:],
-                                m.seq_lens[nd:], m.query_start_loc[nd:], self.scale, output[:T])
+                                m.seq_lens[nd:], m.query_start_loc[nd:], self.scale, output[:T],
+                                workspace=m.workspace)
         return output
 
 

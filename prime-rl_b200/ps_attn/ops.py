@@ -400,19 +400,26 @@ def chunked_prefill(q: torch.Tensor, key_cache: torch.Tensor, value_cache: torch
                     block_table: torch.Tensor, seq_lens: torch.Tensor,
                     query_start_loc: torch.Tensor, softmax_scale: float, out: torch.Tensor,
                     lse: torch.Tensor | None = None,
-                    status: torch.Tensor | None = None) -> torch.Tensor:
+                    status: torch.Tensor | None = None,
+                    workspace: "DecodeWorkspace | None" = None) -> torch.Tensor:
     """Causal (bottom-right) varlen attention over the paged cache; any q_len >= 1.
 
     ``query_start_loc`` [B+1] holds absolute row offsets into ``q``/``out``
     (a slice of a larger batch's offsets is fine).  ``status`` (int32 [1],
-    optional) receives PS_DEV_* bits from device-side checks.
+    optional) receives PS_DEV_* bits from device-side checks.  With a
+    ``workspace`` (a :class:`DecodeWorkspace` serves) the work units are
+    handed out dynamically (``ps_chunked_prefill_ws``).
     """
     lib = _lib.load()
     if query_start_loc is None:
         raise ValueError("chunked_prefill needs query_start_loc")
     pr = _problem(q, key_cache, value_cache, block_table, seq_lens, query_start_loc,
                   softmax_scale, out, lse, status)
-    _lib.check(lib.ps_chunked_prefill(ctypes.byref(pr), _stream_ptr(q.device)))
+    if workspace is not None:
+        _lib.check(lib.ps_chunked_prefill_ws(ctypes.byref(pr), workspace.buffer.data_ptr(),
+                                             workspace.nbytes, _stream_ptr(q.device)))
+    else:
+        _lib.check(lib.ps_chunked_prefill(ctypes.byref(pr), _stream_ptr(q.device)))
     return out
 
 

@@ -131,3 +131,27 @@ def test_vllm_impl_forward_mixed_batch(cuda_device):
     torch.cuda.synchronize()
     assert ws.status() == 0
     assert_attn_close(to_np32(out), rout)
+
+
+def test_dynamic_unit_claiming_is_bit_identical(cuda_device):
+    """ps_chunked_prefill_ws hands the units out through the workspace
+    counters; every unit is computed the same way whichever CTA takes it, so
+    the result equals the round-robin call's bit for bit, call after call
+    (the counters return to zero after each launch)."""
+    q_lens, seq_lens, _ = workloads.config_lengths(4)
+    q_lens, seq_lens = q_lens[128:132], seq_lens[128:132]  # 4 chunks of 2048 on contexts
+    batch = workloads.make_batch(q_lens, seq_lens, 32, 8, seed=12).to(cuda_device)
+    ops.kv_append(batch.key, batch.value, batch.kv_cache[0], batch.kv_cache[1], batch.slot_mapping)
+    args = (batch.q, batch.kv_cache[0], batch.kv_cache[1], batch.block_table, batch.seq_lens,
+            batch.query_start_loc, batch.softmax_scale)
+    ref = torch.empty_like(batch.q)
+    ref_lse = torch.empty(32, batch.q.shape[0], device=cuda_device)
+    ops.chunked_prefill(*args, ref, lse=ref_lse)
+    ws = ops.DecodeWorkspace(8, 32, 8, 128, cuda_device)
+    for _ in range(3):
+        out = torch.full_like(batch.q, float("nan"))
+        lse = torch.full_like(ref_lse, float("nan"))
+        ops.chunked_prefill(*args, out, lse=lse, workspace=ws)
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref) and torch.equal(lse, ref_lse)
+        assert ws.buffer[16:24].view(torch.int32).tolist() == [0, 0]
