@@ -268,6 +268,47 @@ __device__ __noinline__ void combine_rows(const DecodeParams& p, int64_t slot0, 
       if (lane == 0 && p.lse != nullptr) p.lse[qh * p.lse_sh + qrow * p.lse_st] = lse;
     }
   };
+  if (ntot <= 4 && nrows <= 4) {
+    // few sources (the common split count): every partial row this lane
+    // needs is loaded together with the LSEs, so the merge waits on one L2
+    // round trip instead of two
+    float4 ov[4][4];
+    float ls[4][4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const bool use = k < ntot && j < nrows;
+        ov[k][j] = use ? __ldcg(reinterpret_cast<const float4*>(slot_o<kRec>(p, src_slot(k), src_row(k, j))) + lane)
+                       : make_float4(0.f, 0.f, 0.f, 0.f);
+        ls[k][j] = use ? __ldcg(slot_lse<kRec>(p, src_slot(k), src_row(k, j))) : -INFINITY;
+      }
+    __syncwarp();  // every lane's reads precede the writes
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (j >= nrows) break;
+      const float mx = fmaxf(fmaxf(ls[0][j], ls[1][j]), fmaxf(ls[2][j], ls[3][j]));
+      const float mx_cur = (mx == -INFINITY) ? 0.f : mx;
+      float e[4], sum = 0.f;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        e[k] = k < ntot ? ex2(ls[k][j] * kLog2e - mx_cur * kLog2e) : 0.f;
+        sum += e[k];
+      }
+      const float inv = (sum == 0.f || sum != sum) ? 0.f : 1.f / sum;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float w = e[k] * inv;
+        acc.x += w * ov[k][j].x;
+        acc.y += w * ov[k][j].y;
+        acc.z += w * ov[k][j].z;
+        acc.w += w * ov[k][j].w;
+      }
+      emit(j, acc, __logf(sum) + mx);
+    }
+    return;
+  }
   if (ntot <= 32) {
     // fast path: lane k owns source k; one LSE load per lane and row, and the
     // O loads of a phase are independent of one another and of the weights
@@ -1046,10 +1087,11 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, kDecodeCtasPerSm)
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + tid;
        i < static_cast<int64_t>(B) * p.num_q_heads; i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     const int b = static_cast<int>(i / p.num_q_heads);
+    if (prefix[b + 1] != prefix[b]) continue;  // has pages: no global load needed
     const int qh = static_cast<int>(i - static_cast<int64_t>(b) * p.num_q_heads);
     int qlen = 1;
     if (p.qsl) qlen = __ldg(p.qsl + b + 1) - __ldg(p.qsl + b);
-    if (qlen != 1 || prefix[b + 1] != prefix[b]) continue;
+    if (qlen != 1) continue;
     const int qrow = p.qsl ? __ldg(p.qsl + b) : b;
     for (int d = 0; d < kHeadDim; ++d) store_out2<kBF16>(p.out, qrow * p.o_st + qh * p.o_sh + d, 0.f);
     if (p.lse) p.lse[qh * p.lse_sh + qrow * p.lse_st] = -INFINITY;
