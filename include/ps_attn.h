@@ -283,6 +283,81 @@ int ps_chunked_prefill(const ps_paged_problem* problem, void* stream);
 int ps_chunked_prefill_ws(const ps_paged_problem* problem, void* workspace,
                           int64_t workspace_bytes, void* stream);
 
+/*
+ * Decode context parallelism (DCP).  The `world` ranks of a DCP group (one
+ * GPU each, up to PS_DCP_MAX_WORLD, NVLink peers) hold interleaved slices of
+ * every sequence's KV tokens: position p is stored by rank (p / I) % world
+ * (I = interleave) at local index (p / (world*I)) * I + p % I of that rank's
+ * paged cache, under a block table that is the same on every rank -- vLLM's
+ * placement (vllm/v1/worker/block_table.py:357-376, cp_kv_cache_interleave_size).
+ * Each rank holds hq_local query heads; the group attends with the
+ * world * hq_local heads in rank order.
+ *
+ * Ranks exchange data through a "slab" of device memory each allocates
+ * (ps_dcp_slab_alloc, zeroed) and the others map (ps_dcp_ipc_handle /
+ * ps_dcp_ipc_open, CUDA IPC).  One slab serves every layer and every call.
+ * Replaces: vLLM's query all_gather and context attention with LSE
+ * (flash_attn.py:906-940), cp_lse_ag_out_rs (vllm/v1/attention/ops/common.py:195-225
+ * with correct_attn_out :99-170), the new tokens' attention and
+ * merge_attn_states (flash_attn.py:950-983), and reshape_and_cache_flash of
+ * the new tokens -- without NCCL: peer loads plus two flag barriers per call
+ * whose waits are bounded (1 s; then PS_DEV_WAIT_TIMEOUT, after which the
+ * workspace must be zeroed and the slabs recreated).
+ */
+#define PS_DCP_MAX_WORLD 8
+#define PS_DCP_IPC_HANDLE_BYTES 64
+
+/* Slab bytes for calls of up to max_tokens decode tokens (<= 4096). */
+int64_t ps_dcp_slab_bytes(int32_t max_tokens, int32_t hq_local, int32_t world);
+/* cudaMalloc + zero a slab on the current device (synchronous). */
+int ps_dcp_slab_alloc(int64_t bytes, void** slab);
+int ps_dcp_slab_free(void* slab);
+/* 64-byte CUDA IPC handle of a slab from ps_dcp_slab_alloc, for the peers. */
+int ps_dcp_ipc_handle(const void* slab, void* handle);
+/* Map a peer's slab into this process (another process's handle). */
+int ps_dcp_ipc_open(const void* handle, void** peer_slab);
+int ps_dcp_ipc_close(void* peer_slab);
+
+typedef struct {
+  /* This rank's call, decode only (one query row per sequence):
+     q / out [num_seqs, hq_local, 128] (num_q_heads = hq_local), lse
+     (nullable) [hq_local, num_seqs]; key_cache / value_cache / num_blocks:
+     this rank's cache; block_table: the group's; seq_lens: GLOBAL lengths,
+     the new token included; query_start_loc must be NULL; num_tokens =
+     num_seqs; new_key / new_value [num_seqs, num_kv_heads, 128]: the new
+     tokens' rows (every rank has them); slot_mapping: this rank's slots,
+     < 0 where another rank stores the token. */
+  ps_paged_problem local;
+  int32_t world, rank, interleave; /* interleave divides block_size */
+  int32_t max_tokens;              /* the slabs were sized for it */
+  void* slabs[PS_DCP_MAX_WORLD];   /* every rank's slab, addressed from this GPU */
+} ps_dcp_problem;
+
+/*
+ * One DCP decode step on this rank (every rank of the group makes the same
+ * calls in the same order, each on its own GPU): out[t, h] = attention of
+ * the group's query head rank*hq_local + h over the sequence's whole context
+ * (all ranks' slices plus the new token), the new token appended where
+ * slot_mapping >= 0.  The workspace is a ps_paged_decode workspace for
+ * (num_seqs, world * hq_local, num_kv_heads); its status word receives the
+ * PS_DEV_* bits.  Four launches on `stream`, no host synchronisation, CUDA
+ * graph safe.
+ */
+int ps_dcp_decode(const ps_dcp_problem* problem, void* workspace, int64_t workspace_bytes,
+                  void* stream);
+
+/*
+ * The same step split at its barriers, for one process that drives every
+ * rank of a group on one GPU in turn (a rank's barrier wait must not run
+ * before the other ranks have signalled, since kernels on one GPU are not
+ * guaranteed to run concurrently): phase 0 stages the query rows, 1
+ * signals barrier 0, 2 gathers the queries and attends over the local
+ * context, 3 signals barrier 1, 4 combines and appends.  Run phase k for
+ * every rank before phase k+1 for any.
+ */
+int ps_dcp_decode_phase(const ps_dcp_problem* problem, int32_t phase, void* workspace,
+                        int64_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -382,3 +382,113 @@ def rope(x, positions, cos_sin_rows, rotary_dim, is_neox, dtype):
     else:
         out[..., 0:rotary_dim:2], out[..., 1:rotary_dim:2] = o1, o2
     return out
+
+
+# --------------------------------------------------------------------------
+# decode context parallelism (DCP)
+# --------------------------------------------------------------------------
+def dcp_local_lens(lens, world, rank, interleave=1):
+    """Tokens of each length-``lens`` prefix stored by ``rank``: positions p
+    with ``(p // interleave) % world == rank``.  Restates
+    ``get_dcp_local_seq_lens`` (``vllm/v1/attention/backends/utils.py:857-894``):
+    ``base = L // I // N * I``, ``rem = L - base * N``,
+    ``local = base + clip(rem - rank * I, 0, I)``."""
+    L = np.asarray(lens, dtype=np.int64)
+    base = L // interleave // world * interleave
+    rem = L - base * world
+    return (base + np.clip(rem - rank * interleave, 0, interleave)).astype(np.int32)
+
+
+def dcp_placement(positions, block_table_row, block_size, world, rank, interleave=1):
+    """Local slot of each position on ``rank`` (-1 where another rank stores
+    it), restating ``_compute_slot_mapping_kernel``
+    (``vllm/v1/worker/block_table.py:326-380``): virtual blocks of
+    ``block_size * world`` positions; offset ``o`` of a virtual block is
+    stored by rank ``(o // I) % world`` at ``(o // (world*I)) * I + o % I`` of
+    the block ``block_table_row[pos // (block_size*world)]``."""
+    pos = np.asarray(positions, dtype=np.int64)
+    vbs = block_size * world
+    blk = pos // vbs
+    o = pos - blk * vbs
+    local = (o // interleave) % world == rank
+    off = (o // (world * interleave)) * interleave + o % interleave
+    slots = np.asarray(block_table_row, dtype=np.int64)[blk] * block_size + off
+    return np.where(local, slots, -1)
+
+
+def dcp_decode(q_all, key_caches, value_caches, block_table, seq_lens, new_key, new_value,
+               softmax_scale, interleave=1, partial_dtype="fp32"):
+    """One DCP decode step of the whole group, the way vLLM evaluates it
+    (``FlashAttentionImpl._forward_with_dcp``, ``flash_attn.py:885-983``):
+
+    * rank r attends with every query head over its context slice (the first
+      ``dcp_local_lens(seq_lens - 1, ...)`` local tokens, non-causal), giving
+      ``(o_r, lse_r)``; ``o_r`` is stored in ``partial_dtype`` (vLLM: the model
+      dtype);
+    * ``correct_attn_out`` (``ops/common.py:42-96``): NaN and +inf LSEs count
+      as -inf, ``lse = log(sum_r exp(lse_r - m)) + m`` with a max of -inf
+      counted as 0, ``o_r *= exp(lse_r - lse)`` (NaN/+inf exponents -> 0);
+      the reduce_scatter sums the corrected ``o_r`` over ranks;
+    * the new token attends to itself (``o = v``, ``lse = scale * q.k``) and
+      ``merge_attn_states`` (``triton_merge_attn_states.py:58-140``) merges it.
+
+    q_all [T, Hq, D]; key_caches/value_caches: per rank [NB, bs, Hkv, D];
+    new_key/new_value [T, Hkv, D].  Returns (out [T, Hq, D], lse [Hq, T]) fp32
+    for all heads (rank r keeps heads [r*Hq/N, (r+1)*Hq/N)).
+    """
+    q_all = np.asarray(q_all, dtype=np.float32)
+    T, hq, d = q_all.shape
+    world = len(key_caches)
+    ctx = np.asarray(seq_lens, dtype=np.int64) - 1
+    qsl = np.arange(T + 1)
+    outs, lses = [], []
+    for r in range(world):
+        lens_r = dcp_local_lens(ctx, world, r, interleave)
+        o, l = paged_attention(q_all, key_caches[r], value_caches[r], block_table, lens_r, qsl,
+                               softmax_scale, causal=False)
+        outs.append(round_to(o, partial_dtype))
+        lses.append(l)
+    k = np.asarray(new_key, dtype=np.float32)
+    v = np.asarray(new_value, dtype=np.float32)
+    g = hq // k.shape[1]
+    kk, vv = np.repeat(k, g, axis=1), np.repeat(v, g, axis=1)
+    s_lse = (np.float32(softmax_scale) * np.einsum("thd,thd->ht", q_all, kk)).astype(np.float32)
+    out, lse, _, _ = dcp_combine(np.stack(outs), np.stack(lses), vv, s_lse)
+    return out, lse
+
+
+def dcp_combine(o_r, lse_r, s_out, s_lse, rounding="fp32"):
+    """The cross-rank half of a DCP decode step.
+
+    o_r [N, T, H, D], lse_r [N, H, T]: every rank's partial output and LSE;
+    s_out [T, H, D], s_lse [H, T]: the new tokens' attention over themselves.
+    ``correct_attn_out`` (``ops/common.py:42-96``) then the sum over ranks
+    (``reduce_scatter``, ``common.py:218``) then ``merge_attn_states``
+    (``triton_merge_attn_states.py:58-140``).  ``rounding`` = "bf16"/"fp16"
+    rounds where vLLM stores in the model dtype (each corrected partial, their
+    sum, the merged output); "fp32" rounds nowhere.
+    Returns (out [T, H, D], lse [H, T], o_ctx [T, H, D], lse_ctx [H, T]).
+    """
+    o_r = np.asarray(o_r, dtype=np.float32)
+    lse_r = np.asarray(lse_r, dtype=np.float32)
+    lse_r = np.where(np.isnan(lse_r) | (lse_r == np.inf), -np.inf, lse_r).astype(np.float32)
+    m = lse_r.max(axis=0)
+    m = np.where(m == -np.inf, 0.0, m).astype(np.float32)
+    with np.errstate(divide="ignore", invalid="ignore", over="ignore"):
+        lse_ctx = (np.log(np.exp(lse_r - m).sum(axis=0)) + m).astype(np.float32)
+        f = lse_r - lse_ctx
+    f = np.where(np.isnan(f) | (f == np.inf), -np.inf, f)
+    fac = np.exp(f).astype(np.float32)  # [N, H, T]
+    corrected = round_to(o_r * np.transpose(fac, (0, 2, 1))[..., None], rounding)
+    o_ctx = round_to(corrected.sum(axis=0), rounding)
+    s_out = np.asarray(s_out, dtype=np.float32)
+    s_lse = np.asarray(s_lse, dtype=np.float32)
+    p = np.where(lse_ctx == np.inf, -np.inf, lse_ctx)
+    s = np.where(s_lse == np.inf, -np.inf, s_lse)
+    mx = np.maximum(p, s)
+    with np.errstate(invalid="ignore"):
+        pse, sse = np.exp(p - mx), np.exp(s - mx)
+    tot = pse + sse
+    out = o_ctx * (pse / tot).T[..., None] + s_out * (sse / tot).T[..., None]
+    return (round_to(out, rounding), (np.log(tot) + mx).astype(np.float32), o_ctx,
+            lse_ctx.astype(np.float32))

@@ -560,3 +560,216 @@ int ps_chunked_prefill_ws(const ps_paged_problem* pr, void* workspace, int64_t w
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------ DCP
+// Slab layout: see dcp.cu.  Offsets depend only on (max_tokens, hq_local,
+// world), which every rank of a group passes identically.
+namespace {
+struct DcpLayout {
+  int64_t off_q, off_part, off_lse, off_qall, off_lens, total;
+};
+DcpLayout dcp_layout(int64_t max_tokens, int64_t hq_local, int64_t world) {
+  const int64_t hq_all = hq_local * world;
+  DcpLayout l;
+  l.off_q = 256;
+  l.off_part = round_up(l.off_q + max_tokens * hq_local * 256, 256);
+  l.off_lse = round_up(l.off_part + max_tokens * hq_all * 256, 256);
+  l.off_qall = round_up(l.off_lse + hq_all * max_tokens * 4, 256);
+  l.off_lens = round_up(l.off_qall + max_tokens * hq_all * 256, 256);
+  l.total = round_up(l.off_lens + max_tokens * 4, 256);
+  return l;
+}
+
+// phase -1: the whole step; 0..4: one phase (ps_dcp_decode_phase)
+int dcp_impl(const ps_dcp_problem* dp, int phase, void* workspace, int64_t workspace_bytes,
+             void* stream) {
+  if (!dp) return fail(PS_ERR_INVALID_ARGUMENT, "problem is NULL");
+  if (phase < -1 || phase > 4) return fail(PS_ERR_INVALID_ARGUMENT, "phase %d outside [0, 4]", phase);
+  const ps_paged_problem& lp = dp->local;
+  if (dp->world < 1 || dp->world > PS_DCP_MAX_WORLD || dp->rank < 0 || dp->rank >= dp->world)
+    return fail(PS_ERR_INVALID_ARGUMENT, "world %d / rank %d invalid (world <= %d)", dp->world,
+                dp->rank, PS_DCP_MAX_WORLD);
+  if (dp->interleave < 1 || lp.block_size % dp->interleave != 0)
+    return fail(PS_ERR_INVALID_ARGUMENT, "interleave %d must divide block_size %d", dp->interleave,
+                lp.block_size);
+  if (dp->max_tokens < 1 || dp->max_tokens > ps::kDecodeMaxSeqs)
+    return fail(PS_ERR_INVALID_ARGUMENT, "max_tokens %d outside [1, %d]", dp->max_tokens,
+                ps::kDecodeMaxSeqs);
+  for (int r = 0; r < dp->world; ++r)
+    if (!dp->slabs[r] || !aligned(dp->slabs[r], 256))
+      return fail(PS_ERR_INVALID_ARGUMENT, "slab of rank %d is NULL or not 256-byte aligned", r);
+  if (lp.num_seqs < 0 || lp.num_seqs > dp->max_tokens)
+    return fail(PS_ERR_INVALID_ARGUMENT, "num_seqs %d outside [0, max_tokens %d]", lp.num_seqs,
+                dp->max_tokens);
+  if (lp.query_start_loc != nullptr || lp.num_tokens != lp.num_seqs)
+    return fail(PS_ERR_INVALID_ARGUMENT,
+                "DCP decode takes one query row per sequence (query_start_loc NULL, num_tokens = num_seqs)");
+  const int hq_local = lp.num_q_heads;
+  if (hq_local <= 0) return fail(PS_ERR_INVALID_ARGUMENT, "num_q_heads must be positive");
+  ps_paged_problem g = lp;  // the group's attention problem
+  g.num_q_heads = hq_local * dp->world;
+  int rc = validate_problem(&g, true);
+  if (rc != PS_OK) return rc;
+  if (!lp.new_key || !lp.new_value || !lp.slot_mapping)
+    return fail(PS_ERR_INVALID_ARGUMENT, "DCP decode needs new_key, new_value and slot_mapping");
+  if (!aligned(lp.new_key, 16) || !aligned(lp.new_value, 16) || lp.new_key_stride_token % 8 ||
+      lp.new_key_stride_head % 8 || lp.new_value_stride_token % 8 || lp.new_value_stride_head % 8)
+    return fail(PS_ERR_INVALID_ARGUMENT, "new key/value rows must be 16-byte aligned");
+  if (!workspace || !aligned(workspace, 256))
+    return fail(PS_ERR_WORKSPACE, "DCP decode needs a 256-byte aligned decode workspace");
+  if (lp.num_seqs == 0) return PS_OK;
+  int dev = 0;
+  const int sms = sm_count_current(&dev);
+  if (sms <= 0) return fail(PS_ERR_CUDA, "no CUDA device");
+  const DcpLayout lay = dcp_layout(dp->max_tokens, hq_local, dp->world);
+  char* own = static_cast<char*>(dp->slabs[dp->rank]);
+  const int64_t eb = 2;
+  ps::DcpArgs a;
+  a.world = dp->world;
+  a.rank = dp->rank;
+  a.interleave = dp->interleave;
+  for (int r = 0; r < ps::kDcpMaxWorld; ++r)
+    a.slab[r] = r < dp->world ? static_cast<char*>(dp->slabs[r]) : nullptr;
+  a.off_q = lay.off_q;
+  a.off_part = lay.off_part;
+  a.off_lse = lay.off_lse;
+  a.off_qall = lay.off_qall;
+  a.off_lens = lay.off_lens;
+  a.signal_first = phase == -1 ? 1 : 0;
+  a.q = static_cast<const char*>(lp.q);
+  a.q_st = lp.q_stride_token * eb;
+  a.q_sh = lp.q_stride_head * eb;
+  a.out = static_cast<char*>(lp.out);
+  a.o_st = lp.out_stride_token * eb;
+  a.o_sh = lp.out_stride_head * eb;
+  a.lse = lp.lse;
+  a.lse_sh = lp.lse_stride_head;
+  a.lse_st = lp.lse_stride_token;
+  a.new_key = static_cast<const char*>(lp.new_key);
+  a.nk_st = lp.new_key_stride_token * eb;
+  a.nk_sh = lp.new_key_stride_head * eb;
+  a.new_value = static_cast<const char*>(lp.new_value);
+  a.nv_st = lp.new_value_stride_token * eb;
+  a.nv_sh = lp.new_value_stride_head * eb;
+  a.slot_mapping = lp.slot_mapping;
+  a.key_cache = static_cast<char*>(const_cast<void*>(lp.key_cache));
+  a.value_cache = static_cast<char*>(const_cast<void*>(lp.value_cache));
+  a.c_sblock = lp.cache_stride_block * eb;
+  a.c_sslot = lp.cache_stride_slot * eb;
+  a.c_shead = lp.cache_stride_head * eb;
+  a.num_slots = lp.num_blocks * lp.block_size;
+  a.block_size = lp.block_size;
+  a.seq_lens = lp.seq_lens;
+  a.num_tokens = lp.num_seqs;
+  a.hq_local = hq_local;
+  a.hq_all = g.num_q_heads;
+  a.num_kv_heads = lp.num_kv_heads;
+  a.group = g.num_q_heads / lp.num_kv_heads;
+  a.softmax_scale = lp.softmax_scale;
+  a.bf16 = lp.dtype == PS_DTYPE_BF16 ? 1 : 0;
+  a.status = static_cast<int32_t*>(workspace);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  auto launch = [&](int which) -> int {
+    const int e = ps_launch_dcp(a, which, sms, s);
+    return e != 0 ? cuda_fail(static_cast<cudaError_t>(e), "dcp launch") : PS_OK;
+  };
+  auto attend_local = [&]() -> int {
+    // plain decode of the group's heads over this rank's slice; partial
+    // outputs and LSEs into the slab, no fused append
+    ps_paged_problem d = g;
+    d.q = own + lay.off_qall;
+    d.q_stride_token = static_cast<int64_t>(g.num_q_heads) * 128;
+    d.q_stride_head = 128;
+    d.seq_lens = reinterpret_cast<const int32_t*>(own + lay.off_lens);
+    d.out = own + lay.off_part;
+    d.out_stride_token = static_cast<int64_t>(g.num_q_heads) * 128;
+    d.out_stride_head = 128;
+    d.lse = reinterpret_cast<float*>(own + lay.off_lse);
+    d.lse_stride_head = lp.num_seqs;
+    d.lse_stride_token = 1;
+    d.new_key = nullptr;
+    d.new_value = nullptr;
+    d.slot_mapping = nullptr;
+    return decode_impl(&d, nullptr, 0, workspace, workspace_bytes, stream, false);
+  };
+  switch (phase) {
+    case -1:
+      if ((rc = launch(0)) != PS_OK || (rc = launch(2)) != PS_OK || (rc = attend_local()) != PS_OK)
+        return rc;
+      return launch(4);
+    case 2:
+      if ((rc = launch(2)) != PS_OK) return rc;
+      return attend_local();
+    default:
+      return launch(phase);
+  }
+}
+}  // namespace
+
+extern "C" {
+
+int64_t ps_dcp_slab_bytes(int32_t max_tokens, int32_t hq_local, int32_t world) {
+  if (max_tokens < 1 || max_tokens > ps::kDecodeMaxSeqs || hq_local < 1 || world < 1 ||
+      world > PS_DCP_MAX_WORLD) {
+    fail(PS_ERR_INVALID_ARGUMENT, "slab size: bad shape");
+    return -1;
+  }
+  return dcp_layout(max_tokens, hq_local, world).total;
+}
+
+int ps_dcp_slab_alloc(int64_t bytes, void** slab) {
+  if (!slab || bytes <= 0) return fail(PS_ERR_INVALID_ARGUMENT, "slab alloc: bad arguments");
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, static_cast<size_t>(bytes));
+  if (e != cudaSuccess) return cuda_fail(e, "slab cudaMalloc");
+  e = cudaMemset(p, 0, static_cast<size_t>(bytes));
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return cuda_fail(e, "slab zeroing");
+  }
+  *slab = p;
+  return PS_OK;
+}
+
+int ps_dcp_slab_free(void* slab) {
+  if (!slab) return PS_OK;
+  const cudaError_t e = cudaFree(slab);
+  return e == cudaSuccess ? PS_OK : cuda_fail(e, "slab cudaFree");
+}
+
+int ps_dcp_ipc_handle(const void* slab, void* handle) {
+  if (!slab || !handle) return fail(PS_ERR_INVALID_ARGUMENT, "ipc handle: NULL argument");
+  static_assert(sizeof(cudaIpcMemHandle_t) == PS_DCP_IPC_HANDLE_BYTES, "IPC handle size");
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(slab));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcGetMemHandle");
+  std::memcpy(handle, &h, sizeof(h));
+  return PS_OK;
+}
+
+int ps_dcp_ipc_open(const void* handle, void** peer_slab) {
+  if (!handle || !peer_slab) return fail(PS_ERR_INVALID_ARGUMENT, "ipc open: NULL argument");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  const cudaError_t e = cudaIpcOpenMemHandle(peer_slab, h, cudaIpcMemLazyEnablePeerAccess);
+  return e == cudaSuccess ? PS_OK : cuda_fail(e, "cudaIpcOpenMemHandle");
+}
+
+int ps_dcp_ipc_close(void* peer_slab) {
+  if (!peer_slab) return PS_OK;
+  const cudaError_t e = cudaIpcCloseMemHandle(peer_slab);
+  return e == cudaSuccess ? PS_OK : cuda_fail(e, "cudaIpcCloseMemHandle");
+}
+
+int ps_dcp_decode(const ps_dcp_problem* problem, void* workspace, int64_t workspace_bytes,
+                  void* stream) {
+  return dcp_impl(problem, -1, workspace, workspace_bytes, stream);
+}
+
+int ps_dcp_decode_phase(const ps_dcp_problem* problem, int32_t phase, void* workspace,
+                        int64_t workspace_bytes, void* stream) {
+  return dcp_impl(problem, phase, workspace, workspace_bytes, stream);
+}
+
+}  // extern "C"

@@ -169,7 +169,43 @@ struct RopeArgs {
   int32_t bf16;
   int32_t* status;
 };
+
+// Decode context parallelism: one rank's view of its group and of one call.
+// Byte strides unless noted.
+constexpr int kDcpMaxWorld = 8;
+struct DcpArgs {
+  int32_t world, rank, interleave;
+  char* slab[kDcpMaxWorld];  // every rank's slab as addressed from this GPU
+  int64_t off_q, off_part, off_lse, off_qall, off_lens;
+  int32_t signal_first;      // gather/combine publish their phase at their start
+  // this rank's query rows [T, hq_local, 128] and output
+  const char* q;
+  int64_t q_st, q_sh;
+  char* out;
+  int64_t o_st, o_sh;
+  float* lse;                // nullable, element strides
+  int64_t lse_sh, lse_st;
+  // the new tokens' key/value rows [T, num_kv_heads, 128]
+  const char* new_key;
+  int64_t nk_st, nk_sh;
+  const char* new_value;
+  int64_t nv_st, nv_sh;
+  const int64_t* slot_mapping;  // local slots, < 0: stored by another rank
+  char* key_cache;
+  char* value_cache;
+  int64_t c_sblock, c_sslot, c_shead;
+  int64_t num_slots;
+  int32_t block_size;
+  const int32_t* seq_lens;   // global lengths, the new token included
+  int32_t num_tokens;        // = sequences (one query row each)
+  int32_t hq_local, hq_all, num_kv_heads, group;
+  float softmax_scale;
+  int32_t bf16;
+  int32_t* status;
+};
 }  // namespace ps
+int ps_launch_dcp(const ps::DcpArgs& a, int which, int sm_count, cudaStream_t stream);
+
 // vec: the 16-byte path (rows, strides and cos/sin rows 16-byte aligned,
 // head_size % 8 == 0, rotary_dim % 16 == 0)
 int ps_launch_rope_kv_append(const ps::RopeArgs& a, int sm_count, int vec, cudaStream_t stream);

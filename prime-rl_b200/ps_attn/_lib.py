@@ -45,7 +45,18 @@ EXPORTED_SYMBOLS = (
     "ps_paged_decode_cascade",
     "ps_rope_kv_append",
     "ps_chunked_prefill_ws",
+    "ps_dcp_slab_bytes",
+    "ps_dcp_slab_alloc",
+    "ps_dcp_slab_free",
+    "ps_dcp_ipc_handle",
+    "ps_dcp_ipc_open",
+    "ps_dcp_ipc_close",
+    "ps_dcp_decode",
+    "ps_dcp_decode_phase",
 )
+
+PS_DCP_MAX_WORLD = 8
+PS_DCP_IPC_HANDLE_BYTES = 64
 
 
 class PSError(RuntimeError):
@@ -136,6 +147,19 @@ class RopeAppendProblem(ctypes.Structure):
     ]
 
 
+class DcpProblem(ctypes.Structure):
+    """Mirror of ``ps_dcp_problem`` in include/ps_attn.h (same field order)."""
+
+    _fields_ = [
+        ("local", PagedProblem),
+        ("world", ctypes.c_int32),
+        ("rank", ctypes.c_int32),
+        ("interleave", ctypes.c_int32),
+        ("max_tokens", ctypes.c_int32),
+        ("slabs", ctypes.c_void_p * PS_DCP_MAX_WORLD),
+    ]
+
+
 def lib_path() -> Path:
     """The in-tree library, or a tuning variant named by ``PS_ATTN_LIB``."""
     override = os.environ.get("PS_ATTN_LIB")
@@ -180,6 +204,23 @@ def _declare(lib):
     lib.ps_paged_decode_cascade.restype = c.c_int
     lib.ps_paged_decode_cascade.argtypes = [c.POINTER(PagedProblem), c.c_void_p, c.c_int64,
                                             c.c_void_p, c.c_int64, c.c_void_p]
+    lib.ps_dcp_slab_bytes.restype = c.c_int64
+    lib.ps_dcp_slab_bytes.argtypes = [c.c_int32] * 3
+    lib.ps_dcp_slab_alloc.restype = c.c_int
+    lib.ps_dcp_slab_alloc.argtypes = [c.c_int64, c.POINTER(c.c_void_p)]
+    lib.ps_dcp_slab_free.restype = c.c_int
+    lib.ps_dcp_slab_free.argtypes = [c.c_void_p]
+    lib.ps_dcp_ipc_handle.restype = c.c_int
+    lib.ps_dcp_ipc_handle.argtypes = [c.c_void_p, c.c_void_p]
+    lib.ps_dcp_ipc_open.restype = c.c_int
+    lib.ps_dcp_ipc_open.argtypes = [c.c_void_p, c.POINTER(c.c_void_p)]
+    lib.ps_dcp_ipc_close.restype = c.c_int
+    lib.ps_dcp_ipc_close.argtypes = [c.c_void_p]
+    lib.ps_dcp_decode.restype = c.c_int
+    lib.ps_dcp_decode.argtypes = [c.POINTER(DcpProblem), c.c_void_p, c.c_int64, c.c_void_p]
+    lib.ps_dcp_decode_phase.restype = c.c_int
+    lib.ps_dcp_decode_phase.argtypes = [c.POINTER(DcpProblem), c.c_int32, c.c_void_p, c.c_int64,
+                                        c.c_void_p]
 
 
 def load(build_if_stale: bool = True):

@@ -23,6 +23,17 @@ Run in a container where vLLM 0.22 is installed (not needed at test time):
   (``rope_*.npz``); only the cos/sin rows at the tested positions are stored.
   ``python tests/golden/make_golden.py --only rope`` regenerates just these.
 
+* Decode context parallelism (``dcp_*.npz``): vLLM's Triton slot-mapping
+  kernel ``_compute_slot_mapping_kernel`` (``vllm/v1/worker/block_table.py:326-380``)
+  for several (world, interleave, rank), and the LSE correction + merge of
+  the DCP decode: ``correct_attn_out`` (``vllm/v1/attention/ops/common.py:99-170``,
+  Triton kernel ``_correct_attn_cp_out_kernel``) on every rank's partial,
+  the sum over ranks (what ``reduce_scatter`` computes), then the Triton
+  ``merge_attn_states`` (``triton_merge_attn_states.py:14-140``) with the new
+  tokens' own attention -- all under the interpreter, on inputs that include
+  empty slices (LSE -inf), FA2's +inf and NaN LSEs.
+  ``python tests/golden/make_golden.py --only dcp`` regenerates just these.
+
 Inputs are regenerated at test time from the seeds recorded here by
 ``ps_attn.workloads.make_batch`` (CPU generator); a checksum of the inputs is
 stored so a generator change is detected instead of silently comparing
@@ -189,10 +200,93 @@ def main_rope(meta):
         print(f"rope_{name}: written")
 
 
+DCP_SLOT_CASES = {
+    # name: (world, interleave, seed)
+    "w2_i1": (2, 1, 41),
+    "w4_i1": (4, 1, 42),
+    "w2_i4": (2, 4, 43),
+    "w8_i16": (8, 16, 44),
+    "w3_i2": (3, 2, 45),
+}
+DCP_COMBINE_CASES = {
+    # name: (world, dtype of the partial outputs, seed).  fp32 only: the
+    # Triton interpreter converts fp32 to bf16 by truncation where the GPU
+    # rounds to nearest even, so bf16 stores would pin the interpreter.
+    "w2_fp32": (2, torch.float32, 51),
+    "w4_fp32": (4, torch.float32, 52),
+}
+
+
+def dcp_slot_golden(world, interleave, seed):
+    """vLLM's slot mapping for every rank of a DCP group."""
+    from vllm.v1.worker import block_table as btm
+
+    g = torch.Generator().manual_seed(seed)
+    B, P, bs = 3, 12, 16
+    bt = torch.randperm(B * P + 7, generator=g)[:B * P].to(torch.int32).view(B, P)
+    cap = P * bs * world  # positions a row of P virtual blocks covers
+    counts = [5, 9, 14]
+    qsl = torch.tensor([0] + list(np.cumsum(counts)), dtype=torch.int32)
+    pos = torch.cat([torch.randint(0, cap, (c,), generator=g) for c in counts]).to(torch.int64)
+    T = int(qsl[-1])
+    slots = []
+    for r in range(world):
+        out = torch.full((T + 4,), -7, dtype=torch.int64)
+        btm._compute_slot_mapping_kernel[(B + 1,)](
+            T, T + 4, qsl, pos, bt, bt.stride(0), bs, out, TOTAL_CP_WORLD_SIZE=world,
+            TOTAL_CP_RANK=r, CP_KV_CACHE_INTERLEAVE_SIZE=interleave, PAD_ID=-1, BLOCK_SIZE=1024)
+        slots.append(out[:T].numpy())
+    return dict(block_table=bt.numpy(), query_start_loc=qsl.numpy(), positions=pos.numpy(),
+                slots=np.stack(slots), shape=np.array([world, interleave, bs]))
+
+
+def dcp_combine_golden(world, dtype, seed):
+    """correct_attn_out on every rank, the sum over ranks, merge_attn_states."""
+    from vllm.v1.attention.ops import common as cm
+    from vllm.v1.attention.ops import triton_merge_attn_states as tm
+
+    g = torch.Generator().manual_seed(seed)
+    T, H, D = 6, 4, 128
+    o_r = torch.randn(world, T, H, D, generator=g).to(dtype)
+    lse_r = (torch.randn(world, T, H, generator=g) * 3.0).float()  # [N, B, H] as cp_lse_* takes
+    lse_r[1, 0, :] = -float("inf")   # rank 1 holds none of token 0's context
+    o_r[1, 0] = 0
+    lse_r[:, 1, :] = -float("inf")   # token 1: empty context on every rank
+    o_r[:, 1] = 0
+    lse_r[0, 2, 1] = float("inf")    # FA2's empty-sum convention
+    lse_r[world - 1, 3, 2] = float("nan")
+    s_out = torch.randn(T, H, D, generator=g).to(dtype)
+    s_lse = (torch.randn(H, T, generator=g) * 3.0).float()
+    corrected, lse_ctx = [], None
+    for r in range(world):
+        o, lse_ctx = cm.correct_attn_out(o_r[r].clone(), lse_r, r, None)
+        corrected.append(o.float())
+    o_ctx = torch.stack(corrected).sum(0).to(dtype)  # reduce_scatter sums in the model dtype
+    out = torch.empty(T, H, D, dtype=dtype)
+    out_lse = torch.empty(H, T, dtype=torch.float32)
+    tm.merge_attn_states(out, o_ctx, lse_ctx.transpose(0, 1).contiguous(), s_out, s_lse, out_lse)
+    f32 = lambda t: t.float().numpy()  # noqa: E731
+    return dict(o_r=f32(o_r), lse_r=lse_r.numpy(), s_out=f32(s_out), s_lse=s_lse.numpy(),
+                lse_ctx=lse_ctx.numpy(), o_ctx=f32(o_ctx), out=f32(out), out_lse=out_lse.numpy())
+
+
+def main_dcp(meta):
+    meta["dcp"] = {"slots": {}, "combine": {}}
+    for name, (world, il, seed) in DCP_SLOT_CASES.items():
+        np.savez_compressed(HERE / f"dcp_slots_{name}.npz", **dcp_slot_golden(world, il, seed))
+        meta["dcp"]["slots"][name] = {"world": world, "interleave": il, "seed": seed}
+        print(f"dcp_slots_{name}: written")
+    for name, (world, dtype, seed) in DCP_COMBINE_CASES.items():
+        np.savez_compressed(HERE / f"dcp_combine_{name}.npz", **dcp_combine_golden(world, dtype, seed))
+        meta["dcp"]["combine"][name] = {"world": world, "dtype": str(dtype), "seed": seed}
+        print(f"dcp_combine_{name}: written")
+
+
 def main():
-    if "--only" in sys.argv and sys.argv[sys.argv.index("--only") + 1] == "rope":
+    only = sys.argv[sys.argv.index("--only") + 1] if "--only" in sys.argv else None
+    if only in ("rope", "dcp"):
         meta = json.loads((HERE / "golden_meta.json").read_text())
-        main_rope(meta)
+        (main_rope if only == "rope" else main_dcp)(meta)
         (HERE / "golden_meta.json").write_text(json.dumps(meta, indent=1, default=str) + "\n")
         return
     attention_ref = load_attention_ref()
@@ -210,6 +304,7 @@ def main():
         meta["append"][name] = {"dtype": str(dtype), "seed": seed}
         print(f"append_{name}: written")
     main_rope(meta)
+    main_dcp(meta)
     (HERE / "golden_meta.json").write_text(json.dumps(meta, indent=1, default=str) + "\n")
 
 

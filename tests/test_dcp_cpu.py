@@ -1,0 +1,178 @@
+"""CPU: decode context parallelism -- the placement and the combine pinned to
+vLLM's own code (golden vectors from its Triton kernels), the oracle's DCP
+step equal to unsharded attention, the two-rank data flow over gloo, and the
+C-ABI's host-side validation."""
+from __future__ import annotations
+
+import ctypes
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from dcp_helpers import make_dcp_case
+from helpers import GOLDEN, golden_meta
+from oracle import ps_oracle
+from ps_attn import _lib, dcp
+
+SLOT_CASES = sorted(golden_meta()["dcp"]["slots"])
+COMBINE_CASES = sorted(golden_meta()["dcp"]["combine"])
+
+
+@pytest.mark.parametrize("world,interleave", [(1, 1), (2, 1), (3, 1), (4, 2), (8, 16), (2, 16)])
+def test_local_lens_match_vllm(world, interleave):
+    from vllm.v1.attention.backends.utils import get_dcp_local_seq_lens
+
+    L = torch.arange(1, 400, dtype=torch.int32)  # global lengths, the new token included
+    for r in range(world):
+        ref = get_dcp_local_seq_lens(L - 1, world, r, interleave)
+        assert torch.equal(dcp.local_context_lens(L, world, r, interleave), ref)
+        assert np.array_equal(ps_oracle.dcp_local_lens(L.numpy() - 1, world, r, interleave), ref.numpy())
+
+
+@pytest.mark.parametrize("name", SLOT_CASES)
+def test_placement_matches_vllm_slot_mapping(name):
+    d = dict(np.load(GOLDEN / f"dcp_slots_{name}.npz"))
+    world, interleave, bs = (int(x) for x in d["shape"])
+    qsl, pos, bt = d["query_start_loc"], d["positions"], d["block_table"]
+    rows = np.repeat(np.arange(len(qsl) - 1), np.diff(qsl))
+    for r in range(world):
+        want = d["slots"][r]
+        got_o = np.concatenate([ps_oracle.dcp_placement(pos[qsl[b]:qsl[b + 1]], bt[b], bs, world, r, interleave)
+                                for b in range(len(qsl) - 1)])
+        got_p = dcp.local_slots(torch.from_numpy(pos), torch.from_numpy(bt[rows]), bs, world, r, interleave)
+        assert np.array_equal(got_o, want) and np.array_equal(got_p.numpy(), want)
+    # every position is stored by exactly one rank
+    assert ((d["slots"] >= 0).sum(axis=0) == 1).all()
+
+
+@pytest.mark.parametrize("name", COMBINE_CASES)
+def test_combine_matches_vllm_correct_and_merge(name):
+    """vLLM: correct_attn_out per rank, sum over ranks, merge_attn_states."""
+    d = dict(np.load(GOLDEN / f"dcp_combine_{name}.npz"))
+    out, lse, o_ctx, lse_ctx = ps_oracle.dcp_combine(d["o_r"], np.transpose(d["lse_r"], (0, 2, 1)),
+                                                     d["s_out"], d["s_lse"])
+    assert np.array_equal(np.isinf(lse_ctx), np.isinf(d["lse_ctx"].T))
+    fin = np.isfinite(lse_ctx)
+    np.testing.assert_allclose(lse_ctx[fin], d["lse_ctx"].T[fin], rtol=1e-6, atol=1e-6)
+    np.testing.assert_allclose(lse, d["out_lse"], rtol=1e-6, atol=1e-6)
+    np.testing.assert_allclose(o_ctx, d["o_ctx"], rtol=1e-6, atol=1e-6)
+    np.testing.assert_allclose(out, d["out"], rtol=1e-6, atol=1e-6)
+
+
+@pytest.mark.parametrize("world,interleave", [(1, 1), (2, 1), (3, 1), (4, 2), (2, 16)])
+def test_oracle_dcp_step_equals_unsharded_attention(world, interleave):
+    # lengths 1 (no context) and short ones leave some ranks without tokens
+    lens = [1, 2, 3, 17, 40, 129, 300]
+    case = make_dcp_case(lens, world, interleave, hq=8 * world, hkv=4, dtype=torch.float32, seed=5)
+    want, want_lse = case.expected()
+    out, lse = ps_oracle.dcp_decode(case.q_all.numpy(), [c.numpy() for c in case.key_caches],
+                                    [c.numpy() for c in case.value_caches], case.block_table.numpy(),
+                                    case.seq_lens.numpy(), case.new_key.numpy(), case.new_value.numpy(),
+                                    case.softmax_scale, interleave)
+    np.testing.assert_allclose(out, want, atol=2e-5)
+    np.testing.assert_allclose(lse, want_lse, atol=2e-5)
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _gloo_worker(rank, world, port, result_q):
+    import sys
+    from pathlib import Path
+
+    repo = Path(__file__).resolve().parent.parent
+    for p in (repo / "prime-rl_b200", repo, repo / "tests"):
+        sys.path.insert(0, str(p))
+    from dcp_helpers import make_dcp_case
+    from oracle import ps_oracle
+    from ps_attn import dcp
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        # the slab-handle exchange the GPU group makes once
+        handles = dcp.exchange_handles(bytes([rank]) * 64)
+        assert handles == [bytes([r]) * 64 for r in range(world)]
+        case = make_dcp_case([1, 5, 33, 200], world, 1, hq=8, hkv=2, dtype=torch.float32, seed=9)
+        # this rank: attention of the group's heads over its slice
+        lens = ps_oracle.dcp_local_lens(case.seq_lens.numpy() - 1, world, rank)
+        B = len(lens)
+        o, l = ps_oracle.paged_attention(case.q_all.numpy(), case.key_caches[rank].numpy(),
+                                         case.value_caches[rank].numpy(), case.block_table.numpy(),
+                                         lens, np.arange(B + 1), case.softmax_scale, causal=False)
+        # the exchange: every rank's partial output and LSE
+        o_all = [torch.empty(o.shape) for _ in range(world)]
+        l_all = [torch.empty(l.shape) for _ in range(world)]
+        dist.all_gather(o_all, torch.from_numpy(o))
+        dist.all_gather(l_all, torch.from_numpy(l))
+        h0, h1 = rank * case.hq_local, (rank + 1) * case.hq_local
+        g = case.hq // case.hkv
+        kk = np.repeat(case.new_key.numpy(), g, axis=1)[:, h0:h1]
+        vv = np.repeat(case.new_value.numpy(), g, axis=1)[:, h0:h1]
+        s = case.softmax_scale * np.einsum("thd,thd->ht", case.q_all.numpy()[:, h0:h1], kk)
+        out, lse, _, _ = ps_oracle.dcp_combine(np.stack([x.numpy()[:, h0:h1] for x in o_all]),
+                                               np.stack([x.numpy()[h0:h1] for x in l_all]), vv, s)
+        want, want_lse = case.expected()
+        np.testing.assert_allclose(out, want[:, h0:h1], atol=2e-5)
+        np.testing.assert_allclose(lse, want_lse[h0:h1], atol=2e-5)
+        result_q.put((rank, "ok"))
+    except Exception as e:  # surface the failure to the parent at once
+        result_q.put((rank, repr(e)))
+        raise
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_dcp_dataflow_over_gloo():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_gloo_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=240) for _ in range(world))
+    for p in procs:
+        p.join(timeout=120)
+    assert results == {0: "ok", 1: "ok"}
+    assert all(p.exitcode == 0 for p in procs)
+
+
+def test_dcp_abi_validates_on_the_host():
+    lib = _lib.load()
+    assert [f for f, _ in _lib.DcpProblem._fields_] == ["local", "world", "rank", "interleave",
+                                                         "max_tokens", "slabs"]
+    assert ctypes.sizeof(_lib.DcpProblem) == ctypes.sizeof(_lib.PagedProblem) + 16 + 8 * 8
+    # slab layout: header, staged q, partials, LSEs, gathered q, local lengths
+    T, hl, w = 64, 8, 2
+    want = 256 + T * hl * 256 + T * hl * w * 256 + hl * w * T * 4 + T * hl * w * 256 + 256
+    assert lib.ps_dcp_slab_bytes(T, hl, w) == want
+    assert lib.ps_dcp_slab_bytes(0, hl, w) == -1 and lib.ps_dcp_slab_bytes(T, hl, 9) == -1
+    assert lib.ps_dcp_decode(None, None, 0, None) == _lib.PS_ERR_INVALID_ARGUMENT
+    dp = _lib.DcpProblem()
+    dp.world, dp.rank, dp.interleave, dp.max_tokens = 9, 0, 1, 64
+    assert lib.ps_dcp_decode(ctypes.byref(dp), None, 0, None) == _lib.PS_ERR_INVALID_ARGUMENT
+    dp.world, dp.rank = 2, 2
+    assert lib.ps_dcp_decode(ctypes.byref(dp), None, 0, None) == _lib.PS_ERR_INVALID_ARGUMENT
+    dp.rank, dp.local.block_size, dp.interleave = 1, 16, 3
+    assert lib.ps_dcp_decode(ctypes.byref(dp), None, 0, None) == _lib.PS_ERR_INVALID_ARGUMENT
+    assert b"interleave" in lib.ps_last_error()
+    dp.interleave = 4
+    assert lib.ps_dcp_decode(ctypes.byref(dp), None, 0, None) == _lib.PS_ERR_INVALID_ARGUMENT
+    assert b"slab" in lib.ps_last_error()  # NULL slabs
+    dp.slabs[0], dp.slabs[1] = 256, 512
+    dp.local.num_seqs, dp.local.num_tokens = 4, 4
+    dp.local.query_start_loc = 16
+    assert lib.ps_dcp_decode(ctypes.byref(dp), None, 0, None) == _lib.PS_ERR_INVALID_ARGUMENT
+    assert b"one query row" in lib.ps_last_error()
+    assert lib.ps_dcp_decode_phase(ctypes.byref(dp), 5, None, 0, None) == _lib.PS_ERR_INVALID_ARGUMENT
