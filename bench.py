@@ -400,6 +400,167 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_dcp(args):
+    """Config 5 under decode context parallelism: every GPU holds all KV heads
+    of a 1/N slice of every sequence; one ps_dcp_decode per step per rank
+    (query gather, local decode, cross-rank combine + new-token merge +
+    append, exchanged over NVLink peer memory, no NCCL)."""
+    from ps_attn import _lib, dcp, workloads
+
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    import datetime
+
+    import torch.distributed as dist
+
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    _lib.load(build_if_stale=False)
+    cfg = args.config
+    batch = workloads.make_dcp_config(cfg, world, rank, args.interleave, device=dev)
+    B, hl = batch.q.shape[0], batch.q.shape[1]
+    hkv = batch.kv_cache.shape[3]
+    kc, vc = batch.kv_cache[0], batch.kv_cache[1]
+    if world > 1:
+        comm = dcp.DcpComm.from_process_group(B, hl, args.interleave, device=dev)
+    else:
+        comm = dcp.DcpComm.emulated(1, B, hl, args.interleave, dev)[0]
+    ws = comm.workspace(B, hkv)
+    out = torch.empty_like(batch.q)
+    lse = torch.empty(hl, B, dtype=torch.float32, device=dev)
+    kw = dict(q=batch.q, key_cache=kc, value_cache=vc, block_table=batch.block_table,
+              seq_lens=batch.seq_lens, softmax_scale=batch.softmax_scale, out=out,
+              new_key=batch.key, new_value=batch.value, slot_mapping=batch.slot_mapping,
+              workspace=ws, lse=lse)
+    stream = torch.cuda.Stream(dev)
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            dcp.dcp_decode(comm, **kw)
+        stream.synchronize()
+        graph = None
+        if not args.no_graph:
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                dcp.dcp_decode(comm, **kw)
+
+    def step():
+        if graph is not None:
+            graph.replay()
+        else:
+            dcp.dcp_decode(comm, **kw)
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step()
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.25)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        t0.record(stream)
+        for _ in range(args.steps):
+            step()
+        t1.record(stream)
+    torch.cuda.synchronize(dev)
+    elapsed_ms = t0.elapsed_time(t1)
+    extra_t = time.perf_counter()
+    with torch.cuda.stream(stream):
+        while time.perf_counter() - extra_t < max(0.0, 1.5 - elapsed_ms / 1e3):
+            for _ in range(20):
+                step()
+            stream.synchronize()
+    clocks = sampler.stop()
+    if world > 1:
+        t = torch.tensor([elapsed_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms = float(t.item())
+    assert ws.status() == 0, f"device status {ws.status():#x}"
+
+    # end to end: this step's new-token rows (q, k, v) and slots from pinned
+    # host memory in, the output back to the host, every step
+    hq_in = batch.q.cpu().pin_memory()
+    hk_in, hv_in = batch.key.cpu().pin_memory(), batch.value.cpu().pin_memory()
+    hs_in = batch.slot_mapping.cpu().pin_memory()
+    h_out = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    dq, dk, dv, ds = (torch.empty_like(batch.q), torch.empty_like(batch.key),
+                      torch.empty_like(batch.value), torch.empty_like(batch.slot_mapping))
+    ekw = dict(kw, q=dq, new_key=dk, new_value=dv, slot_mapping=ds)
+    with torch.cuda.stream(stream):
+        def one():
+            dq.copy_(hq_in, non_blocking=True)
+            dk.copy_(hk_in, non_blocking=True)
+            dv.copy_(hv_in, non_blocking=True)
+            ds.copy_(hs_in, non_blocking=True)
+            dcp.dcp_decode(comm, **ekw)
+            h_out.copy_(out, non_blocking=True)
+
+        for _ in range(3):
+            one()
+        stream.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            one()
+        e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    h2d = sum(x.numel() * x.element_size() for x in (hq_in, hk_in, hv_in, hs_in))
+    d2h = h_out.numel() * h_out.element_size()
+
+    ms = elapsed_ms / args.steps
+    es = batch.kv_cache.element_size()
+    hq_all = hl * world
+    # per rank: its context slice of K and V, the group's query rows gathered
+    # and their partial outputs written, the peers' partials read for its heads
+    kv_bytes = batch.unique_tokens * hkv * 128 * 2 * es
+    ex_bytes = B * hq_all * 128 * es * 3 + B * hl * 128 * es * (world + 2)
+    step_bytes = kv_bytes + ex_bytes + batch.block_table.numel() * 4 + B * 4 * 2
+    achieved = step_bytes / (ms / 1e3) / 1e9
+    peak, peak_kind = measured_peaks()
+    res = {
+        "metric": METRIC, "value": round(B / (ms / 1e3), 1), "unit": "tokens/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": CONFIG_NAMES[cfg] + " -- decode context parallel", "num_seqs": B,
+                   "num_q_heads": hq_all, "num_kv_heads": hkv, "head_size": 128, "block_size": 16,
+                   "kv_tokens": batch.logical_tokens, "kv_tokens_this_rank": batch.unique_tokens,
+                   "parallelism": f"dcp{world} (interleave {args.interleave}), peer-memory exchange",
+                   "l2": "inputs larger than L2 (KV pool > 126 MB); no flush",
+                   "cuda_graph": graph is not None},
+        "gpu_launches": 4 * args.steps,
+        "roofline": {"kernel": "dcp step (gather + paged_decode + combine)", "bound": "hbm",
+                     "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind,
+                     "unit": "GB/s", "frac": round(achieved / peak, 4),
+                     "frac_of_8tbs": round(achieved / NOMINAL_HBM_GBS, 4),
+                     "bytes_per_launch": step_bytes, "ms_per_launch": round(ms, 5), "traffic": None},
+        "e2e": {"value": round(B / (e2e_ms / args.steps / 1e3), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "clocks": clocks,
+    }
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+    graph = None
+    if world > 1:
+        dist.barrier()
+    comm.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def run_e2e(batch, ws, dev, steps, world, nd=None, replicas=1, fused=True, cascade=False):
     """Same step through the public ops with per-step host->device inputs
     (pinned) and the device->host read of the attention output.  ``nd``:
@@ -581,12 +742,20 @@ def main():
                     help="separate append launch instead of the append fused into decode")
     ap.add_argument("--cascade", action="store_true",
                     help="config 3: shared-prefix (cascade) decode with a per-step plan")
+    ap.add_argument("--dcp", action="store_true",
+                    help="config 5 under decode context parallelism (tokens sharded, not heads)")
+    ap.add_argument("--interleave", type=int, default=1,
+                    help="DCP: consecutive positions per rank (vLLM cp_kv_cache_interleave_size)")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--quick", action="store_true",
                     help="timed steps only: no end-to-end, CPU baseline or clock sampling")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.dcp:
+        if args.config not in (2, 3, 5):
+            ap.error("--dcp takes a decode config (2, 3 or 5)")
+        run_dcp(args)
     else:
         run_ours(args)
 

@@ -190,3 +190,54 @@ def hbm_bytes(batch: PagedBatch, head_size=128, with_append=True, unique=True) -
     app = (T * hkv * head_size * 2 * es * 2) if with_append else 0
     meta = batch.block_table.numel() * 4 + batch.seq_lens.numel() * 4 + batch.slot_mapping.numel() * 8
     return int(kv + qo + app + meta)
+
+
+def make_dcp_config(cfg: int, world: int, rank: int, interleave: int = 1, device="cpu",
+                    seed: int = 0, block_size: int = BLOCK) -> PagedBatch:
+    """Rank ``rank``'s share of config ``cfg`` under decode context
+    parallelism over ``world`` GPUs: every sequence's tokens interleaved over
+    the ranks (vLLM's placement), all KV heads on every rank, the query heads
+    split in rank order.  The block table (virtual blocks of ``block_size *
+    world`` positions) and the new tokens' key/value rows are the same on
+    every rank; ``slot_mapping`` is this rank's (-1 where another rank stores
+    the token); ``seq_lens`` are the global lengths.  Cache contents are
+    synthetic N(0, 1) values."""
+    from . import dcp
+
+    q_lens, seq_lens, kw = config_lengths(cfg, seed)
+    if any(q != 1 for q in q_lens):
+        raise ValueError("decode context parallelism takes decode batches")
+    hq, hkv = kw["num_q_heads"], kw["num_kv_heads"]
+    if hq % world:
+        raise ValueError(f"{hq} query heads do not divide over {world} ranks")
+    dtype = kw.get("dtype", torch.bfloat16)
+    B = len(seq_lens)
+    g = torch.Generator().manual_seed(seed)
+    vbs = block_size * world
+    pages = [(L + vbs - 1) // vbs for L in seq_lens]
+    nb = sum(pages) + 16
+    perm = torch.randperm(nb, generator=g).to(torch.int32)
+    bt = torch.zeros(B, max(pages), dtype=torch.int32)
+    cur = 0
+    for b in range(B):
+        bt[b, :pages[b]] = perm[cur:cur + pages[b]]
+        cur += pages[b]
+    lens = torch.tensor(seq_lens, dtype=torch.int32)
+    slots = dcp.local_slots(lens.to(torch.int64) - 1, bt, block_size, world, rank, interleave)
+    dev = torch.device(device)
+    gq = torch.Generator(device=dev).manual_seed(seed + 1)
+    q_all = torch.randn(B, hq, 128, generator=gq, dtype=dtype, device=dev)
+    key = torch.randn(B, hkv, 128, generator=gq, dtype=dtype, device=dev)
+    value = torch.randn(B, hkv, 128, generator=gq, dtype=dtype, device=dev)
+    gc = torch.Generator(device=dev).manual_seed(seed + 7 + 1000 * rank)
+    kv_cache = torch.randn(2, nb, block_size, hkv, 128, generator=gc, dtype=dtype, device=dev)
+    hl = hq // world
+    local_tokens = int(dcp.local_context_lens(lens, world, rank, interleave).sum())
+    return PagedBatch(
+        q=q_all[:, rank * hl:(rank + 1) * hl].contiguous(), key=key, value=value, kv_cache=kv_cache,
+        block_table=bt.to(dev), seq_lens=lens.to(dev),
+        query_start_loc=torch.arange(B + 1, dtype=torch.int32, device=dev), slot_mapping=slots.to(dev),
+        max_query_len=1, max_seq_len=max(seq_lens), softmax_scale=1.0 / math.sqrt(128),
+        unique_tokens=local_tokens, logical_tokens=sum(seq_lens),
+        meta={"num_q_heads_total": hq, "num_kv_heads_total": hkv, "dcp_world": world,
+              "dcp_rank": rank, "interleave": interleave})
