@@ -27,7 +27,7 @@
 extern "C" {
 #endif
 
-#define PS_ATTN_ABI_VERSION 1
+#define PS_ATTN_ABI_VERSION 2
 
 /* host-side return codes */
 typedef enum {
@@ -46,6 +46,10 @@ typedef enum {
 
 /* element types */
 typedef enum { PS_DTYPE_FP16 = 0, PS_DTYPE_BF16 = 1, PS_DTYPE_FP32 = 2 } ps_dtype;
+
+/* KV-cache element type (ps_paged_problem.kv_cache_dtype). */
+#define PS_KV_AUTO 0      /* the problem's dtype */
+#define PS_KV_FP8_E4M3 1  /* e4m3fn codes (uint8), per-tensor scales k_scale / v_scale */
 
 int ps_abi_version(void);
 const char* ps_last_error(void);
@@ -125,7 +129,35 @@ typedef struct {
   const void* new_value;
   int64_t new_value_stride_token, new_value_stride_head;
   const int64_t* slot_mapping;
+  /* KV-cache element type, PS_KV_AUTO (0) or PS_KV_FP8_E4M3.  An fp8 cache
+     holds e4m3(x / scale) codes (ps_kv_append_fp8, or the fused append) and
+     is read as code * scale with the per-tensor scales below (device fp32
+     scalars, NULL = 1.0) -- vLLM's kv_cache_dtype "fp8" with layer._k_scale
+     / _v_scale.  Cache strides are then in bytes.  Taken by ps_paged_decode
+     only; the other attention entry points return PS_ERR_UNSUPPORTED. */
+  int32_t kv_cache_dtype;
+  const float* k_scale;
+  const float* v_scale;
 } ps_paged_problem;
+
+/*
+ * KV append into an fp8 (e4m3) cache: cache[slot] = e4m3(x / k_scale) for
+ * the key, e4m3(x / v_scale) for the value (the quotient rounded to fp32,
+ * then to the nearest e4m3, ties to even, saturating at +-448), slot < 0
+ * skipped -- reshape_and_cache_flash with kv_cache_dtype "fp8"
+ * (triton_reshape_and_cache_flash.py:93-110).  key/value: fp16 or bf16
+ * (dtype), rows 16-byte aligned; caches: uint8 [num_blocks, block_size,
+ * num_kv_heads, head_size] with byte strides that are multiples of 8;
+ * head_size a multiple of 8; k_scale / v_scale: device fp32 scalars (NULL =
+ * 1.0).
+ */
+int ps_kv_append_fp8(const void* key, int64_t key_stride_token, int64_t key_stride_head,
+                     const void* value, int64_t value_stride_token, int64_t value_stride_head,
+                     void* key_cache, void* value_cache, int64_t cache_stride_block,
+                     int64_t cache_stride_slot, int64_t cache_stride_head, int64_t num_blocks,
+                     const int64_t* slot_mapping, int64_t num_tokens, int32_t num_kv_heads,
+                     int32_t head_size, int32_t block_size, int32_t dtype, const float* k_scale,
+                     const float* v_scale, int32_t* status, void* stream);
 
 /*
  * Bytes of workspace ps_paged_decode needs for up to num_seqs sequences on

@@ -492,3 +492,58 @@ def dcp_combine(o_r, lse_r, s_out, s_lse, rounding="fp32"):
     out = o_ctx * (pse / tot).T[..., None] + s_out * (sse / tot).T[..., None]
     return (round_to(out, rounding), (np.log(tot) + mx).astype(np.float32), o_ctx,
             lse_ctx.astype(np.float32))
+
+
+# --------------------------------------------------------------------------
+# fp8 (e4m3) KV cache
+# --------------------------------------------------------------------------
+def _e4m3_values():
+    """Value of each non-negative e4m3fn code 0..126 (0x7F is NaN): 4
+    exponent bits with bias 7, 3 mantissa bits, subnormals at exponent 0,
+    no infinities (OCP 8-bit floating point, E4M3)."""
+    codes = np.arange(127)
+    e, m = codes >> 3, codes & 7
+    return np.where(e == 0, m / 8.0 * 2.0 ** -6, (1 + m / 8.0) * 2.0 ** (e - 7.0))
+
+
+_E4M3 = _e4m3_values()
+
+
+def e4m3_encode(x):
+    """float32 -> e4m3fn codes (uint8): nearest value, ties to the even
+    code, magnitudes past 448 saturate to 448 (the ``satfinite`` conversion
+    of CUDA's ``__nv_cvt_float_to_fp8`` and of Triton's fp8 store), NaN ->
+    0x7F."""
+    x = np.asarray(x, dtype=np.float32)
+    a = np.abs(x).astype(np.float64)
+    hi = np.clip(np.searchsorted(_E4M3, a), 0, 126)
+    lo = np.clip(hi - 1, 0, 126)
+    dlo, dhi = np.abs(a - _E4M3[lo]), np.abs(_E4M3[hi] - a)
+    pick = np.where(dlo < dhi, lo, np.where(dhi < dlo, hi, np.where(lo % 2 == 0, lo, hi)))
+    pick = np.where(a >= 448.0, 126, pick)
+    code = pick.astype(np.uint8) | (np.signbit(x).astype(np.uint8) << 7)
+    return np.where(np.isnan(x), np.uint8(0x7F), code).astype(np.uint8)
+
+
+def e4m3_decode(codes):
+    """e4m3fn codes (uint8) -> float32."""
+    c = np.asarray(codes, dtype=np.uint8)
+    mag = c & 0x7F
+    v = np.where(mag == 0x7F, np.nan, _E4M3[np.minimum(mag, 126)])
+    return np.where(c & 0x80, -v, v).astype(np.float32)
+
+
+def kv_append_fp8(key, value, key_cache, value_cache, slot_mapping, k_scale, v_scale):
+    """``reshape_and_cache_flash`` with kv_cache_dtype "fp8"
+    (``triton_reshape_and_cache_flash.py:93-110``): rows stored as
+    e4m3(x / k_scale) and e4m3(x / v_scale), the quotient in float32.
+    Caches are uint8 code arrays, updated in place."""
+    ks, vs = np.float32(k_scale), np.float32(v_scale)
+    kq = e4m3_encode(np.asarray(key, dtype=np.float32) / ks)
+    vq = e4m3_encode(np.asarray(value, dtype=np.float32) / vs)
+    kv_append(kq, vq, key_cache, value_cache, slot_mapping)
+
+
+def dequantize_cache(codes, scale):
+    """An fp8 cache read as attention sees it: code * scale, float32."""
+    return (e4m3_decode(codes) * np.float32(scale)).astype(np.float32)

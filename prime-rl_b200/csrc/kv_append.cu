@@ -92,3 +92,58 @@ int ps_launch_kv_append(const ps::AppendArgs& a, int vec, int sm_count, cudaStre
   }
   return static_cast<int>(cudaGetLastError());
 }
+
+namespace ps {
+
+// fp8 (e4m3) cache: each 8-element piece of a head row (16 source bytes) is
+// stored as 8 e4m3 codes of x / scale -- the fp8 branch of the Triton twin
+// (:93-110: key / k_scale, value / v_scale, converted to the cache's fp8 type
+// by the store), rounded to the nearest e4m3 (ties to even) and saturating
+// at +-448.  vecs_per_head counts 8-element pieces.
+template <bool kBF16>
+__global__ void __launch_bounds__(256) kv_append_fp8_kernel(AppendArgs a, const float* k_scale,
+                                                            const float* v_scale) {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const float ks = k_scale ? __ldg(k_scale) : 1.f;
+  const float vs = v_scale ? __ldg(v_scale) : 1.f;
+  const int per_tensor = a.num_heads * a.vecs_per_head;
+  const int per_token = 2 * per_tensor;
+  for (int64_t t = blockIdx.x; t < a.num_tokens; t += gridDim.x) {
+    const int64_t slot = __ldg(a.slot_mapping + t);
+    if (slot < 0) continue;  // padding token
+    if (slot >= a.num_slots) {
+      if (threadIdx.x == 0) set_status(a.status, PS_DEV_SLOT_OUT_OF_RANGE);
+      continue;
+    }
+    const int64_t blk = slot / a.block_size;
+    const int64_t off = slot - blk * a.block_size;
+    const int64_t dst_tok = blk * a.c_sblock + off * a.c_sslot;
+    for (int j = threadIdx.x; j < per_token; j += blockDim.x) {
+      const bool is_v = j >= per_tensor;
+      const int r = is_v ? j - per_tensor : j;
+      const int h = r / a.vecs_per_head;
+      const int c = r - h * a.vecs_per_head;
+      const char* src = is_v ? a.value + t * a.val_st + h * a.val_sh
+                             : a.key + t * a.key_st + h * a.key_sh;
+      char* dst = (is_v ? a.value_cache : a.key_cache) + dst_tok + h * a.c_shead;
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>(src) + c);
+      reinterpret_cast<uint2*>(dst)[c] = quantize8_e4m3<kBF16>(v, is_v ? vs : ks);
+    }
+  }
+}
+
+}  // namespace ps
+
+int ps_launch_kv_append_fp8(const ps::AppendArgs& a, const float* k_scale, const float* v_scale,
+                            int dtype_bf16, int sm_count, cudaStream_t stream) {
+  if (a.num_tokens == 0) return 0;
+  int64_t blocks = a.num_tokens;
+  const int64_t cap = static_cast<int64_t>(sm_count) * 8;
+  if (blocks > cap) blocks = cap;
+  if (dtype_bf16)
+    ps::kv_append_fp8_kernel<true><<<static_cast<int>(blocks), 256, 0, stream>>>(a, k_scale, v_scale);
+  else
+    ps::kv_append_fp8_kernel<false><<<static_cast<int>(blocks), 256, 0, stream>>>(a, k_scale, v_scale);
+  return static_cast<int>(cudaGetLastError());
+}

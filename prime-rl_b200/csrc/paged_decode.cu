@@ -51,6 +51,8 @@ constexpr int kPageTokens = 16;
 constexpr int kHeadDim = 128;
 constexpr int kBoxBytes = kPageTokens * 64 * 2;  // 2 KB: 16 rows x 128 bytes
 constexpr int kStageBytes = 4 * kBoxBytes;       // K lo, K hi, V lo, V hi
+// fp8 (e4m3) cache: one box per page of K or V, 16 rows x 128 one-byte dims
+constexpr int kBoxBytesF8 = kPageTokens * kHeadDim;  // 2 KB
 constexpr int kQRowBytes = kHeadDim * 2 + 16;    // padded query row (conflict-free ldmatrix)
 constexpr int kPrefixNT = 2;                     // prefix segments: 16 query columns
 #ifndef PS_CASCADE_PREFIX_COST16
@@ -268,10 +270,11 @@ __device__ __noinline__ void combine_rows(const DecodeParams& p, int64_t slot0, 
       if (lane == 0 && p.lse != nullptr) p.lse[qh * p.lse_sh + qrow * p.lse_st] = lse;
     }
   };
-  if (ntot <= 4 && nrows <= 4) {
+  if (kRec == 8 && ntot <= 4 && nrows <= 4) {
     // few sources (the common split count): every partial row this lane
     // needs is loaded together with the LSEs, so the merge waits on one L2
-    // round trip instead of two
+    // round trip instead of two (8-column kernels only: the 16-column ones
+    // have no registers to spare for it)
     float4 ov[4][4];
     float ls[4][4];
 #pragma unroll
@@ -433,11 +436,24 @@ __host__ __device__ constexpr int decode_qslot_bytes() {
   return 8 * NT * kQRowBytes;
 }
 
-template <int kQNT>
+// Page stages per warp and their size.  An fp8 page-head is half the bytes,
+// so the fp8 kernels keep about as many bytes in flight with more stages
+// (4 with 8 query columns; 3 with 16, whose query slots are twice the size).
+template <bool kFP8, int kQNT>
+__host__ __device__ constexpr int decode_stages() {
+  return kFP8 ? (kQNT == 1 ? 2 * kDecodeStages : kDecodeStages + 1) : kDecodeStages;
+}
+template <bool kFP8>
+__host__ __device__ constexpr int decode_stage_bytes() {
+  return kFP8 ? 2 * kBoxBytesF8 : kStageBytes;
+}
+
+template <int kQNT, bool kFP8 = false>
 __host__ __device__ constexpr int decode_smem_bytes_before_table() {
   // stages | per-warp query slots | mbarriers
-  return kDecodeWarps * kDecodeStages * kStageBytes +
-         kDecodeWarps * kDecodeStages * decode_qslot_bytes<kQNT>() + kDecodeWarps * kDecodeStages * 8;
+  constexpr int D = decode_stages<kFP8, kQNT>();
+  return kDecodeWarps * D * decode_stage_bytes<kFP8>() + kDecodeWarps * D * decode_qslot_bytes<kQNT>() +
+         kDecodeWarps * D * 8;
 }
 
 // Own segment of sequence b (cascade modes): its split geometry in the list.
@@ -475,18 +491,37 @@ __device__ __forceinline__ void prefix_result(const DecodeParams& p, const Table
 // list, cascade prefix region, or cascade own-segment region; indices are
 // global list positions).  k0: ring uses so far by this warp.  Returns the ring
 // uses after the range, or -1 after a wait timeout.
-template <bool kBF16, int NT, int kRec, int kQNT, int kMode>
+// Dim (within a 16-dim output tile) of accumulator row g (hi = 0) or g + 8
+// (hi = 1): in order for 16-bit caches, (2g, 2g+1) for fp8 caches.
+template <bool kFP8>
+__device__ __forceinline__ int out_row(int g, int hi) {
+  return kFP8 ? 2 * g + hi : g + 8 * hi;
+}
+
+template <bool kBF16, int NT, int kRec, int kQNT, int kMode, bool kFP8 = false>
 __device__ __forceinline__ int stream_range(const DecodeParams& p, const CUtensorMap* kmap,
                                             const CUtensorMap* vmap, const Tables& tb,
                                             int64_t start, int64_t end, int64_t gw,
                                             uint8_t* wsm, uint8_t* wq, uint64_t* wbar, int k0,
                                             int lane) {
-  constexpr int D = kDecodeStages;
+  constexpr int D = decode_stages<kFP8, kQNT>();
+  constexpr int SB = decode_stage_bytes<kFP8>();
+  // MMA operand type: the model dtype, or f16 for an fp8 cache (e4m3 codes
+  // convert to f16 exactly)
+  constexpr bool kMathBF16 = kBF16 && !kFP8;
   const int Hkv = p.num_kv_heads;
   const int sub_per_block = p.block_size / kPageTokens;
   const int group = p.group;
   const int cnt = static_cast<int>(end - start);
   const int64_t base = (kMode == kCasSuffix) ? tb.pre_total : 0;
+  // fp8 cache: the dequantization scales fold into the score scale (K) and
+  // the output normalisation (V)
+  float scale_log2 = p.scale_log2, k_scale = 1.f, v_scale = 1.f;
+  if constexpr (kFP8) {
+    k_scale = p.k_scale ? __ldg(p.k_scale) : 1.f;
+    v_scale = p.v_scale ? __ldg(p.v_scale) : 1.f;
+    scale_log2 *= k_scale;
+  }
 
   if (k0 > 0) {
     // the ring and query slots were last read by this warp's generic-proxy
@@ -512,7 +547,7 @@ __device__ __forceinline__ int stream_range(const DecodeParams& p, const CUtenso
     }
     int blk = __shfl_sync(0xffffffffu, bt_reg, e - bt_e0);
     const int sub = pg - e * sub_per_block;
-    uint8_t* dst = wsm + stage * kStageBytes;
+    uint8_t* dst = wsm + stage * SB;
     uint64_t* bar = wbar + stage;
     const int nrows = (kMode == kCasPrefix) ? c.ncols : group;
     const uint32_t qbytes = seg_start ? static_cast<uint32_t>(nrows) * (kHeadDim * 2) : 0u;
@@ -521,12 +556,17 @@ __device__ __forceinline__ int stream_range(const DecodeParams& p, const CUtenso
         set_status(p.status, PS_DEV_BLOCK_OUT_OF_RANGE);
         blk = 0;
       }
-      mbar_arrive_expect_tx(bar, kStageBytes + qbytes);
+      mbar_arrive_expect_tx(bar, SB + qbytes);
       const int tok = sub * kPageTokens;
-      tma_load_4d(dst + 0 * kBoxBytes, kmap, bar, 0, c.h, tok, blk);
-      tma_load_4d(dst + 1 * kBoxBytes, kmap, bar, 64, c.h, tok, blk);
-      tma_load_4d(dst + 2 * kBoxBytes, vmap, bar, 0, c.h, tok, blk);
-      tma_load_4d(dst + 3 * kBoxBytes, vmap, bar, 64, c.h, tok, blk);
+      if constexpr (kFP8) {
+        tma_load_4d(dst, kmap, bar, 0, c.h, tok, blk);
+        tma_load_4d(dst + kBoxBytesF8, vmap, bar, 0, c.h, tok, blk);
+      } else {
+        tma_load_4d(dst + 0 * kBoxBytes, kmap, bar, 0, c.h, tok, blk);
+        tma_load_4d(dst + 1 * kBoxBytes, kmap, bar, 64, c.h, tok, blk);
+        tma_load_4d(dst + 2 * kBoxBytes, vmap, bar, 0, c.h, tok, blk);
+        tma_load_4d(dst + 3 * kBoxBytes, vmap, bar, 64, c.h, tok, blk);
+      }
     }
     if (seg_start) {
       __syncwarp();  // expect_tx is armed before the row copies complete_tx
@@ -582,7 +622,7 @@ __device__ __forceinline__ int stream_range(const DecodeParams& p, const CUtenso
     const int kr = k0 + k;
     const int stage = kr % D;
     const uint32_t phase = static_cast<uint32_t>((kr / D) & 1);
-    uint8_t* st = wsm + stage * kStageBytes;
+    uint8_t* st = wsm + stage * SB;
     if (!mbar_wait_bounded(wbar + stage, phase)) {
       if (lane == 0) set_status(p.status, PS_DEV_WAIT_TIMEOUT);
       // drain copies still in flight into this warp's ring, bounded
@@ -615,16 +655,31 @@ __device__ __forceinline__ int stream_range(const DecodeParams& p, const CUtenso
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
         const bool ok = nt * 8 + g < ncols;
+        if constexpr (kFP8) {
+          // f16 B fragments with the reduction dims of each 16-dim step in
+          // the order the fp8 K fragments arrive: k = 2t, 2t+1 -> dims 4t,
+          // 4t+1 and k = 2t+8, 2t+9 -> dims 4t+2, 4t+3 (a permutation of the
+          // dot product's terms, the same on both operands)
+          const uint8_t* qrow = wq + (cseg - 1) % D * decode_qslot_bytes<kQNT>() + (nt * 8 + g) * kQRowBytes;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          // matrices: heads nt*8..+7 x dims 32i + 8*(lane/8) .. +7
-          const uint32_t addr = qbase + (nt * 8 + (lane & 7)) * kQRowBytes + (32 * i + 8 * k_mi) * 2;
-          uint32_t r0, r1, r2, r3;
-          ldsm_x4(addr, r0, r1, r2, r3);
-          qf[nt][2 * i][0] = ok ? r0 : 0u;
-          qf[nt][2 * i][1] = ok ? r1 : 0u;
-          qf[nt][2 * i + 1][0] = ok ? r2 : 0u;
-          qf[nt][2 * i + 1][1] = ok ? r3 : 0u;
+          for (int ks = 0; ks < 8; ++ks) {
+            const uint2 w = *reinterpret_cast<const uint2*>(qrow + (16 * ks + 4 * t) * 2);
+            const float2 lo = unpack2<kBF16>(w.x), hi = unpack2<kBF16>(w.y);
+            qf[nt][ks][0] = ok ? pack2<false>(lo.x, lo.y) : 0u;
+            qf[nt][ks][1] = ok ? pack2<false>(hi.x, hi.y) : 0u;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            // matrices: heads nt*8..+7 x dims 32i + 8*(lane/8) .. +7
+            const uint32_t addr = qbase + (nt * 8 + (lane & 7)) * kQRowBytes + (32 * i + 8 * k_mi) * 2;
+            uint32_t r0, r1, r2, r3;
+            ldsm_x4(addr, r0, r1, r2, r3);
+            qf[nt][2 * i][0] = ok ? r0 : 0u;
+            qf[nt][2 * i][1] = ok ? r1 : 0u;
+            qf[nt][2 * i + 1][0] = ok ? r2 : 0u;
+            qf[nt][2 * i + 1][1] = ok ? r3 : 0u;
+          }
         }
 #pragma unroll
         for (int mi = 0; mi < 8; ++mi)
@@ -647,13 +702,24 @@ __device__ __forceinline__ int stream_range(const DecodeParams& p, const CUtenso
         // write the row into this stage's copy of the page (K lanes 0-15, V 16-31)
         const int r = pos & (kPageTokens - 1);
         const int c = lane & 15;
-        const int part = (lane < 16 ? 0 : 2) + (c >> 3);  // K lo/hi, V lo/hi box
-        *reinterpret_cast<uint4*>(st + part * kBoxBytes + r * 128 + (((c & 7) ^ (r & 7)) << 4)) = new_row;
-        // and into the cache, as ps_kv_append would
         const int64_t blk = new_slot / p.block_size, off = new_slot - blk * p.block_size;
-        uint16_t* dst = reinterpret_cast<uint16_t*>(lane < 16 ? p.key_cache : p.value_cache) +
-                        blk * p.c_sblock + off * p.c_sslot + cc.h * p.c_shead;
-        reinterpret_cast<uint4*>(dst)[c] = new_row;
+        if constexpr (kFP8) {
+          // this lane's 8 elements (dims 8c..8c+7) as e4m3(x / scale), as
+          // ps_kv_append_fp8 stores them
+          const uint2 q8 = quantize8_e4m3<kBF16>(new_row, lane < 16 ? k_scale : v_scale);
+          *reinterpret_cast<uint2*>(st + (lane < 16 ? 0 : kBoxBytesF8) + r * 128 +
+                                    ((((c >> 1) ^ (r & 7)) << 4) | ((c & 1) << 3))) = q8;
+          uint8_t* dst = reinterpret_cast<uint8_t*>(lane < 16 ? p.key_cache : p.value_cache) +
+                         blk * p.c_sblock + off * p.c_sslot + cc.h * p.c_shead;
+          reinterpret_cast<uint2*>(dst)[c] = q8;
+        } else {
+          const int part = (lane < 16 ? 0 : 2) + (c >> 3);  // K lo/hi, V lo/hi box
+          *reinterpret_cast<uint4*>(st + part * kBoxBytes + r * 128 + (((c & 7) ^ (r & 7)) << 4)) = new_row;
+          // and into the cache, as ps_kv_append would
+          uint16_t* dst = reinterpret_cast<uint16_t*>(lane < 16 ? p.key_cache : p.value_cache) +
+                          blk * p.c_sblock + off * p.c_sslot + cc.h * p.c_shead;
+          reinterpret_cast<uint4*>(dst)[c] = new_row;
+        }
       } else if (lane == 0) {
         set_status(p.status, PS_DEV_BAD_METADATA);
       }
@@ -665,15 +731,36 @@ __device__ __forceinline__ int stream_range(const DecodeParams& p, const CUtenso
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
     const uint32_t kbase = smem_u32(st);
+    if constexpr (kFP8) {
+      // one ldmatrix.x4 per two 16-dim steps: matrices (tokens 0-7 | 8-15) x
+      // (chunk 2j | 2j+1); a lane receives 4 consecutive e4m3 dims 4t..4t+3
+      // of token g (or g+8), converted to the f16 pairs (4t, 4t+1) and
+      // (4t+2, 4t+3) that match the permuted query fragments
 #pragma unroll
-    for (int ks = 0; ks < 8; ++ks) {
-      const int half = ks >> 2;
-      const int chunk = ((ks & 3) << 1) + k_chk;
-      const uint32_t addr = kbase + half * kBoxBytes + k_row * 128 + ((chunk ^ (k_row & 7)) << 4);
-      uint32_t a0, a1, a2, a3;
-      ldsm_x4(addr, a0, a1, a2, a3);
+      for (int j = 0; j < 4; ++j) {
+        const int chunk = 2 * j + k_chk;
+        const uint32_t addr = kbase + k_row * 128 + ((chunk ^ (k_row & 7)) << 4);
+        uint32_t r0, r1, r2, r3;
+        ldsm_x4(addr, r0, r1, r2, r3);
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) mma_16816<kBF16>(s[nt], a0, a1, a2, a3, qf[nt][ks][0], qf[nt][ks][1]);
+        for (int nt = 0; nt < NT; ++nt) {
+          mma_16816<false>(s[nt], e4m3x2_to_f16x2(r0), e4m3x2_to_f16x2(r1), e4m3x2_to_f16x2(r0 >> 16),
+                           e4m3x2_to_f16x2(r1 >> 16), qf[nt][2 * j][0], qf[nt][2 * j][1]);
+          mma_16816<false>(s[nt], e4m3x2_to_f16x2(r2), e4m3x2_to_f16x2(r3), e4m3x2_to_f16x2(r2 >> 16),
+                           e4m3x2_to_f16x2(r3 >> 16), qf[nt][2 * j + 1][0], qf[nt][2 * j + 1][1]);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        const int half = ks >> 2;
+        const int chunk = ((ks & 3) << 1) + k_chk;
+        const uint32_t addr = kbase + half * kBoxBytes + k_row * 128 + ((chunk ^ (k_row & 7)) << 4);
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4(addr, a0, a1, a2, a3);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) mma_16816<kBF16>(s[nt], a0, a1, a2, a3, qf[nt][ks][0], qf[nt][ks][1]);
+      }
     }
 
     // ---- online softmax (exp2 domain) ----------------------------------------
@@ -681,10 +768,10 @@ __device__ __forceinline__ int stream_range(const DecodeParams& p, const CUtenso
     uint32_t pb[NT][2];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
-      s[nt][0] = v0 ? s[nt][0] * p.scale_log2 : -INFINITY;
-      s[nt][1] = v0 ? s[nt][1] * p.scale_log2 : -INFINITY;
-      s[nt][2] = v1 ? s[nt][2] * p.scale_log2 : -INFINITY;
-      s[nt][3] = v1 ? s[nt][3] * p.scale_log2 : -INFINITY;
+      s[nt][0] = v0 ? s[nt][0] * scale_log2 : -INFINITY;
+      s[nt][1] = v0 ? s[nt][1] * scale_log2 : -INFINITY;
+      s[nt][2] = v1 ? s[nt][2] * scale_log2 : -INFINITY;
+      s[nt][3] = v1 ? s[nt][3] * scale_log2 : -INFINITY;
       float alpha[2];
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
@@ -709,15 +796,48 @@ __device__ __forceinline__ int stream_range(const DecodeParams& p, const CUtenso
           o[nt][mi][3] *= alpha[1];
         }
       }
-      pb[nt][0] = movmatrix_t(pack2<kBF16>(p0, p1));
-      pb[nt][1] = movmatrix_t(pack2<kBF16>(p2, p3));
+      pb[nt][0] = movmatrix_t(pack2<kMathBF16>(p0, p1));
+      pb[nt][1] = movmatrix_t(pack2<kMathBF16>(p2, p3));
     }
 
     // ---- O^T += V^T P^T ------------------------------------------------------
-    const uint32_t vbase = kbase + 2 * kBoxBytes;
     const bool tail = valid < kPageTokens;
     const bool z0 = 2 * t >= valid, z1 = 2 * t + 1 >= valid;
     const bool z2 = 2 * t + 8 >= valid, z3 = 2 * t + 9 >= valid;
+    if constexpr (kFP8) {
+      // ldmatrix.trans over byte pairs: a lane receives dims (2g, 2g+1) of
+      // tokens (2t, 2t+1) [or 8+...]; one byte permute splits them into the
+      // token pairs of dim 2g and of dim 2g+1, which become accumulator rows
+      // g and g+8 (the output rows of each 16-dim tile are permuted; the
+      // epilogue writes them back in order)
+      const uint32_t vbase = kbase + kBoxBytesF8;
+      const uint32_t m01 = (z0 ? 0u : 0xffffu) | (z1 ? 0u : 0xffff0000u);
+      const uint32_t m23 = (z2 ? 0u : 0xffffu) | (z3 ? 0u : 0xffff0000u);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int chunk = 2 * j + k_chk;
+        const uint32_t addr = vbase + k_row * 128 + ((chunk ^ (k_row & 7)) << 4);
+        uint32_t r0, r1, r2, r3;
+        ldsm_x4_t(addr, r0, r1, r2, r3);
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
+          const uint32_t lo = __byte_perm(h2 ? r2 : r0, 0u, 0x3120);  // tokens 2t, 2t+1
+          const uint32_t hi = __byte_perm(h2 ? r3 : r1, 0u, 0x3120);  // tokens 2t+8, 2t+9
+          uint32_t a0 = e4m3x2_to_f16x2(lo), a1 = e4m3x2_to_f16x2(lo >> 16);
+          uint32_t a2 = e4m3x2_to_f16x2(hi), a3 = e4m3x2_to_f16x2(hi >> 16);
+          if (tail) {  // stale rows past seq_len: P is 0 there, keep NaN codes out too
+            a0 &= m01;
+            a1 &= m01;
+            a2 &= m23;
+            a3 &= m23;
+          }
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+            mma_16816<false>(o[nt][2 * j + h2], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
+        }
+      }
+    } else {
+    const uint32_t vbase = kbase + 2 * kBoxBytes;
 #pragma unroll
     for (int mi = 0; mi < 8; ++mi) {
       const int half = mi >> 2;
@@ -735,6 +855,7 @@ __device__ __forceinline__ int stream_range(const DecodeParams& p, const CUtenso
       }
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) mma_16816<kBF16>(o[nt][mi], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
+    }
     }
     __syncwarp();
 
@@ -774,7 +895,7 @@ __device__ __forceinline__ int stream_range(const DecodeParams& p, const CUtenso
         for (int j = 0; j < 2; ++j) {
           const float lt = warp_sum_xor_4_8_16(l[nt][j]);
           const bool zero = (lt == 0.f) || (lt != lt);
-          inv[nt][j] = zero ? 0.f : 1.f / lt;
+          inv[nt][j] = zero ? 0.f : v_scale / lt;
           lse[nt][j] = zero ? -INFINITY : (m[nt][j] + __log2f(lt)) * 0.6931471805599453f;
         }
       if (kMode != kCasPrefix && nsplit == 1 && !member) {
@@ -789,8 +910,8 @@ __device__ __forceinline__ int stream_range(const DecodeParams& p, const CUtenso
               const int64_t ob = qrow * p.o_st + qh * p.o_sh;
 #pragma unroll
               for (int mi = 0; mi < 8; ++mi) {
-                store_out2<kBF16>(p.out, ob + mi * 16 + g, o[nt][mi][j] * inv[nt][j]);
-                store_out2<kBF16>(p.out, ob + mi * 16 + g + 8, o[nt][mi][j + 2] * inv[nt][j]);
+                store_out2<kBF16>(p.out, ob + mi * 16 + out_row<kFP8>(g, 0), o[nt][mi][j] * inv[nt][j]);
+                store_out2<kBF16>(p.out, ob + mi * 16 + out_row<kFP8>(g, 1), o[nt][mi][j + 2] * inv[nt][j]);
               }
               if (g == 0 && p.lse) p.lse[qh * p.lse_sh + qrow * p.lse_st] = lse[nt][j];
             }
@@ -806,8 +927,8 @@ __device__ __forceinline__ int stream_range(const DecodeParams& p, const CUtenso
               float* po = slot_o<kRec>(p, slot, col);
 #pragma unroll
               for (int mi = 0; mi < 8; ++mi) {
-                po[mi * 16 + g] = o[nt][mi][j] * inv[nt][j];
-                po[mi * 16 + g + 8] = o[nt][mi][j + 2] * inv[nt][j];
+                po[mi * 16 + out_row<kFP8>(g, 0)] = o[nt][mi][j] * inv[nt][j];
+                po[mi * 16 + out_row<kFP8>(g, 1)] = o[nt][mi][j + 2] * inv[nt][j];
               }
               if (g == 0) *slot_lse<kRec>(p, slot, col) = lse[nt][j];
             }
@@ -915,19 +1036,20 @@ __device__ __forceinline__ int own_pages_of(const DecodeParams& p, int b, int su
   return min(P, p.max_blocks_per_seq * sub_per_block);
 }
 
-template <bool kBF16, int NT, bool kCascade>
+template <bool kBF16, int NT, bool kCascade, bool kFP8>
 __global__ void __launch_bounds__(kDecodeWarps * 32, kDecodeCtasPerSm)
     paged_decode_kernel(const __grid_constant__ DecodeParams p,
                         const __grid_constant__ CUtensorMap kmap,
                         const __grid_constant__ CUtensorMap vmap) {
-  constexpr int D = kDecodeStages;
   constexpr int kQNT = kCascade ? kPrefixNT : NT;
+  constexpr int D = decode_stages<kFP8, kQNT>();
+  constexpr int SB = decode_stage_bytes<kFP8>();
   constexpr int kRec = kCascade ? 8 * kPrefixNT : 8 * NT;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment for the 128B-swizzled TMA destinations.
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  uint8_t* qslots = smem + kDecodeWarps * D * kStageBytes;
+  uint8_t* qslots = smem + kDecodeWarps * D * SB;
   uint64_t* bars =
       reinterpret_cast<uint64_t*>(qslots + kDecodeWarps * D * decode_qslot_bytes<kQNT>());
   int* prefix = reinterpret_cast<int*>(bars + kDecodeWarps * D);
@@ -1102,7 +1224,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, kDecodeCtasPerSm)
   const int64_t end = min(total, list_at_cost(tb, (gw + 1) * tb.Qc));
   if (start >= end) return;
 
-  uint8_t* wsm = smem + warp * D * kStageBytes;
+  uint8_t* wsm = smem + warp * D * SB;
   uint8_t* wq = qslots + warp * D * decode_qslot_bytes<kQNT>();
   uint64_t* wbar = bars + warp * D;
 
@@ -1115,12 +1237,12 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, kDecodeCtasPerSm)
       stream_range<kBF16, NT, kRec, kQNT, kCasSuffix>(p, &kmap, &vmap, tb, max(start, tb.pre_total),
                                                       end, gw, wsm, wq, wbar, k, lane);
   } else {
-    stream_range<kBF16, NT, kRec, kQNT, kPlain>(p, &kmap, &vmap, tb, start, end, gw, wsm, wq,
-                                                wbar, 0, lane);
+    stream_range<kBF16, NT, kRec, kQNT, kPlain, kFP8>(p, &kmap, &vmap, tb, start, end, gw, wsm, wq,
+                                                      wbar, 0, lane);
   }
 }
 
-template <bool kBF16, int NT, bool kCascade>
+template <bool kBF16, int NT, bool kCascade, bool kFP8 = false>
 static int launch_t(const DecodeParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap,
                     int sm_count, cudaStream_t stream) {
   constexpr int kQNT = kCascade ? kPrefixNT : NT;
@@ -1129,7 +1251,7 @@ static int launch_t(const DecodeParams& p, const CUtensorMap& kmap, const CUtens
   auto table_ints = [](int B, int gmax) {
     return kCascade ? (2 * B + 1) + 2 * (gmax + 1) : B + 1;
   };
-  const size_t smem = 1024 + decode_smem_bytes_before_table<kQNT>() +
+  const size_t smem = 1024 + decode_smem_bytes_before_table<kQNT, kFP8>() +
                       static_cast<size_t>(table_ints(p.num_seqs, p.cas_max_groups)) * 4;
   // the attribute is per function and per device
   static bool configured[64] = {false};
@@ -1137,8 +1259,8 @@ static int launch_t(const DecodeParams& p, const CUtensorMap& kmap, const CUtens
   if (cudaGetDevice(&dev) != cudaSuccess || dev >= 64) return static_cast<int>(cudaErrorInvalidDevice);
   if (!configured[dev]) {
     const cudaError_t e = cudaFuncSetAttribute(
-        paged_decode_kernel<kBF16, NT, kCascade>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-        static_cast<int>(1024 + decode_smem_bytes_before_table<kQNT>() +
+        paged_decode_kernel<kBF16, NT, kCascade, kFP8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        static_cast<int>(1024 + decode_smem_bytes_before_table<kQNT, kFP8>() +
                          static_cast<size_t>(table_ints(max_seqs, max_seqs / 2)) * 4));
     if (e != cudaSuccess) return static_cast<int>(e);
     configured[dev] = true;
@@ -1153,7 +1275,7 @@ static int launch_t(const DecodeParams& p, const CUtensorMap& kmap, const CUtens
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, paged_decode_kernel<kBF16, NT, kCascade>, p, kmap, vmap);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, paged_decode_kernel<kBF16, NT, kCascade, kFP8>, p, kmap, vmap);
   return static_cast<int>(e != cudaSuccess ? e : cudaGetLastError());
 }
 
@@ -1168,8 +1290,15 @@ int64_t ps_decode_partial_slots(int num_seqs, int num_kv_heads, int sm_count, in
 
 int ps_launch_paged_decode(const ps::DecodeParams& p, const CUtensorMap& kmap,
                            const CUtensorMap& vmap, int dtype_bf16, int sm_count,
-                           cudaStream_t stream) {
+                           cudaStream_t stream, int fp8_cache) {
   const int nt = p.group <= 8 ? 1 : 2;
+  if (fp8_cache) {  // plain decode only (checked by the caller)
+    if (dtype_bf16)
+      return nt == 1 ? ps::launch_t<true, 1, false, true>(p, kmap, vmap, sm_count, stream)
+                     : ps::launch_t<true, 2, false, true>(p, kmap, vmap, sm_count, stream);
+    return nt == 1 ? ps::launch_t<false, 1, false, true>(p, kmap, vmap, sm_count, stream)
+                   : ps::launch_t<false, 2, false, true>(p, kmap, vmap, sm_count, stream);
+  }
   if (p.cas_num_groups != nullptr) {  // cascade: group <= 8 (checked by the caller)
     return dtype_bf16 ? ps::launch_t<true, 1, true>(p, kmap, vmap, sm_count, stream)
                       : ps::launch_t<false, 1, true>(p, kmap, vmap, sm_count, stream);

@@ -60,18 +60,22 @@ EncodeTiledFn encode_fn() {
 
 // Tensor map over one cache half viewed as [num_blocks][block_size][Hkv][128]
 // 16-bit elements; box = one 16-token page of one head, 64 dims (128 B) wide,
-// 128-byte swizzle.
+// 128-byte swizzle.  elem_bytes = 1 (fp8 cache): the box is all 128 dims,
+// again 128 bytes wide.
 int make_page_map(CUtensorMap* map, const void* base, int64_t num_blocks, int block_size,
-                  int num_kv_heads, int64_t s_block, int64_t s_slot, int64_t s_head) {
+                  int num_kv_heads, int64_t s_block, int64_t s_slot, int64_t s_head,
+                  int elem_bytes = 2) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return fail(PS_ERR_CUDA, "cuTensorMapEncodeTiled unavailable from the driver");
+  const cuuint64_t eb = static_cast<cuuint64_t>(elem_bytes);
   cuuint64_t dims[4] = {128, static_cast<cuuint64_t>(num_kv_heads),
                         static_cast<cuuint64_t>(block_size), static_cast<cuuint64_t>(num_blocks)};
-  cuuint64_t strides[3] = {static_cast<cuuint64_t>(s_head) * 2, static_cast<cuuint64_t>(s_slot) * 2,
-                           static_cast<cuuint64_t>(s_block) * 2};
-  cuuint32_t box[4] = {64, 1, 16, 1};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(s_head) * eb, static_cast<cuuint64_t>(s_slot) * eb,
+                           static_cast<cuuint64_t>(s_block) * eb};
+  cuuint32_t box[4] = {elem_bytes == 1 ? 128u : 64u, 1, 16, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 4, const_cast<void*>(base), dims, strides,
+  CUresult r = fn(map, elem_bytes == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT16,
+                  4, const_cast<void*>(base), dims, strides,
                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
@@ -164,9 +168,12 @@ int validate_problem(const ps_paged_problem* pr, bool decode) {
     return fail(PS_ERR_INVALID_ARGUMENT, "num_blocks out of range");
   if (pr->max_blocks_per_seq < 0 || pr->block_table_stride < pr->max_blocks_per_seq)
     return fail(PS_ERR_INVALID_ARGUMENT, "block_table_stride < max_blocks_per_seq");
-  // 16-byte rows for TMA / vector access
+  if (pr->kv_cache_dtype != PS_KV_AUTO && pr->kv_cache_dtype != PS_KV_FP8_E4M3)
+    return fail(PS_ERR_INVALID_ARGUMENT, "kv_cache_dtype %d unknown", pr->kv_cache_dtype);
+  // 16-byte rows for TMA / vector access (strides in cache elements)
+  const int64_t cv = pr->kv_cache_dtype == PS_KV_FP8_E4M3 ? 16 : 8;
   if (!aligned(pr->key_cache, 16) || !aligned(pr->value_cache, 16) ||
-      pr->cache_stride_head % 8 || pr->cache_stride_slot % 8 || pr->cache_stride_block % 8)
+      pr->cache_stride_head % cv || pr->cache_stride_slot % cv || pr->cache_stride_block % cv)
     return fail(PS_ERR_INVALID_ARGUMENT, "cache base/strides must be 16-byte aligned");
   if (!aligned(pr->q, 16) || pr->q_stride_head % 8 || pr->q_stride_token % 8)
     return fail(PS_ERR_INVALID_ARGUMENT, "q base/strides must be 16-byte aligned");
@@ -199,6 +206,8 @@ int decode_impl(const ps_paged_problem* pr, const void* plan, int64_t plan_bytes
       return fail(PS_ERR_INVALID_ARGUMENT, "cascade plan must be >= %lld bytes, 16-byte aligned",
                   static_cast<long long>(ps_cascade_plan_words(pr->num_seqs) * 4));
   }
+  const bool fp8 = pr->kv_cache_dtype == PS_KV_FP8_E4M3;
+  if (fp8 && cascade) return fail(PS_ERR_UNSUPPORTED, "cascade decode over an fp8 cache is not built");
   const DecodeWorkspaceLayout lay =
       decode_layout(pr->num_seqs, pr->num_q_heads, pr->num_kv_heads, sms, cascade);
   if (!workspace || workspace_bytes < lay.total || !aligned(workspace, 256))
@@ -206,10 +215,10 @@ int decode_impl(const ps_paged_problem* pr, const void* plan, int64_t plan_bytes
                 static_cast<long long>(lay.total));
   CUtensorMap kmap, vmap;
   rc = make_page_map(&kmap, pr->key_cache, pr->num_blocks, pr->block_size, pr->num_kv_heads,
-                     pr->cache_stride_block, pr->cache_stride_slot, pr->cache_stride_head);
+                     pr->cache_stride_block, pr->cache_stride_slot, pr->cache_stride_head, fp8 ? 1 : 2);
   if (rc != PS_OK) return rc;
   rc = make_page_map(&vmap, pr->value_cache, pr->num_blocks, pr->block_size, pr->num_kv_heads,
-                     pr->cache_stride_block, pr->cache_stride_slot, pr->cache_stride_head);
+                     pr->cache_stride_block, pr->cache_stride_slot, pr->cache_stride_head, fp8 ? 1 : 2);
   if (rc != PS_OK) return rc;
   char* ws = static_cast<char*>(workspace);
   ps::DecodeParams p;
@@ -264,6 +273,8 @@ int decode_impl(const ps_paged_problem* pr, const void* plan, int64_t plan_bytes
   p.c_sblock = pr->cache_stride_block;
   p.c_sslot = pr->cache_stride_slot;
   p.c_shead = pr->cache_stride_head;
+  p.k_scale = fp8 ? pr->k_scale : nullptr;
+  p.v_scale = fp8 ? pr->v_scale : nullptr;
   if (pr->new_key != nullptr) {
     if (!pr->new_value || !pr->slot_mapping)
       return fail(PS_ERR_INVALID_ARGUMENT, "fused append needs new_key, new_value and slot_mapping");
@@ -272,7 +283,7 @@ int decode_impl(const ps_paged_problem* pr, const void* plan, int64_t plan_bytes
       return fail(PS_ERR_INVALID_ARGUMENT, "new key/value rows must be 16-byte aligned");
   }
   const int e = ps_launch_paged_decode(p, kmap, vmap, pr->dtype == PS_DTYPE_BF16, sms,
-                                       static_cast<cudaStream_t>(stream));
+                                       static_cast<cudaStream_t>(stream), fp8 ? 1 : 0);
   if (e != 0) return cuda_fail(static_cast<cudaError_t>(e), "paged_decode launch");
   return PS_OK;
 }
@@ -341,6 +352,55 @@ int ps_kv_append(const void* key, int64_t key_stride_token, int64_t key_stride_h
   a.status = status;
   const int e = ps_launch_kv_append(a, vec, sms, static_cast<cudaStream_t>(stream));
   if (e != 0) return cuda_fail(static_cast<cudaError_t>(e), "kv_append launch");
+  return PS_OK;
+}
+
+int ps_kv_append_fp8(const void* key, int64_t key_stride_token, int64_t key_stride_head,
+                     const void* value, int64_t value_stride_token, int64_t value_stride_head,
+                     void* key_cache, void* value_cache, int64_t cache_stride_block,
+                     int64_t cache_stride_slot, int64_t cache_stride_head, int64_t num_blocks,
+                     const int64_t* slot_mapping, int64_t num_tokens, int32_t num_kv_heads,
+                     int32_t head_size, int32_t block_size, int32_t dtype, const float* k_scale,
+                     const float* v_scale, int32_t* status, void* stream) {
+  if (num_tokens < 0) return fail(PS_ERR_INVALID_ARGUMENT, "num_tokens < 0");
+  if (num_tokens == 0) return PS_OK;
+  if (!key || !value || !key_cache || !value_cache || !slot_mapping)
+    return fail(PS_ERR_INVALID_ARGUMENT, "a required pointer is NULL");
+  if (dtype != PS_DTYPE_BF16 && dtype != PS_DTYPE_FP16)
+    return fail(PS_ERR_UNSUPPORTED, "fp8 append takes fp16 or bf16 rows (dtype %d)", dtype);
+  if (num_kv_heads <= 0 || head_size <= 0 || head_size % 8 || block_size <= 0 || num_blocks <= 0)
+    return fail(PS_ERR_INVALID_ARGUMENT, "non-positive shape or head_size not a multiple of 8");
+  if (!aligned(key, 16) || !aligned(value, 16) || key_stride_token % 8 || key_stride_head % 8 ||
+      value_stride_token % 8 || value_stride_head % 8)
+    return fail(PS_ERR_INVALID_ARGUMENT, "key/value rows must be 16-byte aligned");
+  if (!aligned(key_cache, 8) || !aligned(value_cache, 8) || cache_stride_block % 8 ||
+      cache_stride_slot % 8 || cache_stride_head % 8)
+    return fail(PS_ERR_INVALID_ARGUMENT, "fp8 cache rows must be 8-byte aligned");
+  int dev = 0;
+  const int sms = sm_count_current(&dev);
+  if (sms <= 0) return fail(PS_ERR_CUDA, "no CUDA device");
+  ps::AppendArgs a;
+  a.key = static_cast<const char*>(key);
+  a.value = static_cast<const char*>(value);
+  a.key_cache = static_cast<char*>(key_cache);
+  a.value_cache = static_cast<char*>(value_cache);
+  a.slot_mapping = slot_mapping;
+  a.key_st = key_stride_token * 2;
+  a.key_sh = key_stride_head * 2;
+  a.val_st = value_stride_token * 2;
+  a.val_sh = value_stride_head * 2;
+  a.c_sblock = cache_stride_block;
+  a.c_sslot = cache_stride_slot;
+  a.c_shead = cache_stride_head;
+  a.num_slots = num_blocks * block_size;
+  a.num_tokens = num_tokens;
+  a.num_heads = num_kv_heads;
+  a.block_size = block_size;
+  a.vecs_per_head = head_size / 8;
+  a.status = status;
+  const int e = ps_launch_kv_append_fp8(a, k_scale, v_scale, dtype == PS_DTYPE_BF16, sms,
+                                        static_cast<cudaStream_t>(stream));
+  if (e != 0) return cuda_fail(static_cast<cudaError_t>(e), "kv_append_fp8 launch");
   return PS_OK;
 }
 
@@ -509,6 +569,8 @@ int ps_chunked_prefill_ws(const ps_paged_problem* pr, void* workspace, int64_t w
     return fail(PS_ERR_WORKSPACE, "prefill workspace must be >= 256 bytes, 256-byte aligned");
   int rc = validate_problem(pr, false);
   if (rc != PS_OK) return rc;
+  if (pr->kv_cache_dtype != PS_KV_AUTO)
+    return fail(PS_ERR_UNSUPPORTED, "chunked prefill over an fp8 cache is not built");
   if (pr->num_seqs == 0 || pr->num_tokens == 0) return PS_OK;
   if (pr->num_tokens < 0 || pr->num_tokens > INT32_MAX)
     return fail(PS_ERR_INVALID_ARGUMENT, "num_tokens out of range");
@@ -610,6 +672,8 @@ int dcp_impl(const ps_dcp_problem* dp, int phase, void* workspace, int64_t works
   g.num_q_heads = hq_local * dp->world;
   int rc = validate_problem(&g, true);
   if (rc != PS_OK) return rc;
+  if (lp.kv_cache_dtype != PS_KV_AUTO)
+    return fail(PS_ERR_UNSUPPORTED, "DCP decode over an fp8 cache is not built");
   if (!lp.new_key || !lp.new_value || !lp.slot_mapping)
     return fail(PS_ERR_INVALID_ARGUMENT, "DCP decode needs new_key, new_value and slot_mapping");
   if (!aligned(lp.new_key, 16) || !aligned(lp.new_value, 16) || lp.new_key_stride_token % 8 ||

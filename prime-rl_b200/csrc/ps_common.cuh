@@ -6,6 +6,7 @@
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <cuda_fp8.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -170,6 +171,30 @@ __device__ __forceinline__ float warp_sum_xor_4_8_16(float v) {
   v += __shfl_xor_sync(0xffffffffu, v, 8);
   v += __shfl_xor_sync(0xffffffffu, v, 16);
   return v;
+}
+
+// ---------------------------------------------------------------- fp8 (e4m3)
+// Two e4m3 codes (bits 0-7, 8-15 of v) to an f16x2 (low half from bits 0-7).
+// Every e4m3 value is exact in f16.
+__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t v) {
+  const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(v & 0xffffu), __NV_E4M3);
+  return static_cast<uint32_t>(h.x) | (static_cast<uint32_t>(h.y) << 16);
+}
+
+// Eight model-dtype elements (a 16-byte row piece) to e4m3(x / scale): the
+// quotient rounded to fp32, then to the nearest e4m3 (ties to even),
+// saturating at +-448.
+template <bool kBF16>
+__device__ __forceinline__ uint2 quantize8_e4m3(uint4 v, float scale) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  uint32_t q[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = unpack2<kBF16>(w[i]);
+    q[i] = __nv_cvt_float2_to_fp8x2(make_float2(__fdiv_rn(f.x, scale), __fdiv_rn(f.y, scale)),
+                                    __NV_SATFINITE, __NV_E4M3);
+  }
+  return make_uint2(q[0] | (q[1] << 16), q[2] | (q[3] << 16));
 }
 
 __device__ __forceinline__ void set_status(int32_t* status, int bits) {

@@ -64,6 +64,9 @@ struct DecodeParams {
   const int32_t* cas_group_pages;  // [cas_max_groups] shared 16-token pages
   int32_t cas_max_groups;
   int32_t* pre_counters;           // [num_seqs * num_kv_heads] prefix-segment split counters
+  // fp8 (e4m3) cache: per-tensor dequantization scales (device; nullptr = 1)
+  const float* k_scale;
+  const float* v_scale;
 };
 
 // Static sizing of the decode kernel, shared by the workspace-size query.
@@ -117,9 +120,12 @@ int ps_set_last_error(int code, const char* msg);
 int ps_launch_kv_append(const ps::AppendArgs& a, int vec, int sm_count, cudaStream_t stream);
 
 // Returns a cudaError_t value.
+// fp8_cache: K/V caches of e4m3 codes (plain decode only)
 int ps_launch_paged_decode(const ps::DecodeParams& p, const CUtensorMap& kmap,
                            const CUtensorMap& vmap, int dtype_bf16, int sm_count,
-                           cudaStream_t stream);
+                           cudaStream_t stream, int fp8_cache = 0);
+int ps_launch_kv_append_fp8(const ps::AppendArgs& a, const float* k_scale, const float* v_scale,
+                            int dtype_bf16, int sm_count, cudaStream_t stream);
 
 int64_t ps_decode_partial_slots(int num_seqs, int num_kv_heads, int sm_count, int cascade);
 

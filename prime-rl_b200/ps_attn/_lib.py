@@ -28,13 +28,17 @@ PS_DTYPE_FP16 = 0
 PS_DTYPE_BF16 = 1
 PS_DTYPE_FP32 = 2
 
-ABI_VERSION = 1
+PS_KV_AUTO = 0
+PS_KV_FP8_E4M3 = 1
+
+ABI_VERSION = 2
 
 # every symbol include/ps_attn.h declares
 EXPORTED_SYMBOLS = (
     "ps_abi_version",
     "ps_last_error",
     "ps_kv_append",
+    "ps_kv_append_fp8",
     "ps_paged_decode_workspace_size",
     "ps_paged_decode",
     "ps_chunked_prefill",
@@ -107,6 +111,9 @@ class PagedProblem(ctypes.Structure):
         ("new_value_stride_token", ctypes.c_int64),
         ("new_value_stride_head", ctypes.c_int64),
         ("slot_mapping", ctypes.c_void_p),
+        ("kv_cache_dtype", ctypes.c_int32),
+        ("k_scale", ctypes.c_void_p),
+        ("v_scale", ctypes.c_void_p),
     ]
 
 
@@ -181,6 +188,14 @@ def _declare(lib):
         c.c_void_p, c.c_void_p, c.c_int64, c.c_int64, c.c_int64, c.c_int64,  # caches
         c.c_void_p, c.c_int64, c.c_int, c.c_int, c.c_int, c.c_int,  # slots, shape
         c.c_void_p, c.c_void_p,  # status, stream
+    ]
+    lib.ps_kv_append_fp8.restype = c.c_int
+    lib.ps_kv_append_fp8.argtypes = [
+        c.c_void_p, c.c_int64, c.c_int64,  # key
+        c.c_void_p, c.c_int64, c.c_int64,  # value
+        c.c_void_p, c.c_void_p, c.c_int64, c.c_int64, c.c_int64, c.c_int64,  # caches
+        c.c_void_p, c.c_int64, c.c_int32, c.c_int32, c.c_int32, c.c_int32,  # slots, shape, dtype
+        c.c_void_p, c.c_void_p, c.c_void_p, c.c_void_p,  # scales, status, stream
     ]
     lib.ps_paged_decode_workspace_size.restype = c.c_int64
     lib.ps_paged_decode_workspace_size.argtypes = [c.c_int32] * 4

@@ -41,21 +41,46 @@ def _require_cuda(*tensors):
             raise ValueError("ps_attn ops take CUDA tensors only (no CPU path)")
 
 
+FP8_CACHE_DTYPES = (torch.uint8, torch.float8_e4m3fn)
+
+
+def is_fp8_cache(cache: torch.Tensor) -> bool:
+    """An fp8 (e4m3) KV cache: uint8 codes or torch.float8_e4m3fn."""
+    return cache.dtype in FP8_CACHE_DTYPES
+
+
+def _scale_ptr(scale):
+    if scale is None:
+        return None
+    if scale.dtype != torch.float32 or not scale.is_cuda or scale.numel() != 1:
+        raise ValueError("k_scale / v_scale must be one-element CUDA float32 tensors")
+    return scale.data_ptr()
+
+
 def kv_append(key: torch.Tensor, value: torch.Tensor, key_cache: torch.Tensor,
               value_cache: torch.Tensor, slot_mapping: torch.Tensor,
-              status: torch.Tensor | None = None) -> None:
+              status: torch.Tensor | None = None, k_scale: torch.Tensor | None = None,
+              v_scale: torch.Tensor | None = None) -> None:
     """Write ``key``/``value`` rows into the paged cache at ``slot_mapping``.
 
     key, value: [T', Hkv, D] (T' >= len(slot_mapping)); key_cache,
     value_cache: [num_blocks, block_size, Hkv, D]; slot_mapping: int64 [T].
-    Negative slots are skipped.  Bit-exact copy.
+    Negative slots are skipped.  Bit-exact copy; for an fp8 cache (uint8 or
+    float8_e4m3fn) the rows are stored as e4m3(x / k_scale) and
+    e4m3(x / v_scale) (``reshape_and_cache_flash`` with kv_cache_dtype "fp8";
+    scales: one-element float32 device tensors, None = 1).
     """
     lib = _lib.load()
     _require_cuda(key, value, key_cache, value_cache, slot_mapping)
     if slot_mapping.dtype != torch.int64:
         raise ValueError("slot_mapping must be int64")
-    if key.dtype != key_cache.dtype or value.dtype != value_cache.dtype or key.dtype != value.dtype:
-        raise ValueError("key/value/cache dtypes must match (no fp8 cache in this build)")
+    fp8 = is_fp8_cache(key_cache)
+    if fp8:
+        if value_cache.dtype != key_cache.dtype or key.dtype != value.dtype or \
+                key.dtype not in (torch.float16, torch.bfloat16):
+            raise ValueError("fp8 cache: fp16/bf16 key and value rows, both caches fp8")
+    elif key.dtype != key_cache.dtype or value.dtype != value_cache.dtype or key.dtype != value.dtype:
+        raise ValueError("key/value/cache dtypes must match")
     if key_cache.stride() != value_cache.stride() or key_cache.shape != value_cache.shape:
         raise ValueError("key_cache and value_cache must have the same shape and strides")
     if key.stride(-1) != 1 or value.stride(-1) != 1 or key_cache.stride(-1) != 1:
@@ -68,6 +93,17 @@ def kv_append(key: torch.Tensor, value: torch.Tensor, key_cache: torch.Tensor,
     nb, bs, hkv, d = key_cache.shape
     if key.shape[1:] != (hkv, d) or value.shape[1:] != (hkv, d):
         raise ValueError(f"key/value shape {tuple(key.shape)} does not match cache {tuple(key_cache.shape)}")
+    if fp8:
+        _lib.check(lib.ps_kv_append_fp8(
+            key.data_ptr(), key.stride(0), key.stride(1),
+            value.data_ptr(), value.stride(0), value.stride(1),
+            key_cache.data_ptr(), value_cache.data_ptr(),
+            key_cache.stride(0), key_cache.stride(1), key_cache.stride(2), nb,
+            slot_mapping.data_ptr(), T, hkv, d, bs, _DTYPES[key.dtype],
+            _scale_ptr(k_scale), _scale_ptr(v_scale),
+            status.data_ptr() if status is not None else None,
+            _stream_ptr(key.device)))
+        return
     _lib.check(lib.ps_kv_append(
         key.data_ptr(), key.stride(0), key.stride(1),
         value.data_ptr(), value.stride(0), value.stride(1),
@@ -278,11 +314,15 @@ def cascade_plan(block_table: torch.Tensor, seq_lens: torch.Tensor, num_q_heads:
 
 
 def _problem(q, key_cache, value_cache, block_table, seq_lens, query_start_loc,
-             softmax_scale, out, lse, status=None) -> _lib.PagedProblem:
+             softmax_scale, out, lse, status=None, k_scale=None, v_scale=None) -> _lib.PagedProblem:
     _require_cuda(q, key_cache, value_cache, block_table, seq_lens, out, query_start_loc, lse)
     if q.dtype not in (torch.float16, torch.bfloat16):
         raise ValueError(f"attention dtype {q.dtype} unsupported (fp16/bf16)")
-    if key_cache.dtype != q.dtype or value_cache.dtype != q.dtype or out.dtype != q.dtype:
+    fp8 = is_fp8_cache(key_cache)
+    if fp8:
+        if value_cache.dtype != key_cache.dtype or out.dtype != q.dtype:
+            raise ValueError("fp8 cache: both caches fp8, out in the query dtype")
+    elif key_cache.dtype != q.dtype or value_cache.dtype != q.dtype or out.dtype != q.dtype:
         raise ValueError("q, caches and out must share one dtype")
     if key_cache.stride() != value_cache.stride() or key_cache.shape != value_cache.shape:
         raise ValueError("key_cache and value_cache must have the same shape and strides")
@@ -329,6 +369,10 @@ def _problem(q, key_cache, value_cache, block_table, seq_lens, query_start_loc,
         if status.dtype != torch.int32 or not status.is_cuda:
             raise ValueError("status must be a CUDA int32 tensor")
         pr.status = status.data_ptr()
+    if fp8:
+        pr.kv_cache_dtype = _lib.PS_KV_FP8_E4M3
+        pr.k_scale = _scale_ptr(k_scale)
+        pr.v_scale = _scale_ptr(v_scale)
     return pr
 
 
@@ -339,7 +383,8 @@ def paged_decode(q: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Te
                  workspace: DecodeWorkspace | None = None,
                  new_key: torch.Tensor | None = None, new_value: torch.Tensor | None = None,
                  slot_mapping: torch.Tensor | None = None,
-                 cascade: CascadePlan | None = None) -> torch.Tensor:
+                 cascade: CascadePlan | None = None, k_scale: torch.Tensor | None = None,
+                 v_scale: torch.Tensor | None = None) -> torch.Tensor:
     """Decode attention, one query row per sequence, written into ``out``.
 
     q/out: [T, Hq, D]; caches [num_blocks, block_size, Hkv, D]; block_table
@@ -354,6 +399,10 @@ def paged_decode(q: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Te
     ``cascade``: a :class:`CascadePlan` built by :func:`cascade_plan` for this
     batch; shared prefixes are then read once per group pass (same outputs).
     The workspace must then be a cascade workspace.
+
+    fp8 caches (uint8 codes or float8_e4m3fn): attention over code * k_scale
+    and code * v_scale (one-element float32 device tensors, None = 1); the
+    fused append stores e4m3(x / scale).
     """
     lib = _lib.load()
     B = seq_lens.shape[0]
@@ -365,7 +414,7 @@ def paged_decode(q: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Te
     if cascade is not None and cascade.num_seqs != B:
         raise ValueError(f"cascade plan built for {cascade.num_seqs} sequences, call has {B}")
     pr = _problem(q, key_cache, value_cache, block_table, seq_lens, query_start_loc,
-                  softmax_scale, out, lse)
+                  softmax_scale, out, lse, k_scale=k_scale, v_scale=v_scale)
     if new_key is not None:
         _require_cuda(new_key, new_value, slot_mapping)
         if new_value is None or slot_mapping is None:
@@ -373,7 +422,7 @@ def paged_decode(q: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Te
         if slot_mapping.dtype != torch.int64 or not slot_mapping.is_contiguous():
             raise ValueError("slot_mapping must be contiguous int64")
         if new_key.dtype != q.dtype or new_value.dtype != q.dtype:
-            raise ValueError("new key/value must have the cache dtype")
+            raise ValueError("new key/value must have the query dtype")
         hkv, d = key_cache.shape[2], key_cache.shape[3]
         if new_key.shape[1:] != (hkv, d) or new_value.shape[1:] != (hkv, d):
             raise ValueError("new key/value shape does not match the cache")
