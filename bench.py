@@ -188,6 +188,20 @@ def run_ours(args):
     out = torch.empty_like(batch.q)
     lse = torch.empty(hq, B, dtype=torch.float32, device=dev)
     kc, vc = batch.kv_cache[0], batch.kv_cache[1]
+    skw = {}  # fp8 cache: dequantization scales
+    if args.kv_fp8:
+        # e4m3 codes of the synthetic N(0,1) cache at scale 1/64 (|x| < 7 fits
+        # in 448), quantized a slab of blocks at a time
+        scale = torch.tensor(1.0 / 64.0, dtype=torch.float32, device=dev)
+        codes = torch.empty(batch.kv_cache.shape, dtype=torch.uint8, device=dev)
+        step_nb = 4096
+        for i in range(0, batch.kv_cache.shape[1], step_nb):
+            codes[:, i:i + step_nb] = (batch.kv_cache[:, i:i + step_nb].float() / scale).to(
+                torch.float8_e4m3fn).view(torch.uint8)
+        batch.kv_cache = codes
+        kc, vc = codes[0], codes[1]
+        skw = dict(k_scale=scale, v_scale=scale)
+        torch.cuda.empty_cache()
     mixed = cfg == 4
     nd = B
     gathered = None
@@ -219,7 +233,7 @@ def run_ours(args):
             ops.paged_decode(batch.q, kc, vc, batch.block_table, batch.seq_lens,
                              batch.softmax_scale, out, lse=lse,
                              query_start_loc=batch.query_start_loc, workspace=ws, cascade=plan,
-                             **fkw)
+                             **fkw, **skw)
             return
         ops.paged_decode(batch.q[:nd], kc, vc, batch.block_table[:nd], batch.seq_lens[:nd],
                          batch.softmax_scale, out[:nd], workspace=ws, **fkw)
@@ -327,7 +341,7 @@ def run_ours(args):
     e2e = None if args.quick else run_e2e(batch, ws, dev, args.steps, world,
                                           nd=nd if mixed else None,
                                           replicas=1 if sharded else world, fused=fused,
-                                          cascade=cascade)
+                                          cascade=cascade, scales=skw)
 
     ms = elapsed_ms / args.steps
     tokens_per_step = batch.num_tokens  # every rank produces all tokens (its heads when sharded)
@@ -344,11 +358,12 @@ def run_ours(args):
         qo_bytes = B * hq * 128 * 2 * batch.q.element_size()
         meta_bytes = batch.block_table.numel() * 4 + B * 4 * 2
     # a fused append also reads the new K/V rows and writes them into the cache
-    app_bytes = (nd * hkv * 128 * 2 * batch.kv_cache.element_size() * 2) if fused else 0
+    app_bytes = (nd * hkv * 128 * 2 * (batch.key.element_size() + batch.kv_cache.element_size())
+                 if fused else 0)
     decode_bytes = kv_bytes + qo_bytes + meta_bytes + app_bytes
     step_bytes = workloads.hbm_bytes(batch)
     achieved = decode_bytes / (decode_ms / 1e3) / 1e9
-    traffic = profile_traffic(f"paged_decode_cfg{cfg}")
+    traffic = None if args.kv_fp8 else profile_traffic(f"paged_decode_cfg{cfg}")
     res = {
         "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
@@ -362,6 +377,7 @@ def run_ours(args):
                             (f"batch replicas x{world}" if world > 1 else "single GPU")),
             "l2": "inputs larger than L2 (KV pool > 126 MB); no flush",
             "cuda_graph": use_graph,
+            "kv_cache_dtype": "fp8_e4m3 (per-tensor scale)" if args.kv_fp8 else "bf16",
         },
         "hbm_gbs_step": round(step_bytes / (ms / 1e3) / 1e9, 1),
         "hbm_frac_of_8tbs_step": round(step_bytes / (ms / 1e3) / 1e9 / NOMINAL_HBM_GBS, 4),
@@ -561,7 +577,7 @@ def run_dcp(args):
         dist.destroy_process_group()
 
 
-def run_e2e(batch, ws, dev, steps, world, nd=None, replicas=1, fused=True, cascade=False):
+def run_e2e(batch, ws, dev, steps, world, nd=None, replicas=1, fused=True, cascade=False, scales=None):
     """Same step through the public ops with per-step host->device inputs
     (pinned) and the device->host read of the attention output.  ``nd``:
     number of leading decode sequences of a mixed batch (the rest prefill)."""
@@ -595,7 +611,7 @@ def run_e2e(batch, ws, dev, steps, world, nd=None, replicas=1, fused=True, casca
                                  plan=plan)
             ops.paged_decode(dev_in["q"], kc, vc, dev_in["block_table"], dev_in["seq_lens"],
                              batch.softmax_scale, out, query_start_loc=dev_in["query_start_loc"],
-                             workspace=ws, cascade=plan, **fkw)
+                             workspace=ws, cascade=plan, **fkw, **(scales or {}))
         else:
             ops.paged_decode(dev_in["q"][:nd], kc, vc, dev_in["block_table"][:nd],
                              dev_in["seq_lens"][:nd], batch.softmax_scale, out[:nd], workspace=ws,
@@ -744,6 +760,8 @@ def main():
                     help="config 3: shared-prefix (cascade) decode with a per-step plan")
     ap.add_argument("--dcp", action="store_true",
                     help="config 5 under decode context parallelism (tokens sharded, not heads)")
+    ap.add_argument("--kv-fp8", action="store_true",
+                    help="decode configs over an fp8 (e4m3) KV cache, fused quantizing append")
     ap.add_argument("--interleave", type=int, default=1,
                     help="DCP: consecutive positions per rank (vLLM cp_kv_cache_interleave_size)")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
@@ -753,10 +771,12 @@ def main():
     if args.impl == "reference":
         run_reference(args)
     elif args.dcp:
-        if args.config not in (2, 3, 5):
-            ap.error("--dcp takes a decode config (2, 3 or 5)")
+        if args.config not in (2, 3, 5) or args.kv_fp8:
+            ap.error("--dcp takes a decode config (2, 3 or 5) with a 16-bit cache")
         run_dcp(args)
     else:
+        if args.kv_fp8 and (args.config == 4 or args.cascade or args.unfused):
+            ap.error("--kv-fp8: plain decode configs (2, 3, 5) with the fused append")
         run_ours(args)
 
 
