@@ -441,7 +441,11 @@ __host__ __device__ constexpr int decode_qslot_bytes() {
 // (4 with 8 query columns; 3 with 16, whose query slots are twice the size).
 template <bool kFP8, int kQNT>
 __host__ __device__ constexpr int decode_stages() {
-  return kFP8 ? (kQNT == 1 ? 2 * kDecodeStages : kDecodeStages + 1) : kDecodeStages;
+  return kFP8 ? kDecodeFp8Stages : kDecodeStages;
+}
+template <bool kFP8>
+__host__ __device__ constexpr int decode_warps() {
+  return kFP8 ? kDecodeFp8Warps : kDecodeWarps;
 }
 template <bool kFP8>
 __host__ __device__ constexpr int decode_stage_bytes() {
@@ -452,8 +456,8 @@ template <int kQNT, bool kFP8 = false>
 __host__ __device__ constexpr int decode_smem_bytes_before_table() {
   // stages | per-warp query slots | mbarriers
   constexpr int D = decode_stages<kFP8, kQNT>();
-  return kDecodeWarps * D * decode_stage_bytes<kFP8>() + kDecodeWarps * D * decode_qslot_bytes<kQNT>() +
-         kDecodeWarps * D * 8;
+  constexpr int W = decode_warps<kFP8>();
+  return W * D * decode_stage_bytes<kFP8>() + W * D * decode_qslot_bytes<kQNT>() + W * D * 8;
 }
 
 // Own segment of sequence b (cascade modes): its split geometry in the list.
@@ -1005,7 +1009,7 @@ __device__ __forceinline__ int stream_range(const DecodeParams& p, const CUtenso
 }
 
 // Exclusive scan over the block of one int per thread; *total gets the sum.
-// s_warp: kDecodeWarps ints of shared memory.  Contains __syncthreads.
+// s_warp: one int per warp of the block.  Contains __syncthreads.
 __device__ __forceinline__ int block_exclusive_scan(int v, int* s_warp, int* total) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   int incl = v;
@@ -1017,7 +1021,8 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* s_warp, int* tot
   if (lane == 31) s_warp[warp] = incl;
   __syncthreads();
   int off = 0, tot = 0;
-  for (int w = 0; w < kDecodeWarps; ++w) {
+  const int nw = static_cast<int>(blockDim.x >> 5);
+  for (int w = 0; w < nw; ++w) {
     const int x = s_warp[w];
     if (w < warp) off += x;
     tot += x;
@@ -1037,7 +1042,7 @@ __device__ __forceinline__ int own_pages_of(const DecodeParams& p, int b, int su
 }
 
 template <bool kBF16, int NT, bool kCascade, bool kFP8>
-__global__ void __launch_bounds__(kDecodeWarps * 32, kDecodeCtasPerSm)
+__global__ void __launch_bounds__(decode_warps<kFP8>() * 32, kDecodeCtasPerSm)
     paged_decode_kernel(const __grid_constant__ DecodeParams p,
                         const __grid_constant__ CUtensorMap kmap,
                         const __grid_constant__ CUtensorMap vmap) {
@@ -1049,11 +1054,12 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, kDecodeCtasPerSm)
   // 1024-byte alignment for the 128B-swizzled TMA destinations.
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  uint8_t* qslots = smem + kDecodeWarps * D * SB;
+  constexpr int W = decode_warps<kFP8>();
+  uint8_t* qslots = smem + W * D * SB;
   uint64_t* bars =
-      reinterpret_cast<uint64_t*>(qslots + kDecodeWarps * D * decode_qslot_bytes<kQNT>());
-  int* prefix = reinterpret_cast<int*>(bars + kDecodeWarps * D);
-  __shared__ int s_warp_tot[kDecodeWarps];
+      reinterpret_cast<uint64_t*>(qslots + W * D * decode_qslot_bytes<kQNT>());
+  int* prefix = reinterpret_cast<int*>(bars + W * D);
+  __shared__ int s_warp_tot[W];
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -1200,7 +1206,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, kDecodeCtasPerSm)
   if (tid == 0 && any_bad) set_status(p.status, PS_DEV_BAD_METADATA);
 
   const int64_t total = tb.pre_total + static_cast<int64_t>(total_own) * Hkv;
-  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * kDecodeWarps;
+  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * W;
   const int64_t total_cost = list_cost(tb, total);
   tb.Qc = max(static_cast<int64_t>(max(tb.wp, tb.wo)),
               total_cost > 0 ? (total_cost + nwarps - 1) / nwarps : 1);
@@ -1219,7 +1225,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, kDecodeCtasPerSm)
     if (p.lse) p.lse[qh * p.lse_sh + qrow * p.lse_st] = -INFINITY;
   }
 
-  const int64_t gw = static_cast<int64_t>(blockIdx.x) * kDecodeWarps + warp;
+  const int64_t gw = static_cast<int64_t>(blockIdx.x) * W + warp;
   const int64_t start = min(total, list_at_cost(tb, gw * tb.Qc));
   const int64_t end = min(total, list_at_cost(tb, (gw + 1) * tb.Qc));
   if (start >= end) return;
@@ -1267,7 +1273,7 @@ static int launch_t(const DecodeParams& p, const CUtensorMap& kmap, const CUtens
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(sm_count * kDecodeCtasPerSm);
-  cfg.blockDim = dim3(kDecodeWarps * 32);
+  cfg.blockDim = dim3(decode_warps<kFP8>() * 32);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -1281,11 +1287,12 @@ static int launch_t(const DecodeParams& p, const CUtensorMap& kmap, const CUtens
 
 }  // namespace ps
 
-int64_t ps_decode_partial_slots(int num_seqs, int num_kv_heads, int sm_count, int cascade) {
+int64_t ps_decode_partial_slots(int num_seqs, int num_kv_heads, int sm_count, int cascade, int fp8) {
   // slot = global warp index + unit index; units: (sequence, kv head) and, in
   // cascade mode, at most one prefix segment per (sequence, kv head) more
   const int64_t units = static_cast<int64_t>(num_seqs) * num_kv_heads * (cascade ? 2 : 1);
-  return static_cast<int64_t>(sm_count) * ps::kDecodeCtasPerSm * ps::kDecodeWarps + units;
+  return static_cast<int64_t>(sm_count) * ps::kDecodeCtasPerSm *
+             (fp8 ? ps::kDecodeFp8Warps : ps::kDecodeWarps) + units;
 }
 
 int ps_launch_paged_decode(const ps::DecodeParams& p, const CUtensorMap& kmap,

@@ -54,9 +54,16 @@ void* scratch_on_current_device() {
 extern "C" int ps_paged_decode_static_scratch(const ps_paged_problem* pr, void* stream) {
   if (pr == nullptr) return ps_paged_decode(pr, nullptr, 0, stream);  // reports the NULL problem
   if (pr->num_seqs <= 0) return ps_paged_decode(pr, nullptr, 0, stream);
-  const int64_t need = ps_paged_decode_workspace_size(pr->num_seqs, pr->num_q_heads,
-                                                      pr->num_kv_heads, pr->head_size);
-  if (need < 0) return PS_ERR_INVALID_ARGUMENT;  // message already set
+  if (ps_paged_decode_workspace_size(pr->num_seqs, pr->num_q_heads, pr->num_kv_heads,
+                                     pr->head_size) < 0)
+    return PS_ERR_INVALID_ARGUMENT;  // message already set
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return ps_set_last_error(PS_ERR_CUDA, "no CUDA device");
+  // the scratch this problem's kernel needs (16-bit and fp8 caches differ)
+  const int64_t need = ps_decode_workspace_bytes(pr->num_seqs, pr->num_q_heads, pr->num_kv_heads, sms, 0,
+                                                 pr->kv_cache_dtype == PS_KV_FP8_E4M3 ? 1 : 0);
   if (need > kStaticScratchBytes)
     return ps_set_last_error(PS_ERR_WORKSPACE,
                              "problem needs more decode scratch than the library's static 16 MiB "

@@ -128,10 +128,11 @@ struct DecodeWorkspaceLayout {
 };
 
 DecodeWorkspaceLayout decode_layout(int num_seqs, int num_q_heads, int num_kv_heads, int sm_count,
-                                    bool cascade) {
+                                    bool cascade, bool fp8 = false) {
   const int group = num_q_heads / num_kv_heads;
   const int kg = (group <= 8 && !cascade) ? 8 : 16;
-  const int64_t slots = ps_decode_partial_slots(num_seqs, num_kv_heads, sm_count, cascade ? 1 : 0);
+  const int64_t slots =
+      ps_decode_partial_slots(num_seqs, num_kv_heads, sm_count, cascade ? 1 : 0, fp8 ? 1 : 0);
   const int64_t counter_bytes = static_cast<int64_t>(ps::kDecodeMaxSeqs) * num_kv_heads * 4;
   DecodeWorkspaceLayout l;
   l.counters_off = 256;
@@ -209,7 +210,7 @@ int decode_impl(const ps_paged_problem* pr, const void* plan, int64_t plan_bytes
   const bool fp8 = pr->kv_cache_dtype == PS_KV_FP8_E4M3;
   if (fp8 && cascade) return fail(PS_ERR_UNSUPPORTED, "cascade decode over an fp8 cache is not built");
   const DecodeWorkspaceLayout lay =
-      decode_layout(pr->num_seqs, pr->num_q_heads, pr->num_kv_heads, sms, cascade);
+      decode_layout(pr->num_seqs, pr->num_q_heads, pr->num_kv_heads, sms, cascade, fp8);
   if (!workspace || workspace_bytes < lay.total || !aligned(workspace, 256))
     return fail(PS_ERR_WORKSPACE, "decode workspace must be >= %lld bytes, 256-byte aligned",
                 static_cast<long long>(lay.total));
@@ -246,7 +247,8 @@ int decode_impl(const ps_paged_problem* pr, const void* plan, int64_t plan_bytes
   p.status = reinterpret_cast<int32_t*>(ws);
   p.counters = reinterpret_cast<int32_t*>(ws + lay.counters_off);
   p.part = reinterpret_cast<float*>(ws + lay.part_off);
-  p.num_part_slots = ps_decode_partial_slots(pr->num_seqs, pr->num_kv_heads, sms, cascade ? 1 : 0);
+  p.num_part_slots =
+      ps_decode_partial_slots(pr->num_seqs, pr->num_kv_heads, sms, cascade ? 1 : 0, fp8 ? 1 : 0);
   p.pre_counters = reinterpret_cast<int32_t*>(ws + lay.pre_counters_off);
   p.cas_num_groups = nullptr;
   p.cas_seq_group = p.cas_group_first = p.cas_group_size = p.cas_group_pages = nullptr;
@@ -291,6 +293,11 @@ int decode_impl(const ps_paged_problem* pr, const void* plan, int64_t plan_bytes
 }  // namespace
 
 int ps_set_last_error(int code, const char* msg) { return fail(code, "%s", msg); }
+
+int64_t ps_decode_workspace_bytes(int num_seqs, int num_q_heads, int num_kv_heads, int sm_count,
+                                  int cascade, int fp8) {
+  return decode_layout(num_seqs, num_q_heads, num_kv_heads, sm_count, cascade != 0, fp8 != 0).total;
+}
 
 extern "C" {
 
@@ -415,7 +422,10 @@ int64_t ps_paged_decode_workspace_size(int32_t num_seqs, int32_t num_q_heads,
     fail(PS_ERR_CUDA, "no CUDA device");
     return -1;
   }
-  return decode_layout(num_seqs, num_q_heads, num_kv_heads, sms, false).total;
+  // large enough for the 16-bit-cache and the fp8-cache kernels
+  const int64_t a = decode_layout(num_seqs, num_q_heads, num_kv_heads, sms, false, false).total;
+  const int64_t b = decode_layout(num_seqs, num_q_heads, num_kv_heads, sms, false, true).total;
+  return a > b ? a : b;
 }
 
 int ps_paged_decode(const ps_paged_problem* pr, void* workspace, int64_t workspace_bytes,

@@ -80,7 +80,18 @@ struct DecodeParams {
 #ifndef PS_DECODE_CTAS_PER_SM
 #define PS_DECODE_CTAS_PER_SM 1
 #endif
+#ifndef PS_DECODE_FP8_WARPS
+#define PS_DECODE_FP8_WARPS 12
+#endif
+#ifndef PS_DECODE_FP8_STAGES
+#define PS_DECODE_FP8_STAGES 2
+#endif
 constexpr int kDecodeWarps = PS_DECODE_WARPS;           // warps per CTA
+// fp8 caches: a page-head is half the bytes and the per-warp instruction
+// stream, not HBM, sets the pace, so more warps with fewer stages each
+constexpr int kDecodeFp8Warps = PS_DECODE_FP8_WARPS;
+constexpr int kDecodeFp8Stages = PS_DECODE_FP8_STAGES;
+constexpr int kDecodeMaxWarps = kDecodeWarps > kDecodeFp8Warps ? kDecodeWarps : kDecodeFp8Warps;
 constexpr int kDecodeStages = PS_DECODE_STAGES;         // pages in flight per warp
 constexpr int kDecodeCtasPerSm = PS_DECODE_CTAS_PER_SM; // persistent CTAs per SM
 constexpr int kDecodeMaxSeqs = 4096;                    // sequences per launch (prefix table in smem)
@@ -127,7 +138,12 @@ int ps_launch_paged_decode(const ps::DecodeParams& p, const CUtensorMap& kmap,
 int ps_launch_kv_append_fp8(const ps::AppendArgs& a, const float* k_scale, const float* v_scale,
                             int dtype_bf16, int sm_count, cudaStream_t stream);
 
-int64_t ps_decode_partial_slots(int num_seqs, int num_kv_heads, int sm_count, int cascade);
+// Split-record slots a decode launch may use: its warps plus one per unit.
+int64_t ps_decode_partial_slots(int num_seqs, int num_kv_heads, int sm_count, int cascade, int fp8 = 0);
+// Workspace bytes of the decode kernel a problem of this kind launches
+// (ps_paged_decode_workspace_size returns the largest over the kinds).
+int64_t ps_decode_workspace_bytes(int num_seqs, int num_q_heads, int num_kv_heads, int sm_count,
+                                  int cascade, int fp8);
 
 // Shared-prefix plan (cascade_plan.cu).  Plan buffer layout in int32 words,
 // Gm = max(1, num_seqs / 2):
