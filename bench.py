@@ -205,9 +205,16 @@ def run_ours(args):
     mixed = cfg == 4
     nd = B
     gathered = None
+    peer_gather = None
     if sharded:
         gathered = torch.empty(world, B, hq, 128, dtype=batch.q.dtype, device=dev)
         full_out = torch.empty(B, hq * world, 128, dtype=batch.q.dtype, device=dev)
+        if args.gather == "peer":
+            # head outputs exchanged over NVLink peer memory (ps_head_gather)
+            from ps_attn import sharding
+
+            shard = sharding.HeadShard(world, rank, hq * world, hkv * world)
+            peer_gather = sharding.PeerHeadGather.from_process_group(shard, B, batch.q.dtype, device=dev)
 
     fused = not args.unfused
 
@@ -229,6 +236,11 @@ def run_ours(args):
     fkw = dict(new_key=batch.key, new_value=batch.value, slot_mapping=batch.slot_mapping) if fused else {}
 
     def decode():
+        if peer_gather is not None:  # this rank's heads into its slab
+            peer_gather.decode(batch.q, kc, vc, batch.block_table, batch.seq_lens, batch.softmax_scale,
+                               full_out, lse=lse, query_start_loc=batch.query_start_loc, workspace=ws,
+                               **fkw, **skw)
+            return
         if not mixed:
             ops.paged_decode(batch.q, kc, vc, batch.block_table, batch.seq_lens,
                              batch.softmax_scale, out, lse=lse,
@@ -243,6 +255,9 @@ def run_ours(args):
                             batch.query_start_loc[nd:], batch.softmax_scale, out, workspace=ws)
 
     def gather():
+        if peer_gather is not None:
+            peer_gather.gather(B, full_out)
+            return
         import torch.distributed as dist
 
         dist.all_gather_into_tensor(gathered, out)
@@ -255,13 +270,15 @@ def run_ours(args):
         for _ in range(3):  # warm up before capture
             append()
             decode()
+            if peer_gather is not None:
+                gather()
         stream.synchronize()
         if mixed:
             prefill()
             stream.synchronize()
         if use_graph:
             fns = ([("append", append)] if (not fused or mixed or cascade) else []) + [("decode", decode)] + (
-                [("prefill", prefill)] if mixed else [])
+                [("prefill", prefill)] if mixed else []) + ([("gather", gather)] if peer_gather else [])
             for name, fn in fns:
                 g = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(g, stream=stream):
@@ -292,7 +309,10 @@ def run_ours(args):
             if ev is not None:
                 ev[3].record(stream)
         if sharded:
-            gather()
+            if use_graph and "gather" in graphs:
+                graphs["gather"].replay()
+            else:
+                gather()
 
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
@@ -373,7 +393,8 @@ def run_ours(args):
             "workload": CONFIG_NAMES[cfg], "num_seqs": B, "num_q_heads": hq * (world if sharded else 1),
             "num_kv_heads": hkv * (world if sharded else 1), "head_size": 128, "block_size": 16,
             "kv_tokens": batch.logical_tokens, "kv_pool_bytes": batch.kv_cache.numel() * batch.kv_cache.element_size(),
-            "parallelism": (f"kv-head tp{world} + NCCL all-gather" if sharded else
+            "parallelism": (f"kv-head tp{world} + " + ("NVLink peer-memory head gather (ps_head_gather)"
+                                                       if peer_gather else "NCCL all-gather") if sharded else
                             (f"batch replicas x{world}" if world > 1 else "single GPU")),
             "l2": "inputs larger than L2 (KV pool > 126 MB); no flush",
             "cuda_graph": use_graph,
@@ -382,7 +403,7 @@ def run_ours(args):
         "hbm_gbs_step": round(step_bytes / (ms / 1e3) / 1e9, 1),
         "hbm_frac_of_8tbs_step": round(step_bytes / (ms / 1e3) / 1e9 / NOMINAL_HBM_GBS, 4),
         "gpu_launches": ((3 if mixed else 2) - (1 if fused and not mixed else 0)
-                         + (1 if cascade else 0)) * args.steps,
+                         + (1 if cascade else 0) + (1 if peer_gather else 0)) * args.steps,
         "append_fused_into_decode": fused,
         "cascade": (None if not cascade else {
             "groups": int(plan.views()["num_groups"].item()),
@@ -413,6 +434,8 @@ def run_ours(args):
 
         dist.barrier()
         graphs.clear()
+        if peer_gather is not None:
+            peer_gather.close()  # after the barrier: no peer still reads this slab
         dist.destroy_process_group()
 
 
@@ -760,6 +783,8 @@ def main():
                     help="config 3: shared-prefix (cascade) decode with a per-step plan")
     ap.add_argument("--dcp", action="store_true",
                     help="config 5 under decode context parallelism (tokens sharded, not heads)")
+    ap.add_argument("--gather", default="peer", choices=["nccl", "peer"],
+                    help="config 5 on N GPUs: head outputs all-gathered by NCCL or over peer memory")
     ap.add_argument("--kv-fp8", action="store_true",
                     help="decode configs over an fp8 (e4m3) KV cache, fused quantizing append")
     ap.add_argument("--interleave", type=int, default=1,

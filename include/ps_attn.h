@@ -390,6 +390,41 @@ int ps_dcp_decode(const ps_dcp_problem* problem, void* workspace, int64_t worksp
 int ps_dcp_decode_phase(const ps_dcp_problem* problem, int32_t phase, void* workspace,
                         int64_t workspace_bytes, void* stream);
 
+/*
+ * Head all-gather of a KV-head-sharded decode over peer memory: the
+ * all_gather_into_tensor + permute that follows tensor-parallel attention
+ * (each rank owns KV heads [r*Hkv/world, ...) and their query heads), done by
+ * NVLink loads instead of NCCL.  Each rank's decode writes its rows
+ * [num_tokens, hq_local, 128] (2-byte elements, contiguous) into its own slab
+ * at byte offset PS_HEAD_GATHER_ROWS_OFFSET (ps_paged_decode with that `out`);
+ * ps_head_gather then writes every rank's rows into out[t, r*hq_local + j, :].
+ * Slabs: ps_dcp_slab_alloc of ps_head_gather_slab_bytes, mapped in the peers
+ * with ps_dcp_ipc_handle / ps_dcp_ipc_open, one per rank, reused by every
+ * call.  Two flag barriers per call (rows ready; rows pulled, so that no
+ * rank's next decode overwrites rows a peer still reads), bounded as in
+ * ps_dcp_decode: PS_DEV_WAIT_TIMEOUT in *status (required, device int32).
+ */
+#define PS_HEAD_GATHER_ROWS_OFFSET 256
+int64_t ps_head_gather_slab_bytes(int32_t max_tokens, int32_t hq_local);
+
+typedef struct {
+  int32_t world, rank;
+  int32_t num_tokens, hq_local;
+  int32_t max_tokens;             /* the slabs were sized for it */
+  int32_t dtype;                  /* PS_DTYPE_BF16 or PS_DTYPE_FP16 */
+  void* slabs[PS_DCP_MAX_WORLD];  /* every rank's slab, addressed from this GPU */
+  void* out;                      /* [num_tokens, world * hq_local, 128] */
+  int64_t out_stride_token, out_stride_head;
+  int32_t* status;
+} ps_head_gather_problem;
+
+int ps_head_gather(const ps_head_gather_problem* problem, void* stream);
+/* Split at the barriers, for one process playing every rank on one GPU:
+   phase 0 signals "rows ready", 1 pulls and signals "rows pulled", 2 waits
+   for every rank's "rows pulled".  Run phase k for every rank before phase
+   k+1 for any. */
+int ps_head_gather_phase(const ps_head_gather_problem* problem, int32_t phase, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -26,11 +26,8 @@
 // and rewrites its partials only after all ranks entered phase 0 of the next
 // call.
 //
-// Slab layout (identical on every rank, offsets from ps_dcp_layout):
-//   [0, 64)     int32 flags[2][8]: flags[ph][r] = last call epoch rank r
-//               signalled for phase ph (written by rank r, remotely)
-//   128         int32 epoch: calls completed on this rank (local)
-//   132         int32 done: combine CTAs finished in this call (local)
+// Slab layout (identical on every rank, offsets from dcp_layout):
+//   [0, 256)    the synchronisation header of peer_sync.cuh
 //   off_q       [max_tokens, hq_local, 128] query rows staged for the peers
 //   off_part    [max_tokens, hq_all, 128] partial outputs over the local context
 //   off_lse     [hq_all, max_tokens] fp32 partial LSEs (natural log)
@@ -39,84 +36,22 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include "peer_sync.cuh"
 #include "ps_common.cuh"
 #include "ps_launch.h"
 
 namespace ps {
 namespace {
 
-constexpr int kEpochWord = 32;   // byte 128
-constexpr int kDoneWord = 33;    // byte 132
-constexpr long long kDcpWaitNs = 1000000000LL;  // 1 s per barrier wait
+__device__ __forceinline__ int32_t call_epoch(const DcpArgs& a) { return peer::call_epoch(a.slab[a.rank]); }
 
-__device__ __forceinline__ int32_t* slab_words(char* slab) { return reinterpret_cast<int32_t*>(slab); }
-
-__device__ __forceinline__ long long global_ns() {
-  long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
-__device__ __forceinline__ void store_release_sys(int32_t* p, int32_t v) {
-  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-__device__ __forceinline__ int32_t load_acquire_sys(const int32_t* p) {
-  int32_t v;
-  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-__device__ __forceinline__ int32_t load_volatile(const int32_t* p) {
-  return *reinterpret_cast<const volatile int32_t*>(p);
-}
-
-// The epoch of the call in progress on this rank: one more than the calls
-// completed.  Read by every kernel of the call; advanced by the last combine
-// CTA, so it is stable for the whole call.
-__device__ __forceinline__ int32_t call_epoch(const DcpArgs& a) {
-  return load_volatile(slab_words(a.slab[a.rank]) + kEpochWord) + 1;
-}
-
-// Threads [0, world) of one CTA: publish "phase ph of call e done on this
-// rank" into every rank's flag array (own included).  Everything this rank
-// wrote for the phase was written by earlier kernels of the stream, which
-// completed before griddepcontrol.wait returned.
 __device__ __forceinline__ void signal_phase(const DcpArgs& a, int ph, int32_t e) {
-  const int r = threadIdx.x;
-  if (r < a.world) {
-    __threadfence_system();
-    store_release_sys(slab_words(a.slab[r]) + ph * 8 + a.rank, e);
-  }
+  peer::signal(a.slab, a.world, a.rank, ph, e);
 }
 
-// Every thread of the CTA returns whether all ranks signalled phase ph of
-// call e; threads [0, world) poll one rank's flag each, bounded by
-// kDcpWaitNs, after which the CTA reports PS_DEV_WAIT_TIMEOUT and returns
-// false (the caller skips the phase's reads of peer data).
+// false after a timeout: the caller skips the phase's reads of peer data
 __device__ __forceinline__ bool wait_phase(const DcpArgs& a, int ph, int32_t e) {
-  __shared__ int s_ok;
-  if (threadIdx.x == 0) s_ok = 1;
-  __syncthreads();
-  const int r = threadIdx.x;
-  if (r < a.world) {
-    const int32_t* f = slab_words(a.slab[a.rank]) + ph * 8 + r;
-    if (load_acquire_sys(f) < e) {
-      const long long t0 = global_ns();
-      while (load_acquire_sys(f) < e) {
-        // give up after kDcpWaitNs, or at once if a wait of this call (or an
-        // earlier one: the bit stays set until the workspace is zeroed) did
-        if (global_ns() - t0 > kDcpWaitNs || (load_volatile(a.status) & PS_DEV_WAIT_TIMEOUT)) {
-          set_status(a.status, PS_DEV_WAIT_TIMEOUT);
-          atomicAnd(&s_ok, 0);
-          break;
-        }
-        __nanosleep(64);
-      }
-    }
-  }
-  __syncthreads();
-  return s_ok != 0;
+  return peer::wait_all(a.slab[a.rank], a.world, ph, e, a.status);
 }
 
 __device__ __forceinline__ uint4 ld16(const char* p) { return *reinterpret_cast<const uint4*>(p); }
@@ -128,7 +63,7 @@ __device__ __forceinline__ void st16(char* p, uint4 v) { *reinterpret_cast<uint4
 // local context length of every sequence: the count of positions
 // p < seq_len - 1 (the new token excluded) with (p / I) % N == rank, as
 // vllm/v1/attention/backends/utils.py:857-894 (get_dcp_local_seq_lens) does.
-__global__ void __launch_bounds__(256) dcp_stage_kernel(const DcpArgs a) {
+__global__ void __launch_bounds__(256) dcp_stage_kernel(const __grid_constant__ DcpArgs a) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
   char* own = a.slab[a.rank];
   const int64_t gtid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -158,7 +93,7 @@ __global__ void __launch_bounds__(256) dcp_stage_kernel(const DcpArgs a) {
 // Publish phase `ph` of the current call to every rank (one CTA).  Used when
 // one process drives every rank of a group in turn; otherwise the gather and
 // combine kernels signal at their start.
-__global__ void dcp_signal_kernel(const DcpArgs a, int ph) {
+__global__ void dcp_signal_kernel(const __grid_constant__ DcpArgs a, int ph) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
   signal_phase(a, ph, call_epoch(a));
 }
@@ -167,7 +102,7 @@ __global__ void dcp_signal_kernel(const DcpArgs a, int ph) {
 // rank's slab (rank r's rows come from rank r's slab over NVLink), the
 // all_gather(query, dim=1) of flash_attn.py:907.  Four 16-byte loads in
 // flight per thread.
-__global__ void __launch_bounds__(256) dcp_gather_kernel(const DcpArgs a) {
+__global__ void __launch_bounds__(256) dcp_gather_kernel(const __grid_constant__ DcpArgs a) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int32_t e = call_epoch(a);
   if (a.signal_first && blockIdx.x == 0) signal_phase(a, 0, e);
@@ -208,7 +143,7 @@ __global__ void __launch_bounds__(256) dcp_gather_kernel(const DcpArgs a) {
 // rule.  All in fp32, rounded once to the output dtype.  Before waiting, the
 // CTAs append the new tokens this rank stores (slot >= 0) to its cache.
 template <bool kBF16>
-__global__ void __launch_bounds__(256) dcp_combine_kernel(const DcpArgs a) {
+__global__ void __launch_bounds__(256) dcp_combine_kernel(const __grid_constant__ DcpArgs a) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int32_t e = call_epoch(a);
   if (a.signal_first && blockIdx.x == 0) signal_phase(a, 1, e);
@@ -304,16 +239,7 @@ __global__ void __launch_bounds__(256) dcp_combine_kernel(const DcpArgs a) {
     }
   }
   // the last CTA out closes the call on this rank
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    int32_t* w = slab_words(a.slab[a.rank]);
-    __threadfence();
-    if (atomicAdd(w + kDoneWord, 1) == static_cast<int>(gridDim.x) - 1) {
-      w[kDoneWord] = 0;
-      __threadfence();
-      *reinterpret_cast<volatile int32_t*>(w + kEpochWord) = e;
-    }
-  }
+  if (peer::last_cta(a.slab[a.rank])) peer::close_call(a.slab[a.rank], e);
 }
 
 }  // namespace ps

@@ -847,3 +847,62 @@ int ps_dcp_decode_phase(const ps_dcp_problem* problem, int32_t phase, void* work
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------ head gather
+namespace {
+int head_gather_impl(const ps_head_gather_problem* hp, int which, void* stream) {
+  if (!hp) return fail(PS_ERR_INVALID_ARGUMENT, "problem is NULL");
+  if (hp->world < 1 || hp->world > PS_DCP_MAX_WORLD || hp->rank < 0 || hp->rank >= hp->world)
+    return fail(PS_ERR_INVALID_ARGUMENT, "world %d / rank %d invalid (world <= %d)", hp->world, hp->rank,
+                PS_DCP_MAX_WORLD);
+  if (hp->max_tokens < 1 || hp->num_tokens < 0 || hp->num_tokens > hp->max_tokens || hp->hq_local < 1)
+    return fail(PS_ERR_INVALID_ARGUMENT, "num_tokens %d / max_tokens %d / hq_local %d invalid",
+                hp->num_tokens, hp->max_tokens, hp->hq_local);
+  if (hp->dtype != PS_DTYPE_BF16 && hp->dtype != PS_DTYPE_FP16)
+    return fail(PS_ERR_UNSUPPORTED, "head gather moves 2-byte rows (dtype %d)", hp->dtype);
+  for (int r = 0; r < hp->world; ++r)
+    if (!hp->slabs[r] || !aligned(hp->slabs[r], 256))
+      return fail(PS_ERR_INVALID_ARGUMENT, "slab of rank %d is NULL or not 256-byte aligned", r);
+  if (!hp->out || !aligned(hp->out, 16) || hp->out_stride_token % 8 || hp->out_stride_head % 8)
+    return fail(PS_ERR_INVALID_ARGUMENT, "out base/strides must be 16-byte aligned");
+  if (!hp->status) return fail(PS_ERR_INVALID_ARGUMENT, "head gather needs a device status word");
+  if (hp->num_tokens == 0) return PS_OK;
+  const int sms = sm_count_current(nullptr);
+  if (sms <= 0) return fail(PS_ERR_CUDA, "no CUDA device");
+  ps::HeadGatherArgs a;
+  a.world = hp->world;
+  a.rank = hp->rank;
+  for (int r = 0; r < ps::kDcpMaxWorld; ++r)
+    a.slab[r] = r < hp->world ? static_cast<char*>(hp->slabs[r]) : nullptr;
+  a.num_tokens = hp->num_tokens;
+  a.hq_local = hp->hq_local;
+  a.out = static_cast<char*>(hp->out);
+  a.o_st = hp->out_stride_token * 2;
+  a.o_sh = hp->out_stride_head * 2;
+  a.status = hp->status;
+  a.mode = 0;
+  const int e = ps_launch_head_gather(a, which, sms, static_cast<cudaStream_t>(stream));
+  return e != 0 ? cuda_fail(static_cast<cudaError_t>(e), "head gather launch") : PS_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int64_t ps_head_gather_slab_bytes(int32_t max_tokens, int32_t hq_local) {
+  if (max_tokens < 1 || hq_local < 1) {
+    fail(PS_ERR_INVALID_ARGUMENT, "head gather slab size: bad shape");
+    return -1;
+  }
+  return round_up(PS_HEAD_GATHER_ROWS_OFFSET + static_cast<int64_t>(max_tokens) * hq_local * 256, 256);
+}
+
+int ps_head_gather(const ps_head_gather_problem* problem, void* stream) {
+  return head_gather_impl(problem, 0, stream);
+}
+
+int ps_head_gather_phase(const ps_head_gather_problem* problem, int32_t phase, void* stream) {
+  if (phase < 0 || phase > 2) return fail(PS_ERR_INVALID_ARGUMENT, "phase %d outside [0, 2]", phase);
+  return head_gather_impl(problem, phase + 1, stream);  // launcher: 1 signal, 2 pull, 3 finish
+}
+
+}  // extern "C"

@@ -225,8 +225,21 @@ struct DcpArgs {
   int32_t bf16;
   int32_t* status;
 };
+
+// Head all-gather over peer memory (KV-head-sharded decode).  Byte strides.
+constexpr int64_t kHeadGatherRowsOffset = 256;  // this rank's rows in its slab
+struct HeadGatherArgs {
+  int32_t world, rank;
+  char* slab[kDcpMaxWorld];
+  int32_t num_tokens, hq_local;
+  char* out;              // [T, world * hq_local, 128]
+  int64_t o_st, o_sh;
+  int32_t* status;
+  int32_t mode;           // set by the launcher
+};
 }  // namespace ps
 int ps_launch_dcp(const ps::DcpArgs& a, int which, int sm_count, cudaStream_t stream);
+int ps_launch_head_gather(const ps::HeadGatherArgs& a, int which, int sm_count, cudaStream_t stream);
 
 // vec: the 16-byte path (rows, strides and cos/sin rows 16-byte aligned,
 // head_size % 8 == 0, rotary_dim % 16 == 0)

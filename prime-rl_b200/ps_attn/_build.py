@@ -19,8 +19,9 @@ INCLUDE = REPO / "include"
 LIB_PATH = PKG_DIR / "libps_attn.so"
 
 SOURCES = ["ps_attn_api.cu", "kv_append.cu", "paged_decode.cu", "chunked_prefill.cu",
-           "paged_decode_static.cu", "cascade_plan.cu", "rope_append.cu", "dcp.cu"]
-HEADERS = ["ps_common.cuh", "ps_launch.h", "tcgen05.cuh"]
+           "paged_decode_static.cu", "cascade_plan.cu", "rope_append.cu", "dcp.cu",
+           "head_gather.cu"]
+HEADERS = ["ps_common.cuh", "ps_launch.h", "tcgen05.cuh", "peer_sync.cuh"]
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

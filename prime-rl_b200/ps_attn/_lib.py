@@ -57,7 +57,11 @@ EXPORTED_SYMBOLS = (
     "ps_dcp_ipc_close",
     "ps_dcp_decode",
     "ps_dcp_decode_phase",
+    "ps_head_gather_slab_bytes",
+    "ps_head_gather",
+    "ps_head_gather_phase",
 )
+PS_HEAD_GATHER_ROWS_OFFSET = 256
 
 PS_DCP_MAX_WORLD = 8
 PS_DCP_IPC_HANDLE_BYTES = 64
@@ -167,6 +171,24 @@ class DcpProblem(ctypes.Structure):
     ]
 
 
+class HeadGatherProblem(ctypes.Structure):
+    """Mirror of ``ps_head_gather_problem`` in include/ps_attn.h (same field order)."""
+
+    _fields_ = [
+        ("world", ctypes.c_int32),
+        ("rank", ctypes.c_int32),
+        ("num_tokens", ctypes.c_int32),
+        ("hq_local", ctypes.c_int32),
+        ("max_tokens", ctypes.c_int32),
+        ("dtype", ctypes.c_int32),
+        ("slabs", ctypes.c_void_p * 8),
+        ("out", ctypes.c_void_p),
+        ("out_stride_token", ctypes.c_int64),
+        ("out_stride_head", ctypes.c_int64),
+        ("status", ctypes.c_void_p),
+    ]
+
+
 def lib_path() -> Path:
     """The in-tree library, or a tuning variant named by ``PS_ATTN_LIB``."""
     override = os.environ.get("PS_ATTN_LIB")
@@ -233,6 +255,12 @@ def _declare(lib):
     lib.ps_dcp_ipc_close.argtypes = [c.c_void_p]
     lib.ps_dcp_decode.restype = c.c_int
     lib.ps_dcp_decode.argtypes = [c.POINTER(DcpProblem), c.c_void_p, c.c_int64, c.c_void_p]
+    lib.ps_head_gather_slab_bytes.restype = c.c_int64
+    lib.ps_head_gather_slab_bytes.argtypes = [c.c_int32, c.c_int32]
+    lib.ps_head_gather.restype = c.c_int
+    lib.ps_head_gather.argtypes = [c.POINTER(HeadGatherProblem), c.c_void_p]
+    lib.ps_head_gather_phase.restype = c.c_int
+    lib.ps_head_gather_phase.argtypes = [c.POINTER(HeadGatherProblem), c.c_int32, c.c_void_p]
     lib.ps_dcp_decode_phase.restype = c.c_int
     lib.ps_dcp_decode_phase.argtypes = [c.POINTER(DcpProblem), c.c_int32, c.c_void_p, c.c_int64,
                                         c.c_void_p]

@@ -29,7 +29,7 @@ from dataclasses import dataclass
 
 import torch
 
-from . import _lib
+from . import _lib, peer
 from .ops import DecodeWorkspace, _problem, _require_cuda, _stream_ptr
 
 
@@ -92,27 +92,33 @@ def shard_sequence_kv(keys: list, values: list, block_table: torch.Tensor, key_c
 # ------------------------------------------------------------ the group
 def exchange_handles(handle: bytes, group=None) -> list:
     """All ranks' 64-byte slab handles, in rank order (one all_gather_object)."""
-    import torch.distributed as dist
-
-    out = [None] * dist.get_world_size(group)
-    dist.all_gather_object(out, bytes(handle), group=group)
-    return out
+    return peer.exchange_handles(handle, group)
 
 
 @dataclass
 class DcpComm:
     """One rank's view of a DCP group: its slab and every rank's slab address."""
 
-    world: int
-    rank: int
     interleave: int
     max_tokens: int
     hq_local: int
-    slabs: list            # device addresses, rank order, valid on this GPU
-    device: torch.device
-    _own: int = 0          # this rank's allocation (freed by close)
-    _opened: tuple = ()    # peer mappings (closed by close)
-    _emulated_owner: bool = False
+    peers: peer.PeerSlabs
+
+    @property
+    def world(self) -> int:
+        return self.peers.world
+
+    @property
+    def rank(self) -> int:
+        return self.peers.rank
+
+    @property
+    def slabs(self) -> list:
+        return self.peers.slabs
+
+    @property
+    def device(self) -> torch.device:
+        return self.peers.device
 
     @staticmethod
     def slab_bytes(max_tokens: int, hq_local: int, world: int) -> int:
@@ -121,13 +127,6 @@ class DcpComm:
             _lib.check(_lib.PS_ERR_INVALID_ARGUMENT)
         return int(n)
 
-    @staticmethod
-    def _alloc(nbytes: int) -> int:
-        lib = _lib.load()
-        p = ctypes.c_void_p()
-        _lib.check(lib.ps_dcp_slab_alloc(nbytes, ctypes.byref(p)))
-        return int(p.value)
-
     @classmethod
     def from_process_group(cls, max_tokens: int, hq_local: int, interleave: int = 1,
                            group=None, device=None) -> "DcpComm":
@@ -135,51 +134,23 @@ class DcpComm:
         slab on ``device`` and map every peer's."""
         import torch.distributed as dist
 
-        lib = _lib.load()
-        dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
-        world, rank = dist.get_world_size(group), dist.get_rank(group)
+        world = dist.get_world_size(group)
         if world > _lib.PS_DCP_MAX_WORLD:
             raise ValueError(f"DCP groups have at most {_lib.PS_DCP_MAX_WORLD} ranks")
-        with torch.cuda.device(dev):
-            own = cls._alloc(cls.slab_bytes(max_tokens, hq_local, world))
-            h = ctypes.create_string_buffer(_lib.PS_DCP_IPC_HANDLE_BYTES)
-            _lib.check(lib.ps_dcp_ipc_handle(own, h))
-            handles = exchange_handles(h.raw, group)
-            slabs, opened = [], []
-            for r, hr in enumerate(handles):
-                if r == rank:
-                    slabs.append(own)
-                    continue
-                p = ctypes.c_void_p()
-                buf = ctypes.create_string_buffer(hr, _lib.PS_DCP_IPC_HANDLE_BYTES)
-                _lib.check(lib.ps_dcp_ipc_open(buf, ctypes.byref(p)))
-                slabs.append(int(p.value))
-                opened.append(int(p.value))
-        dist.barrier(group)  # every mapping exists before any rank signals
-        return cls(world, rank, interleave, max_tokens, hq_local, slabs, dev, own, tuple(opened))
+        slabs = peer.PeerSlabs.from_process_group(cls.slab_bytes(max_tokens, hq_local, world),
+                                                  group, device)
+        return cls(interleave, max_tokens, hq_local, slabs)
 
     @classmethod
     def emulated(cls, world: int, max_tokens: int, hq_local: int, interleave: int = 1,
                  device=None) -> list:
         """``world`` ranks of a group on one GPU (one process): every slab is
         local.  Use with :func:`dcp_decode_group`."""
-        dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
-        with torch.cuda.device(dev):
-            nbytes = cls.slab_bytes(max_tokens, hq_local, world)
-            slabs = [cls._alloc(nbytes) for _ in range(world)]
-        comms = [cls(world, r, interleave, max_tokens, hq_local, list(slabs), dev, slabs[r])
-                 for r in range(world)]
-        return comms
+        views = peer.PeerSlabs.emulated(world, cls.slab_bytes(max_tokens, hq_local, world), device)
+        return [cls(interleave, max_tokens, hq_local, v) for v in views]
 
     def close(self) -> None:
-        lib = _lib.load()
-        with torch.cuda.device(self.device):
-            torch.cuda.synchronize(self.device)
-            for p in self._opened:
-                _lib.check(lib.ps_dcp_ipc_close(p))
-            if self._own:
-                _lib.check(lib.ps_dcp_slab_free(self._own))
-        self._opened, self._own = (), 0
+        self.peers.close()
 
     def workspace(self, max_num_seqs: int, num_kv_heads: int, head_size: int = 128) -> DecodeWorkspace:
         """A decode workspace sized for the group's heads."""

@@ -384,7 +384,7 @@ def paged_decode(q: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Te
                  new_key: torch.Tensor | None = None, new_value: torch.Tensor | None = None,
                  slot_mapping: torch.Tensor | None = None,
                  cascade: CascadePlan | None = None, k_scale: torch.Tensor | None = None,
-                 v_scale: torch.Tensor | None = None) -> torch.Tensor:
+                 v_scale: torch.Tensor | None = None, out_address: int | None = None) -> torch.Tensor:
     """Decode attention, one query row per sequence, written into ``out``.
 
     q/out: [T, Hq, D]; caches [num_blocks, block_size, Hkv, D]; block_table
@@ -403,6 +403,11 @@ def paged_decode(q: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Te
     fp8 caches (uint8 codes or float8_e4m3fn): attention over code * k_scale
     and code * v_scale (one-element float32 device tensors, None = 1); the
     fused append stores e4m3(x / scale).
+
+    ``out_address``: write the output rows to this device address instead,
+    contiguous [T, Hq, D] in ``out``'s dtype (``out`` then only supplies the
+    dtype and shape) -- a peer-memory slab for :mod:`ps_attn.sharding`'s
+    NVLink head gather.
     """
     lib = _lib.load()
     B = seq_lens.shape[0]
@@ -415,6 +420,11 @@ def paged_decode(q: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Te
         raise ValueError(f"cascade plan built for {cascade.num_seqs} sequences, call has {B}")
     pr = _problem(q, key_cache, value_cache, block_table, seq_lens, query_start_loc,
                   softmax_scale, out, lse, k_scale=k_scale, v_scale=v_scale)
+    if out_address is not None:
+        if out_address % 16:
+            raise ValueError("out_address must be 16-byte aligned")
+        pr.out = out_address
+        pr.out_stride_token, pr.out_stride_head = q.shape[1] * q.shape[2], q.shape[2]
     if new_key is not None:
         _require_cuda(new_key, new_value, slot_mapping)
         if new_value is None or slot_mapping is None:

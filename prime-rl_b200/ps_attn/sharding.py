@@ -110,6 +110,117 @@ class HeadShardedDecode:
         return full
 
 
+class PeerHeadGather:
+    """KV-head-sharded decode whose head outputs are exchanged over NVLink
+    peer memory instead of NCCL (``ps_head_gather``).
+
+    Each rank's decode writes its rows ``[T, Hq/n, D]`` into its own slab
+    (:meth:`decode`, through ``ops.paged_decode(out_address=...)``); one
+    :meth:`gather` launch then pulls every rank's rows into ``out[T, Hq, D]``
+    at head offset ``r * Hq/n`` -- the all_gather + permute of
+    :class:`HeadShardedDecode` in one kernel, with two flag barriers and no
+    NCCL call.  Build with :meth:`from_process_group` (one process per GPU)
+    or :meth:`emulated` (every rank on one GPU; run :func:`gather_group`).
+    """
+
+    def __init__(self, shard: HeadShard, max_tokens: int, dtype, slabs, status: torch.Tensor):
+        self.shard = shard
+        self.max_tokens = max_tokens
+        self.dtype = dtype
+        self.slabs = slabs
+        self.status = status
+
+    @staticmethod
+    def slab_bytes(max_tokens: int, q_per_rank: int) -> int:
+        from . import _lib
+
+        n = _lib.load().ps_head_gather_slab_bytes(max_tokens, q_per_rank)
+        if n < 0:
+            _lib.check(_lib.PS_ERR_INVALID_ARGUMENT)
+        return int(n)
+
+    @classmethod
+    def from_process_group(cls, shard: HeadShard, max_tokens: int, dtype, group=None, device=None):
+        from .peer import PeerSlabs
+
+        slabs = PeerSlabs.from_process_group(cls.slab_bytes(max_tokens, shard.q_per_rank), group, device)
+        status = torch.zeros(1, dtype=torch.int32, device=slabs.device)
+        return cls(shard, max_tokens, dtype, slabs, status)
+
+    @classmethod
+    def emulated(cls, num_q_heads: int, num_kv_heads: int, world: int, max_tokens: int, dtype,
+                 device=None) -> list:
+        from .peer import PeerSlabs
+
+        views = PeerSlabs.emulated(world, cls.slab_bytes(max_tokens, num_q_heads // world), device)
+        return [cls(HeadShard(world, r, num_q_heads, num_kv_heads), max_tokens, dtype, v,
+                    torch.zeros(1, dtype=torch.int32, device=v.device)) for r, v in enumerate(views)]
+
+    def rows_address(self) -> int:
+        from . import _lib
+
+        return self.slabs.own + _lib.PS_HEAD_GATHER_ROWS_OFFSET
+
+    def decode(self, q_local, key_cache, value_cache, block_table, seq_lens, softmax_scale,
+               out: torch.Tensor, **kw) -> None:
+        """This rank's decode (its heads) into its slab; ``out`` [T, Hq, D] is
+        the gather's destination and supplies dtype and rows."""
+        from . import ops
+
+        T = q_local.shape[0]
+        if T > self.max_tokens:
+            raise ValueError(f"{T} tokens > the slabs' {self.max_tokens}")
+        shape_ref = out[:T, :self.shard.q_per_rank]
+        ops.paged_decode(q_local, key_cache, value_cache, block_table, seq_lens, softmax_scale,
+                         shape_ref, out_address=self.rows_address(), **kw)
+
+    def _problem(self, num_tokens: int, out: torch.Tensor):
+        from . import _lib, ops
+
+        if out.dtype != self.dtype or out.stride(-1) != 1 or not out.is_cuda:
+            raise ValueError("out must be a CUDA tensor of the gather's dtype, last dim contiguous")
+        if out.shape[1] != self.shard.num_q_heads or out.shape[0] < num_tokens:
+            raise ValueError(f"out must be [>= {num_tokens}, {self.shard.num_q_heads}, D]")
+        hp = _lib.HeadGatherProblem()
+        hp.world, hp.rank = self.shard.world, self.shard.rank
+        hp.num_tokens, hp.hq_local, hp.max_tokens = num_tokens, self.shard.q_per_rank, self.max_tokens
+        hp.dtype = ops._DTYPES[self.dtype]
+        for r, a in enumerate(self.slabs.slabs):
+            hp.slabs[r] = a
+        hp.out = out.data_ptr()
+        hp.out_stride_token, hp.out_stride_head = out.stride(0), out.stride(1)
+        hp.status = self.status.data_ptr()
+        return hp
+
+    def gather(self, num_tokens: int, out: torch.Tensor) -> torch.Tensor:
+        """Every rank's rows into ``out[:num_tokens]`` (same call on every rank)."""
+        import ctypes
+
+        from . import _lib, ops
+
+        hp = self._problem(num_tokens, out)
+        _lib.check(_lib.load().ps_head_gather(ctypes.byref(hp), ops._stream_ptr(out.device)))
+        return out
+
+    def close(self) -> None:
+        self.slabs.close()
+
+
+def gather_group(gathers: list, num_tokens: int, outs: list) -> None:
+    """The head gather of an emulated group (:meth:`PeerHeadGather.emulated`):
+    phase k for every rank before phase k+1 for any."""
+    import ctypes
+
+    from . import _lib, ops
+
+    lib = _lib.load()
+    probs = [g._problem(num_tokens, o) for g, o in zip(gathers, outs)]
+    stream = ops._stream_ptr(outs[0].device)
+    for phase in range(3):
+        for hp in probs:
+            _lib.check(lib.ps_head_gather_phase(ctypes.byref(hp), phase, stream))
+
+
 def balance_sequences(seq_lens, world: int, group_size: int = 1) -> list[list[int]]:
     """Greedy longest-first assignment of sequences (or GRPO groups of
     ``group_size`` consecutive sequences) to ``world`` ranks by total length."""

@@ -118,7 +118,7 @@ def _struct_fields(name):
     start = text.rindex("typedef struct {", 0, end) + len("typedef struct {")
     names = []
     for decl in text[start:end].split(";"):
-        toks = decl.replace("*", " ").replace(",", " ").split()
+        toks = re.sub(r"\[[^\]]*\]", "", decl).replace("*", " ").replace(",", " ").split()
         for i, tok in enumerate(toks):
             if tok not in ("const", "void", "int64_t", "int32_t", "float"):
                 names.extend(toks[i:])
@@ -144,3 +144,29 @@ def test_rope_struct_layout_and_validation():
     pr.dtype, pr.head_size, pr.rotary_dim = _lib.PS_DTYPE_BF16, 128, 63
     assert lib.ps_rope_kv_append(ctypes.byref(pr), None) == _lib.PS_ERR_INVALID_ARGUMENT
     assert b"rotary_dim" in lib.ps_last_error()
+
+
+def test_head_gather_struct_and_validation():
+    assert _struct_fields("ps_head_gather_problem") == [
+        "world", "rank", "num_tokens", "hq_local", "max_tokens", "dtype", "slabs", "out",
+        "out_stride_token", "out_stride_head", "status"]
+    assert [f for f, _ in _lib.HeadGatherProblem._fields_] == _struct_fields("ps_head_gather_problem")
+    lib = _lib.load()
+    assert lib.ps_head_gather_slab_bytes(64, 8) == 256 + 64 * 8 * 256
+    assert lib.ps_head_gather_slab_bytes(0, 8) == -1
+    assert lib.ps_head_gather(None, None) == _lib.PS_ERR_INVALID_ARGUMENT
+    hp = _lib.HeadGatherProblem()
+    hp.world, hp.rank, hp.num_tokens, hp.hq_local, hp.max_tokens = 9, 0, 4, 8, 8
+    hp.dtype = _lib.PS_DTYPE_BF16
+    assert lib.ps_head_gather(ctypes.byref(hp), None) == _lib.PS_ERR_INVALID_ARGUMENT
+    hp.world = 2
+    hp.slabs[0], hp.slabs[1] = 256, 512
+    hp.out, hp.out_stride_token, hp.out_stride_head = 1024, 16 * 128, 128
+    assert lib.ps_head_gather(ctypes.byref(hp), None) == _lib.PS_ERR_INVALID_ARGUMENT
+    assert b"status" in lib.ps_last_error()
+    hp.status = 4096
+    hp.dtype = _lib.PS_DTYPE_FP32
+    assert lib.ps_head_gather(ctypes.byref(hp), None) == _lib.PS_ERR_UNSUPPORTED
+    hp.dtype, hp.num_tokens = _lib.PS_DTYPE_BF16, 9  # more rows than the slabs hold
+    assert lib.ps_head_gather(ctypes.byref(hp), None) == _lib.PS_ERR_INVALID_ARGUMENT
+    assert lib.ps_head_gather_phase(ctypes.byref(hp), 3, None) == _lib.PS_ERR_INVALID_ARGUMENT
