@@ -130,11 +130,13 @@ typedef struct {
   int64_t new_value_stride_token, new_value_stride_head;
   const int64_t* slot_mapping;
   /* KV-cache element type, PS_KV_AUTO (0) or PS_KV_FP8_E4M3.  An fp8 cache
-     holds e4m3(x / scale) codes (ps_kv_append_fp8, or the fused append) and
-     is read as code * scale with the per-tensor scales below (device fp32
-     scalars, NULL = 1.0) -- vLLM's kv_cache_dtype "fp8" with layer._k_scale
-     / _v_scale.  Cache strides are then in bytes.  Taken by ps_paged_decode
-     only; the other attention entry points return PS_ERR_UNSUPPORTED. */
+     holds e4m3(x / scale) codes (ps_kv_append_fp8, or the fused append) --
+     vLLM's kv_cache_dtype "fp8" with layer._k_scale / _v_scale; its strides
+     are in bytes.  ps_paged_decode takes it; chunked prefill attends over
+     the pages ps_kv_dequant_gather copies out (the other entry points return
+     PS_ERR_UNSUPPORTED).  k_scale / v_scale (device fp32 scalars, NULL =
+     1.0): attention reads K * k_scale and V * v_scale, for any cache dtype
+     (ps_paged_decode, the cascade decode, chunked prefill; DCP takes none). */
   int32_t kv_cache_dtype;
   const float* k_scale;
   const float* v_scale;
@@ -158,6 +160,22 @@ int ps_kv_append_fp8(const void* key, int64_t key_stride_token, int64_t key_stri
                      const int64_t* slot_mapping, int64_t num_tokens, int32_t num_kv_heads,
                      int32_t head_size, int32_t block_size, int32_t dtype, const float* k_scale,
                      const float* v_scale, int32_t* status, void* stream);
+
+/*
+ * The pages of an fp8 cache that a batch of sequences reads, dequantized
+ * into a 16-bit scratch cache, for the entry points that take 16-bit pages
+ * (chunked prefill over an fp8 cache): page p < ceil(seq_lens[b] /
+ * block_size) of sequence b -- cache block block_table[b * stride + p] --
+ * becomes scratch block b * max_pages + p of out_key / out_value
+ * ([num_seqs * max_pages, block_size, num_kv_heads, 128], problem->dtype),
+ * each element code * scale rounded to that dtype.  Other scratch blocks are
+ * left untouched; attend over the scratch with the block table
+ * [b][p] = b * max_pages + p.  Uses the problem's fp8 cache (contiguous
+ * blocks), block table, seq_lens, num_seqs, shape, dtype, k_scale / v_scale
+ * and status (nullable).
+ */
+int ps_kv_dequant_gather(const ps_paged_problem* problem, int32_t max_pages, void* out_key,
+                         void* out_value, void* stream);
 
 /*
  * Bytes of workspace ps_paged_decode needs for up to num_seqs sequences on

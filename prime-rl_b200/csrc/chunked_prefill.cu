@@ -474,7 +474,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
     const uint32_t s_addr = lane_addr + x * 128;
     const uint32_t o_addr = lane_addr + 256 + x * 128;
-    const float sl2 = p.scale_log2;
+    // per-tensor cache scales fold into the score scale (K) and the output
+    // normalisation (V)
+    const float sl2 = p.scale_log2 * (p.k_scale ? __ldg(p.k_scale) : 1.f);
+    const float v_scale = p.v_scale ? __ldg(p.v_scale) : 1.f;
     int t = 0, uit = 0;
     for (int u = blockIdx.x; u < total_units; ++uit) {
       const UnitInfo ui = unit_info(p, prefix, u);
@@ -601,7 +604,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!pwait(bars.pv_done + x, static_cast<uint32_t>((t - 1) & 1), abort_flag, p.status)) break;
       tc::fence_after_sync();
       const bool zero = (l_run == 0.f) || (l_run != l_run);
-      const float inv = zero ? 0.f : 1.f / l_run;
+      const float inv = zero ? 0.f : v_scale / l_run;
       const int qh = ui.h * G + hin;
       const int64_t orow = static_cast<int64_t>(ui.qrow0 + tok);
 #pragma unroll

@@ -147,3 +147,73 @@ int ps_launch_kv_append_fp8(const ps::AppendArgs& a, const float* k_scale, const
     ps::kv_append_fp8_kernel<false><<<static_cast<int>(blocks), 256, 0, stream>>>(a, k_scale, v_scale);
   return static_cast<int>(cudaGetLastError());
 }
+
+namespace ps {
+
+// The pages of an fp8 cache that a batch of sequences reads, dequantized into
+// a 16-bit scratch cache for kernels that take 16-bit pages (chunked
+// prefill): page p < ceil(seq_lens[b] / block_size) of sequence b (cache
+// block block_table[b][p]) becomes scratch block b * max_pages + p, each
+// element code * scale (fp32) rounded to the model dtype.  Cache blocks are
+// contiguous [block_size, num_kv_heads, 128] bytes; 16 codes per thread step.
+template <bool kBF16>
+__global__ void __launch_bounds__(256) kv_dequant_gather_kernel(const DequantArgs a) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const float ks = a.k_scale ? __ldg(a.k_scale) : 1.f;
+  const float vs = a.v_scale ? __ldg(a.v_scale) : 1.f;
+  const int64_t cpb = a.block_bytes / 16;  // 16-code chunks per block
+  const int64_t units = static_cast<int64_t>(a.num_seqs) * a.max_pages * 2 * cpb;
+  const int64_t gstride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t u = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; u < units; u += gstride) {
+    const int64_t c = u % cpb;
+    const int64_t rest = u / cpb;
+    const int which = static_cast<int>(rest & 1);  // 0 key, 1 value
+    const int64_t page = rest >> 1;                // b * max_pages + p
+    const int b = static_cast<int>(page / a.max_pages);
+    const int p = static_cast<int>(page - static_cast<int64_t>(b) * a.max_pages);
+    const int L = __ldg(a.seq_lens + b);
+    if (p * a.block_size >= L) continue;
+    if (p >= a.max_blocks_per_seq) {
+      if (c == 0 && which == 0) set_status(a.status, PS_DEV_BAD_METADATA);
+      continue;
+    }
+    const int blk = __ldg(a.block_table + static_cast<int64_t>(b) * a.bt_stride + p);
+    if (blk < 0 || blk >= a.num_blocks) {
+      if (c == 0 && which == 0) set_status(a.status, PS_DEV_BLOCK_OUT_OF_RANGE);
+      continue;
+    }
+    const uint4 codes = __ldg(reinterpret_cast<const uint4*>(
+        (which ? a.value_cache : a.key_cache) + blk * a.c_sblock + c * 16));
+    const float s = which ? vs : ks;
+    const uint32_t w[4] = {codes.x, codes.y, codes.z, codes.w};
+    uint32_t o[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t lo16 = e4m3x2_to_f16x2(w[i]);
+      const uint32_t hi16 = e4m3x2_to_f16x2(w[i] >> 16);
+      const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&lo16));
+      const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&hi16));
+      o[2 * i] = pack2<kBF16>(lo.x * s, lo.y * s);
+      o[2 * i + 1] = pack2<kBF16>(hi.x * s, hi.y * s);
+    }
+    uint4* dst = reinterpret_cast<uint4*>((which ? a.out_value : a.out_key) + (page * a.block_bytes + c * 16) * 2);
+    dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+    dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+  }
+}
+
+}  // namespace ps
+
+int ps_launch_kv_dequant_gather(const ps::DequantArgs& a, int dtype_bf16, int sm_count,
+                                cudaStream_t stream) {
+  const int64_t units = static_cast<int64_t>(a.num_seqs) * a.max_pages * 2 * (a.block_bytes / 16);
+  if (units == 0) return 0;
+  int64_t g = (units + 255) / 256;
+  const int64_t cap = 8LL * sm_count;
+  if (g > cap) g = cap;
+  if (dtype_bf16)
+    ps::kv_dequant_gather_kernel<true><<<static_cast<unsigned>(g), 256, 0, stream>>>(a);
+  else
+    ps::kv_dequant_gather_kernel<false><<<static_cast<unsigned>(g), 256, 0, stream>>>(a);
+  return static_cast<int>(cudaGetLastError());
+}

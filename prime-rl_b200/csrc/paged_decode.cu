@@ -518,14 +518,11 @@ __device__ __forceinline__ int stream_range(const DecodeParams& p, const CUtenso
   const int group = p.group;
   const int cnt = static_cast<int>(end - start);
   const int64_t base = (kMode == kCasSuffix) ? tb.pre_total : 0;
-  // fp8 cache: the dequantization scales fold into the score scale (K) and
-  // the output normalisation (V)
-  float scale_log2 = p.scale_log2, k_scale = 1.f, v_scale = 1.f;
-  if constexpr (kFP8) {
-    k_scale = p.k_scale ? __ldg(p.k_scale) : 1.f;
-    v_scale = p.v_scale ? __ldg(p.v_scale) : 1.f;
-    scale_log2 *= k_scale;
-  }
+  // per-tensor cache scales (an fp8 cache's dequantization) fold into the
+  // score scale (K) and the output normalisation (V)
+  const float k_scale = p.k_scale ? __ldg(p.k_scale) : 1.f;
+  const float v_scale = p.v_scale ? __ldg(p.v_scale) : 1.f;
+  const float scale_log2 = p.scale_log2 * k_scale;
 
   if (k0 > 0) {
     // the ring and query slots were last read by this warp's generic-proxy

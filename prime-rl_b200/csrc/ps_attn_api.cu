@@ -275,8 +275,8 @@ int decode_impl(const ps_paged_problem* pr, const void* plan, int64_t plan_bytes
   p.c_sblock = pr->cache_stride_block;
   p.c_sslot = pr->cache_stride_slot;
   p.c_shead = pr->cache_stride_head;
-  p.k_scale = fp8 ? pr->k_scale : nullptr;
-  p.v_scale = fp8 ? pr->v_scale : nullptr;
+  p.k_scale = pr->k_scale;
+  p.v_scale = pr->v_scale;
   if (pr->new_key != nullptr) {
     if (!pr->new_value || !pr->slot_mapping)
       return fail(PS_ERR_INVALID_ARGUMENT, "fused append needs new_key, new_value and slot_mapping");
@@ -621,6 +621,8 @@ int ps_chunked_prefill_ws(const ps_paged_problem* pr, void* workspace, int64_t w
   p.block_size = pr->block_size;
   p.num_blocks = pr->num_blocks;
   p.scale_log2 = pr->softmax_scale * 1.4426950408889634f;
+  p.k_scale = pr->k_scale;
+  p.v_scale = pr->v_scale;
   p.status = pr->status;
   // dynamic unit scheduling: two counters in the workspace's reserved header
   // (bytes 16..23; the decode uses bytes 0..3 of the same header)
@@ -682,8 +684,8 @@ int dcp_impl(const ps_dcp_problem* dp, int phase, void* workspace, int64_t works
   g.num_q_heads = hq_local * dp->world;
   int rc = validate_problem(&g, true);
   if (rc != PS_OK) return rc;
-  if (lp.kv_cache_dtype != PS_KV_AUTO)
-    return fail(PS_ERR_UNSUPPORTED, "DCP decode over an fp8 cache is not built");
+  if (lp.kv_cache_dtype != PS_KV_AUTO || lp.k_scale || lp.v_scale)
+    return fail(PS_ERR_UNSUPPORTED, "DCP decode over an fp8 or scaled cache is not built");
   if (!lp.new_key || !lp.new_value || !lp.slot_mapping)
     return fail(PS_ERR_INVALID_ARGUMENT, "DCP decode needs new_key, new_value and slot_mapping");
   if (!aligned(lp.new_key, 16) || !aligned(lp.new_value, 16) || lp.new_key_stride_token % 8 ||
@@ -906,3 +908,48 @@ int ps_head_gather_phase(const ps_head_gather_problem* problem, int32_t phase, v
 }
 
 }  // extern "C"
+
+extern "C" int ps_kv_dequant_gather(const ps_paged_problem* pr, int32_t max_pages, void* out_key,
+                                    void* out_value, void* stream) {
+  if (!pr) return fail(PS_ERR_INVALID_ARGUMENT, "problem is NULL");
+  if (pr->kv_cache_dtype != PS_KV_FP8_E4M3)
+    return fail(PS_ERR_INVALID_ARGUMENT, "dequantizing gather reads an fp8 cache");
+  if (pr->num_seqs < 0 || max_pages < 0) return fail(PS_ERR_INVALID_ARGUMENT, "negative shape");
+  if (pr->num_seqs == 0 || max_pages == 0) return PS_OK;
+  if (!pr->key_cache || !pr->value_cache || !pr->block_table || !pr->seq_lens || !out_key || !out_value)
+    return fail(PS_ERR_INVALID_ARGUMENT, "a required pointer is NULL");
+  if (pr->dtype != PS_DTYPE_BF16 && pr->dtype != PS_DTYPE_FP16)
+    return fail(PS_ERR_UNSUPPORTED, "scratch dtype must be fp16 or bf16 (dtype %d)", pr->dtype);
+  if (pr->head_size != 128 || pr->num_kv_heads <= 0 || pr->block_size <= 0 || pr->block_size % 16)
+    return fail(PS_ERR_INVALID_ARGUMENT, "shape: head_size 128, block_size a multiple of 16");
+  if (pr->cache_stride_head != 128 || pr->cache_stride_slot != static_cast<int64_t>(pr->num_kv_heads) * 128 ||
+      pr->cache_stride_block % 16 || !aligned(pr->key_cache, 16) || !aligned(pr->value_cache, 16))
+    return fail(PS_ERR_INVALID_ARGUMENT, "fp8 cache blocks must be contiguous and 16-byte aligned");
+  if (!aligned(out_key, 16) || !aligned(out_value, 16))
+    return fail(PS_ERR_INVALID_ARGUMENT, "scratch must be 16-byte aligned");
+  if (pr->block_table_stride < pr->max_blocks_per_seq)
+    return fail(PS_ERR_INVALID_ARGUMENT, "block_table_stride < max_blocks_per_seq");
+  const int sms = sm_count_current(nullptr);
+  if (sms <= 0) return fail(PS_ERR_CUDA, "no CUDA device");
+  ps::DequantArgs a;
+  a.key_cache = static_cast<const char*>(pr->key_cache);
+  a.value_cache = static_cast<const char*>(pr->value_cache);
+  a.c_sblock = pr->cache_stride_block;
+  a.block_bytes = static_cast<int64_t>(pr->block_size) * pr->num_kv_heads * 128;
+  a.num_blocks = pr->num_blocks;
+  a.block_table = pr->block_table;
+  a.bt_stride = pr->block_table_stride;
+  a.max_blocks_per_seq = pr->max_blocks_per_seq;
+  a.seq_lens = pr->seq_lens;
+  a.num_seqs = pr->num_seqs;
+  a.max_pages = max_pages;
+  a.block_size = pr->block_size;
+  a.k_scale = pr->k_scale;
+  a.v_scale = pr->v_scale;
+  a.out_key = static_cast<char*>(out_key);
+  a.out_value = static_cast<char*>(out_value);
+  a.status = pr->status;
+  const int e = ps_launch_kv_dequant_gather(a, pr->dtype == PS_DTYPE_BF16, sms,
+                                            static_cast<cudaStream_t>(stream));
+  return e != 0 ? cuda_fail(static_cast<cudaError_t>(e), "dequantizing gather launch") : PS_OK;
+}

@@ -64,7 +64,8 @@ struct DecodeParams {
   const int32_t* cas_group_pages;  // [cas_max_groups] shared 16-token pages
   int32_t cas_max_groups;
   int32_t* pre_counters;           // [num_seqs * num_kv_heads] prefix-segment split counters
-  // fp8 (e4m3) cache: per-tensor dequantization scales (device; nullptr = 1)
+  // per-tensor cache scales (device; nullptr = 1): attention reads K * k_scale,
+  // V * v_scale (an fp8 cache's dequantization)
   const float* k_scale;
   const float* v_scale;
 };
@@ -117,6 +118,9 @@ struct PrefillParams {
   int32_t block_size;
   int64_t num_blocks;
   float scale_log2;
+  // per-tensor cache scales (device; nullptr = 1): attention reads K * k_scale, V * v_scale
+  const float* k_scale;
+  const float* v_scale;
   int32_t* status;
   // dynamic unit scheduling: [0] units claimed past the grid, [1] CTAs done
   // (both zero between launches); nullptr: static round-robin
@@ -226,6 +230,25 @@ struct DcpArgs {
   int32_t* status;
 };
 
+// Dequantizing page gather (fp8 cache -> 16-bit scratch).  Byte strides.
+struct DequantArgs {
+  const char* key_cache;
+  const char* value_cache;
+  int64_t c_sblock;
+  int64_t block_bytes;      // block_size * num_kv_heads * head_size
+  int64_t num_blocks;
+  const int32_t* block_table;
+  int64_t bt_stride;
+  int32_t max_blocks_per_seq;
+  const int32_t* seq_lens;
+  int32_t num_seqs, max_pages, block_size;
+  const float* k_scale;
+  const float* v_scale;
+  char* out_key;            // [num_seqs * max_pages, block_size, num_kv_heads, head_size]
+  char* out_value;
+  int32_t* status;
+};
+
 // Head all-gather over peer memory (KV-head-sharded decode).  Byte strides.
 constexpr int64_t kHeadGatherRowsOffset = 256;  // this rank's rows in its slab
 struct HeadGatherArgs {
@@ -240,6 +263,8 @@ struct HeadGatherArgs {
 }  // namespace ps
 int ps_launch_dcp(const ps::DcpArgs& a, int which, int sm_count, cudaStream_t stream);
 int ps_launch_head_gather(const ps::HeadGatherArgs& a, int which, int sm_count, cudaStream_t stream);
+int ps_launch_kv_dequant_gather(const ps::DequantArgs& a, int dtype_bf16, int sm_count,
+                                cudaStream_t stream);
 
 // vec: the 16-byte path (rows, strides and cos/sin rows 16-byte aligned,
 // head_size % 8 == 0, rotary_dim % 16 == 0)

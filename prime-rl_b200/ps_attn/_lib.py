@@ -60,6 +60,7 @@ EXPORTED_SYMBOLS = (
     "ps_head_gather_slab_bytes",
     "ps_head_gather",
     "ps_head_gather_phase",
+    "ps_kv_dequant_gather",
 )
 PS_HEAD_GATHER_ROWS_OFFSET = 256
 
@@ -255,6 +256,9 @@ def _declare(lib):
     lib.ps_dcp_ipc_close.argtypes = [c.c_void_p]
     lib.ps_dcp_decode.restype = c.c_int
     lib.ps_dcp_decode.argtypes = [c.POINTER(DcpProblem), c.c_void_p, c.c_int64, c.c_void_p]
+    lib.ps_kv_dequant_gather.restype = c.c_int
+    lib.ps_kv_dequant_gather.argtypes = [c.POINTER(PagedProblem), c.c_int32, c.c_void_p, c.c_void_p,
+                                         c.c_void_p]
     lib.ps_head_gather_slab_bytes.restype = c.c_int64
     lib.ps_head_gather_slab_bytes.argtypes = [c.c_int32, c.c_int32]
     lib.ps_head_gather.restype = c.c_int

@@ -39,8 +39,14 @@ requests that share their leading KV pages (GRPO samples of one prompt; vLLM
 itself only uses cascade attention when every request shares one prefix,
 ``flash_attn.py:1088-1130``) once per step, and the decode reads each shared
 prefix once per group pass.
-Unsupported options (ALiBi, sliding window, soft-cap, sinks, fp8 KV cache,
-encoder attention) raise ``NotImplementedError`` at construction.
+An fp8 KV cache (``kv_cache_dtype`` "fp8" / "fp8_e4m3", per-tensor scales
+``layer._k_scale`` / ``layer._v_scale``) is stored as e4m3(x / scale) by the
+append (bit-identical to ``reshape_and_cache_flash`` with "fp8") and read by
+the decode kernel's fp8 mode; prefill requests attend over their pages
+copied into a 16-bit scratch (``ops.dequant_gather``: the e4m3 values are
+exact in bf16) and attended with the scales applied in the prefill kernel.
+Unsupported options (ALiBi, sliding window, soft-cap, sinks, other KV-cache
+dtypes, encoder attention) raise ``NotImplementedError`` at construction.
 """
 from __future__ import annotations
 
@@ -62,7 +68,7 @@ BACKEND_NAME = "CUSTOM"
 
 class PSAttentionBackend(AttentionBackend):
     supported_dtypes: ClassVar[list[torch.dtype]] = [torch.float16, torch.bfloat16]
-    supported_kv_cache_dtypes: ClassVar[list[str]] = ["auto", "float16", "bfloat16"]
+    supported_kv_cache_dtypes: ClassVar[list[str]] = ["auto", "float16", "bfloat16", "fp8", "fp8_e4m3"]
     forward_includes_kv_cache_update: bool = True
 
     @staticmethod
@@ -209,7 +215,7 @@ class PSAttentionImpl(AttentionImpl):
             raise NotImplementedError("logits soft-cap is not supported by the PS backend")
         if sinks is not None:
             raise NotImplementedError("attention sinks are not supported by the PS backend")
-        if kv_cache_dtype not in ("auto", "float16", "bfloat16"):
+        if kv_cache_dtype not in ("auto", "float16", "bfloat16", "fp8", "fp8_e4m3"):
             raise NotImplementedError(f"kv_cache_dtype {kv_cache_dtype} not supported")
         if attn_type != AttentionType.DECODER:
             raise NotImplementedError("the PS backend implements decoder attention only")
@@ -220,14 +226,22 @@ class PSAttentionImpl(AttentionImpl):
         self.scale = float(scale)
         self.num_kv_heads = num_kv_heads
         self.kv_cache_dtype = kv_cache_dtype
+        self.fp8 = kv_cache_dtype in ("fp8", "fp8_e4m3")
         self.kv_sharing_target_layer_name = kv_sharing_target_layer_name
         self.attn_type = attn_type
         self.num_queries_per_kv = num_heads // num_kv_heads
 
+    def _scales(self, layer) -> dict:
+        """The layer's fp8 dequantization scales (vLLM's ``_k_scale`` /
+        ``_v_scale``), none for a 16-bit cache."""
+        if not self.fp8:
+            return {}
+        return dict(k_scale=getattr(layer, "_k_scale", None), v_scale=getattr(layer, "_v_scale", None))
+
     def do_kv_cache_update(self, layer, key: torch.Tensor, value: torch.Tensor,
                            kv_cache: torch.Tensor, slot_mapping: torch.Tensor) -> None:
         key_cache, value_cache = kv_cache.unbind(0)
-        ops.kv_append(key, value, key_cache, value_cache, slot_mapping)
+        ops.kv_append(key, value, key_cache, value_cache, slot_mapping, **self._scales(layer))
 
     def forward(self, layer, query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
                 kv_cache: torch.Tensor, attn_metadata: PSAttentionMetadata, output: torch.Tensor,
@@ -244,18 +258,25 @@ class PSAttentionImpl(AttentionImpl):
         # key/value are None when this layer shares another layer's cache
         append = (self.appends_in_forward and key is not None and value is not None
                   and self.kv_sharing_target_layer_name is None)
+        sc = self._scales(layer)
         if append and T > ndt:  # prefill tokens: into the cache before their attention
-            ops.kv_append(key[ndt:T], value[ndt:T], key_cache, value_cache, m.slot_mapping[ndt:T])
+            ops.kv_append(key[ndt:T], value[ndt:T], key_cache, value_cache, m.slot_mapping[ndt:T], **sc)
         if nd > 0:
             fused = dict(new_key=key, new_value=value, slot_mapping=m.slot_mapping) if append else {}
             ops.paged_decode(query[:ndt], key_cache, value_cache, m.block_table[:nd],
                              m.seq_lens[:nd], self.scale, output[:ndt],
                              query_start_loc=m.query_start_loc[:nd + 1], workspace=m.workspace,
-                             cascade=m.cascade_plan, **fused)
+                             cascade=None if self.fp8 else m.cascade_plan, **fused, **sc)
         if m.num_prefills > 0:
-            ops.chunked_prefill(query[:T], key_cache, value_cache, m.block_table[nd:],
-                                m.seq_lens[nd:], m.query_start_loc[nd:], self.scale, output[:T],
-                                workspace=m.workspace)
+            kc, vc, bt = key_cache, value_cache, m.block_table[nd:]
+            if self.fp8:
+                # the prefill kernel reads 16-bit pages: the e4m3 values
+                # exactly (unscaled), with the scales applied in the kernel
+                bs = key_cache.shape[1]
+                kc, vc, bt = ops.dequant_gather(key_cache, value_cache, bt, m.seq_lens[nd:],
+                                                (m.max_seq_len + bs - 1) // bs, query.dtype)
+            ops.chunked_prefill(query[:T], kc, vc, bt, m.seq_lens[nd:], m.query_start_loc[nd:],
+                                self.scale, output[:T], workspace=m.workspace, **sc)
         return output
 
 

@@ -371,8 +371,8 @@ def _problem(q, key_cache, value_cache, block_table, seq_lens, query_start_loc,
         pr.status = status.data_ptr()
     if fp8:
         pr.kv_cache_dtype = _lib.PS_KV_FP8_E4M3
-        pr.k_scale = _scale_ptr(k_scale)
-        pr.v_scale = _scale_ptr(v_scale)
+    pr.k_scale = _scale_ptr(k_scale)
+    pr.v_scale = _scale_ptr(v_scale)
     return pr
 
 
@@ -455,13 +455,49 @@ def paged_decode(q: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Te
     return out
 
 
+def dequant_gather(key_cache: torch.Tensor, value_cache: torch.Tensor, block_table: torch.Tensor,
+                   seq_lens: torch.Tensor, max_pages: int, dtype: torch.dtype,
+                   k_scale: torch.Tensor | None = None, v_scale: torch.Tensor | None = None,
+                   status: torch.Tensor | None = None):
+    """The pages ``seq_lens`` covers of an fp8 cache, dequantized into a
+    16-bit scratch cache: returns (key, value [B * max_pages, bs, Hkv, D] of
+    ``dtype``, block table [B, max_pages] int32 into them).  Pages past a
+    sequence's length are left uninitialised (never read).  Without scales
+    the scratch holds the e4m3 values exactly (attend over it with the
+    scales); with them, code * scale rounded to ``dtype``."""
+    lib = _lib.load()
+    _require_cuda(key_cache, value_cache, block_table, seq_lens)
+    if not is_fp8_cache(key_cache) or value_cache.dtype != key_cache.dtype:
+        raise ValueError("dequant_gather reads an fp8 cache")
+    B = seq_lens.shape[0]
+    nb, bs, hkv, d = key_cache.shape
+    dev = key_cache.device
+    kd = torch.empty(B * max_pages, bs, hkv, d, dtype=dtype, device=dev)
+    vd = torch.empty_like(kd)
+    bt = torch.arange(B * max_pages, dtype=torch.int32, device=dev).view(B, max_pages)
+    if B == 0 or max_pages == 0:
+        return kd, vd, bt
+    q_like = torch.empty(1, 1, d, dtype=dtype, device=dev)
+    pr = _problem(q_like, key_cache, value_cache, block_table, seq_lens, None, 1.0, q_like, None,
+                  status=status, k_scale=k_scale, v_scale=v_scale)
+    _lib.check(lib.ps_kv_dequant_gather(ctypes.byref(pr), max_pages, kd.data_ptr(), vd.data_ptr(),
+                                        _stream_ptr(dev)))
+    return kd, vd, bt
+
+
 def chunked_prefill(q: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Tensor,
                     block_table: torch.Tensor, seq_lens: torch.Tensor,
                     query_start_loc: torch.Tensor, softmax_scale: float, out: torch.Tensor,
                     lse: torch.Tensor | None = None,
                     status: torch.Tensor | None = None,
-                    workspace: "DecodeWorkspace | None" = None) -> torch.Tensor:
+                    workspace: "DecodeWorkspace | None" = None,
+                    k_scale: torch.Tensor | None = None,
+                    v_scale: torch.Tensor | None = None) -> torch.Tensor:
     """Causal (bottom-right) varlen attention over the paged cache; any q_len >= 1.
+
+    ``k_scale``/``v_scale`` (one-element float32 device tensors): the cache
+    is read as K * k_scale, V * v_scale -- attention over the unscaled
+    scratch of :func:`dequant_gather` with an fp8 cache's scales.
 
     ``query_start_loc`` [B+1] holds absolute row offsets into ``q``/``out``
     (a slice of a larger batch's offsets is fine).  ``status`` (int32 [1],
@@ -473,7 +509,7 @@ def chunked_prefill(q: torch.Tensor, key_cache: torch.Tensor, value_cache: torch
     if query_start_loc is None:
         raise ValueError("chunked_prefill needs query_start_loc")
     pr = _problem(q, key_cache, value_cache, block_table, seq_lens, query_start_loc,
-                  softmax_scale, out, lse, status)
+                  softmax_scale, out, lse, status, k_scale=k_scale, v_scale=v_scale)
     if workspace is not None:
         _lib.check(lib.ps_chunked_prefill_ws(ctypes.byref(pr), workspace.buffer.data_ptr(),
                                              workspace.nbytes, _stream_ptr(q.device)))

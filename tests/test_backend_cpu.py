@@ -40,7 +40,7 @@ def test_registration_overrides_registry():
 
 
 @pytest.mark.parametrize("kw", [dict(alibi_slopes=[1.0]), dict(sliding_window=128),
-                                dict(logits_soft_cap=30.0), dict(kv_cache_dtype="fp8")])
+                                dict(logits_soft_cap=30.0), dict(kv_cache_dtype="fp8_e5m2")])
 def test_impl_rejects_unsupported_options(kw):
     base = dict(num_heads=16, head_size=128, scale=0.088, num_kv_heads=8, alibi_slopes=None,
                 sliding_window=None, kv_cache_dtype="auto")
@@ -188,3 +188,38 @@ def test_rope_fusion_variant(monkeypatch):
     impl.forward(None, torch.zeros(8, 16, 128), torch.zeros(8, 8, 128), torch.zeros(8, 8, 128),
                  kv, md, torch.zeros(8, 16, 128))
     assert calls[0][0] == "decode" and "new_key" not in calls[0][1] and calls[1] == "prefill"
+
+
+def test_fp8_cache_routes_scales_and_dequantized_prefill(monkeypatch):
+    calls = []
+    monkeypatch.setattr(psb.ops, "kv_append", lambda *a, **k: calls.append(("append", a, k)))
+    monkeypatch.setattr(psb.ops, "paged_decode", lambda *a, **k: calls.append(("decode", a, k)))
+    monkeypatch.setattr(psb.ops, "chunked_prefill", lambda *a, **k: calls.append(("prefill", a, k)))
+
+    def fake_gather(kc, vc, bt, sl, max_pages, dtype, **k):
+        calls.append(("gather", (bt, sl, max_pages, dtype), k))
+        return "kd", "vd", "bt"
+
+    monkeypatch.setattr(psb.ops, "dequant_gather", fake_gather)
+    assert "fp8" in psb.PSAttentionBackend.supported_kv_cache_dtypes
+    impl = psb.PSAttentionImpl(16, 128, 0.088, 8, None, None, "fp8")
+
+    class Layer:
+        _k_scale = torch.tensor(0.5)
+        _v_scale = torch.tensor(0.25)
+
+    md = _builder().build(0, _common([1, 1, 5], [10, 20, 40]))
+    T = 7
+    q = torch.zeros(T, 16, 128, dtype=torch.bfloat16)
+    kv = torch.zeros(2, 4, 16, 8, 128, dtype=torch.uint8)
+    impl.forward(Layer(), q, torch.zeros(T, 8, 128), torch.zeros(T, 8, 128), kv, md,
+                 torch.zeros(T, 16, 128, dtype=torch.bfloat16))
+    assert [c[0] for c in calls] == ["append", "decode", "gather", "prefill"]
+    for name, _, k in calls:
+        if name in ("append", "decode", "prefill"):
+            assert k["k_scale"] is Layer._k_scale and k["v_scale"] is Layer._v_scale
+    assert "k_scale" not in calls[2][2]  # the scratch holds the unscaled e4m3 values
+    _, (bt, sl, max_pages, dtype), _ = calls[2]
+    assert max_pages == 3 and sl.tolist() == [40] and dtype == torch.bfloat16  # ceil(40 / 16)
+    _, a, _ = calls[3]
+    assert a[1] == "kd" and a[2] == "vd" and a[3] == "bt"

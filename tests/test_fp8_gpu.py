@@ -20,9 +20,10 @@ def _scales(dev, ks=0.037, vs=0.021):
             torch.tensor(vs, dtype=torch.float32, device=dev))
 
 
-def _fp8_batch(q_lens, seq_lens, hq, hkv, dtype, seed, block_size=16, stale_nan=True):
-    """A decode batch whose cache is fp8: the cached tokens are e4m3 codes of
-    N(0,1)/scale data; unused rows hold random codes, NaN codes included."""
+def _fp8_batch(q_lens, seq_lens, hq, hkv, dtype, seed, block_size=16, stale_nan=True, gain=2.0):
+    """A batch whose cache is fp8: the cached tokens are e4m3 codes of
+    gain * N(0,1) / scale data; unused rows hold random codes, NaN codes
+    included."""
     b = workloads.make_batch(q_lens, seq_lens, hq, hkv, dtype=dtype, seed=seed, block_size=block_size)
     g = torch.Generator().manual_seed(seed + 5)
     codes = torch.randint(0, 256, tuple(b.kv_cache.shape), generator=g, dtype=torch.uint8)
@@ -30,7 +31,7 @@ def _fp8_batch(q_lens, seq_lens, hq, hkv, dtype, seed, block_size=16, stale_nan=
         codes[(codes & 0x7F) == 0x7F] = 0
     ks, vs = 0.037, 0.021
     # cached tokens of every sequence: quantized N(0,1) values
-    real = ps_oracle.e4m3_encode(b.kv_cache.float().numpy() * np.float32(2.0) /
+    real = ps_oracle.e4m3_encode(b.kv_cache.float().numpy() * np.float32(gain) /
                                  np.array([ks, vs], np.float32)[:, None, None, None, None])
     bt, L = b.block_table.numpy(), b.seq_lens.numpy()
     mask = np.zeros(tuple(b.kv_cache.shape[1:3]), bool)
@@ -161,3 +162,62 @@ def test_fp8_cache_refused_where_not_built(cuda_device):
         ops.chunked_prefill(b.q, kc, kc.clone(), b.block_table, b.seq_lens, b.query_start_loc,
                             b.softmax_scale, out)
     assert e.value.code == _lib.PS_ERR_UNSUPPORTED
+
+
+def test_dequant_gather_matches_oracle(cuda_device):
+    """Pages each sequence covers, dequantized to bf16 (code * scale rounded
+    once), at the compact block table's positions."""
+    g = torch.Generator().manual_seed(21)
+    NB, bs, H, D = 40, 16, 4, 128
+    codes = torch.randint(0, 256, (2, NB, bs, H, D), generator=g, dtype=torch.uint8)
+    codes[(codes & 0x7F) == 0x7F] = 1  # no NaN codes in covered pages
+    lens = torch.tensor([1, 16, 17, 100, 0], dtype=torch.int32)
+    maxp = 8
+    bt = torch.randperm(NB, generator=g)[:5 * maxp].to(torch.int32).view(5, maxp)
+    ks, vs = _scales(cuda_device, 0.75, 1.5)
+    kd, vd, cbt = ops.dequant_gather(codes[0].to(cuda_device), codes[1].to(cuda_device),
+                                     bt.to(cuda_device), lens.to(cuda_device), maxp, torch.bfloat16,
+                                     k_scale=ks, v_scale=vs)
+    torch.cuda.synchronize()
+    assert torch.equal(cbt.cpu(), torch.arange(5 * maxp, dtype=torch.int32).view(5, maxp))
+    for b, L in enumerate(lens.tolist()):
+        for p in range((L + bs - 1) // bs):
+            for src, dst, s in ((codes[0], kd, 0.75), (codes[1], vd, 1.5)):
+                want = ps_oracle.round_to(ps_oracle.dequantize_cache(src[bt[b, p]].numpy(), s), "bf16")
+                assert np.array_equal(dst[b * maxp + p].float().cpu().numpy(), want)
+
+
+def test_backend_forward_over_fp8_cache(cuda_device):
+    """vLLM backend with kv_cache_dtype "fp8": a decode-first mixed batch
+    appends (quantized), decodes (fp8 kernel) and prefills (the e4m3 pages
+    copied to bf16, scales in the kernel) -- attention over the updated,
+    dequantized cache, N(0,1)-scale data as the attention tolerances assume."""
+    pytest.importorskip("vllm.v1.attention.backend")
+    from ps_attn import backend as psb
+
+    q_lens, lens = [1, 1, 1, 37, 200], [40, 300, 17, 1025, 700]
+    b, codes, ks, vs = _fp8_batch(q_lens, lens, 32, 8, torch.bfloat16, seed=61, stale_nan=False, gain=1.0)
+    kc_ref, vc_ref = codes[0].numpy().copy(), codes[1].numpy().copy()
+    ps_oracle.kv_append_fp8(to_np32(b.key), to_np32(b.value), kc_ref, vc_ref, b.slot_mapping.numpy(), ks, vs)
+    rout, _ = ps_oracle.paged_attention(
+        to_np32(b.q), ps_oracle.dequantize_cache(kc_ref, ks), ps_oracle.dequantize_cache(vc_ref, vs),
+        b.block_table.numpy(), b.seq_lens.numpy(), b.query_start_loc.numpy(), b.softmax_scale)
+    g = b.to(cuda_device)
+    kv = codes.to(cuda_device)
+    impl = psb.PSAttentionImpl(32, 128, g.softmax_scale, 8, None, None, "fp8")
+
+    class Layer:
+        _k_scale, _v_scale = _scales(cuda_device, ks, vs)
+
+    T = g.q.shape[0]
+    ws = ops.DecodeWorkspace(len(lens), 32, 8, 128, cuda_device)
+    md = psb.PSAttentionMetadata(
+        num_actual_tokens=T, max_query_len=max(q_lens), query_start_loc=g.query_start_loc,
+        max_seq_len=max(lens), seq_lens=g.seq_lens, block_table=g.block_table,
+        slot_mapping=g.slot_mapping, num_decodes=3, num_decode_tokens=3, num_prefills=2, workspace=ws)
+    out = torch.full_like(g.q, float("nan"))
+    impl.forward(Layer(), g.q, g.key, g.value, kv, md, out)
+    torch.cuda.synchronize()
+    assert ws.status() == 0
+    assert np.array_equal(kv[0].cpu().numpy(), kc_ref) and np.array_equal(kv[1].cpu().numpy(), vc_ref)
+    assert_attn_close(to_np32(out), rout)
