@@ -221,6 +221,14 @@ class PSAttentionImpl(AttentionImpl):
             raise NotImplementedError("the PS backend implements decoder attention only")
         if head_size != 128:
             raise NotImplementedError(f"head_size {head_size} not supported (128)")
+        # vLLM's AttentionImpl.__new__ reads the DCP group size.  Decode
+        # context parallelism runs the whole batch, prefills included, through
+        # forward (flash_attn.py:776-789); this backend has the DCP decode
+        # (ps_attn.dcp) but no DCP prefill, and attending over the local slice
+        # alone would be wrong, so it refuses the configuration.
+        if getattr(self, "dcp_world_size", 1) > 1:
+            raise NotImplementedError("decode context parallelism is not supported by the PS vLLM "
+                                      "backend (the DCP decode is available in ps_attn.dcp)")
         self.num_heads = num_heads
         self.head_size = head_size
         self.scale = float(scale)

@@ -223,3 +223,17 @@ def test_fp8_cache_routes_scales_and_dequantized_prefill(monkeypatch):
     assert max_pages == 3 and sl.tolist() == [40] and dtype == torch.bfloat16  # ceil(40 / 16)
     _, a, _ = calls[3]
     assert a[1] == "kd" and a[2] == "vd" and a[3] == "bt"
+
+
+def test_impl_refuses_decode_context_parallelism(monkeypatch):
+    """Under DCP vLLM hands the whole batch (prefills included) to forward;
+    without a DCP prefill the impl must refuse rather than attend over the
+    local slice."""
+    import vllm.distributed.parallel_state as ps_state
+
+    class Group:
+        world_size, rank_in_group = 2, 0
+
+    monkeypatch.setattr(ps_state, "get_dcp_group", lambda: Group())
+    with pytest.raises(NotImplementedError, match="context parallelism"):
+        psb.PSAttentionImpl(16, 128, 0.088, 8, None, None, "auto")
