@@ -295,7 +295,9 @@ class PSRopeAttentionImpl(PSAttentionImpl):
     appends_in_forward: bool = False
 
     def fused_rope_kvcache_supported(self) -> bool:
-        return True
+        # the fused kernel stores 16-bit rows; an fp8 cache takes the plain
+        # (quantizing) KV update instead
+        return not self.fp8
 
     def do_rope_and_kv_cache_update(self, layer, query: torch.Tensor, key: torch.Tensor,
                                     value: torch.Tensor, positions: torch.Tensor,

@@ -237,3 +237,9 @@ def test_impl_refuses_decode_context_parallelism(monkeypatch):
     monkeypatch.setattr(ps_state, "get_dcp_group", lambda: Group())
     with pytest.raises(NotImplementedError, match="context parallelism"):
         psb.PSAttentionImpl(16, 128, 0.088, 8, None, None, "auto")
+
+
+def test_rope_fusion_variant_declines_fp8_cache():
+    impl = psb.PSRopeAttentionImpl(16, 128, 0.088, 8, None, None, "fp8")
+    assert impl.fused_rope_kvcache_supported() is False
+    assert psb.PSRopeAttentionImpl(16, 128, 0.088, 8, None, None, "auto").fused_rope_kvcache_supported()
