@@ -358,10 +358,17 @@ def run_ours(args):
     assert ws.status() == 0, f"device status {ws.status():#x}"
 
     # ---- end to end through the public API: host inputs in, host output back ----
-    e2e = None if args.quick else run_e2e(batch, ws, dev, args.steps, world,
-                                          nd=nd if mixed else None,
-                                          replicas=1 if sharded else world, fused=fused,
-                                          cascade=cascade, scales=skw)
+    def nccl_gather(local_out):
+        import torch.distributed as dist
+
+        dist.all_gather_into_tensor(gathered, local_out)
+        full_out.view(B, world, hq, 128).copy_(gathered.permute(1, 0, 2, 3))
+
+    e2e = None if args.quick else run_e2e(
+        batch, ws, dev, args.steps, world, nd=nd if mixed else None,
+        replicas=1 if sharded else world, fused=fused, cascade=cascade, scales=skw,
+        full_out=full_out if sharded else None, peer=peer_gather,
+        gather=nccl_gather if sharded and peer_gather is None else None)
 
     ms = elapsed_ms / args.steps
     tokens_per_step = batch.num_tokens  # every rank produces all tokens (its heads when sharded)
@@ -600,10 +607,14 @@ def run_dcp(args):
         dist.destroy_process_group()
 
 
-def run_e2e(batch, ws, dev, steps, world, nd=None, replicas=1, fused=True, cascade=False, scales=None):
+def run_e2e(batch, ws, dev, steps, world, nd=None, replicas=1, fused=True, cascade=False, scales=None,
+            full_out=None, peer=None, gather=None):
     """Same step through the public ops with per-step host->device inputs
     (pinned) and the device->host read of the attention output.  ``nd``:
-    number of leading decode sequences of a mixed batch (the rest prefill)."""
+    number of leading decode sequences of a mixed batch (the rest prefill).
+    KV-head sharded runs (``full_out``) include the head all-gather -- over
+    peer memory (``peer``) or NCCL (``gather(local_out)``) -- and read back
+    the whole output."""
     from ps_attn import ops
 
     B, hq = batch.num_seqs, batch.q.shape[1]
@@ -612,9 +623,10 @@ def run_e2e(batch, ws, dev, steps, world, nd=None, replicas=1, fused=True, casca
             ("q", "key", "value", "slot_mapping", "seq_lens", "block_table", "query_start_loc")}
     dev_in = {k: torch.empty_like(v, device=dev) for k, v in host.items()}
     out = torch.empty_like(batch.q)
-    out_host = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    result = out if full_out is None else full_out
+    out_host = torch.empty(result.shape, dtype=result.dtype).pin_memory()
     h2d = sum(v.numel() * v.element_size() for v in host.values())
-    d2h = out.numel() * out.element_size()
+    d2h = result.numel() * result.element_size()
     kc, vc = batch.kv_cache[0], batch.kv_cache[1]
     plan = ops.CascadePlan(B, dev) if cascade else None
 
@@ -627,7 +639,12 @@ def run_e2e(batch, ws, dev, steps, world, nd=None, replicas=1, fused=True, casca
             ops.kv_append(dev_in["key"], dev_in["value"], kc, vc, dev_in["slot_mapping"])
         elif nd is not None:
             ops.kv_append(dev_in["key"][nd:], dev_in["value"][nd:], kc, vc, dev_in["slot_mapping"][nd:])
-        if nd is None:
+        if peer is not None:
+            peer.decode(dev_in["q"], kc, vc, dev_in["block_table"], dev_in["seq_lens"],
+                        batch.softmax_scale, full_out, query_start_loc=dev_in["query_start_loc"],
+                        workspace=ws, **fkw, **(scales or {}))
+            peer.gather(T, full_out)
+        elif nd is None:
             if cascade:
                 ops.cascade_plan(dev_in["block_table"], dev_in["seq_lens"], hq,
                                  kc.shape[2], kc.shape[1], query_start_loc=dev_in["query_start_loc"],
@@ -642,7 +659,9 @@ def run_e2e(batch, ws, dev, steps, world, nd=None, replicas=1, fused=True, casca
             ops.chunked_prefill(dev_in["q"], kc, vc, dev_in["block_table"][nd:],
                                 dev_in["seq_lens"][nd:], dev_in["query_start_loc"][nd:],
                                 batch.softmax_scale, out, workspace=ws)
-        out_host.copy_(out, non_blocking=True)
+        if gather is not None:
+            gather(out)
+        out_host.copy_(result, non_blocking=True)
 
     n = max(3, min(steps, 200))
     for _ in range(3):
