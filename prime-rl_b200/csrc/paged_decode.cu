@@ -743,12 +743,15 @@ __device__ __forceinline__ int stream_range(const DecodeParams& p, const CUtenso
         const uint32_t addr = kbase + k_row * 128 + ((chunk ^ (k_row & 7)) << 4);
         uint32_t r0, r1, r2, r3;
         ldsm_x4(addr, r0, r1, r2, r3);
+        uint32_t k0l, k0h, k1l, k1h, k2l, k2h, k3l, k3h;
+        e4m3x4_to_f16x2x2(r0, k0l, k0h);
+        e4m3x4_to_f16x2x2(r1, k1l, k1h);
+        e4m3x4_to_f16x2x2(r2, k2l, k2h);
+        e4m3x4_to_f16x2x2(r3, k3l, k3h);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
-          mma_16816<false>(s[nt], e4m3x2_to_f16x2(r0), e4m3x2_to_f16x2(r1), e4m3x2_to_f16x2(r0 >> 16),
-                           e4m3x2_to_f16x2(r1 >> 16), qf[nt][2 * j][0], qf[nt][2 * j][1]);
-          mma_16816<false>(s[nt], e4m3x2_to_f16x2(r2), e4m3x2_to_f16x2(r3), e4m3x2_to_f16x2(r2 >> 16),
-                           e4m3x2_to_f16x2(r3 >> 16), qf[nt][2 * j + 1][0], qf[nt][2 * j + 1][1]);
+          mma_16816<false>(s[nt], k0l, k1l, k0h, k1h, qf[nt][2 * j][0], qf[nt][2 * j][1]);
+          mma_16816<false>(s[nt], k2l, k3l, k2h, k3h, qf[nt][2 * j + 1][0], qf[nt][2 * j + 1][1]);
         }
       }
     } else {
@@ -824,8 +827,9 @@ __device__ __forceinline__ int stream_range(const DecodeParams& p, const CUtenso
         for (int h2 = 0; h2 < 2; ++h2) {
           const uint32_t lo = __byte_perm(h2 ? r2 : r0, 0u, 0x3120);  // tokens 2t, 2t+1
           const uint32_t hi = __byte_perm(h2 ? r3 : r1, 0u, 0x3120);  // tokens 2t+8, 2t+9
-          uint32_t a0 = e4m3x2_to_f16x2(lo), a1 = e4m3x2_to_f16x2(lo >> 16);
-          uint32_t a2 = e4m3x2_to_f16x2(hi), a3 = e4m3x2_to_f16x2(hi >> 16);
+          uint32_t a0, a1, a2, a3;
+          e4m3x4_to_f16x2x2(lo, a0, a1);
+          e4m3x4_to_f16x2x2(hi, a2, a3);
           if (tail) {  // stale rows past seq_len: P is 0 there, keep NaN codes out too
             a0 &= m01;
             a1 &= m01;

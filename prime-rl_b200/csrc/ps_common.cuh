@@ -181,6 +181,16 @@ __device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t v) {
   return static_cast<uint32_t>(h.x) | (static_cast<uint32_t>(h.y) << 16);
 }
 
+// Four e4m3 codes (bytes 0-3 of v) to two f16x2: `lo` from bytes 0-1, `hi`
+// from bytes 2-3 (low half from the lower byte).  PTX cvt.rn.f16x2.e4m3x2 on
+// the two 16-bit halves of v, with no repacking.
+__device__ __forceinline__ void e4m3x4_to_f16x2x2(uint32_t v, uint32_t& lo, uint32_t& hi) {
+  asm("{\n\t.reg .b16 a, b;\n\tmov.b32 {a, b}, %2;\n\t"
+      "cvt.rn.f16x2.e4m3x2 %0, a;\n\tcvt.rn.f16x2.e4m3x2 %1, b;\n\t}"
+      : "=r"(lo), "=r"(hi)
+      : "r"(v));
+}
+
 // Eight model-dtype elements (a 16-byte row piece) to e4m3(x / scale): the
 // quotient rounded to fp32, then to the nearest e4m3 (ties to even),
 // saturating at +-448.
