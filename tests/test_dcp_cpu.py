@@ -176,3 +176,36 @@ def test_dcp_abi_validates_on_the_host():
     assert lib.ps_dcp_decode(ctypes.byref(dp), None, 0, None) == _lib.PS_ERR_INVALID_ARGUMENT
     assert b"one query row" in lib.ps_last_error()
     assert lib.ps_dcp_decode_phase(ctypes.byref(dp), 5, None, 0, None) == _lib.PS_ERR_INVALID_ARGUMENT
+
+
+@pytest.mark.parametrize("world,interleave", [(2, 1), (4, 4)])
+def test_dcp_workload_places_every_new_token_once(world, interleave):
+    """bench.py's per-rank DCP batches: one shared block table, the new
+    token of every sequence stored by exactly one rank, at the slot the
+    oracle's placement gives; local context lengths add up to the global."""
+    from ps_attn import workloads
+
+    batches = [workloads.make_dcp_config(2, world, r, interleave) for r in range(world)]
+    bt = batches[0].block_table
+    assert all(torch.equal(b.block_table, bt) for b in batches)
+    slots = torch.stack([b.slot_mapping for b in batches])  # [world, B]
+    assert ((slots >= 0).sum(0) == 1).all()
+    lens = batches[0].seq_lens.numpy()
+    for r, b in enumerate(batches):
+        want = np.array([ps_oracle.dcp_placement([L - 1], bt[i].numpy(), 16, world, r, interleave)[0]
+                         for i, L in enumerate(lens)])
+        assert np.array_equal(b.slot_mapping.numpy(), want)
+    assert sum(b.unique_tokens for b in batches) == int((lens - 1).sum())
+
+
+def test_bench_rejects_unsupported_mode_combinations():
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    repo = Path(__file__).resolve().parent.parent
+    for args in (["--dcp", "--kv-fp8"], ["--dcp", "--config", "4"], ["--kv-fp8", "--config", "4"],
+                 ["--kv-fp8", "--cascade", "--config", "3"]):
+        r = subprocess.run([sys.executable, str(repo / "bench.py"), *args], capture_output=True,
+                           text=True, timeout=120, cwd=repo)
+        assert r.returncode == 2 and "error" in r.stderr, (args, r.returncode, r.stderr[-300:])
