@@ -481,17 +481,72 @@ def dcp_combine(o_r, lse_r, s_out, s_lse, rounding="fp32"):
     fac = np.exp(f).astype(np.float32)  # [N, H, T]
     corrected = round_to(o_r * np.transpose(fac, (0, 2, 1))[..., None], rounding)
     o_ctx = round_to(corrected.sum(axis=0), rounding)
+    out, lse = merge_states(o_ctx, lse_ctx, s_out, s_lse)
+    return round_to(out, rounding), lse, o_ctx, lse_ctx.astype(np.float32)
+
+
+def merge_states(p_out, p_lse, s_out, s_lse):
+    """``merge_attn_states`` (``triton_merge_attn_states.py:58-140``): two
+    partial attentions over disjoint key sets, outputs [T, H, D] and LSEs
+    [H, T]; +inf LSEs count as -inf.  Returns (out, lse)."""
+    p_out = np.asarray(p_out, dtype=np.float32)
     s_out = np.asarray(s_out, dtype=np.float32)
-    s_lse = np.asarray(s_lse, dtype=np.float32)
-    p = np.where(lse_ctx == np.inf, -np.inf, lse_ctx)
-    s = np.where(s_lse == np.inf, -np.inf, s_lse)
+    p = np.asarray(p_lse, dtype=np.float32)
+    s = np.asarray(s_lse, dtype=np.float32)
+    p = np.where(p == np.inf, -np.inf, p)
+    s = np.where(s == np.inf, -np.inf, s)
     mx = np.maximum(p, s)
     with np.errstate(invalid="ignore"):
         pse, sse = np.exp(p - mx), np.exp(s - mx)
     tot = pse + sse
-    out = o_ctx * (pse / tot).T[..., None] + s_out * (sse / tot).T[..., None]
-    return (round_to(out, rounding), (np.log(tot) + mx).astype(np.float32), o_ctx,
-            lse_ctx.astype(np.float32))
+    out = p_out * (pse / tot).T[..., None] + s_out * (sse / tot).T[..., None]
+    return out.astype(np.float32), (np.log(tot) + mx).astype(np.float32)
+
+
+def dcp_prefill(q_all, key_caches, value_caches, block_table, seq_lens, query_start_loc, new_key,
+                new_value, softmax_scale, interleave=1):
+    """A DCP step with multi-token query chunks, the way vLLM evaluates it
+    (``FlashAttentionImpl._forward_with_dcp``, ``flash_attn.py:885-983``):
+
+    * the context of sequence b is its first ``seq_lens[b] - q_len(b)``
+      tokens; rank r attends from every query row over its slice of them,
+      non-causally (all of the context precedes the chunk);
+    * the ranks' partials are corrected and summed (``cp_lse_ag_out_rs``);
+    * the chunk attends causally over its own new keys/values
+      (``flash_attn_varlen_func(q, key, value, cu_seqlens_q, cu_seqlens_k =
+      cu_seqlens_q, causal=True)``);
+    * ``merge_attn_states`` merges the two.
+
+    q_all [T, Hq, D] (rows in ``query_start_loc`` order); key_caches /
+    value_caches: per rank [NB, bs, Hkv, D] holding the context only;
+    new_key / new_value [T, Hkv, D].  Returns (out [T, Hq, D], lse [Hq, T]).
+    """
+    q_all = np.asarray(q_all, dtype=np.float32)
+    T, hq, d = q_all.shape
+    world = len(key_caches)
+    qsl = np.asarray(query_start_loc, dtype=np.int64)
+    L = np.asarray(seq_lens, dtype=np.int64)
+    ctx = L - np.diff(qsl)
+    outs, lses = [], []
+    for r in range(world):
+        lens_r = dcp_local_lens(ctx, world, r, interleave)
+        o, l = paged_attention(q_all, key_caches[r], value_caches[r], block_table, lens_r, qsl,
+                               softmax_scale, causal=False)
+        outs.append(o)
+        lses.append(l)
+    _, _, o_ctx, lse_ctx = dcp_combine(np.stack(outs), np.stack(lses), np.zeros_like(q_all),
+                                       np.full((hq, T), -np.inf, np.float32))
+    o_q = np.zeros_like(q_all)
+    lse_q = np.full((hq, T), -np.inf, np.float32)
+    k = np.asarray(new_key, dtype=np.float32)
+    v = np.asarray(new_value, dtype=np.float32)
+    for b in range(len(L)):
+        t0, t1 = int(qsl[b]), int(qsl[b + 1])
+        if t1 > t0:
+            o, l = attention_ref(q_all[t0:t1], k[t0:t1], v[t0:t1], causal=True,
+                                 softmax_scale=softmax_scale)
+            o_q[t0:t1], lse_q[:, t0:t1] = o, l
+    return merge_states(o_ctx, lse_ctx, o_q, lse_q)
 
 
 # --------------------------------------------------------------------------

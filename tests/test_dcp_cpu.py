@@ -209,3 +209,45 @@ def test_bench_rejects_unsupported_mode_combinations():
         r = subprocess.run([sys.executable, str(repo / "bench.py"), *args], capture_output=True,
                            text=True, timeout=120, cwd=repo)
         assert r.returncode == 2 and "error" in r.stderr, (args, r.returncode, r.stderr[-300:])
+
+
+@pytest.mark.parametrize("world,interleave", [(1, 1), (2, 1), (3, 2), (4, 16)])
+def test_oracle_dcp_prefill_equals_causal_attention(world, interleave):
+    """vLLM's DCP evaluation of multi-token chunks (context over the ranks'
+    slices, non-causal; the chunk causal over itself; merged) equals causal
+    attention over the whole sequence.  Contexts of 0 tokens and chunks of 1
+    (a decode row) included."""
+    import math
+
+    from ps_attn import dcp
+
+    g = torch.Generator().manual_seed(17)
+    ctx = [0, 5, 40, 300, 1]
+    qlen = [3, 1, 17, 9, 6]
+    hq, hkv, D, bs = 8, 2, 128, 16
+    B = len(ctx)
+    span = world * interleave
+    P = max(math.ceil((c + 1) / span) * interleave for c in ctx) // bs + 2
+    NB = B * P + 3
+    bt = torch.randperm(NB, generator=g)[:B * P].to(torch.int32).view(B, P)
+    kcs = [torch.randn(NB, bs, hkv, D, generator=g) for _ in range(world)]  # stale contents
+    vcs = [torch.randn(NB, bs, hkv, D, generator=g) for _ in range(world)]
+    ctx_k = [torch.randn(c, hkv, D, generator=g) for c in ctx]
+    ctx_v = [torch.randn(c, hkv, D, generator=g) for c in ctx]
+    dcp.shard_sequence_kv(ctx_k, ctx_v, bt, kcs, vcs, interleave)
+    T = sum(qlen)
+    qsl = np.concatenate([[0], np.cumsum(qlen)])
+    q = torch.randn(T, hq, D, generator=g)
+    nk = torch.randn(T, hkv, D, generator=g)
+    nv = torch.randn(T, hkv, D, generator=g)
+    lens = np.array(ctx) + np.array(qlen)
+    scale = 1.0 / math.sqrt(D)
+    out, lse = ps_oracle.dcp_prefill(q.numpy(), [c.numpy() for c in kcs], [c.numpy() for c in vcs],
+                                     bt.numpy(), lens, qsl, nk.numpy(), nv.numpy(), scale, interleave)
+    for b in range(B):
+        t0, t1 = qsl[b], qsl[b + 1]
+        k = torch.cat([ctx_k[b], nk[t0:t1]]).numpy()
+        v = torch.cat([ctx_v[b], nv[t0:t1]]).numpy()
+        want, want_lse = ps_oracle.attention_ref(q[t0:t1].numpy(), k, v, causal=True, softmax_scale=scale)
+        np.testing.assert_allclose(out[t0:t1], want, atol=2e-5)
+        np.testing.assert_allclose(lse[:, t0:t1], want_lse, atol=2e-5)
