@@ -27,7 +27,7 @@
 extern "C" {
 #endif
 
-#define PS_ATTN_ABI_VERSION 2
+#define PS_ATTN_ABI_VERSION 3
 
 /* host-side return codes */
 typedef enum {
@@ -381,7 +381,16 @@ typedef struct {
   int32_t world, rank, interleave; /* interleave divides block_size */
   int32_t max_tokens;              /* the slabs were sized for it */
   void* slabs[PS_DCP_MAX_WORLD];   /* every rank's slab, addressed from this GPU */
+  int32_t flags;                   /* PS_DCP_* */
 } ps_dcp_problem;
+
+/* ps_dcp_problem.flags: PS_DCP_CONTEXT_ONLY -- the step stops after the
+   cross-rank correction: out / lse receive the attention over the context
+   alone (the new tokens' own attention and the append are left to the
+   caller; new_key / new_value / slot_mapping are not read).  The first half
+   of a DCP step over multi-token chunks: one row per chunk token, each row a
+   one-row "sequence" whose seq_lens entry is its context length + 1. */
+#define PS_DCP_CONTEXT_ONLY 1
 
 /*
  * One DCP decode step on this rank (every rank of the group makes the same
@@ -407,6 +416,22 @@ int ps_dcp_decode(const ps_dcp_problem* problem, void* workspace, int64_t worksp
  */
 int ps_dcp_decode_phase(const ps_dcp_problem* problem, int32_t phase, void* workspace,
                         int64_t workspace_bytes, void* stream);
+
+/*
+ * merge_attn_states (vllm/v1/attention/ops/merge_attn_states.py:9, Triton
+ * kernel triton_merge_attn_states.py:58-140): two partial attentions of the
+ * same query rows over disjoint key sets, outputs [num_tokens, num_heads, 128]
+ * (fp16/bf16, element strides) and natural-log LSEs [num_heads, num_tokens]
+ * (fp32, contiguous; +inf counts as -inf), into out (may alias an input) and
+ * out_lse (nullable).
+ */
+int ps_merge_attn_states(const void* prefix_out, int64_t prefix_stride_token,
+                         int64_t prefix_stride_head, const float* prefix_lse,
+                         const void* suffix_out, int64_t suffix_stride_token,
+                         int64_t suffix_stride_head, const float* suffix_lse, void* out,
+                         int64_t out_stride_token, int64_t out_stride_head, float* out_lse,
+                         int64_t num_tokens, int32_t num_heads, int32_t head_size, int32_t dtype,
+                         void* stream);
 
 /*
  * Head all-gather of a KV-head-sharded decode over peer memory: the

@@ -149,7 +149,7 @@ __global__ void __launch_bounds__(256) dcp_combine_kernel(const __grid_constant_
   if (a.signal_first && blockIdx.x == 0) signal_phase(a, 1, e);
   const int64_t gtid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t gstride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  {  // reshape_and_cache_flash of the tokens stored here
+  if (!a.context_only) {  // reshape_and_cache_flash of the tokens stored here
     const int64_t nvec = static_cast<int64_t>(a.num_tokens) * a.num_kv_heads * 16;
     for (int64_t i = gtid; i < nvec; i += gstride) {
       const int64_t row = i >> 4;
@@ -189,9 +189,12 @@ __global__ void __launch_bounds__(256) dcp_combine_kernel(const __grid_constant_
         if (r < world)
           pv[r] = *reinterpret_cast<const uint2*>(a.slab[r] + a.off_part +
                                                   ((t * a.hq_all + hg) * 128 + lane * 4) * 2);
-      const uint2 qv = *reinterpret_cast<const uint2*>(a.q + t * a.q_st + h * a.q_sh + lane * 8);
-      const uint2 kv = *reinterpret_cast<const uint2*>(a.new_key + t * a.nk_st + kvh * a.nk_sh + lane * 8);
-      const uint2 vv = *reinterpret_cast<const uint2*>(a.new_value + t * a.nv_st + kvh * a.nv_sh + lane * 8);
+      uint2 qv = make_uint2(0u, 0u), kv = qv, vv = qv;
+      if (!a.context_only) {
+        qv = *reinterpret_cast<const uint2*>(a.q + t * a.q_st + h * a.q_sh + lane * 8);
+        kv = *reinterpret_cast<const uint2*>(a.new_key + t * a.nk_st + kvh * a.nk_sh + lane * 8);
+        vv = *reinterpret_cast<const uint2*>(a.new_value + t * a.nv_st + kvh * a.nv_sh + lane * 8);
+      }
       // LSE over the ranks' partials
       if (l != l || l == INFINITY) l = -INFINITY;
       float mx = l;
@@ -216,6 +219,14 @@ __global__ void __launch_bounds__(256) dcp_combine_kernel(const __grid_constant_
           acc[2] += fr * x1.x;
           acc[3] += fr * x1.y;
         }
+      }
+      if (a.context_only) {  // the corrected context attention, its LSE
+        uint2 o;
+        o.x = pack2<kBF16>(acc[0], acc[1]);
+        o.y = pack2<kBF16>(acc[2], acc[3]);
+        *reinterpret_cast<uint2*>(a.out + t * a.o_st + h * a.o_sh + lane * 8) = o;
+        if (a.lse != nullptr && lane == 0) a.lse[h * a.lse_sh + t * a.lse_st] = lse_ctx;
+        continue;
       }
       // the new token attending to itself
       const float2 q0 = unpack2<kBF16>(qv.x), q1 = unpack2<kBF16>(qv.y);
@@ -287,5 +298,61 @@ int ps_launch_dcp(const ps::DcpArgs& a, int which, int sm_count, cudaStream_t st
     default:
       return static_cast<int>(cudaErrorInvalidValue);
   }
+  return static_cast<int>(e != cudaSuccess ? e : cudaGetLastError());
+}
+
+namespace ps {
+
+// merge_attn_states: one warp per (token, head) row, 4 elements per lane.
+template <bool kBF16>
+__global__ void __launch_bounds__(256) merge_attn_states_kernel(const MergeArgs a) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t rows = a.num_tokens * a.num_heads;
+  for (int64_t row = static_cast<int64_t>(blockIdx.x) * 8 + warp; row < rows;
+       row += static_cast<int64_t>(gridDim.x) * 8) {
+    const int64_t t = row / a.num_heads;
+    const int h = static_cast<int>(row - t * a.num_heads);
+    float p = a.p_lse[h * a.num_tokens + t];
+    float s = a.s_lse[h * a.num_tokens + t];
+    p = p == INFINITY ? -INFINITY : p;
+    s = s == INFINITY ? -INFINITY : s;
+    const float mx = fmaxf(p, s);
+    const float pse = __expf(p - mx), sse = __expf(s - mx);
+    const float tot = pse + sse;
+    const float wp = pse / tot, ws = sse / tot;
+    const uint2 pv = *reinterpret_cast<const uint2*>(a.p_out + t * a.p_st + h * a.p_sh + lane * 8);
+    const uint2 sv = *reinterpret_cast<const uint2*>(a.s_out + t * a.s_st + h * a.s_sh + lane * 8);
+    const float2 p0 = unpack2<kBF16>(pv.x), p1 = unpack2<kBF16>(pv.y);
+    const float2 s0 = unpack2<kBF16>(sv.x), s1 = unpack2<kBF16>(sv.y);
+    uint2 o;
+    o.x = pack2<kBF16>(p0.x * wp + s0.x * ws, p0.y * wp + s0.y * ws);
+    o.y = pack2<kBF16>(p1.x * wp + s1.x * ws, p1.y * wp + s1.y * ws);
+    __syncwarp();  // out may alias an input: every lane has read its row
+    *reinterpret_cast<uint2*>(a.out + t * a.o_st + h * a.o_sh + lane * 8) = o;
+    if (a.out_lse != nullptr && lane == 0) a.out_lse[h * a.num_tokens + t] = __logf(tot) + mx;
+  }
+}
+
+}  // namespace ps
+
+int ps_launch_merge_attn_states(const ps::MergeArgs& a, int dtype_bf16, int sm_count,
+                                cudaStream_t stream) {
+  const int64_t rows = a.num_tokens * a.num_heads;
+  if (rows == 0) return 0;
+  int64_t g = (rows + 7) / 8;
+  const int64_t cap = 8LL * sm_count;
+  if (g > cap) g = cap;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(g));
+  cfg.blockDim = dim3(256);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = dtype_bf16 ? cudaLaunchKernelEx(&cfg, ps::merge_attn_states_kernel<true>, a)
+                                   : cudaLaunchKernelEx(&cfg, ps::merge_attn_states_kernel<false>, a);
   return static_cast<int>(e != cudaSuccess ? e : cudaGetLastError());
 }

@@ -686,11 +686,15 @@ int dcp_impl(const ps_dcp_problem* dp, int phase, void* workspace, int64_t works
   if (rc != PS_OK) return rc;
   if (lp.kv_cache_dtype != PS_KV_AUTO || lp.k_scale || lp.v_scale)
     return fail(PS_ERR_UNSUPPORTED, "DCP decode over an fp8 or scaled cache is not built");
-  if (!lp.new_key || !lp.new_value || !lp.slot_mapping)
-    return fail(PS_ERR_INVALID_ARGUMENT, "DCP decode needs new_key, new_value and slot_mapping");
-  if (!aligned(lp.new_key, 16) || !aligned(lp.new_value, 16) || lp.new_key_stride_token % 8 ||
-      lp.new_key_stride_head % 8 || lp.new_value_stride_token % 8 || lp.new_value_stride_head % 8)
-    return fail(PS_ERR_INVALID_ARGUMENT, "new key/value rows must be 16-byte aligned");
+  const bool context_only = (dp->flags & PS_DCP_CONTEXT_ONLY) != 0;
+  if (dp->flags & ~PS_DCP_CONTEXT_ONLY) return fail(PS_ERR_INVALID_ARGUMENT, "unknown DCP flags");
+  if (!context_only) {
+    if (!lp.new_key || !lp.new_value || !lp.slot_mapping)
+      return fail(PS_ERR_INVALID_ARGUMENT, "DCP decode needs new_key, new_value and slot_mapping");
+    if (!aligned(lp.new_key, 16) || !aligned(lp.new_value, 16) || lp.new_key_stride_token % 8 ||
+        lp.new_key_stride_head % 8 || lp.new_value_stride_token % 8 || lp.new_value_stride_head % 8)
+      return fail(PS_ERR_INVALID_ARGUMENT, "new key/value rows must be 16-byte aligned");
+  }
   if (!workspace || !aligned(workspace, 256))
     return fail(PS_ERR_WORKSPACE, "DCP decode needs a 256-byte aligned decode workspace");
   if (lp.num_seqs == 0) return PS_OK;
@@ -712,6 +716,7 @@ int dcp_impl(const ps_dcp_problem* dp, int phase, void* workspace, int64_t works
   a.off_qall = lay.off_qall;
   a.off_lens = lay.off_lens;
   a.signal_first = phase == -1 ? 1 : 0;
+  a.context_only = context_only ? 1 : 0;
   a.q = static_cast<const char*>(lp.q);
   a.q_st = lp.q_stride_token * eb;
   a.q_sh = lp.q_stride_head * eb;
@@ -952,4 +957,45 @@ extern "C" int ps_kv_dequant_gather(const ps_paged_problem* pr, int32_t max_page
   const int e = ps_launch_kv_dequant_gather(a, pr->dtype == PS_DTYPE_BF16, sms,
                                             static_cast<cudaStream_t>(stream));
   return e != 0 ? cuda_fail(static_cast<cudaError_t>(e), "dequantizing gather launch") : PS_OK;
+}
+
+extern "C" int ps_merge_attn_states(const void* prefix_out, int64_t prefix_stride_token,
+                                    int64_t prefix_stride_head, const float* prefix_lse,
+                                    const void* suffix_out, int64_t suffix_stride_token,
+                                    int64_t suffix_stride_head, const float* suffix_lse, void* out,
+                                    int64_t out_stride_token, int64_t out_stride_head, float* out_lse,
+                                    int64_t num_tokens, int32_t num_heads, int32_t head_size,
+                                    int32_t dtype, void* stream) {
+  if (num_tokens < 0 || num_heads < 0) return fail(PS_ERR_INVALID_ARGUMENT, "negative shape");
+  if (num_tokens == 0 || num_heads == 0) return PS_OK;
+  if (!prefix_out || !prefix_lse || !suffix_out || !suffix_lse || !out)
+    return fail(PS_ERR_INVALID_ARGUMENT, "a required pointer is NULL");
+  if (head_size != 128) return fail(PS_ERR_UNSUPPORTED, "head_size %d unsupported (128)", head_size);
+  if (dtype != PS_DTYPE_BF16 && dtype != PS_DTYPE_FP16)
+    return fail(PS_ERR_UNSUPPORTED, "merge takes fp16 or bf16 outputs (dtype %d)", dtype);
+  const int64_t st[6] = {prefix_stride_token, prefix_stride_head, suffix_stride_token,
+                         suffix_stride_head, out_stride_token, out_stride_head};
+  for (int64_t x : st)
+    if (x % 4) return fail(PS_ERR_INVALID_ARGUMENT, "output strides must be 8-byte aligned");
+  if (!aligned(prefix_out, 8) || !aligned(suffix_out, 8) || !aligned(out, 8))
+    return fail(PS_ERR_INVALID_ARGUMENT, "outputs must be 8-byte aligned");
+  const int sms = sm_count_current(nullptr);
+  if (sms <= 0) return fail(PS_ERR_CUDA, "no CUDA device");
+  ps::MergeArgs a;
+  a.p_out = static_cast<const char*>(prefix_out);
+  a.p_st = prefix_stride_token * 2;
+  a.p_sh = prefix_stride_head * 2;
+  a.p_lse = prefix_lse;
+  a.s_out = static_cast<const char*>(suffix_out);
+  a.s_st = suffix_stride_token * 2;
+  a.s_sh = suffix_stride_head * 2;
+  a.s_lse = suffix_lse;
+  a.out = static_cast<char*>(out);
+  a.o_st = out_stride_token * 2;
+  a.o_sh = out_stride_head * 2;
+  a.out_lse = out_lse;
+  a.num_tokens = num_tokens;
+  a.num_heads = num_heads;
+  const int e = ps_launch_merge_attn_states(a, dtype == PS_DTYPE_BF16, sms, static_cast<cudaStream_t>(stream));
+  return e != 0 ? cuda_fail(static_cast<cudaError_t>(e), "merge launch") : PS_OK;
 }

@@ -204,6 +204,7 @@ struct DcpArgs {
   char* slab[kDcpMaxWorld];  // every rank's slab as addressed from this GPU
   int64_t off_q, off_part, off_lse, off_qall, off_lens;
   int32_t signal_first;      // gather/combine publish their phase at their start
+  int32_t context_only;      // combine: corrected context attention only (no self term, no append)
   // this rank's query rows [T, hq_local, 128] and output
   const char* q;
   int64_t q_st, q_sh;
@@ -264,6 +265,23 @@ struct HeadGatherArgs {
 int ps_launch_dcp(const ps::DcpArgs& a, int which, int sm_count, cudaStream_t stream);
 int ps_launch_head_gather(const ps::HeadGatherArgs& a, int which, int sm_count, cudaStream_t stream);
 int ps_launch_kv_dequant_gather(const ps::DequantArgs& a, int dtype_bf16, int sm_count,
+                                cudaStream_t stream);
+namespace ps {
+struct MergeArgs {
+  const char* p_out;
+  int64_t p_st, p_sh;  // bytes
+  const float* p_lse;
+  const char* s_out;
+  int64_t s_st, s_sh;
+  const float* s_lse;
+  char* out;
+  int64_t o_st, o_sh;
+  float* out_lse;
+  int64_t num_tokens;
+  int32_t num_heads;
+};
+}  // namespace ps
+int ps_launch_merge_attn_states(const ps::MergeArgs& a, int dtype_bf16, int sm_count,
                                 cudaStream_t stream);
 
 // vec: the 16-byte path (rows, strides and cos/sin rows 16-byte aligned,

@@ -31,7 +31,7 @@ PS_DTYPE_FP32 = 2
 PS_KV_AUTO = 0
 PS_KV_FP8_E4M3 = 1
 
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 # every symbol include/ps_attn.h declares
 EXPORTED_SYMBOLS = (
@@ -61,6 +61,7 @@ EXPORTED_SYMBOLS = (
     "ps_head_gather",
     "ps_head_gather_phase",
     "ps_kv_dequant_gather",
+    "ps_merge_attn_states",
 )
 PS_HEAD_GATHER_ROWS_OFFSET = 256
 
@@ -169,7 +170,11 @@ class DcpProblem(ctypes.Structure):
         ("interleave", ctypes.c_int32),
         ("max_tokens", ctypes.c_int32),
         ("slabs", ctypes.c_void_p * PS_DCP_MAX_WORLD),
+        ("flags", ctypes.c_int32),
     ]
+
+
+PS_DCP_CONTEXT_ONLY = 1
 
 
 class HeadGatherProblem(ctypes.Structure):
@@ -256,6 +261,13 @@ def _declare(lib):
     lib.ps_dcp_ipc_close.argtypes = [c.c_void_p]
     lib.ps_dcp_decode.restype = c.c_int
     lib.ps_dcp_decode.argtypes = [c.POINTER(DcpProblem), c.c_void_p, c.c_int64, c.c_void_p]
+    lib.ps_merge_attn_states.restype = c.c_int
+    lib.ps_merge_attn_states.argtypes = [
+        c.c_void_p, c.c_int64, c.c_int64, c.c_void_p,  # prefix out, strides, lse
+        c.c_void_p, c.c_int64, c.c_int64, c.c_void_p,  # suffix
+        c.c_void_p, c.c_int64, c.c_int64, c.c_void_p,  # out, strides, out lse
+        c.c_int64, c.c_int32, c.c_int32, c.c_int32, c.c_void_p,
+    ]
     lib.ps_kv_dequant_gather.restype = c.c_int
     lib.ps_kv_dequant_gather.argtypes = [c.POINTER(PagedProblem), c.c_int32, c.c_void_p, c.c_void_p,
                                          c.c_void_p]

@@ -160,8 +160,7 @@ class DcpComm:
 
 # ------------------------------------------------------------ the step
 def _dcp_problem(comm: DcpComm, q, key_cache, value_cache, block_table, seq_lens, softmax_scale,
-                 out, new_key, new_value, slot_mapping, lse) -> _lib.DcpProblem:
-    _require_cuda(new_key, new_value, slot_mapping)
+                 out, new_key, new_value, slot_mapping, lse, context_only=False) -> _lib.DcpProblem:
     T = q.shape[0]
     if q.shape[1] != comm.hq_local:
         raise ValueError(f"q has {q.shape[1]} heads, the group was built for {comm.hq_local}")
@@ -169,30 +168,34 @@ def _dcp_problem(comm: DcpComm, q, key_cache, value_cache, block_table, seq_lens
         raise ValueError("DCP decode takes one query row per sequence")
     if T > comm.max_tokens:
         raise ValueError(f"{T} tokens > the slabs' {comm.max_tokens}")
-    if slot_mapping.dtype != torch.int64 or not slot_mapping.is_contiguous() or slot_mapping.shape[0] < T:
-        raise ValueError("slot_mapping must be contiguous int64 with a slot per token")
-    hkv, d = key_cache.shape[2], key_cache.shape[3]
-    for t in (new_key, new_value):
-        if t.dtype != q.dtype or t.shape[0] < T or t.shape[1:] != (hkv, d) or t.stride(-1) != 1:
-            raise ValueError("new key/value must be [T, num_kv_heads, head_size] in the cache dtype")
     dp = _lib.DcpProblem()
     dp.local = _problem(q, key_cache, value_cache, block_table, seq_lens, None, softmax_scale, out, lse)
-    dp.local.new_key = new_key.data_ptr()
-    dp.local.new_key_stride_token, dp.local.new_key_stride_head = new_key.stride(0), new_key.stride(1)
-    dp.local.new_value = new_value.data_ptr()
-    dp.local.new_value_stride_token, dp.local.new_value_stride_head = new_value.stride(0), new_value.stride(1)
-    dp.local.slot_mapping = slot_mapping.data_ptr()
+    if context_only:
+        dp.flags = _lib.PS_DCP_CONTEXT_ONLY
+    else:
+        _require_cuda(new_key, new_value, slot_mapping)
+        if slot_mapping.dtype != torch.int64 or not slot_mapping.is_contiguous() or slot_mapping.shape[0] < T:
+            raise ValueError("slot_mapping must be contiguous int64 with a slot per token")
+        hkv, d = key_cache.shape[2], key_cache.shape[3]
+        for t in (new_key, new_value):
+            if t.dtype != q.dtype or t.shape[0] < T or t.shape[1:] != (hkv, d) or t.stride(-1) != 1:
+                raise ValueError("new key/value must be [T, num_kv_heads, head_size] in the cache dtype")
+        dp.local.new_key = new_key.data_ptr()
+        dp.local.new_key_stride_token, dp.local.new_key_stride_head = new_key.stride(0), new_key.stride(1)
+        dp.local.new_value = new_value.data_ptr()
+        dp.local.new_value_stride_token, dp.local.new_value_stride_head = new_value.stride(0), new_value.stride(1)
+        dp.local.slot_mapping = slot_mapping.data_ptr()
     dp.world, dp.rank, dp.interleave, dp.max_tokens = comm.world, comm.rank, comm.interleave, comm.max_tokens
-    for r, s in enumerate(comm.slabs):
-        dp.slabs[r] = s
+    for r, a in enumerate(comm.slabs):
+        dp.slabs[r] = a
     return dp
 
 
 def dcp_decode(comm: DcpComm, q: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Tensor,
                block_table: torch.Tensor, seq_lens: torch.Tensor, softmax_scale: float,
-               out: torch.Tensor, new_key: torch.Tensor, new_value: torch.Tensor,
-               slot_mapping: torch.Tensor, workspace: DecodeWorkspace,
-               lse: torch.Tensor | None = None) -> torch.Tensor:
+               out: torch.Tensor, new_key: torch.Tensor | None, new_value: torch.Tensor | None,
+               slot_mapping: torch.Tensor | None, workspace: DecodeWorkspace,
+               lse: torch.Tensor | None = None, context_only: bool = False) -> torch.Tensor:
     """One DCP decode step on this rank; every rank of the group makes the
     same call (same T, same layer order) on its own GPU.
 
@@ -201,11 +204,14 @@ def dcp_decode(comm: DcpComm, q: torch.Tensor, key_cache: torch.Tensor, value_ca
     token; new_key/new_value [T, Hkv, D]; slot_mapping [T] this rank's slots
     (-1 where another rank stores the token, :func:`local_slots`); lse
     [hq_local, T] or None.  The workspace must hold ``world * hq_local`` heads
-    (:meth:`DcpComm.workspace`).
+    (:meth:`DcpComm.workspace`).  ``context_only``: stop after the cross-rank
+    correction (out/lse = attention over the context alone; new_key,
+    new_value and slot_mapping unused) -- the first half of
+    :func:`dcp_prefill`.
     """
     lib = _lib.load()
     dp = _dcp_problem(comm, q, key_cache, value_cache, block_table, seq_lens, softmax_scale, out,
-                      new_key, new_value, slot_mapping, lse)
+                      new_key, new_value, slot_mapping, lse, context_only)
     _lib.check(lib.ps_dcp_decode(ctypes.byref(dp), workspace.buffer.data_ptr(), workspace.nbytes,
                                  _stream_ptr(q.device)))
     return out
@@ -220,10 +226,119 @@ def dcp_decode_group(comms: list, calls: list, workspaces: list) -> None:
     probs = []
     for c, kw in zip(comms, calls):
         probs.append(_dcp_problem(c, kw["q"], kw["key_cache"], kw["value_cache"], kw["block_table"],
-                                  kw["seq_lens"], kw["softmax_scale"], kw["out"], kw["new_key"],
-                                  kw["new_value"], kw["slot_mapping"], kw.get("lse")))
+                                  kw["seq_lens"], kw["softmax_scale"], kw["out"], kw.get("new_key"),
+                                  kw.get("new_value"), kw.get("slot_mapping"), kw.get("lse"),
+                                  kw.get("context_only", False)))
     stream = _stream_ptr(comms[0].device)
     for phase in range(5):
         for dp, ws in zip(probs, workspaces):
             _lib.check(lib.ps_dcp_decode_phase(ctypes.byref(dp), phase, ws.buffer.data_ptr(),
                                                ws.nbytes, stream))
+
+
+# ------------------------------------------------------------ multi-token chunks
+def _chunk_rows(block_table, seq_lens, query_start_loc, num_tokens):
+    """One row per chunk token: its sequence, the block-table rows and the
+    one-row "sequence" lengths (context + 1) of the context part."""
+    B = seq_lens.shape[0]
+    dev = seq_lens.device
+    qlens = (query_start_loc[1:] - query_start_loc[:-1]).to(torch.int64)
+    b_of_t = torch.repeat_interleave(torch.arange(B, device=dev), qlens, output_size=num_tokens)
+    ctx = seq_lens.to(torch.int64) - qlens
+    return b_of_t, qlens, block_table[b_of_t], (ctx[b_of_t] + 1).to(torch.int32)
+
+
+def _chunk_attention(comm: DcpComm, q, new_key, new_value, query_start_loc, qlens, b_of_t,
+                     max_query_len: int, block_size: int, softmax_scale: float, q_out, q_lse):
+    """This rank's query heads over the chunks' own keys/values, causal: the
+    chunks' rows of its KV heads appended into a scratch paged cache, then
+    the chunked-prefill kernel."""
+    from . import ops
+
+    T, hl, d = q.shape
+    hkv = new_key.shape[1]
+    group = hl * comm.world // hkv
+    kv0 = comm.rank * hl // group
+    kv1 = (comm.rank * hl + hl - 1) // group + 1
+    if hl % (kv1 - kv0):
+        raise ValueError("the rank's query heads do not map onto whole KV-head groups")
+    B = qlens.shape[0]
+    maxp = max(1, (max_query_len + block_size - 1) // block_size)
+    dev = q.device
+    sk = torch.empty(B * maxp, block_size, kv1 - kv0, d, dtype=q.dtype, device=dev)
+    sv = torch.empty_like(sk)
+    bt = torch.arange(B * maxp, dtype=torch.int32, device=dev).view(B, maxp)
+    pos = torch.arange(T, device=dev) - query_start_loc.to(torch.int64)[b_of_t]
+    slots = b_of_t * (maxp * block_size) + pos
+    ops.kv_append(new_key[:T, kv0:kv1], new_value[:T, kv0:kv1], sk, sv, slots)
+    ops.chunked_prefill(q, sk, sv, bt, qlens.to(torch.int32), query_start_loc, softmax_scale, q_out,
+                        lse=q_lse)
+
+
+def dcp_prefill(comm: DcpComm, q: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Tensor,
+                block_table: torch.Tensor, seq_lens: torch.Tensor, query_start_loc: torch.Tensor,
+                max_query_len: int, softmax_scale: float, out: torch.Tensor, new_key: torch.Tensor,
+                new_value: torch.Tensor, slot_mapping: torch.Tensor, workspace: DecodeWorkspace,
+                lse: torch.Tensor | None = None) -> torch.Tensor:
+    """A DCP step over multi-token query chunks on this rank (every rank makes
+    the same call), vLLM's ``_forward_with_dcp`` for prefill batches
+    (``flash_attn.py:885-983``):
+
+    1. the chunk tokens this rank stores are appended to its cache;
+    2. every chunk row attends over its sequence's context -- the tokens
+       before the chunk -- across the group (:func:`dcp_decode` with
+       ``context_only``, each row a one-row sequence);
+    3. the chunk attends causally over its own keys/values (this rank's
+       heads; every rank has the chunk's key/value rows);
+    4. ``merge_attn_states`` of the two.
+
+    q/out [T, hq_local, D] (rows in ``query_start_loc`` order, T = total
+    chunk tokens <= the slabs' max_tokens); seq_lens [B] global lengths with
+    the chunk; new_key/new_value [T, Hkv, D]; slot_mapping [T] this rank's
+    slots; workspace sized for T rows and the group's heads.
+    """
+    from . import ops
+
+    T = q.shape[0]
+    b_of_t, qlens, bt_rows, seq_rows = _chunk_rows(block_table, seq_lens, query_start_loc, T)
+    ops.kv_append(new_key[:T], new_value[:T], key_cache, value_cache, slot_mapping[:T])
+    ctx_out = torch.empty_like(out[:T])
+    ctx_lse = torch.empty(q.shape[1], T, dtype=torch.float32, device=q.device)
+    dcp_decode(comm, q, key_cache, value_cache, bt_rows, seq_rows, softmax_scale, ctx_out, None, None,
+               None, workspace, lse=ctx_lse, context_only=True)
+    q_out = torch.empty_like(ctx_out)
+    q_lse = torch.empty_like(ctx_lse)
+    _chunk_attention(comm, q, new_key, new_value, query_start_loc, qlens, b_of_t, max_query_len,
+                     key_cache.shape[1], softmax_scale, q_out, q_lse)
+    ops.merge_attn_states(out[:T], ctx_out, ctx_lse, q_out, q_lse, output_lse=lse)
+    return out
+
+
+def dcp_prefill_group(comms: list, calls: list, workspaces: list) -> None:
+    """:func:`dcp_prefill` for every rank of an emulated group on one GPU
+    (the cross-rank part phase by phase, as :func:`dcp_decode_group`).
+    ``calls[r]``: rank r's :func:`dcp_prefill` keyword arguments (without
+    comm and workspace)."""
+    from . import ops
+
+    staged = []
+    for c, kw in zip(comms, calls):
+        T = kw["q"].shape[0]
+        b_of_t, qlens, bt_rows, seq_rows = _chunk_rows(kw["block_table"], kw["seq_lens"],
+                                                       kw["query_start_loc"], T)
+        ops.kv_append(kw["new_key"][:T], kw["new_value"][:T], kw["key_cache"], kw["value_cache"],
+                      kw["slot_mapping"][:T])
+        ctx_out = torch.empty_like(kw["out"][:T])
+        ctx_lse = torch.empty(kw["q"].shape[1], T, dtype=torch.float32, device=kw["q"].device)
+        staged.append((b_of_t, qlens, ctx_out, ctx_lse, dict(
+            q=kw["q"], key_cache=kw["key_cache"], value_cache=kw["value_cache"], block_table=bt_rows,
+            seq_lens=seq_rows, softmax_scale=kw["softmax_scale"], out=ctx_out, lse=ctx_lse,
+            context_only=True)))
+    dcp_decode_group(comms, [st[4] for st in staged], workspaces)
+    for c, kw, (b_of_t, qlens, ctx_out, ctx_lse, _) in zip(comms, calls, staged):
+        q_out = torch.empty_like(ctx_out)
+        q_lse = torch.empty_like(ctx_lse)
+        _chunk_attention(c, kw["q"], kw["new_key"], kw["new_value"], kw["query_start_loc"], qlens, b_of_t,
+                         kw["max_query_len"], kw["key_cache"].shape[1], kw["softmax_scale"], q_out, q_lse)
+        ops.merge_attn_states(kw["out"][:kw["q"].shape[0]], ctx_out, ctx_lse, q_out, q_lse,
+                              output_lse=kw.get("lse"))

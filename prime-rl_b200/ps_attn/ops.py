@@ -485,6 +485,31 @@ def dequant_gather(key_cache: torch.Tensor, value_cache: torch.Tensor, block_tab
     return kd, vd, bt
 
 
+def merge_attn_states(output: torch.Tensor, prefix_output: torch.Tensor, prefix_lse: torch.Tensor,
+                      suffix_output: torch.Tensor, suffix_lse: torch.Tensor,
+                      output_lse: torch.Tensor | None = None) -> torch.Tensor:
+    """vLLM's ``merge_attn_states`` (``vllm/v1/attention/ops/merge_attn_states.py:9``):
+    two partial attentions of the same rows over disjoint keys, outputs
+    [T, H, D] and LSEs [H, T] (fp32, contiguous), into ``output`` (may alias
+    an input) and ``output_lse``."""
+    lib = _lib.load()
+    _require_cuda(output, prefix_output, prefix_lse, suffix_output, suffix_lse, output_lse)
+    T, H, D = output.shape
+    for t in (prefix_output, suffix_output):
+        if t.dtype != output.dtype or tuple(t.shape) != (T, H, D) or t.stride(-1) != 1:
+            raise ValueError("prefix/suffix outputs must match output [T, H, D]")
+    for t in (prefix_lse, suffix_lse) + ((output_lse,) if output_lse is not None else ()):
+        if t.dtype != torch.float32 or tuple(t.shape) != (H, T) or not t.is_contiguous():
+            raise ValueError("LSEs must be contiguous float32 [H, T]")
+    _lib.check(lib.ps_merge_attn_states(
+        prefix_output.data_ptr(), prefix_output.stride(0), prefix_output.stride(1), prefix_lse.data_ptr(),
+        suffix_output.data_ptr(), suffix_output.stride(0), suffix_output.stride(1), suffix_lse.data_ptr(),
+        output.data_ptr(), output.stride(0), output.stride(1),
+        output_lse.data_ptr() if output_lse is not None else None,
+        T, H, D, _DTYPES[output.dtype], _stream_ptr(output.device)))
+    return output
+
+
 def chunked_prefill(q: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Tensor,
                     block_table: torch.Tensor, seq_lens: torch.Tensor,
                     query_start_loc: torch.Tensor, softmax_scale: float, out: torch.Tensor,

@@ -91,3 +91,47 @@ def make_dcp_case(lens, world, interleave=1, hq=32, hkv=8, block_size=16, dtype=
     slots = [dcp.local_slots(pos, block_table, block_size, world, r, interleave) for r in range(world)]
     return DcpCase(world, interleave, hq, hkv, block_size, seq_lens, block_table, q_all, new_key,
                    new_value, key_caches, value_caches, slots, ctx_keys, ctx_values, 1.0 / math.sqrt(D))
+
+
+def make_dcp_prefill_case(ctx, qlen, world, interleave=1, hq=32, hkv=8, block_size=16,
+                          dtype=torch.bfloat16, seed=0):
+    """Sequences with ``ctx[b]`` cached tokens (sharded over the ranks) and a
+    chunk of ``qlen[b]`` new tokens.  Returns a dict of the pieces and the
+    expected output (causal attention over context + chunk)."""
+    g = torch.Generator().manual_seed(seed)
+    B, D = len(ctx), 128
+    lens = [c + q for c, q in zip(ctx, qlen)]
+    span = world * interleave
+    P = math.ceil(max(math.ceil(L / span) * interleave for L in lens) / block_size) + 1
+    NB = B * P + 3
+    bt = torch.randperm(NB, generator=g)[:B * P].to(torch.int32).view(B, P)
+    kcs = [torch.randn(NB, block_size, hkv, D, generator=g).to(dtype) for _ in range(world)]
+    vcs = [torch.randn(NB, block_size, hkv, D, generator=g).to(dtype) for _ in range(world)]
+    ck = [torch.randn(c, hkv, D, generator=g).to(dtype) for c in ctx]
+    cv = [torch.randn(c, hkv, D, generator=g).to(dtype) for c in ctx]
+    dcp.shard_sequence_kv(ck, cv, bt, kcs, vcs, interleave)
+    T = sum(qlen)
+    qsl = torch.tensor([0] + list(np.cumsum(qlen)), dtype=torch.int32)
+    q = torch.randn(T, hq, D, generator=g).to(dtype)
+    nk = torch.randn(T, hkv, D, generator=g).to(dtype)
+    nv = torch.randn(T, hkv, D, generator=g).to(dtype)
+    pos = torch.cat([torch.arange(c, c + n) for c, n in zip(ctx, qlen)]).to(torch.int64)
+    rows = torch.repeat_interleave(torch.arange(B), torch.tensor(qlen))
+    slots = [dcp.local_slots(pos, bt[rows], block_size, world, r, interleave) for r in range(world)]
+    scale = 1.0 / math.sqrt(D)
+    want = np.zeros((T, hq, D), np.float32)
+    for b in range(B):
+        t0, t1 = int(qsl[b]), int(qsl[b + 1])
+        k = torch.cat([ck[b], nk[t0:t1]]).float().numpy()
+        v = torch.cat([cv[b], nv[t0:t1]]).float().numpy()
+        want[t0:t1], _ = ps_oracle.attention_ref(q[t0:t1].float().numpy(), k, v, causal=True,
+                                                 softmax_scale=scale)
+    kc_ref, vc_ref = [], []
+    for r in range(world):
+        kr, vr = kcs[r].float().numpy().copy(), vcs[r].float().numpy().copy()
+        ps_oracle.kv_append(nk.float().numpy(), nv.float().numpy(), kr, vr, slots[r].numpy())
+        kc_ref.append(kr)
+        vc_ref.append(vr)
+    return dict(q=q, new_key=nk, new_value=nv, block_table=bt, seq_lens=torch.tensor(lens, dtype=torch.int32),
+                query_start_loc=qsl, max_query_len=max(qlen), key_caches=kcs, value_caches=vcs,
+                slots=slots, scale=scale, want=want, kc_ref=kc_ref, vc_ref=vc_ref, hq=hq, hkv=hkv)

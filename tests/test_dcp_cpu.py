@@ -151,8 +151,8 @@ def test_two_rank_dcp_dataflow_over_gloo():
 def test_dcp_abi_validates_on_the_host():
     lib = _lib.load()
     assert [f for f, _ in _lib.DcpProblem._fields_] == ["local", "world", "rank", "interleave",
-                                                         "max_tokens", "slabs"]
-    assert ctypes.sizeof(_lib.DcpProblem) == ctypes.sizeof(_lib.PagedProblem) + 16 + 8 * 8
+                                                         "max_tokens", "slabs", "flags"]
+    assert ctypes.sizeof(_lib.DcpProblem) == ctypes.sizeof(_lib.PagedProblem) + 16 + 8 * 8 + 8
     # slab layout: header, staged q, partials, LSEs, gathered q, local lengths
     T, hl, w = 64, 8, 2
     want = 256 + T * hl * 256 + T * hl * w * 256 + hl * w * T * 4 + T * hl * w * 256 + 256
@@ -176,6 +176,16 @@ def test_dcp_abi_validates_on_the_host():
     assert lib.ps_dcp_decode(ctypes.byref(dp), None, 0, None) == _lib.PS_ERR_INVALID_ARGUMENT
     assert b"one query row" in lib.ps_last_error()
     assert lib.ps_dcp_decode_phase(ctypes.byref(dp), 5, None, 0, None) == _lib.PS_ERR_INVALID_ARGUMENT
+    dp.flags = 2  # unknown flag
+    dp.local.query_start_loc = None
+    assert lib.ps_dcp_decode(ctypes.byref(dp), None, 0, None) == _lib.PS_ERR_INVALID_ARGUMENT
+    # merge_attn_states: shape and dtype checks on the host
+    assert lib.ps_merge_attn_states(None, 0, 0, None, None, 0, 0, None, None, 0, 0, None, 4, 8, 128,
+                                    _lib.PS_DTYPE_BF16, None) == _lib.PS_ERR_INVALID_ARGUMENT
+    args = [256, 1024, 128, 512, 256, 1024, 128, 512, 256, 1024, 128, None, 4, 8, 128, _lib.PS_DTYPE_FP32, None]
+    assert lib.ps_merge_attn_states(*args) == _lib.PS_ERR_UNSUPPORTED
+    args[15], args[14] = _lib.PS_DTYPE_BF16, 64
+    assert lib.ps_merge_attn_states(*args) == _lib.PS_ERR_UNSUPPORTED
 
 
 @pytest.mark.parametrize("world,interleave", [(2, 1), (4, 4)])

@@ -164,3 +164,65 @@ def test_two_gpu_group_over_nvlink():
         p.join(timeout=120)
     assert results == {0: "ok", 1: "ok"}
     assert all(p.exitcode == 0 for p in procs)
+
+
+@pytest.mark.parametrize("world,interleave,hq,hkv", [(2, 1, 32, 8), (4, 16, 16, 8), (2, 1, 16, 2)])
+def test_emulated_group_prefill_chunks(cuda_device, world, interleave, hq, hkv):
+    """dcp_prefill: multi-token chunks on contexts spread over the ranks
+    (context part across the group, the chunk's own causal part locally,
+    merged) equal causal attention over the whole sequence; the chunk tokens
+    each rank stores are appended bit-exactly."""
+    from dcp_helpers import make_dcp_prefill_case
+
+    c = make_dcp_prefill_case([0, 7, 300, 1500, 33], [5, 1, 40, 17, 9], world, interleave, hq, hkv, seed=11)
+    T = c["q"].shape[0]
+    hl = hq // world
+    comms = dcp.DcpComm.emulated(world, T, hl, interleave, cuda_device)
+    wss = [cm.workspace(T, hkv) for cm in comms]
+    try:
+        calls = []
+        for r in range(world):
+            calls.append(dict(
+                q=c["q"][:, r * hl:(r + 1) * hl].to(cuda_device),
+                key_cache=c["key_caches"][r].to(cuda_device), value_cache=c["value_caches"][r].to(cuda_device),
+                block_table=c["block_table"].to(cuda_device), seq_lens=c["seq_lens"].to(cuda_device),
+                query_start_loc=c["query_start_loc"].to(cuda_device), max_query_len=c["max_query_len"],
+                softmax_scale=c["scale"],
+                out=torch.full((T, hl, 128), float("nan"), dtype=torch.bfloat16, device=cuda_device),
+                new_key=c["new_key"].to(cuda_device), new_value=c["new_value"].to(cuda_device),
+                slot_mapping=c["slots"][r].to(cuda_device)))
+        dcp.dcp_prefill_group(comms, calls, wss)
+        torch.cuda.synchronize()
+        for r in range(world):
+            assert wss[r].status() == 0
+            assert_attn_close(calls[r]["out"].float().cpu().numpy(), c["want"][:, r * hl:(r + 1) * hl])
+            assert np.array_equal(calls[r]["key_cache"].float().cpu().numpy(), c["kc_ref"][r])
+            assert np.array_equal(calls[r]["value_cache"].float().cpu().numpy(), c["vc_ref"][r])
+    finally:
+        for cm in comms:
+            cm.close()
+
+
+def test_merge_attn_states_matches_oracle(cuda_device):
+    """ps_merge_attn_states against the oracle's merge (vLLM's rule; +inf
+    and -inf LSEs included), in place on the prefix output."""
+    from oracle import ps_oracle
+
+    g = torch.Generator().manual_seed(4)
+    T, H = 37, 8
+    po = torch.randn(T, H, 128, generator=g).to(torch.bfloat16)
+    so = torch.randn(T, H, 128, generator=g).to(torch.bfloat16)
+    pl = torch.randn(H, T, generator=g) * 4
+    sl = torch.randn(H, T, generator=g) * 4
+    pl[0, :3] = -float("inf")
+    pl[1, 3] = float("inf")
+    want, want_lse = ps_oracle.merge_states(po.float().numpy(), pl.numpy(), so.float().numpy(), sl.numpy())
+    out = po.to(cuda_device)
+    lse = torch.empty(H, T, device=cuda_device)
+    from ps_attn import ops
+
+    ops.merge_attn_states(out, out, pl.to(cuda_device), so.to(cuda_device), sl.to(cuda_device), output_lse=lse)
+    torch.cuda.synchronize()
+    np.testing.assert_allclose(out.float().cpu().numpy(), want, atol=2e-2)
+    assert np.abs(out.float().cpu().numpy() - want).mean() < 2e-3
+    np.testing.assert_allclose(lse.cpu().numpy(), want_lse, atol=1e-5)
