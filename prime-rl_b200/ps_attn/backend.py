@@ -137,6 +137,7 @@ class PSAttentionMetadata:
     workspace: ops.DecodeWorkspace
     causal: bool = True
     cascade_plan: ops.CascadePlan | None = None  # shared-prefix plan of the decode rows
+    dcp_comm: object | None = None               # decode context parallel group (ps_attn.dcp.DcpComm)
 
 
 class PSAttentionMetadataBuilder(AttentionMetadataBuilder[PSAttentionMetadata]):
@@ -157,8 +158,24 @@ class PSAttentionMetadataBuilder(AttentionMetadataBuilder[PSAttentionMetadata]):
         self.block_size = kv_cache_spec.block_size
         self.cascade = (cascade_enabled() and max_seqs <= ops.CASCADE_MAX_SEQS
                         and self.num_heads_q // self.num_heads_kv <= 8)
-        self.workspace = ops.DecodeWorkspace(max_seqs, self.num_heads_q, self.num_heads_kv,
-                                             self.head_size, device, cascade=self.cascade)
+        self.dcp_comm = None
+        if getattr(pc, "decode_context_parallel_size", 1) > 1:
+            # decode context parallelism: one peer-memory slab per rank of the
+            # DCP group, mapped once here (collective over the group, before any
+            # graph capture); rows of both decode and prefill steps go through it
+            from vllm.distributed.parallel_state import get_dcp_group
+
+            from . import dcp
+
+            self.cascade = False
+            rows = max(max_seqs, vllm_config.scheduler_config.max_num_batched_tokens)
+            self.dcp_comm = dcp.DcpComm.from_process_group(
+                rows, self.num_heads_q, getattr(pc, "cp_kv_cache_interleave_size", 1),
+                group=get_dcp_group().cpu_group, device=device)
+            self.workspace = self.dcp_comm.workspace(rows, self.num_heads_kv, self.head_size)
+        else:
+            self.workspace = ops.DecodeWorkspace(max_seqs, self.num_heads_q, self.num_heads_kv,
+                                                 self.head_size, device, cascade=self.cascade)
         self.plan = ops.CascadePlan(max_seqs, device) if self.cascade else None
 
     def build(self, common_prefix_len: int, common_attn_metadata: CommonAttentionMetadata,
@@ -180,7 +197,7 @@ class PSAttentionMetadataBuilder(AttentionMetadataBuilder[PSAttentionMetadata]):
             query_start_loc=m.query_start_loc, max_seq_len=m.max_seq_len, seq_lens=m.seq_lens,
             block_table=m.block_table_tensor, slot_mapping=m.slot_mapping, num_decodes=nd,
             num_decode_tokens=ndt, num_prefills=npf, workspace=self.workspace, causal=True,
-            cascade_plan=plan)
+            cascade_plan=plan, dcp_comm=getattr(self, "dcp_comm", None))
 
     def update_block_table(self, metadata: PSAttentionMetadata, blk_table: torch.Tensor,
                            slot_mapping: torch.Tensor) -> PSAttentionMetadata:
@@ -221,14 +238,14 @@ class PSAttentionImpl(AttentionImpl):
             raise NotImplementedError("the PS backend implements decoder attention only")
         if head_size != 128:
             raise NotImplementedError(f"head_size {head_size} not supported (128)")
-        # vLLM's AttentionImpl.__new__ reads the DCP group size.  Decode
-        # context parallelism runs the whole batch, prefills included, through
-        # forward (flash_attn.py:776-789); this backend has the DCP decode
-        # (ps_attn.dcp) but no DCP prefill, and attending over the local slice
-        # alone would be wrong, so it refuses the configuration.
-        if getattr(self, "dcp_world_size", 1) > 1:
-            raise NotImplementedError("decode context parallelism is not supported by the PS vLLM "
-                                      "backend (the DCP decode is available in ps_attn.dcp)")
+        # vLLM's AttentionImpl.__new__ reads the DCP group size.  Under decode
+        # context parallelism vLLM hands the whole batch to forward
+        # (flash_attn.py:776-789): decode rows go through dcp.dcp_decode,
+        # prefill chunks through dcp.dcp_prefill (the group's slabs are set up
+        # by the metadata builder).
+        self.dcp = getattr(self, "dcp_world_size", 1) > 1
+        if self.dcp and kv_cache_dtype not in ("auto", "float16", "bfloat16"):
+            raise NotImplementedError("decode context parallelism over an fp8 cache is not supported")
         self.num_heads = num_heads
         self.head_size = head_size
         self.scale = float(scale)
@@ -263,6 +280,8 @@ class PSAttentionImpl(AttentionImpl):
         key_cache, value_cache = kv_cache.unbind(0)
         nd, ndt = m.num_decodes, m.num_decode_tokens
         T = m.num_actual_tokens
+        if self.dcp:
+            return self._forward_dcp(query, key, value, key_cache, value_cache, m, output)
         # key/value are None when this layer shares another layer's cache
         append = (self.appends_in_forward and key is not None and value is not None
                   and self.kv_sharing_target_layer_name is None)
@@ -285,6 +304,29 @@ class PSAttentionImpl(AttentionImpl):
                                                 (m.max_seq_len + bs - 1) // bs, query.dtype)
             ops.chunked_prefill(query[:T], kc, vc, bt, m.seq_lens[nd:], m.query_start_loc[nd:],
                                 self.scale, output[:T], workspace=m.workspace, **sc)
+        return output
+
+
+    def _forward_dcp(self, query, key, value, key_cache, value_cache, m, output):
+        """Decode context parallelism (``flash_attn.py:885-983``): the cache
+        holds this rank's slice of every sequence (vLLM's DCP slot mapping),
+        ``seq_lens`` are global; every rank of the group runs the same rows."""
+        from . import dcp
+
+        if m.dcp_comm is None:
+            raise RuntimeError("DCP metadata without a DCP group (the builder sets it up)")
+        if key is None or value is None or self.kv_sharing_target_layer_name is not None:
+            raise NotImplementedError("decode context parallelism needs the layer's own key/value")
+        nd, ndt, T = m.num_decodes, m.num_decode_tokens, m.num_actual_tokens
+        if nd > 0:
+            dcp.dcp_decode(m.dcp_comm, query[:ndt], key_cache, value_cache, m.block_table[:nd],
+                           m.seq_lens[:nd], self.scale, output[:ndt], key[:ndt], value[:ndt],
+                           m.slot_mapping[:ndt], m.workspace)
+        if m.num_prefills > 0:
+            qsl = m.query_start_loc[nd:] - m.query_start_loc[nd]
+            dcp.dcp_prefill(m.dcp_comm, query[ndt:T], key_cache, value_cache, m.block_table[nd:],
+                            m.seq_lens[nd:], qsl, m.max_query_len, self.scale, output[ndt:T],
+                            key[ndt:T], value[ndt:T], m.slot_mapping[ndt:T], m.workspace)
         return output
 
 

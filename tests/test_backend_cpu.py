@@ -225,21 +225,76 @@ def test_fp8_cache_routes_scales_and_dequantized_prefill(monkeypatch):
     assert a[1] == "kd" and a[2] == "vd" and a[3] == "bt"
 
 
-def test_impl_refuses_decode_context_parallelism(monkeypatch):
-    """Under DCP vLLM hands the whole batch (prefills included) to forward;
-    without a DCP prefill the impl must refuse rather than attend over the
-    local slice."""
+def test_forward_routes_dcp_batches(monkeypatch):
+    """Under decode context parallelism (vLLM's DCP group of 2) decode rows go
+    to dcp.dcp_decode and prefill chunks to dcp.dcp_prefill, with the chunk
+    offsets rebased to the first prefill row; fp8 caches are refused."""
     import vllm.distributed.parallel_state as ps_state
+
+    from ps_attn import dcp
 
     class Group:
         world_size, rank_in_group = 2, 0
 
     monkeypatch.setattr(ps_state, "get_dcp_group", lambda: Group())
-    with pytest.raises(NotImplementedError, match="context parallelism"):
-        psb.PSAttentionImpl(16, 128, 0.088, 8, None, None, "auto")
+    with pytest.raises(NotImplementedError, match="fp8"):
+        psb.PSAttentionImpl(16, 128, 0.088, 8, None, None, "fp8")
+    impl = psb.PSAttentionImpl(16, 128, 0.088, 8, None, None, "auto")
+    calls = []
+    monkeypatch.setattr(dcp, "dcp_decode", lambda *a, **k: calls.append(("decode", a, k)))
+    monkeypatch.setattr(dcp, "dcp_prefill", lambda *a, **k: calls.append(("prefill", a, k)))
+    md = _builder().build(0, _common([1, 1, 5, 3], [10, 20, 40, 9]))
+    md.dcp_comm = "comm"
+    T = 10
+    q = torch.zeros(T, 16, 128)
+    key, val = torch.randn(T, 8, 128), torch.randn(T, 8, 128)
+    out = torch.zeros(T, 16, 128)
+    impl.forward(None, q, key, val, torch.zeros(2, 4, 16, 8, 128), md, out)
+    assert [c[0] for c in calls] == ["decode", "prefill"]
+    _, a, _ = calls[0]
+    assert a[0] == "comm" and a[1].shape[0] == 2 and a[5].tolist() == [10, 20] and a[8].shape[0] == 2
+    _, a, _ = calls[1]
+    assert a[1].shape[0] == 8 and a[5].tolist() == [40, 9] and a[6].tolist() == [0, 5, 8]
+    assert a[7] == 5 and a[10].shape[0] == 8 and a[12].tolist() == list(range(2, 10))
 
 
 def test_rope_fusion_variant_declines_fp8_cache():
     impl = psb.PSRopeAttentionImpl(16, 128, 0.088, 8, None, None, "fp8")
     assert impl.fused_rope_kvcache_supported() is False
     assert psb.PSRopeAttentionImpl(16, 128, 0.088, 8, None, None, "auto").fused_rope_kvcache_supported()
+
+
+def test_builder_sets_up_the_dcp_group(monkeypatch):
+    """With decode_context_parallel_size > 1 the metadata builder maps the
+    group's slabs once (over the DCP group's CPU process group), sizes the
+    rows for a whole prefill step and hands the group to every metadata."""
+    from types import SimpleNamespace
+
+    import vllm.distributed.parallel_state as ps_state
+
+    from ps_attn import dcp
+
+    seen = {}
+
+    class Comm:
+        def workspace(self, rows, hkv, head_size):
+            seen["ws"] = (rows, hkv, head_size)
+            return "ws"
+
+    def fake_from_pg(rows, hq_local, interleave, group=None, device=None):
+        seen.update(rows=rows, hq_local=hq_local, interleave=interleave, group=group)
+        return Comm()
+
+    monkeypatch.setattr(ps_state, "get_dcp_group", lambda: SimpleNamespace(cpu_group="cpu-group"))
+    monkeypatch.setattr(dcp.DcpComm, "from_process_group", staticmethod(fake_from_pg))
+    mc = SimpleNamespace(get_num_attention_heads=lambda pc: 16, get_num_kv_heads=lambda pc: 8,
+                         get_head_size=lambda: 128)
+    pc = SimpleNamespace(decode_context_parallel_size=2, cp_kv_cache_interleave_size=4)
+    cfg = SimpleNamespace(model_config=mc, parallel_config=pc,
+                          scheduler_config=SimpleNamespace(max_num_seqs=64, max_num_batched_tokens=8192),
+                          compilation_config=SimpleNamespace(max_cudagraph_capture_size=128))
+    b = psb.PSAttentionMetadataBuilder(SimpleNamespace(block_size=16), ["l0"], cfg, torch.device("cpu"))
+    assert seen["rows"] == 8192 and seen["hq_local"] == 16 and seen["interleave"] == 4
+    assert seen["group"] == "cpu-group" and seen["ws"] == (8192, 8, 128)
+    md = b.build(0, _common([1, 3], [10, 20]))
+    assert isinstance(md.dcp_comm, Comm) and md.workspace == "ws" and md.cascade_plan is None
