@@ -67,6 +67,8 @@ PS_HEAD_GATHER_ROWS_OFFSET = 256
 
 PS_DCP_MAX_WORLD = 8
 PS_DCP_IPC_HANDLE_BYTES = 64
+# rows of one ps_dcp_decode call (ps_dcp_slab_bytes' max_tokens limit)
+PS_DCP_MAX_TOKENS = 4096
 
 
 class PSError(RuntimeError):

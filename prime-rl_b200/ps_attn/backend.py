@@ -61,7 +61,7 @@ from vllm.v1.attention.backend import (AttentionBackend, AttentionCGSupport, Att
                                        CommonAttentionMetadata, MultipleOf)
 from vllm.v1.attention.backends.utils import split_decodes_and_prefills
 
-from . import ops
+from . import _lib, ops
 
 BACKEND_NAME = "CUSTOM"
 
@@ -168,7 +168,10 @@ class PSAttentionMetadataBuilder(AttentionMetadataBuilder[PSAttentionMetadata]):
             from . import dcp
 
             self.cascade = False
-            rows = max(max_seqs, vllm_config.scheduler_config.max_num_batched_tokens)
+            # one call carries at most PS_DCP_MAX_TOKENS rows; dcp_decode and
+            # dcp_prefill run larger steps in pieces of the slabs' rows
+            rows = min(max(max_seqs, vllm_config.scheduler_config.max_num_batched_tokens),
+                       _lib.PS_DCP_MAX_TOKENS)
             self.dcp_comm = dcp.DcpComm.from_process_group(
                 rows, self.num_heads_q, getattr(pc, "cp_kv_cache_interleave_size", 1),
                 group=get_dcp_group().cpu_group, device=device)

@@ -208,12 +208,25 @@ def dcp_decode(comm: DcpComm, q: torch.Tensor, key_cache: torch.Tensor, value_ca
     correction (out/lse = attention over the context alone; new_key,
     new_value and slot_mapping unused) -- the first half of
     :func:`dcp_prefill`.
+
+    More rows than the slabs hold (``comm.max_tokens``) run as consecutive
+    calls over pieces of ``comm.max_tokens`` rows; the rows are independent
+    sequences, and every rank cuts the same T the same way.
     """
     lib = _lib.load()
-    dp = _dcp_problem(comm, q, key_cache, value_cache, block_table, seq_lens, softmax_scale, out,
-                      new_key, new_value, slot_mapping, lse, context_only)
-    _lib.check(lib.ps_dcp_decode(ctypes.byref(dp), workspace.buffer.data_ptr(), workspace.nbytes,
-                                 _stream_ptr(q.device)))
+    T = q.shape[0]
+    step = comm.max_tokens
+    for i in range(0, T, step) if T > step else (0,):
+        j = min(T, i + step)
+        sl = slice(i, j)
+        dp = _dcp_problem(comm, q[sl], key_cache, value_cache, block_table[sl], seq_lens[sl],
+                          softmax_scale, out[sl],
+                          None if new_key is None else new_key[sl],
+                          None if new_value is None else new_value[sl],
+                          None if slot_mapping is None else slot_mapping[sl],
+                          None if lse is None else lse[:, sl], context_only)
+        _lib.check(lib.ps_dcp_decode(ctypes.byref(dp), workspace.buffer.data_ptr(), workspace.nbytes,
+                                     _stream_ptr(q.device)))
     return out
 
 
@@ -237,15 +250,16 @@ def dcp_decode_group(comms: list, calls: list, workspaces: list) -> None:
 
 
 # ------------------------------------------------------------ multi-token chunks
-def _chunk_rows(block_table, seq_lens, query_start_loc, num_tokens):
-    """One row per chunk token: its sequence, the block-table rows and the
-    one-row "sequence" lengths (context + 1) of the context part."""
+def _chunk_rows(seq_lens, query_start_loc, num_tokens):
+    """One row per chunk token: its sequence and the one-row "sequence"
+    length (context + 1) of the context part; the row's block table is its
+    sequence's (``block_table[b_of_t]``)."""
     B = seq_lens.shape[0]
     dev = seq_lens.device
     qlens = (query_start_loc[1:] - query_start_loc[:-1]).to(torch.int64)
     b_of_t = torch.repeat_interleave(torch.arange(B, device=dev), qlens, output_size=num_tokens)
     ctx = seq_lens.to(torch.int64) - qlens
-    return b_of_t, qlens, block_table[b_of_t], (ctx[b_of_t] + 1).to(torch.int32)
+    return b_of_t, qlens, (ctx[b_of_t] + 1).to(torch.int32)
 
 
 def _chunk_attention(comm: DcpComm, q, new_key, new_value, query_start_loc, qlens, b_of_t,
@@ -265,11 +279,18 @@ def _chunk_attention(comm: DcpComm, q, new_key, new_value, query_start_loc, qlen
     B = qlens.shape[0]
     maxp = max(1, (max_query_len + block_size - 1) // block_size)
     dev = q.device
-    sk = torch.empty(B * maxp, block_size, kv1 - kv0, d, dtype=q.dtype, device=dev)
+    # sequence b gets ceil(q_b / block_size) scratch blocks at a running
+    # offset: at most T / block_size + B blocks in all, whatever the mix of
+    # chunk lengths (no host synchronisation: the bound uses T and B only)
+    nblk = T // block_size + B + 1
+    pages = (qlens + block_size - 1) // block_size
+    first = torch.cumsum(pages, 0) - pages
+    sk = torch.empty(nblk, block_size, kv1 - kv0, d, dtype=q.dtype, device=dev)
     sv = torch.empty_like(sk)
-    bt = torch.arange(B * maxp, dtype=torch.int32, device=dev).view(B, maxp)
+    # entries past a sequence's own pages are never read; clamped into the pool
+    bt = (first[:, None] + torch.arange(maxp, device=dev)[None, :]).clamp_(max=nblk - 1).to(torch.int32)
     pos = torch.arange(T, device=dev) - query_start_loc.to(torch.int64)[b_of_t]
-    slots = b_of_t * (maxp * block_size) + pos
+    slots = first[b_of_t] * block_size + pos
     ops.kv_append(new_key[:T, kv0:kv1], new_value[:T, kv0:kv1], sk, sv, slots)
     ops.chunked_prefill(q, sk, sv, bt, qlens.to(torch.int32), query_start_loc, softmax_scale, q_out,
                         lse=q_lse)
@@ -293,19 +314,26 @@ def dcp_prefill(comm: DcpComm, q: torch.Tensor, key_cache: torch.Tensor, value_c
     4. ``merge_attn_states`` of the two.
 
     q/out [T, hq_local, D] (rows in ``query_start_loc`` order, T = total
-    chunk tokens <= the slabs' max_tokens); seq_lens [B] global lengths with
+    chunk tokens; the context part runs in pieces of the slabs' max_tokens
+    rows); seq_lens [B] global lengths with
     the chunk; new_key/new_value [T, Hkv, D]; slot_mapping [T] this rank's
     slots; workspace sized for T rows and the group's heads.
     """
     from . import ops
 
     T = q.shape[0]
-    b_of_t, qlens, bt_rows, seq_rows = _chunk_rows(block_table, seq_lens, query_start_loc, T)
+    b_of_t, qlens, seq_rows = _chunk_rows(seq_lens, query_start_loc, T)
     ops.kv_append(new_key[:T], new_value[:T], key_cache, value_cache, slot_mapping[:T])
     ctx_out = torch.empty_like(out[:T])
     ctx_lse = torch.empty(q.shape[1], T, dtype=torch.float32, device=q.device)
-    dcp_decode(comm, q, key_cache, value_cache, bt_rows, seq_rows, softmax_scale, ctx_out, None, None,
-               None, workspace, lse=ctx_lse, context_only=True)
+    # the context part in pieces of the slabs' rows (every rank cuts the same
+    # T the same way); each piece gathers only its rows' block tables
+    step = comm.max_tokens
+    for i in range(0, T, step):
+        sl = slice(i, min(T, i + step))
+        dcp_decode(comm, q[sl], key_cache, value_cache, block_table[b_of_t[sl]], seq_rows[sl],
+                   softmax_scale, ctx_out[sl], None, None, None, workspace, lse=ctx_lse[:, sl],
+                   context_only=True)
     q_out = torch.empty_like(ctx_out)
     q_lse = torch.empty_like(ctx_lse)
     _chunk_attention(comm, q, new_key, new_value, query_start_loc, qlens, b_of_t, max_query_len,
@@ -324,8 +352,8 @@ def dcp_prefill_group(comms: list, calls: list, workspaces: list) -> None:
     staged = []
     for c, kw in zip(comms, calls):
         T = kw["q"].shape[0]
-        b_of_t, qlens, bt_rows, seq_rows = _chunk_rows(kw["block_table"], kw["seq_lens"],
-                                                       kw["query_start_loc"], T)
+        b_of_t, qlens, seq_rows = _chunk_rows(kw["seq_lens"], kw["query_start_loc"], T)
+        bt_rows = kw["block_table"][b_of_t]
         ops.kv_append(kw["new_key"][:T], kw["new_value"][:T], kw["key_cache"], kw["value_cache"],
                       kw["slot_mapping"][:T])
         ctx_out = torch.empty_like(kw["out"][:T])

@@ -10,6 +10,7 @@ import torch
 
 vllm_backend = pytest.importorskip("vllm.v1.attention.backend")
 
+from ps_attn import _lib  # noqa: E402
 from ps_attn import backend as psb  # noqa: E402
 
 
@@ -294,7 +295,12 @@ def test_builder_sets_up_the_dcp_group(monkeypatch):
                           scheduler_config=SimpleNamespace(max_num_seqs=64, max_num_batched_tokens=8192),
                           compilation_config=SimpleNamespace(max_cudagraph_capture_size=128))
     b = psb.PSAttentionMetadataBuilder(SimpleNamespace(block_size=16), ["l0"], cfg, torch.device("cpu"))
-    assert seen["rows"] == 8192 and seen["hq_local"] == 16 and seen["interleave"] == 4
-    assert seen["group"] == "cpu-group" and seen["ws"] == (8192, 8, 128)
+    # rows capped at what one ps_dcp_decode call takes (larger steps run in pieces)
+    assert seen["rows"] == _lib.PS_DCP_MAX_TOKENS == 4096
+    assert seen["hq_local"] == 16 and seen["interleave"] == 4
+    assert seen["group"] == "cpu-group" and seen["ws"] == (4096, 8, 128)
+    lib = _lib.load()  # the library accepts the capped rows, and nothing above
+    assert lib.ps_dcp_slab_bytes(seen["rows"], 16, 2) > 0
+    assert lib.ps_dcp_slab_bytes(seen["rows"] + 1, 16, 2) == -1
     md = b.build(0, _common([1, 3], [10, 20]))
     assert isinstance(md.dcp_comm, Comm) and md.workspace == "ws" and md.cascade_plan is None

@@ -261,3 +261,93 @@ def test_oracle_dcp_prefill_equals_causal_attention(world, interleave):
         want, want_lse = ps_oracle.attention_ref(q[t0:t1].numpy(), k, v, causal=True, softmax_scale=scale)
         np.testing.assert_allclose(out[t0:t1], want, atol=2e-5)
         np.testing.assert_allclose(lse[:, t0:t1], want_lse, atol=2e-5)
+
+
+def test_dcp_decode_runs_large_steps_in_pieces(monkeypatch):
+    """More rows than the slabs hold run as consecutive calls over pieces of
+    max_tokens rows, each with its rows' slices of every per-row tensor."""
+    from types import SimpleNamespace
+
+    from ps_attn import dcp
+
+    seen = []
+
+    def fake_problem(comm, q, kc, vc, bt, sl, scale, out, nk, nv, slots, lse, context_only):
+        seen.append((q[:, 0, 0].tolist(), bt[:, 0].tolist(), sl.tolist(), out.data_ptr(),
+                     None if nk is None else nk[:, 0, 0].tolist(),
+                     None if slots is None else slots.tolist(),
+                     None if lse is None else (lse.shape, lse.stride(), lse.data_ptr())))
+        return SimpleNamespace()
+
+    class Lib:
+        def ps_dcp_decode(self, *a):
+            return 0
+
+    monkeypatch.setattr(dcp, "_dcp_problem", fake_problem)
+    monkeypatch.setattr(dcp._lib, "load", lambda *a, **k: Lib())
+    monkeypatch.setattr(dcp, "_stream_ptr", lambda dev: 0)
+    monkeypatch.setattr(dcp.ctypes, "byref", lambda x: x)
+    T, hl = 10, 2
+    q = torch.arange(T, dtype=torch.float32)[:, None, None].expand(T, hl, 4).contiguous()
+    bt = torch.arange(T, dtype=torch.int32)[:, None].expand(T, 3).contiguous()
+    sl = torch.arange(100, 100 + T, dtype=torch.int32)
+    out = torch.zeros(T, hl, 4)
+    nk = q[:, :1].clone()
+    slots = torch.arange(T, dtype=torch.int64) * 7
+    lse = torch.zeros(hl, T)
+    comm = SimpleNamespace(max_tokens=4)
+    ws = SimpleNamespace(buffer=torch.zeros(1), nbytes=1)
+    dcp.dcp_decode(comm, q, None, None, bt, sl, 1.0, out, nk, nk, slots, ws, lse=lse)
+    assert [s[0] for s in seen] == [[0, 1, 2, 3], [4, 5, 6, 7], [8, 9]]
+    assert [s[1] for s in seen] == [[0, 1, 2, 3], [4, 5, 6, 7], [8, 9]]
+    assert [s[2] for s in seen] == [[100, 101, 102, 103], [104, 105, 106, 107], [108, 109]]
+    assert [s[4] for s in seen] == [[0, 1, 2, 3], [4, 5, 6, 7], [8, 9]]
+    assert [s[5] for s in seen] == [[0, 7, 14, 21], [28, 35, 42, 49], [56, 63]]
+    assert [s[3] for s in seen] == [out[i].data_ptr() for i in (0, 4, 8)]
+    # lse pieces: columns of [hl, T] (head stride T, token stride 1)
+    assert [s[6] for s in seen] == [((hl, 4), (T, 1), lse[:, 0].data_ptr()),
+                                    ((hl, 4), (T, 1), lse[:, 4].data_ptr()),
+                                    ((hl, 2), (T, 1), lse[:, 8].data_ptr())]
+    seen.clear()
+    dcp.dcp_decode(comm, q[:3], None, None, bt[:3], sl[:3], 1.0, out[:3], None, None, None, ws,
+                   context_only=True)
+    assert len(seen) == 1 and seen[0][0] == [0, 1, 2]
+
+
+def test_dcp_chunk_scratch_is_bounded_by_the_tokens(monkeypatch):
+    """The chunks' own keys/values go to a scratch paged cache of at most
+    T / block_size + B + 1 blocks (not B x the longest chunk): each sequence
+    gets its own pages at a running offset, every slot lands in its own
+    sequence's pages, and the scratch block table names exactly them."""
+    from types import SimpleNamespace
+
+    from ps_attn import dcp, ops
+
+    calls = {}
+    monkeypatch.setattr(ops, "kv_append", lambda k, v, kc, vc, slots: calls.update(
+        append=(k.shape, kc.shape, slots.clone())))
+    monkeypatch.setattr(ops, "chunked_prefill", lambda q, kc, vc, bt, lens, qsl, scale, out, lse=None:
+                        calls.update(prefill=(bt.clone(), lens.clone(), kc.shape)))
+    bs = 16
+    qlens = [1, 300, 2, 17, 16]  # one long chunk among short ones
+    qsl = torch.tensor([0] + list(torch.tensor(qlens).cumsum(0)), dtype=torch.int32)
+    T, B = int(qsl[-1]), len(qlens)
+    hkv, world, rank, hl = 2, 2, 1, 4
+    q = torch.zeros(T, hl, 8)
+    nk = torch.zeros(T, hkv, 8)
+    b_of_t, ql, _ = dcp._chunk_rows(torch.tensor(qlens, dtype=torch.int32) + 5, qsl, T)
+    comm = SimpleNamespace(world=world, rank=rank)
+    dcp._chunk_attention(comm, q, nk, nk, qsl, ql, b_of_t, max(qlens), bs, 1.0, q.clone(), None)
+    nblk = calls["append"][1][0]
+    assert nblk == T // bs + B + 1 and nblk < B * ((max(qlens) + bs - 1) // bs)
+    slots = calls["append"][2]
+    bt, lens, _ = calls["prefill"]
+    assert lens.tolist() == qlens
+    pages = [(x + bs - 1) // bs for x in qlens]
+    for b in range(B):
+        own = bt[b, :pages[b]].tolist()
+        assert own == list(range(sum(pages[:b]), sum(pages[:b]) + pages[b]))
+        for i in range(qlens[b]):
+            s = int(slots[int(qsl[b]) + i])
+            assert s // bs == own[i // bs] and s % bs == i % bs
+    assert int(bt.max()) < nblk and int(slots.max()) < nblk * bs
