@@ -1,18 +1,28 @@
 """Benchmark: paged PS-attention decode step (KV append + split-KV decode with
 the fused combine) on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2|3|5] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2|3|4|5] [--impl ours|reference]
 
 One "step" = append one new token per sequence through slot_mapping, then
-decode attention for every sequence, on one layer (benchmark config 2 by
-default: Qwen3-0.6B attention shapes 16q/8kv, d=128, bf16, 64 sequences,
-contexts U[1024, 4096], block 16).  Inputs (KV pool 671 MB) exceed the 126 MB
-L2, so no flush is needed between steps.
+decode attention for every sequence, on one layer.  The default workload is
+benchmark config 5 (Qwen3-32B attention shapes 64q/8kv, d=128, bf16, 512
+sequences, contexts log-uniform in [2048, 32768], block 16): the config the
+metric is quoted on at 1/2/4/8 GPUs.  Inputs (KV pool 23 GB) exceed the
+126 MB L2, so no flush is needed between steps.
 
-N > 1 (torchrun, one process per GPU): config 2 runs as independent replicas
-of the batch per GPU (sequence-batch sharding, no data-path collective, weak
-scaling); ``--config 5`` shards KV heads across GPUs and all-gathers the head
-outputs with NCCL (strong scaling).
+N > 1 (torchrun, one process per GPU): config 5 shards KV heads across the
+GPUs (rank r: KV heads [r*8/N, (r+1)*8/N) and their query heads) and
+all-gathers the head outputs over NVLink peer memory (``ps_head_gather``;
+``--gather nccl`` for NCCL's all_gather) -- strong scaling, every rank checks
+sampled gathered rows against a torch fp32 attention of the same rows.
+Configs 2-4 at N > 1 run as independent replicas (sequence-batch sharding,
+no data-path collective, weak scaling).
+
+At N = 1 the line also carries (unless ``--no-side`` / ``--no-fa4``):
+``fa4`` -- vLLM's own path on the same inputs and GPU
+(``reshape_and_cache_flash`` + ``flash_attn_varlen_func(fa_version=4)``),
+timed with CUDA events; ``configs`` -- configs 2, 3 and 4 measured the same
+way; ``prefill`` -- config 4's chunked prefill on the tensor-core roofline.
 
 ``--impl reference`` times the reference's CPU implementation of the same step
 on the host cores (vLLM's fp32 torch ``attention_ref``, loaded by file path,
@@ -22,7 +32,6 @@ from __future__ import annotations
 
 import argparse
 import json
-import math
 import os
 import statistics
 import subprocess
@@ -40,6 +49,11 @@ import torch  # noqa: E402
 METRIC = "paged PS-attn decode tokens/s + HBM GB/s (% of 8 TB/s) at 1/2/4/8 B200"
 NOMINAL_HBM_GBS = 8000.0
 FALLBACK_HBM_GBS = 6650.0
+DEFAULT_CONFIG = 5
+FA4_CALL = ("vllm._custom_ops.reshape_and_cache_flash + vllm.vllm_flash_attn.flash_attn_varlen_func("
+            "q, k_cache, v_cache, out, cu_seqlens_q, max_seqlen_q, seqused_k, max_seqlen_k, "
+            "softmax_scale, causal=True, block_table, fa_version=4, num_splits=0) as "
+            "vllm/v1/attention/backends/flash_attn.py:796-817 calls it on sm_100")
 
 CONFIG_NAMES = {
     2: "cfg2: Qwen3-0.6B attn (16q/8kv, d128) bf16 paged decode, B=64, ctx U[1024,4096], block 16",
@@ -59,19 +73,24 @@ def prefill_flops(q_lens, seq_lens, num_q_heads, head_size=128):
     return 4 * num_q_heads * head_size * pairs
 
 
-def measured_peaks():
+def _peaks_file():
     p = REPO / "MEASURED_PEAKS.json"
-    if p.exists():
-        d = json.loads(p.read_text())
+    return json.loads(p.read_text()) if p.exists() else None
+
+
+def measured_peaks():
+    d = _peaks_file()
+    if d is not None:
         return float(d["hbm_gbs"]), "measured"
     return FALLBACK_HBM_GBS, "fallback"
 
 
-def measured_tensor_peak():
-    p = REPO / "MEASURED_PEAKS.json"
-    if p.exists():
-        return float(json.loads(p.read_text())["bf16_tflops"])
-    return 1590.0
+def measured_tensor_peaks():
+    """(burst, sustained) dense bf16 TFLOP/s and their source."""
+    d = _peaks_file()
+    if d is not None:
+        return float(d["bf16_tflops"]), float(d.get("bf16_tflops_sustained", d["bf16_tflops"])), "measured"
+    return 1590.0, 1400.0, "fallback"
 
 
 def profile_traffic(kernel_tag: str):
@@ -86,6 +105,16 @@ def profile_traffic(kernel_tag: str):
             except ValueError:
                 return None
     return None
+
+
+def config_dict(cfg: int) -> dict:
+    """The workload description shared by both arms (no device needed)."""
+    from ps_attn import workloads
+
+    q_lens, seq_lens, kw = workloads.config_lengths(cfg)
+    return {"workload": CONFIG_NAMES[cfg], "num_seqs": len(seq_lens), "num_q_heads": kw["num_q_heads"],
+            "num_kv_heads": kw["num_kv_heads"], "head_size": 128, "block_size": 16,
+            "kv_tokens": int(sum(seq_lens)), "new_tokens_per_step": int(sum(q_lens))}
 
 
 class ClockSampler:
@@ -150,11 +179,476 @@ def dist_env():
     return world, rank, local
 
 
+def _all_max(x: float, world: int, dev) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+INPUT_KEYS = ("q", "key", "value", "slot_mapping", "seq_lens", "block_table", "query_start_loc")
+
+
 # ----------------------------------------------------------------------------
 # our arm
 # ----------------------------------------------------------------------------
+class Arm:
+    """One benchmark config on this GPU: its batch, buffers and the step's
+    launches as a list of phases (append / plan / decode / prefill / gather),
+    each replayed from its own CUDA graph so CUDA events can bracket it."""
+
+    def __init__(self, cfg, dev, world=1, rank=0, *, kv_fp8=False, cascade=False, fused=True,
+                 gather="peer", use_graph=True):
+        from ps_attn import ops, workloads
+
+        self.cfg, self.dev, self.world, self.rank = cfg, dev, world, rank
+        self.sharded = cfg == 5 and world > 1
+        self.kv_fp8, self.fused, self.use_graph = kv_fp8, fused, use_graph
+        if self.sharded:
+            per = 8 // world
+            batch = workloads.make_config(cfg, device=dev, kv_heads_slice=(rank * per, (rank + 1) * per))
+        else:
+            batch = workloads.make_config(cfg, device=dev, seed=rank if cfg != 5 else 0)
+        self.batch = batch
+        B = self.B = batch.num_seqs
+        self.hq, self.hkv = batch.q.shape[1], batch.kv_cache.shape[3]
+        # GRPO groups share prompt pages: the cascade decode reads each prefix
+        # once per 16-column pass (opt-in: on B200 it is not faster than the
+        # plain decode, whose repeated prefix reads mostly hit L2)
+        self.cascade = cfg == 3 and cascade
+        self.ws = ops.DecodeWorkspace(B, self.hq, self.hkv, 128, dev, cascade=self.cascade)
+        self.plan = ops.CascadePlan(B, dev) if self.cascade else None
+        self.out = torch.empty_like(batch.q)
+        self.lse = torch.empty(self.hq, batch.num_tokens, dtype=torch.float32, device=dev)
+        self.skw = {}
+        if kv_fp8:
+            # e4m3 codes of the synthetic N(0,1) cache at scale 1/64 (|x| < 7
+            # fits in 448), quantized a slab of blocks at a time
+            scale = torch.tensor(1.0 / 64.0, dtype=torch.float32, device=dev)
+            codes = torch.empty(batch.kv_cache.shape, dtype=torch.uint8, device=dev)
+            for i in range(0, batch.kv_cache.shape[1], 4096):
+                codes[:, i:i + 4096] = (batch.kv_cache[:, i:i + 4096].float() / scale).to(
+                    torch.float8_e4m3fn).view(torch.uint8)
+            batch.kv_cache = codes
+            self.skw = dict(k_scale=scale, v_scale=scale)
+            torch.cuda.empty_cache()
+        self.kc, self.vc = batch.kv_cache[0], batch.kv_cache[1]
+        self.mixed = cfg == 4
+        self.nd = B
+        self.pf_flops = 0
+        if self.mixed:
+            qlens = (batch.query_start_loc[1:] - batch.query_start_loc[:-1]).tolist()
+            self.nd = sum(1 for x in qlens if x == 1)
+            assert all(x == 1 for x in qlens[:self.nd]), "decode-first batch expected"
+            self.pf_flops = prefill_flops(qlens, batch.seq_lens.tolist(), self.hq)
+        self.peer_gather = None
+        self.full_out = None
+        self.gathered = None
+        if self.sharded:
+            self.full_out = torch.empty(B, self.hq * world, 128, dtype=batch.q.dtype, device=dev)
+            if gather == "peer":
+                # head outputs exchanged over NVLink peer memory (ps_head_gather)
+                from ps_attn import sharding
+
+                shard = sharding.HeadShard(world, rank, self.hq * world, self.hkv * world)
+                self.peer_gather = sharding.PeerHeadGather.from_process_group(
+                    shard, B, batch.q.dtype, device=dev)
+            else:
+                self.gathered = torch.empty(world, B, self.hq, 128, dtype=batch.q.dtype, device=dev)
+        self.stream = torch.cuda.Stream(dev)
+        self.graphs = []
+        self.names = []
+
+    # -- the step's launches over a set of input tensors -----------------------
+    def inputs(self) -> dict:
+        return {k: getattr(self.batch, k) for k in INPUT_KEYS}
+
+    def phases(self, inp: dict) -> list:
+        from ps_attn import ops
+
+        kc, vc, ws, plan, nd = self.kc, self.vc, self.ws, self.plan, self.nd
+        scale = self.batch.softmax_scale
+        out, lse, skw = self.out, self.lse, self.skw
+        fkw = dict(new_key=inp["key"], new_value=inp["value"],
+                   slot_mapping=inp["slot_mapping"]) if self.fused else {}
+        ph = []
+        if not self.fused:
+            ph.append(("append", lambda: ops.kv_append(inp["key"], inp["value"], kc, vc, inp["slot_mapping"],
+                                                       **skw)))
+        elif self.mixed:  # prefill tokens still go through the append kernel
+            ph.append(("append", lambda: ops.kv_append(inp["key"][nd:], inp["value"][nd:], kc, vc,
+                                                       inp["slot_mapping"][nd:])))
+        if self.cascade:  # the per-step plan (an engine builds it once per step for all layers)
+            ph.append(("plan", lambda: ops.cascade_plan(inp["block_table"], inp["seq_lens"], self.hq, self.hkv,
+                                                        16, query_start_loc=inp["query_start_loc"], plan=plan)))
+        if self.peer_gather is not None:  # this rank's heads into its slab
+            ph.append(("decode", lambda: self.peer_gather.decode(
+                inp["q"], kc, vc, inp["block_table"], inp["seq_lens"], scale, self.full_out, lse=lse,
+                query_start_loc=inp["query_start_loc"], workspace=ws, **fkw, **skw)))
+        elif not self.mixed:
+            ph.append(("decode", lambda: ops.paged_decode(
+                inp["q"], kc, vc, inp["block_table"], inp["seq_lens"], scale, out, lse=lse,
+                query_start_loc=inp["query_start_loc"], workspace=ws, cascade=plan, **fkw, **skw)))
+        else:
+            ph.append(("decode", lambda: ops.paged_decode(
+                inp["q"][:nd], kc, vc, inp["block_table"][:nd], inp["seq_lens"][:nd], scale, out[:nd],
+                lse=lse[:, :nd], workspace=ws, **fkw)))
+            ph.append(("prefill", lambda: ops.chunked_prefill(
+                inp["q"], kc, vc, inp["block_table"][nd:], inp["seq_lens"][nd:], inp["query_start_loc"][nd:],
+                scale, out, lse=lse, workspace=ws)))
+        if self.sharded:
+            if self.peer_gather is not None:
+                ph.append(("gather", lambda: self.peer_gather.gather(self.B, self.full_out)))
+            else:
+                def nccl_gather():
+                    import torch.distributed as dist
+
+                    dist.all_gather_into_tensor(self.gathered, out)
+                    self.full_out.view(self.B, self.world, self.hq, 128).copy_(self.gathered.permute(1, 0, 2, 3))
+
+                ph.append(("gather", nccl_gather))
+        return ph
+
+    def result(self) -> torch.Tensor:
+        """The step's output as the caller reads it."""
+        return self.full_out if self.sharded else self.out
+
+    def capture(self, inp: dict | None = None) -> tuple:
+        """Warm up the phases over ``inp`` and capture one graph per phase.
+        Returns (names, callables, graphs); with --no-graph the callables are
+        the eager phases and there are no graphs."""
+        ph = self.phases(self.inputs() if inp is None else inp)
+        names = [n for n, _ in ph]
+        with torch.cuda.stream(self.stream):
+            for _ in range(3):
+                for _, fn in ph:
+                    fn()
+            self.stream.synchronize()
+            if not self.use_graph:
+                return names, [fn for _, fn in ph], []
+            graphs = []
+            for _, fn in ph:
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=self.stream):
+                    fn()
+                graphs.append(g)
+        return names, [g.replay for g in graphs], graphs
+
+    def setup(self):
+        self.names, self.runs, self.graphs = self.capture()
+
+    def step(self, ev=None):
+        if ev is not None:
+            ev[0].record(self.stream)
+        for i, run in enumerate(self.runs):
+            run()
+            if ev is not None:
+                ev[i + 1].record(self.stream)
+
+    def time(self, steps: int, warmup: int, sampler: ClockSampler | None = None) -> dict:
+        world, dev = self.world, self.dev
+        with torch.cuda.stream(self.stream):
+            for _ in range(warmup):
+                self.step()
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        if sampler is not None:
+            sampler.start()
+            time.sleep(0.25)
+        n_ev = len(self.runs) + 1
+        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(n_ev)] for _ in range(steps)]
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(self.stream):
+            t0.record(self.stream)
+            for i in range(steps):
+                self.step(evs[i])
+            t1.record(self.stream)
+        torch.cuda.synchronize(dev)
+        elapsed_ms = t0.elapsed_time(t1)
+        clocks = None
+        if sampler is not None:
+            # keep the same load on the GPU for ~1.5 s so the sampler sees it
+            extra_t = time.perf_counter()
+            with torch.cuda.stream(self.stream):
+                while time.perf_counter() - extra_t < max(0.0, 1.5 - elapsed_ms / 1e3):
+                    for _ in range(20):
+                        self.step()
+                    self.stream.synchronize()
+            clocks = sampler.stop()
+        elapsed_ms = _all_max(elapsed_ms, world, dev)
+        phase_ms = {n: sum(e[i].elapsed_time(e[i + 1]) for e in evs) / steps for i, n in enumerate(self.names)}
+        assert self.ws.status() == 0, f"device status {self.ws.status():#x}"
+        return {"elapsed_ms": elapsed_ms, "ms": elapsed_ms / steps, "phase_ms": phase_ms, "clocks": clocks}
+
+    # -- roofline bookkeeping ---------------------------------------------------
+    def decode_bytes(self) -> int:
+        """Algorithmic bytes of one decode launch: KV read (config 3: each
+        shared prefix page once), Q in, O out, block table + lengths, and the
+        fused append's row read + write."""
+        b, nd, hkv, hq = self.batch, self.nd, self.hkv, self.hq
+        es = b.kv_cache.element_size()
+        if self.mixed:
+            kv_tokens = int(b.seq_lens[:nd].sum())
+            meta = nd * b.block_table.shape[1] * 4 + nd * 4 * 2
+        else:
+            kv_tokens = b.unique_tokens if self.cfg == 3 else b.logical_tokens
+            meta = b.block_table.numel() * 4 + nd * 4 * 2
+        kv = kv_tokens * hkv * 128 * 2 * es
+        qo = nd * hq * 128 * 2 * b.q.element_size()
+        app = nd * hkv * 128 * 2 * (b.key.element_size() + es) if self.fused else 0
+        return int(kv + qo + meta + app)
+
+    def launches_per_step(self) -> int:
+        return len(self.names)
+
+    def close(self):
+        self.graphs.clear()
+        self.runs = []
+        if self.peer_gather is not None:
+            self.peer_gather.close()
+
+
+def decode_roofline(arm: Arm, decode_ms: float, traffic=None) -> dict:
+    peak, peak_kind = measured_peaks()
+    nbytes = arm.decode_bytes()
+    achieved = nbytes / (decode_ms / 1e3) / 1e9
+    return {"kernel": "paged_decode", "bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+            "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
+            "frac_of_8tbs": round(achieved / NOMINAL_HBM_GBS, 4), "bytes_per_launch": nbytes,
+            "ms_per_launch": round(decode_ms, 5), "traffic": traffic}
+
+
+def prefill_roofline(arm: Arm, prefill_ms: float) -> dict:
+    burst, sustained, kind = measured_tensor_peaks()
+    tf = arm.pf_flops / (prefill_ms / 1e3) / 1e12
+    return {"kernel": "chunked_prefill", "bound": "tensor", "ms_per_launch": round(prefill_ms, 5),
+            "flops_per_launch": arm.pf_flops, "achieved": round(tf, 1), "unit": "TFLOP/s",
+            "peak": sustained, "peak_kind": f"{kind} bf16 dense (cuBLAS), sustained",
+            "frac": round(tf / sustained, 4), "frac_of_burst": round(tf / burst, 4),
+            "traffic": profile_traffic("chunked_prefill_cfg4")}
+
+
+# ----------------------------------------------------------------------------
+# vLLM's FA4 path on the same inputs (the GPU bar)
+# ----------------------------------------------------------------------------
+def _median_ms(fn, stream, n: int) -> float:
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            fn()
+        stream.synchronize()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+        for a, b in evs:
+            a.record(stream)
+            fn()
+            b.record(stream)
+    stream.synchronize()
+    return statistics.median(a.elapsed_time(b) for a, b in evs)
+
+
+def fa4_compare(arm: Arm, steps: int, ours_step_ms: float, ours_phase_ms: dict) -> dict:
+    """Time vLLM's serving call on ``arm``'s inputs (the same cache, block
+    table and new rows; the append writes the same bytes ours does) and
+    compare its output and LSE with ours.  Timed as the faster of eager
+    calls and a CUDA-graph replay (vLLM serves decode from full graphs)."""
+    try:
+        from vllm import _custom_ops as vops
+        from vllm.vllm_flash_attn.flash_attn_interface import flash_attn_varlen_func
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"vLLM FA4 import failed: {e!r}"[:300]}
+    b, dev, nd = arm.batch, arm.dev, arm.nd
+    kc, vc = arm.kc, arm.vc
+    ones = torch.ones(1, dtype=torch.float32, device=dev)
+    qsl_h = b.query_start_loc.cpu()
+    sl_h = b.seq_lens.cpu()
+    out_fa = torch.empty_like(b.q)
+    stream = arm.stream
+
+    def call(rows, seqs, append=True, want_lse=False):
+        q0, q1 = rows
+        s0, s1 = seqs
+        qsl = b.query_start_loc[s0:s1 + 1] - b.query_start_loc[s0] if s0 else b.query_start_loc[s0:s1 + 1]
+        mq = int((qsl_h[s0 + 1:s1 + 1] - qsl_h[s0:s1]).max())
+        mk = int(sl_h[s0:s1].max())
+
+        def fn():
+            if append:
+                vops.reshape_and_cache_flash(b.key[q0:q1], b.value[q0:q1], kc, vc, b.slot_mapping[q0:q1],
+                                             "auto", ones, ones)
+            return flash_attn_varlen_func(
+                q=b.q[q0:q1], k=kc, v=vc, out=out_fa[q0:q1], cu_seqlens_q=qsl, max_seqlen_q=mq,
+                seqused_k=b.seq_lens[s0:s1], max_seqlen_k=mk, softmax_scale=b.softmax_scale, causal=True,
+                block_table=b.block_table[s0:s1], softcap=0.0, fa_version=4, num_splits=0,
+                return_softmax_lse=want_lse)
+        return fn
+
+    T, B = b.num_tokens, arm.B
+    res = {"call": FA4_CALL}
+    try:
+        full = call((0, T), (0, B))
+        t = time.perf_counter()
+        with torch.cuda.stream(stream):
+            _, lse_fa = call((0, T), (0, B), want_lse=True)()
+        stream.synchronize()
+        res["jit_s"] = round(time.perf_counter() - t, 1)
+        d = (out_fa.float() - arm.out.float()).abs()
+        res["max_abs_diff_vs_ours"] = float(d.max())
+        res["mean_abs_diff_vs_ours"] = float(d.mean())
+        res["lse_max_abs_diff_vs_ours"] = float((lse_fa - arm.lse).abs().max())
+        eager = _median_ms(full, stream, steps)
+        with torch.cuda.stream(stream):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                full()
+        graphed = _median_ms(g.replay, stream, steps)
+        del g
+        ms = min(eager, graphed)
+        res.update({"ms_per_step": round(ms, 5), "eager_ms": round(eager, 5), "graph_ms": round(graphed, 5),
+                    "tokens_per_s": round(T / (ms / 1e3), 1),
+                    "ratio_ours_over_fa4": round(ms / ours_step_ms, 4)})
+        if arm.mixed:
+            # the two halves separately (attention only), against our kernels
+            dec = _median_ms(call((0, nd), (0, nd), append=False), stream, steps)
+            pre = _median_ms(call((nd, T), (nd, B), append=False), stream, steps)
+            res["decode_attention_ms"] = round(dec, 5)
+            res["prefill_attention_ms"] = round(pre, 5)
+            res["decode_ratio_ours_over_fa4"] = round(dec / ours_phase_ms["decode"], 4)
+            res["prefill_ratio_ours_over_fa4"] = round(pre / ours_phase_ms["prefill"], 4)
+        else:
+            res["decode_attention_ms"] = round(_median_ms(call((0, T), (0, B), append=False), stream, steps), 5)
+            res["decode_ratio_ours_over_fa4"] = round(res["decode_attention_ms"] / ours_phase_ms["decode"], 4)
+    except Exception as e:  # noqa: BLE001
+        res["unavailable"] = f"FA4 call failed: {e!r}"[:400]
+    torch.cuda.synchronize(dev)
+    return res
+
+
+# ----------------------------------------------------------------------------
+# multi-GPU in-run check
+# ----------------------------------------------------------------------------
+def check_gathered(arm: Arm, nseq: int = 4) -> dict:
+    """Sampled rows of the gathered [B, Hq, 128] output against a torch fp32
+    attention over the same pages: every rank computes its own heads' rows,
+    the rows are all-gathered (outside the timed region) and every rank
+    compares all heads of its gathered output.  Tolerances: bf16 max-abs
+    2e-2, mean-abs 2e-3."""
+    import torch.distributed as dist
+
+    b = arm.batch
+    B, bs = arm.B, arm.kc.shape[1]
+    seqs = sorted({0, B // 3, (2 * B) // 3, B - 1})[:nseq]
+    grp = arm.hq // arm.hkv
+    refs = []
+    for s in seqs:
+        L = int(b.seq_lens[s])
+        npg = (L + bs - 1) // bs
+        blocks = b.block_table[s, :npg].long()
+        k = arm.kc[blocks].reshape(npg * bs, arm.hkv, 128)[:L].float()
+        v = arm.vc[blocks].reshape(npg * bs, arm.hkv, 128)[:L].float()
+        q = b.q[s].float().view(arm.hkv, grp, 128)
+        sc = torch.einsum("hgd,lhd->hgl", q, k) * b.softmax_scale
+        p = torch.softmax(sc, dim=-1)
+        refs.append(torch.einsum("hgl,lhd->hgd", p, v).reshape(arm.hq, 128))
+    ref = torch.stack(refs)  # [n, hq_local, 128]
+    allref = torch.empty(arm.world, *ref.shape, dtype=ref.dtype, device=ref.device)
+    dist.all_gather_into_tensor(allref, ref)
+    want = allref.permute(1, 0, 2, 3).reshape(len(seqs), arm.hq * arm.world, 128)
+    got = arm.full_out[seqs].float()
+    err = (got - want).abs()
+    mx = _all_max(float(err.max()), arm.world, arm.dev)
+    mean = _all_max(float(err.mean()), arm.world, arm.dev)
+    return {"seqs": seqs, "heads": arm.hq * arm.world, "max_abs": mx, "mean_abs": mean,
+            "ok": bool(mx <= 2e-2 and mean <= 2e-3),
+            "reference": "torch fp32 attention over the gathered pages, every rank's heads all-gathered"}
+
+
+# ----------------------------------------------------------------------------
+# end to end through the public ops
+# ----------------------------------------------------------------------------
+def run_e2e(arm: Arm, steps: int) -> dict:
+    """The step as a serving engine runs it: this step's inputs copied from
+    pinned host memory into persistent device buffers, the step's ops
+    replayed from CUDA graphs captured over those buffers (what vLLM does
+    for decode), and the whole attention output read back to the host.
+    KV-head-sharded runs include the head all-gather."""
+    b = arm.batch
+    host = {k: getattr(b, k).cpu().pin_memory() for k in INPUT_KEYS}
+    dev_in = {k: torch.empty_like(getattr(b, k)) for k in INPUT_KEYS}
+    for k in INPUT_KEYS:
+        dev_in[k].copy_(host[k])
+    result = arm.result()
+    out_host = torch.empty(result.shape, dtype=result.dtype).pin_memory()
+    h2d = sum(v.numel() * v.element_size() for v in host.values())
+    d2h = result.numel() * result.element_size()
+    _, runs, graphs = arm.capture(dev_in)
+    stream = arm.stream
+
+    def one():
+        for k in INPUT_KEYS:
+            dev_in[k].copy_(host[k], non_blocking=True)
+        for r in runs:
+            r()
+        out_host.copy_(result, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            one()
+    torch.cuda.synchronize(arm.dev)
+    if arm.world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    a = torch.cuda.Event(enable_timing=True)
+    e = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        a.record(stream)
+        for _ in range(steps):
+            one()
+        e.record(stream)
+    torch.cuda.synchronize(arm.dev)
+    ms = _all_max(a.elapsed_time(e) / steps, arm.world, arm.dev)
+    runs.clear()
+    graphs.clear()  # before any process-group teardown (a graph may hold NCCL calls)
+    replicas = 1 if arm.sharded else arm.world
+    return {"value": round(b.num_tokens * replicas / (ms / 1e3), 1), "unit": "tokens/s",
+            "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+            "ms_per_step": round(ms, 5), "steps": steps, "cuda_graph": arm.use_graph,
+            "note": "per step: pinned host inputs -> device (cudaMemcpyAsync), the ops (graph replay), "
+                    "the whole output -> pinned host"}
+
+
+# ----------------------------------------------------------------------------
+# side configs (N = 1): 2, 3, 4 with the FA4 bar
+# ----------------------------------------------------------------------------
+def side_config(cfg: int, dev, steps: int, warmup: int, fa4: bool) -> dict:
+    arm = Arm(cfg, dev)
+    arm.setup()
+    t = arm.time(steps, warmup)
+    ms = t["ms"]
+    res = {"workload": CONFIG_NAMES[cfg], "tokens_per_s": round(arm.batch.num_tokens / (ms / 1e3), 1),
+           "ms_per_step": round(ms, 5), "phase_ms": {k: round(v, 5) for k, v in t["phase_ms"].items()},
+           "decode": decode_roofline(arm, t["phase_ms"]["decode"], profile_traffic(f"paged_decode_cfg{cfg}"))}
+    if cfg == 3:
+        res["decode"]["note"] = "bytes count each shared prefix page once (unique pages)"
+    if arm.mixed:
+        res["prefill"] = prefill_roofline(arm, t["phase_ms"]["prefill"])
+    if fa4:
+        res["fa4"] = fa4_compare(arm, steps, ms, t["phase_ms"])
+    arm.close()
+    del arm
+    torch.cuda.empty_cache()
+    return res
+
+
 def run_ours(args):
-    from ps_attn import _lib, ops, workloads
+    from ps_attn import _lib, workloads
 
     world, rank, local = dist_env()
     torch.cuda.set_device(local)
@@ -164,285 +658,83 @@ def run_ours(args):
 
         import torch.distributed as dist
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=dev)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     _lib.load(build_if_stale=False)
     cfg = args.config
-    sharded = cfg == 5 and world > 1
-    if sharded:
-        hkv_total = 8
-        assert hkv_total % world == 0, "KV heads must divide across GPUs"
-        per = hkv_total // world
-        batch = workloads.make_config(cfg, device=dev, kv_heads_slice=(rank * per, (rank + 1) * per))
-    else:
-        batch = workloads.make_config(cfg, device=dev, seed=rank if cfg != 5 else 0)
-    B = batch.num_seqs
-    hq = batch.q.shape[1]
-    hkv = batch.kv_cache.shape[3]
-    # GRPO groups share prompt pages: the cascade decode reads each prefix once
-    # per 16-column pass (opt-in: on B200 it is not faster than the plain
-    # decode, whose repeated prefix reads mostly hit L2)
-    cascade = cfg == 3 and args.cascade
-    ws = ops.DecodeWorkspace(B, hq, hkv, 128, dev, cascade=cascade)
-    plan = ops.CascadePlan(B, dev) if cascade else None
-    out = torch.empty_like(batch.q)
-    lse = torch.empty(hq, B, dtype=torch.float32, device=dev)
-    kc, vc = batch.kv_cache[0], batch.kv_cache[1]
-    skw = {}  # fp8 cache: dequantization scales
-    if args.kv_fp8:
-        # e4m3 codes of the synthetic N(0,1) cache at scale 1/64 (|x| < 7 fits
-        # in 448), quantized a slab of blocks at a time
-        scale = torch.tensor(1.0 / 64.0, dtype=torch.float32, device=dev)
-        codes = torch.empty(batch.kv_cache.shape, dtype=torch.uint8, device=dev)
-        step_nb = 4096
-        for i in range(0, batch.kv_cache.shape[1], step_nb):
-            codes[:, i:i + step_nb] = (batch.kv_cache[:, i:i + step_nb].float() / scale).to(
-                torch.float8_e4m3fn).view(torch.uint8)
-        batch.kv_cache = codes
-        kc, vc = codes[0], codes[1]
-        skw = dict(k_scale=scale, v_scale=scale)
-        torch.cuda.empty_cache()
-    mixed = cfg == 4
-    nd = B
-    gathered = None
-    peer_gather = None
-    if sharded:
-        gathered = torch.empty(world, B, hq, 128, dtype=batch.q.dtype, device=dev)
-        full_out = torch.empty(B, hq * world, 128, dtype=batch.q.dtype, device=dev)
-        if args.gather == "peer":
-            # head outputs exchanged over NVLink peer memory (ps_head_gather)
-            from ps_attn import sharding
+    arm = Arm(cfg, dev, world, rank, kv_fp8=args.kv_fp8, cascade=args.cascade, fused=not args.unfused,
+              gather=args.gather, use_graph=not args.no_graph)
+    arm.setup()
+    sampler = None if args.quick else ClockSampler(local)
+    t = arm.time(args.steps, args.warmup, sampler)
+    ms = t["ms"]
+    pm = t["phase_ms"]
+    check = check_gathered(arm) if arm.sharded else None
+    e2e = None if args.quick else run_e2e(arm, args.steps)
 
-            shard = sharding.HeadShard(world, rank, hq * world, hkv * world)
-            peer_gather = sharding.PeerHeadGather.from_process_group(shard, B, batch.q.dtype, device=dev)
-
-    fused = not args.unfused
-
-    def append():
-        if not fused:
-            ops.kv_append(batch.key, batch.value, kc, vc, batch.slot_mapping)
-        elif mixed:  # prefill tokens still go through the append kernel
-            ops.kv_append(batch.key[nd:], batch.value[nd:], kc, vc, batch.slot_mapping[nd:])
-        if cascade:  # the per-step plan (a serving engine builds it once per step for all layers)
-            ops.cascade_plan(batch.block_table, batch.seq_lens, hq, hkv, 16,
-                             query_start_loc=batch.query_start_loc, plan=plan)
-
-    if mixed:
-        qlens = (batch.query_start_loc[1:] - batch.query_start_loc[:-1]).tolist()
-        nd = sum(1 for x in qlens if x == 1)
-        assert all(x == 1 for x in qlens[:nd]), "decode-first batch expected"
-        pf_flops = prefill_flops(qlens, batch.seq_lens.tolist(), hq)
-
-    fkw = dict(new_key=batch.key, new_value=batch.value, slot_mapping=batch.slot_mapping) if fused else {}
-
-    def decode():
-        if peer_gather is not None:  # this rank's heads into its slab
-            peer_gather.decode(batch.q, kc, vc, batch.block_table, batch.seq_lens, batch.softmax_scale,
-                               full_out, lse=lse, query_start_loc=batch.query_start_loc, workspace=ws,
-                               **fkw, **skw)
-            return
-        if not mixed:
-            ops.paged_decode(batch.q, kc, vc, batch.block_table, batch.seq_lens,
-                             batch.softmax_scale, out, lse=lse,
-                             query_start_loc=batch.query_start_loc, workspace=ws, cascade=plan,
-                             **fkw, **skw)
-            return
-        ops.paged_decode(batch.q[:nd], kc, vc, batch.block_table[:nd], batch.seq_lens[:nd],
-                         batch.softmax_scale, out[:nd], workspace=ws, **fkw)
-
-    def prefill():
-        ops.chunked_prefill(batch.q, kc, vc, batch.block_table[nd:], batch.seq_lens[nd:],
-                            batch.query_start_loc[nd:], batch.softmax_scale, out, workspace=ws)
-
-    def gather():
-        if peer_gather is not None:
-            peer_gather.gather(B, full_out)
-            return
-        import torch.distributed as dist
-
-        dist.all_gather_into_tensor(gathered, out)
-        full_out.view(B, world, hq, 128).copy_(gathered.permute(1, 0, 2, 3))
-
-    stream = torch.cuda.Stream(dev)
-    use_graph = not args.no_graph
-    graphs = {}
-    with torch.cuda.stream(stream):
-        for _ in range(3):  # warm up before capture
-            append()
-            decode()
-            if peer_gather is not None:
-                gather()
-        stream.synchronize()
-        if mixed:
-            prefill()
-            stream.synchronize()
-        if use_graph:
-            fns = ([("append", append)] if (not fused or mixed or cascade) else []) + [("decode", decode)] + (
-                [("prefill", prefill)] if mixed else []) + ([("gather", gather)] if peer_gather else [])
-            for name, fn in fns:
-                g = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(g, stream=stream):
-                    fn()
-                graphs[name] = g
-
-    def step(ev=None):
-        if ev is not None:
-            ev[0].record(stream)
-        if use_graph:
-            if "append" in graphs:
-                graphs["append"].replay()
-        else:
-            append()
-        if ev is not None:
-            ev[1].record(stream)
-        if use_graph:
-            graphs["decode"].replay()
-        else:
-            decode()
-        if ev is not None:
-            ev[2].record(stream)
-        if mixed:
-            if use_graph:
-                graphs["prefill"].replay()
-            else:
-                prefill()
-            if ev is not None:
-                ev[3].record(stream)
-        if sharded:
-            if use_graph and "gather" in graphs:
-                graphs["gather"].replay()
-            else:
-                gather()
-
-    with torch.cuda.stream(stream):
-        for _ in range(args.warmup):
-            step()
-    torch.cuda.synchronize(dev)
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.barrier()
-    torch.cuda.synchronize(dev)
-
-    sampler = ClockSampler(local)
-    if not args.quick:
-        sampler.start()
-        time.sleep(0.25)
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
-    t0 = torch.cuda.Event(enable_timing=True)
-    t1 = torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        t0.record(stream)
-        for i in range(args.steps):
-            step(evs[i])
-        t1.record(stream)
-    torch.cuda.synchronize(dev)
-    elapsed_ms = t0.elapsed_time(t1)
-    # keep the same load on the GPU for at least ~1.5 s so the clock sampler sees it
-    extra_t = time.perf_counter()
-    with torch.cuda.stream(stream):
-        while not args.quick and time.perf_counter() - extra_t < max(0.0, 1.5 - elapsed_ms / 1e3):
-            for _ in range(50):
-                step()
-            stream.synchronize()
-    clocks = sampler.stop()
-    if world > 1:
-        import torch.distributed as dist
-
-        t = torch.tensor([elapsed_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        elapsed_ms = float(t.item())
-    append_ms = sum(e[0].elapsed_time(e[1]) for e in evs) / args.steps
-    decode_ms = sum(e[1].elapsed_time(e[2]) for e in evs) / args.steps
-    prefill_ms = sum(e[2].elapsed_time(e[3]) for e in evs) / args.steps if mixed else None
-    assert ws.status() == 0, f"device status {ws.status():#x}"
-
-    # ---- end to end through the public API: host inputs in, host output back ----
-    def nccl_gather(local_out):
-        import torch.distributed as dist
-
-        dist.all_gather_into_tensor(gathered, local_out)
-        full_out.view(B, world, hq, 128).copy_(gathered.permute(1, 0, 2, 3))
-
-    e2e = None if args.quick else run_e2e(
-        batch, ws, dev, args.steps, world, nd=nd if mixed else None,
-        replicas=1 if sharded else world, fused=fused, cascade=cascade, scales=skw,
-        full_out=full_out if sharded else None, peer=peer_gather,
-        gather=nccl_gather if sharded and peer_gather is None else None)
-
-    ms = elapsed_ms / args.steps
-    tokens_per_step = batch.num_tokens  # every rank produces all tokens (its heads when sharded)
-    value = (tokens_per_step * (world if not sharded else 1)) / (ms / 1e3)
-    peak, peak_kind = measured_peaks()
-    if mixed:
-        dec_tokens = int(batch.seq_lens[:nd].sum())
-        kv_bytes = dec_tokens * hkv * 128 * 2 * batch.kv_cache.element_size()
-        qo_bytes = nd * hq * 128 * 2 * batch.q.element_size()
-        meta_bytes = nd * batch.block_table.shape[1] * 4 + nd * 4 * 2
-    else:
-        kv_tokens = batch.unique_tokens if cfg == 3 else batch.logical_tokens
-        kv_bytes = kv_tokens * hkv * 128 * 2 * batch.kv_cache.element_size()
-        qo_bytes = B * hq * 128 * 2 * batch.q.element_size()
-        meta_bytes = batch.block_table.numel() * 4 + B * 4 * 2
-    # a fused append also reads the new K/V rows and writes them into the cache
-    app_bytes = (nd * hkv * 128 * 2 * (batch.key.element_size() + batch.kv_cache.element_size())
-                 if fused else 0)
-    decode_bytes = kv_bytes + qo_bytes + meta_bytes + app_bytes
-    step_bytes = workloads.hbm_bytes(batch)
-    achieved = decode_bytes / (decode_ms / 1e3) / 1e9
-    traffic = None if args.kv_fp8 else profile_traffic(f"paged_decode_cfg{cfg}")
+    tokens = arm.batch.num_tokens  # every rank produces all tokens (its heads when sharded)
+    value = tokens * (1 if arm.sharded else world) / (ms / 1e3)
+    step_bytes = workloads.hbm_bytes(arm.batch)
+    traffic = None if args.kv_fp8 or arm.sharded else profile_traffic(f"paged_decode_cfg{cfg}")
     res = {
         "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
-        "higher_is_better": True, "scaling": "strong" if sharded else "weak",
+        "higher_is_better": True, "scaling": "strong" if arm.sharded else "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {
-            "workload": CONFIG_NAMES[cfg], "num_seqs": B, "num_q_heads": hq * (world if sharded else 1),
-            "num_kv_heads": hkv * (world if sharded else 1), "head_size": 128, "block_size": 16,
-            "kv_tokens": batch.logical_tokens, "kv_pool_bytes": batch.kv_cache.numel() * batch.kv_cache.element_size(),
+        "config": config_dict(cfg),
+        "setup": {
             "parallelism": (f"kv-head tp{world} + " + ("NVLink peer-memory head gather (ps_head_gather)"
-                                                       if peer_gather else "NCCL all-gather") if sharded else
+                                                       if arm.peer_gather else "NCCL all-gather") if arm.sharded else
                             (f"batch replicas x{world}" if world > 1 else "single GPU")),
+            "heads_this_gpu": {"q": arm.hq, "kv": arm.hkv},
+            "kv_pool_bytes_this_gpu": arm.batch.kv_cache.numel() * arm.batch.kv_cache.element_size(),
             "l2": "inputs larger than L2 (KV pool > 126 MB); no flush",
-            "cuda_graph": use_graph,
+            "cuda_graph": arm.use_graph,
             "kv_cache_dtype": "fp8_e4m3 (per-tensor scale)" if args.kv_fp8 else "bf16",
+            "append_fused_into_decode": arm.fused,
+            "cascade": arm.cascade,
         },
+        "gpu_launches": arm.launches_per_step() * args.steps,
+        "phase_ms": {k: round(v, 5) for k, v in pm.items()},
         "hbm_gbs_step": round(step_bytes / (ms / 1e3) / 1e9, 1),
         "hbm_frac_of_8tbs_step": round(step_bytes / (ms / 1e3) / 1e9 / NOMINAL_HBM_GBS, 4),
-        "gpu_launches": ((3 if mixed else 2) - (1 if fused and not mixed else 0)
-                         + (1 if cascade else 0) + (1 if peer_gather else 0)) * args.steps,
-        "append_fused_into_decode": fused,
-        "cascade": (None if not cascade else {
-            "groups": int(plan.views()["num_groups"].item()),
-            "note": "shared prompt pages read once per 16-column pass; plan built every step "
-                    "(timed in append_ms); roofline bytes count each shared page once"}),
-        "roofline": {"kernel": "paged_decode", "bound": "hbm", "achieved": round(achieved, 1),
-                     "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4),
-                     "frac_of_8tbs": round(achieved / NOMINAL_HBM_GBS, 4),
-                     "bytes_per_launch": decode_bytes, "ms_per_launch": round(decode_ms, 5),
-                     "traffic": traffic},
-        "append_ms": round(append_ms, 5),
-        "prefill": (None if not mixed else {
-            "kernel": "chunked_prefill", "bound": "tensor", "ms_per_launch": round(prefill_ms, 5),
-            "flops_per_launch": pf_flops,
-            "achieved_tflops": round(pf_flops / (prefill_ms / 1e3) / 1e12, 1),
-            "peak_tflops": measured_tensor_peak(), "peak_kind": "measured bf16 dense (cuBLAS)",
-            "frac": round(pf_flops / (prefill_ms / 1e3) / 1e12 / measured_tensor_peak(), 4)}),
+        "roofline": decode_roofline(arm, pm["decode"], traffic),
+        "prefill": prefill_roofline(arm, pm["prefill"]) if arm.mixed else None,
         "e2e": e2e,
-        "clocks": clocks,
+        "clocks": t["clocks"],
     }
-    if rank == 0 and world == 1 and not args.quick:
-        res["cpu_baseline"] = cpu_baseline(cfg, budget_s=args.cpu_budget)
+    if arm.sharded:
+        res["gather"] = {"kind": "peer" if arm.peer_gather else "nccl", "ms_per_step": round(pm["gather"], 5),
+                         "share_of_step": round(pm["gather"] / ms, 4),
+                         "bytes_received_per_gpu": (world - 1) * arm.B * arm.hq * 128 * arm.batch.q.element_size()}
+        res["check"] = check
+    if arm.cascade:
+        res["cascade"] = {"groups": int(arm.plan.views()["num_groups"].item()),
+                          "note": "shared prompt pages read once per 16-column pass; plan built every step; "
+                                  "roofline bytes count each shared page once"}
+    if world == 1 and not args.quick:
+        if not args.no_fa4 and not args.kv_fp8 and not arm.cascade and arm.fused:
+            res["fa4"] = fa4_compare(arm, args.steps, ms, pm)
+        if rank == 0:
+            res["cpu_baseline"] = cpu_baseline(cfg, budget_s=args.cpu_budget)
+    if world == 1 and not args.quick and not args.no_side and cfg == DEFAULT_CONFIG and not args.kv_fp8:
+        arm.close()
+        del arm
+        torch.cuda.empty_cache()
+        side = {}
+        for c in (2, 3, 4):
+            side[f"cfg{c}"] = side_config(c, dev, args.steps, args.warmup, not args.no_fa4)
+        res["configs"] = side
+        res["prefill"] = side["cfg4"].get("prefill")
+        if "fa4" in side["cfg4"] and "prefill_attention_ms" in side["cfg4"]["fa4"]:
+            res["prefill"] = dict(res["prefill"], fa4_ms=side["cfg4"]["fa4"]["prefill_attention_ms"],
+                                  ratio_ours_over_fa4=side["cfg4"]["fa4"]["prefill_ratio_ours_over_fa4"])
     if rank == 0:
         print(json.dumps(res), flush=True)
     if world > 1:
         import torch.distributed as dist
 
-        dist.barrier()
-        graphs.clear()
-        if peer_gather is not None:
-            peer_gather.close()  # after the barrier: no peer still reads this slab
+        dist.barrier()  # no peer still reads this rank's slab
+        arm.close()
         dist.destroy_process_group()
 
 
@@ -522,10 +814,7 @@ def run_dcp(args):
                 step()
             stream.synchronize()
     clocks = sampler.stop()
-    if world > 1:
-        t = torch.tensor([elapsed_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        elapsed_ms = float(t.item())
+    elapsed_ms = _all_max(elapsed_ms, world, dev)
     assert ws.status() == 0, f"device status {ws.status():#x}"
 
     # end to end: this step's new-token rows (q, k, v) and slots from pinned
@@ -558,11 +847,7 @@ def run_dcp(args):
             one()
         e1.record(stream)
     torch.cuda.synchronize(dev)
-    e2e_ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+    e2e_ms = _all_max(e0.elapsed_time(e1), world, dev)
     h2d = sum(x.numel() * x.element_size() for x in (hq_in, hk_in, hv_in, hs_in))
     d2h = h_out.numel() * h_out.element_size()
 
@@ -581,12 +866,11 @@ def run_dcp(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic",
-        "config": {"workload": CONFIG_NAMES[cfg] + " -- decode context parallel", "num_seqs": B,
-                   "num_q_heads": hq_all, "num_kv_heads": hkv, "head_size": 128, "block_size": 16,
-                   "kv_tokens": batch.logical_tokens, "kv_tokens_this_rank": batch.unique_tokens,
-                   "parallelism": f"dcp{world} (interleave {args.interleave}), peer-memory exchange",
-                   "l2": "inputs larger than L2 (KV pool > 126 MB); no flush",
-                   "cuda_graph": graph is not None},
+        "config": config_dict(cfg),
+        "setup": {"mode": "decode context parallel", "kv_tokens_this_rank": batch.unique_tokens,
+                  "parallelism": f"dcp{world} (interleave {args.interleave}), peer-memory exchange",
+                  "l2": "inputs larger than L2 (KV pool > 126 MB); no flush",
+                  "cuda_graph": graph is not None},
         "gpu_launches": 4 * args.steps,
         "roofline": {"kernel": "dcp step (gather + paged_decode + combine)", "bound": "hbm",
                      "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind,
@@ -605,85 +889,6 @@ def run_dcp(args):
     comm.close()
     if world > 1:
         dist.destroy_process_group()
-
-
-def run_e2e(batch, ws, dev, steps, world, nd=None, replicas=1, fused=True, cascade=False, scales=None,
-            full_out=None, peer=None, gather=None):
-    """Same step through the public ops with per-step host->device inputs
-    (pinned) and the device->host read of the attention output.  ``nd``:
-    number of leading decode sequences of a mixed batch (the rest prefill).
-    KV-head sharded runs (``full_out``) include the head all-gather -- over
-    peer memory (``peer``) or NCCL (``gather(local_out)``) -- and read back
-    the whole output."""
-    from ps_attn import ops
-
-    B, hq = batch.num_seqs, batch.q.shape[1]
-    T = batch.num_tokens
-    host = {k: getattr(batch, k).cpu().pin_memory() for k in
-            ("q", "key", "value", "slot_mapping", "seq_lens", "block_table", "query_start_loc")}
-    dev_in = {k: torch.empty_like(v, device=dev) for k, v in host.items()}
-    out = torch.empty_like(batch.q)
-    result = out if full_out is None else full_out
-    out_host = torch.empty(result.shape, dtype=result.dtype).pin_memory()
-    h2d = sum(v.numel() * v.element_size() for v in host.values())
-    d2h = result.numel() * result.element_size()
-    kc, vc = batch.kv_cache[0], batch.kv_cache[1]
-    plan = ops.CascadePlan(B, dev) if cascade else None
-
-    def one():
-        for k, v in host.items():
-            dev_in[k].copy_(v, non_blocking=True)
-        fkw = dict(new_key=dev_in["key"], new_value=dev_in["value"],
-                   slot_mapping=dev_in["slot_mapping"]) if fused else {}
-        if not fused:
-            ops.kv_append(dev_in["key"], dev_in["value"], kc, vc, dev_in["slot_mapping"])
-        elif nd is not None:
-            ops.kv_append(dev_in["key"][nd:], dev_in["value"][nd:], kc, vc, dev_in["slot_mapping"][nd:])
-        if peer is not None:
-            peer.decode(dev_in["q"], kc, vc, dev_in["block_table"], dev_in["seq_lens"],
-                        batch.softmax_scale, full_out, query_start_loc=dev_in["query_start_loc"],
-                        workspace=ws, **fkw, **(scales or {}))
-            peer.gather(T, full_out)
-        elif nd is None:
-            if cascade:
-                ops.cascade_plan(dev_in["block_table"], dev_in["seq_lens"], hq,
-                                 kc.shape[2], kc.shape[1], query_start_loc=dev_in["query_start_loc"],
-                                 plan=plan)
-            ops.paged_decode(dev_in["q"], kc, vc, dev_in["block_table"], dev_in["seq_lens"],
-                             batch.softmax_scale, out, query_start_loc=dev_in["query_start_loc"],
-                             workspace=ws, cascade=plan, **fkw, **(scales or {}))
-        else:
-            ops.paged_decode(dev_in["q"][:nd], kc, vc, dev_in["block_table"][:nd],
-                             dev_in["seq_lens"][:nd], batch.softmax_scale, out[:nd], workspace=ws,
-                             **fkw)
-            ops.chunked_prefill(dev_in["q"], kc, vc, dev_in["block_table"][nd:],
-                                dev_in["seq_lens"][nd:], dev_in["query_start_loc"][nd:],
-                                batch.softmax_scale, out, workspace=ws)
-        if gather is not None:
-            gather(out)
-        out_host.copy_(result, non_blocking=True)
-
-    n = max(3, min(steps, 200))
-    for _ in range(3):
-        one()
-    torch.cuda.synchronize(dev)
-    a = torch.cuda.Event(enable_timing=True)
-    b = torch.cuda.Event(enable_timing=True)
-    a.record()
-    for _ in range(n):
-        one()
-    b.record()
-    torch.cuda.synchronize(dev)
-    ms = a.elapsed_time(b) / n
-    if world > 1:
-        import torch.distributed as dist
-
-        t = torch.tensor([ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    return {"value": round(T * replicas / (ms / 1e3), 1), "unit": "tokens/s",
-            "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
-            "ms_per_step": round(ms, 5), "steps": n}
 
 
 # ----------------------------------------------------------------------------
@@ -722,14 +927,18 @@ def reference_step(batch, attention_ref, seqs):
         blocks = batch.block_table[b, :npg].long()
         k = kc[blocks].reshape(npg * bs, hkv, d)[:L].float()
         v = vc[blocks].reshape(npg * bs, hkv, d)[:L].float()
-        q = batch.q[b:b + 1].float()
+        q0, q1 = int(batch.query_start_loc[b]), int(batch.query_start_loc[b + 1])
+        q = batch.q[q0:q1].float()
         o, _, lse = attention_ref(q[None], k[None], v[None], causal=True, return_lse=True)
         outs.append(o)
     return outs
 
 
 def cpu_baseline(cfg, budget_s=20.0, steps=None, warmup=1):
-    """Time the reference CPU step on a bounded sample of the workload."""
+    """Time the reference CPU step on a bounded sample of the workload: a
+    seeded prefix subset of the sequences (all 64 for config 2), repeated
+    until the time budget or ``steps`` is reached; tokens/s = new tokens
+    processed / time."""
     from ps_attn import workloads
 
     attention_ref = load_reference_attention()
@@ -743,13 +952,13 @@ def cpu_baseline(cfg, budget_s=20.0, steps=None, warmup=1):
             o, l = ps_oracle.attention_ref(q[0].numpy(), k[0].numpy(), v[0].numpy(), causal=causal)
             return torch.from_numpy(o)[None], None, torch.from_numpy(l)[None]
 
-    # sequences: seeded prefix subset sized for the time budget
     sub = {2: 64, 3: 16, 4: 16, 5: 16}[cfg]
     batch = workloads.make_config(cfg, device="cpu", max_seqs=sub)
     seqs = list(range(batch.num_seqs))
+    toks = int(batch.num_tokens)
     for _ in range(warmup):
         reference_step(batch, attention_ref, seqs[:2])
-    n_done, t_used = 0, 0.0
+    t_used = 0.0
     step_times = []
     while t_used < budget_s and (steps is None or len(step_times) < steps):
         t = time.perf_counter()
@@ -757,13 +966,13 @@ def cpu_baseline(cfg, budget_s=20.0, steps=None, warmup=1):
         dt = time.perf_counter() - t
         step_times.append(dt)
         t_used += dt
-        n_done += len(seqs)
         if steps is None and len(step_times) >= 200:
             break
-    value = n_done / t_used
+    value = toks * len(step_times) / t_used
+    full = len(workloads.config_lengths(cfg)[1])
     return {"value": round(value, 2), "unit": "tokens/s", "cores": torch.get_num_threads(),
             "kind": kind,
-            "sample": f"cfg{cfg}: {len(seqs)} sequences x {len(step_times)} steps "
+            "sample": f"cfg{cfg}: {len(seqs)} of {full} sequences ({toks} new tokens) x {len(step_times)} steps "
                       f"({t_used:.1f} s), fp32 attention_ref per sequence on gathered pages, "
                       f"torch index-put append; KV pool kept in the config dtype",
             "ms_per_step": round(1e3 * t_used / len(step_times), 3)}
@@ -778,9 +987,10 @@ def run_reference(args):
     res = {
         "metric": METRIC, "impl": "reference", "value": cb["value"], "unit": "tokens/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": cb["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+        "ms_per_step": cb["ms_per_step"], "higher_is_better": True,
+        "scaling": "strong" if args.config == 5 and world > 1 else "weak",
         "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
-        "config": {"workload": CONFIG_NAMES[args.config] + " (CPU reference, seeded sequence subset)"},
+        "config": config_dict(args.config),
         "cpu_baseline": cb,
         "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
@@ -791,9 +1001,9 @@ def run_reference(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=20)
-    ap.add_argument("--config", type=int, default=2, choices=[2, 3, 4, 5])
+    ap.add_argument("--config", type=int, default=DEFAULT_CONFIG, choices=[2, 3, 4, 5])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--unfused", action="store_true",
@@ -809,8 +1019,10 @@ def main():
     ap.add_argument("--interleave", type=int, default=1,
                     help="DCP: consecutive positions per rank (vLLM cp_kv_cache_interleave_size)")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
+    ap.add_argument("--no-fa4", action="store_true", help="skip the vLLM FA4 comparison")
+    ap.add_argument("--no-side", action="store_true", help="N=1: skip configs 2-4 after the headline")
     ap.add_argument("--quick", action="store_true",
-                    help="timed steps only: no end-to-end, CPU baseline or clock sampling")
+                    help="timed steps only: no end-to-end, CPU baseline, FA4, side configs or clock sampling")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
