@@ -49,9 +49,9 @@ constexpr int kThreads = 384;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
 // Of every 8 exponentials in a softmax row, this many are evaluated on the FMA
-// pipe (exp2_fma) instead of the MUFU unit, which the softmax otherwise keeps
-// ~45 % busy next to a ~45 % busy tensor pipe (measured on config 4: 0/8 865,
-// 1/8 891, 2/8 875 TFLOP/s).  The macro exists for sweeps.
+// pipe (exp2_fma) instead of the MUFU unit (16 results per clock per SM),
+// which sets the length of a softmax step when both warpgroups exponentiate
+// the same tile.  The macro exists for sweeps.
 #ifndef PS_PREFILL_EMU_PER8
 #define PS_PREFILL_EMU_PER8 1
 #endif
@@ -105,10 +105,12 @@ struct PrefillSmem {
   static constexpr int k_off = q_off + 2 * kTileBytes;
   static constexpr int v_off = k_off + kKvStages * kTileBytes;
   static constexpr int bar_off = v_off + kKvStages * kTileBytes;
-  static constexpr int n_bars = 4 /*unit_full, unit_empty*/ + 2 /*q*/ + 3 * kKvStages /*kfull vfull kvempty*/ +
-                                2 /*s_full*/ + 2 /*p_full*/ + 2 /*pv_done*/;
+  static constexpr int n_bars = 4 /*unit_full, unit_empty*/ + 2 /*q*/ + 4 * kKvStages /*kfull vfull kempty vempty*/ +
+                                2 /*s_full*/ + 2 /*p_full*/ + 2 /*pv_done*/ + 2 /*mx_full*/ + 1 /*ep_full*/;
   static constexpr int misc_off = bar_off + n_bars * 8;  // tmem base, abort flag, next units[2]
-  static constexpr int table_off = misc_off + 16;
+  // row maxima and sums of the two halves of every row: [tile][half][row] fp32
+  static constexpr int xchg_off = misc_off + 16;
+  static constexpr int table_off = xchg_off + 2 * (2 * 2 * 128 * 4);
   static constexpr int bytes_before_table = table_off;
 };
 
@@ -117,12 +119,15 @@ struct PBars {
   uint64_t* q_empty;
   uint64_t* kfull;    // [kKvStages]
   uint64_t* vfull;    // [kKvStages]
-  uint64_t* kvempty;  // [kKvStages]
+  uint64_t* kempty;   // [kKvStages]: both S products of the stage's K tile completed
+  uint64_t* vempty;   // [kKvStages]: both PV products of the stage's V tile completed
   uint64_t* s_full;   // [2]: tile A, tile B
   uint64_t* p_full;   // [2]
   uint64_t* pv_done;  // [2]
   uint64_t* unit_full;   // [2]: a claimed unit id is in s_unit[k]
   uint64_t* unit_empty;  // [2]: every consumer has read s_unit[k]
+  uint64_t* mx_full;     // [2]: both halves' row maxima of tile A / B are in s_mx
+  uint64_t* ep_full;     // both halves' row sums of the unit are in s_l
 };
 
 // Consumers of the MMA warp (one thread) and the 8 softmax warps release a
@@ -252,16 +257,21 @@ __global__ void __launch_bounds__(kThreads, 1)
   bars.q_empty = bar + 1;
   bars.kfull = bar + 2;
   bars.vfull = bar + 2 + kKvStages;
-  bars.kvempty = bar + 2 + 2 * kKvStages;
-  bars.s_full = bar + 2 + 3 * kKvStages;
-  bars.p_full = bar + 4 + 3 * kKvStages;
-  bars.pv_done = bar + 6 + 3 * kKvStages;
-  bars.unit_full = bar + 8 + 3 * kKvStages;
-  bars.unit_empty = bar + 10 + 3 * kKvStages;
+  bars.kempty = bar + 2 + 2 * kKvStages;
+  bars.vempty = bar + 2 + 3 * kKvStages;
+  bars.s_full = bar + 2 + 4 * kKvStages;
+  bars.p_full = bar + 4 + 4 * kKvStages;
+  bars.pv_done = bar + 6 + 4 * kKvStages;
+  bars.unit_full = bar + 8 + 4 * kKvStages;
+  bars.unit_empty = bar + 10 + 4 * kKvStages;
+  bars.mx_full = bar + 12 + 4 * kKvStages;
+  bars.ep_full = bar + 14 + 4 * kKvStages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::misc_off);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::misc_off + 4);
   volatile int* s_unit = reinterpret_cast<volatile int*>(smem + L::misc_off + 8);
   int* prefix = reinterpret_cast<int*>(smem + L::table_off);
+  float* s_mx = reinterpret_cast<float*>(smem + L::xchg_off);
+  float* s_l = s_mx + 2 * 2 * 128;
   __shared__ int s_warp_tot[kThreads / 32];
 
   const int tid = threadIdx.x;
@@ -296,15 +306,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < kKvStages; ++s) {
       mbar_init(bars.kfull + s, 1);
       mbar_init(bars.vfull + s, 1);
-      mbar_init(bars.kvempty + s, 1);
+      mbar_init(bars.kempty + s, 1);
+      mbar_init(bars.vempty + s, 1);
     }
     for (int x = 0; x < 2; ++x) {
       mbar_init(bars.s_full + x, 1);
-      mbar_init(bars.p_full + x, 4);
+      mbar_init(bars.p_full + x, 8);
+      mbar_init(bars.mx_full + x, 8);
       mbar_init(bars.pv_done + x, 1);
       mbar_init(bars.unit_full + x, 1);
       mbar_init(bars.unit_empty + x, kUnitConsumers);
     }
+    mbar_init(bars.ep_full, 8);
     fence_mbar_init();
     tma_prefetch_desc(&qmap);
     tma_prefetch_desc(&kmap);
@@ -372,23 +385,28 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const int pg = pg0 + (lane < npg ? lane : 0);
         int blk = __shfl_sync(0xffffffffu, bt_reg, pg / spb - bt_e0);
-        if (!pwait(bars.kvempty + s, (n & 1) ^ 1, abort_flag, p.status)) { ok = false; break; }
-        uint8_t* kd = sK + s * kTileBytes;
-        uint8_t* vd = sV + s * kTileBytes;
-        if (lane == 0) {
-          const uint32_t bytes = static_cast<uint32_t>(npg) * 2 * 2048;
-          mbar_arrive_expect_tx(bars.kfull + s, bytes);
-          mbar_arrive_expect_tx(bars.vfull + s, bytes);
+        if (lane < npg && (blk < 0 || blk >= p.num_blocks)) {
+          set_status(p.status, PS_DEV_BLOCK_OUT_OF_RANGE);
+          blk = 0;
         }
-        __syncwarp();  // both barriers armed before any copy completes
+        const int tok = (pg % spb) * 16;
+        const uint32_t bytes = static_cast<uint32_t>(npg) * 2 * 2048;
+        // K as soon as both S products of the stage's previous K tile are
+        // done, V once both PV products of its previous V tile are: the K
+        // tile (needed first) starts loading a PV pair earlier
+        if (!pwait(bars.kempty + s, (n & 1) ^ 1, abort_flag, p.status)) { ok = false; break; }
+        uint8_t* kd = sK + s * kTileBytes;
+        if (lane == 0) mbar_arrive_expect_tx(bars.kfull + s, bytes);
+        __syncwarp();  // armed before any copy completes
         if (lane < npg) {
-          if (blk < 0 || blk >= p.num_blocks) {
-            set_status(p.status, PS_DEV_BLOCK_OUT_OF_RANGE);
-            blk = 0;
-          }
-          const int tok = (pg % spb) * 16;
           tma_load_4d(kd + lane * 2048, &kmap, bars.kfull + s, 0, ui.h, tok, blk);
           tma_load_4d(kd + kRegionBytes + lane * 2048, &kmap, bars.kfull + s, 64, ui.h, tok, blk);
+        }
+        if (!pwait(bars.vempty + s, (n & 1) ^ 1, abort_flag, p.status)) { ok = false; break; }
+        uint8_t* vd = sV + s * kTileBytes;
+        if (lane == 0) mbar_arrive_expect_tx(bars.vfull + s, bytes);
+        __syncwarp();
+        if (lane < npg) {
           tma_load_4d(vd + lane * 2048, &vmap, bars.vfull + s, 0, ui.h, tok, blk);
           tma_load_4d(vd + kRegionBytes + lane * 2048, &vmap, bars.vfull + s, 64, ui.h, tok, blk);
         }
@@ -428,7 +446,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                          (jj > 0 || kk > 0) ? 1u : 0u);
         }
         tc::commit(bars.pv_done + x);
-        if (x == 1) tc::commit(bars.kvempty + s);  // both PVs of this stage issued
+        if (x == 1) tc::commit(bars.vempty + s);  // both PVs of this stage issued
         return true;
       };
       int t = 0, uit = 0;
@@ -443,6 +461,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc::fence_after_sync();
           issue_s(0, s);
           issue_s(1, s);
+          tc::commit(bars.kempty + s);
           if (ui.ntiles == 1) tc::commit(bars.q_empty);
         }
         for (int j = 0; j < ui.ntiles; ++j) {
@@ -459,6 +478,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!issue_pv(1, tt, j)) { ok = false; break; }
           if (more) {
             issue_s(1, sn);
+            tc::commit(bars.kempty + sn);
             if (j + 1 == ui.ntiles - 1) tc::commit(bars.q_empty);
           }
         }
@@ -468,12 +488,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp >= 4) {
     // =========================== softmax + epilogue ===========================
-    const int x = (warp >= 8) ? 1 : 0;        // tile A (warps 4-7) or B (8-11)
+    // Both warpgroups work on every tile, A then B: warpgroup h (warps 4-7:
+    // h = 0, warps 8-11: h = 1) takes keys [64h, 64h + 64) of each row (one
+    // thread per TMEM lane = M row), so a tile's softmax is spread over 256
+    // threads.  The two halves of a row agree on its max through shared
+    // memory (mx_bar) before exponentiating, and on its sum at the epilogue.
+    const int half = (warp >= 8) ? 1 : 0;
     const int quarter = warp & 3;             // TMEM lane quarter this warp may access
     const int row = quarter * 32 + lane;      // M row == TMEM lane
+    const int ctid = half * 128 + row;        // 0..255 over the two warpgroups
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-    const uint32_t s_addr = lane_addr + x * 128;
-    const uint32_t o_addr = lane_addr + 256 + x * 128;
     // per-tensor cache scales fold into the score scale (K) and the output
     // normalisation (V)
     const float sl2 = p.scale_log2 * (p.k_scale ? __ldg(p.k_scale) : 1.f);
@@ -481,159 +505,187 @@ __global__ void __launch_bounds__(kThreads, 1)
     int t = 0, uit = 0;
     for (int u = blockIdx.x; u < total_units; ++uit) {
       const UnitInfo ui = unit_info(p, prefix, u);
-      const int tok = ui.t0 + x * tpt + row / G;
+      int tok[2], limit[2];
+      bool row_valid[2];
+      float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+#pragma unroll
+      for (int x = 0; x < 2; ++x) {
+        tok[x] = ui.t0 + x * tpt + row / G;
+        row_valid[x] = row < tpt * G && tok[x] < ui.qlen;
+        limit[x] = row_valid[x] ? ui.ctx + tok[x] : -1;  // last visible key
+      }
       const int hin = row - (row / G) * G;
-      const bool row_valid = row < tpt * G && tok < ui.qlen;
-      const int limit = row_valid ? ui.ctx + tok : -1;  // last visible key
-      float m_run = -INFINITY, l_run = 0.f;
       bool ok = true;
-      for (int j = 0; j < ui.ntiles; ++j, ++t) {
-        if (!pwait(bars.s_full + x, static_cast<uint32_t>(t & 1), abort_flag, p.status)) { ok = false; break; }
-        tc::fence_after_sync();
-        const int key0 = j * kKeys;
-        const bool need_mask = !__all_sync(0xffffffffu, key0 + kKeys - 1 <= limit);
-        // pass 1: row max of the (masked) raw scores
-        float mxp[8];
+      for (int j = 0; j < ui.ntiles && ok; ++j, ++t) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) mxp[i] = -INFINITY;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t r[32];
-          tc::ld_32x32b_x32(s_addr + c * 32, r);
-          tc::wait_ld();
-          if (need_mask) {
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (key0 + c * 32 + i > limit) r[i] = __float_as_uint(-INFINITY);
-          }
-#pragma unroll
-          for (int i = 0; i < 16; ++i)
-            mxp[i & 7] = max3(mxp[i & 7], __uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
-        }
-        float mx = fmaxf(max3(mxp[0], mxp[1], mxp[2]), max3(mxp[3], mxp[4], max3(mxp[5], mxp[6], mxp[7])));
-        mx *= sl2;  // scale > 0: max of scaled = scaled max
-        float m_new = m_run, factor = 1.f;
-        if (mx > m_run + kRescaleThreshold || (m_run == -INFINITY && mx > -INFINITY)) {
-          m_new = mx;
-          factor = ex2(m_run - m_new);  // 0 when m_run == -inf
-        }
-        const float neg_m = (m_new == -INFINITY) ? 0.f : -m_new;  // fully masked row: all p = 0
-        // O lives in TMEM: rescaling it needs the previous PV of this tile done.
-        if (j > 0 && __any_sync(0xffffffffu, factor != 1.f)) {
-          if (!pwait(bars.pv_done + x, static_cast<uint32_t>((t - 1) & 1), abort_flag, p.status)) {
-            ok = false;
-            break;
-          }
+        for (int x = 0; x < 2; ++x) {
+          const uint32_t s_addr = lane_addr + x * 128;
+          if (!pwait(bars.s_full + x, static_cast<uint32_t>(t & 1), abort_flag, p.status)) { ok = false; break; }
           tc::fence_after_sync();
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            uint32_t r[32];
-            tc::ld_32x32b_x32(o_addr + c * 32, r);
-            tc::wait_ld();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * factor);
-            tc::st_32x32b_x32(o_addr + c * 32, r);
-          }
-        }
-        // pass 2: p = exp2(s * scale - m), packed to 16 bit, written over the S
-        // columns already read (chunk c's P lands in columns [16c, 16c + 16))
-        // (pairs of elements go through the packed f32x2 FMA and add)
-        uint64_t rsp[4] = {0ull, 0ull, 0ull, 0ull};
-        const uint64_t sl2x2 = f2_pack(sl2, sl2), negm_x2 = f2_pack(neg_m, neg_m);
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t r[32];
-          tc::ld_32x32b_x32(s_addr + c * 32, r);
+          const int key0 = j * kKeys + 64 * half;
+          const bool need_mask = !__all_sync(0xffffffffu, key0 + 63 <= limit[x]);
+          // this half's 64 raw scores, one TMEM round trip
+          uint32_t r[2][32];
+          tc::ld_32x32b_x32(s_addr + 64 * half, r[0]);
+          tc::ld_32x32b_x32(s_addr + 64 * half + 32, r[1]);
           tc::wait_ld();
           if (need_mask) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i)
-              if (key0 + c * 32 + i > limit) r[i] = __float_as_uint(-INFINITY);
-          }
-          uint32_t pk[16];
+            for (int c = 0; c < 2; ++c)
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            float x0, x1;
-            f2_unpack(f2_fma(f2_pack(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])), sl2x2,
-                             negm_x2),
-                      x0, x1);
-            const float p0 = ((2 * i) % 8 < PS_PREFILL_EMU_PER8) ? exp2_fma(x0) : ex2(x0);
-            const float p1 = ((2 * i + 1) % 8 < PS_PREFILL_EMU_PER8) ? exp2_fma(x1) : ex2(x1);
-            rsp[i & 3] = f2_add(rsp[i & 3], f2_pack(p0, p1));
-            pk[i] = pack2<kBF16>(p0, p1);
+              for (int i = 0; i < 32; ++i)
+                if (key0 + 32 * c + i > limit[x]) r[c][i] = __float_as_uint(-INFINITY);
           }
-          tmem_st_x16(s_addr + c * 16, pk);
-        }
-        float rs;
-        {
-          float a0, a1, b0, b1;
-          f2_unpack(f2_add(rsp[0], rsp[1]), a0, a1);
-          f2_unpack(f2_add(rsp[2], rsp[3]), b0, b1);
-          rs = (a0 + b0) + (a1 + b1);
-        }
-        l_run = l_run * factor + rs;
-        m_run = m_new;
-        tc::wait_st();
-        // last tile of the unit: V rows at or past kv_end must be finite (zero)
-        // before PV_A reads them (group A does it; PV_B is issued after PV_A)
-        if (x == 0 && j == ui.ntiles - 1) {
-          const int z0 = ui.kv_end - key0;
-          if (z0 < kKeys) {
-            const int s = t % kKvStages;
-            if (!pwait(bars.vfull + s, static_cast<uint32_t>((t / kKvStages) & 1), abort_flag, p.status)) {
+          float mxp[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) mxp[i] = -INFINITY;
+#pragma unroll
+          for (int c = 0; c < 2; ++c)
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              mxp[i & 7] = max3(mxp[i & 7], __uint_as_float(r[c][2 * i]), __uint_as_float(r[c][2 * i + 1]));
+          const float mx_own =
+              fmaxf(max3(mxp[0], mxp[1], mxp[2]), max3(mxp[3], mxp[4], max3(mxp[5], mxp[6], mxp[7])));
+          // exchange with the other half of the row (every S read of this tile
+          // precedes the arrive, so P may then overwrite any S column)
+          s_mx[(x * 2 + half) * 128 + row] = mx_own;
+          tc::fence_before_sync();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bars.mx_full + x);
+          if (!pwait(bars.mx_full + x, static_cast<uint32_t>(t & 1), abort_flag, p.status)) { ok = false; break; }
+          tc::fence_after_sync();
+          float mx = fmaxf(mx_own, s_mx[(x * 2 + (half ^ 1)) * 128 + row]);
+          mx *= sl2;  // scale > 0: max of scaled = scaled max
+          float m_new = m_run[x], factor = 1.f;
+          if (mx > m_run[x] + kRescaleThreshold || (m_run[x] == -INFINITY && mx > -INFINITY)) {
+            m_new = mx;
+            factor = ex2(m_run[x] - m_new);  // 0 when m_run == -inf
+          }
+          const float neg_m = (m_new == -INFINITY) ? 0.f : -m_new;  // fully masked row: all p = 0
+          // O lives in TMEM: rescaling it needs the previous PV of this tile
+          // done; each half rescales its 64 output dims
+          if (j > 0 && __any_sync(0xffffffffu, factor != 1.f)) {
+            if (!pwait(bars.pv_done + x, static_cast<uint32_t>((t - 1) & 1), abort_flag, p.status)) {
               ok = false;
               break;
             }
-            uint8_t* vd = sV + s * kTileBytes;
-            const int nchunks = (kKeys - z0) * 16;  // 16-byte chunks over both regions
-            for (int i = row; i < nchunks; i += 128) {
-              const int rr = z0 + (i >> 4);
-              const int region = (i >> 3) & 1;
-              *reinterpret_cast<uint4*>(vd + region * kRegionBytes + rr * 128 + (i & 7) * 16) =
-                  make_uint4(0u, 0u, 0u, 0u);
+            tc::fence_after_sync();
+            const uint32_t o_addr = lane_addr + 256 + x * 128 + 64 * half;
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+              uint32_t o[32];
+              tc::ld_32x32b_x32(o_addr + c * 32, o);
+              tc::wait_ld();
+#pragma unroll
+              for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * factor);
+              tc::st_32x32b_x32(o_addr + c * 32, o);
             }
-            fence_proxy_async_smem();  // generic writes before the tensor core reads V
           }
+          // p = exp2(s * scale - m), packed to 16 bit into P columns
+          // [32h, 32h + 32) (keys 64h .. 64h + 63); pairs of elements go
+          // through the packed f32x2 FMA and add
+          uint64_t rsp[4] = {0ull, 0ull, 0ull, 0ull};
+          const uint64_t sl2x2 = f2_pack(sl2, sl2), negm_x2 = f2_pack(neg_m, neg_m);
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            uint32_t pk[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              float x0, x1;
+              f2_unpack(f2_fma(f2_pack(__uint_as_float(r[c][2 * i]), __uint_as_float(r[c][2 * i + 1])), sl2x2,
+                               negm_x2),
+                        x0, x1);
+              const float p0 = ((2 * i) % 8 < PS_PREFILL_EMU_PER8) ? exp2_fma(x0) : ex2(x0);
+              const float p1 = ((2 * i + 1) % 8 < PS_PREFILL_EMU_PER8) ? exp2_fma(x1) : ex2(x1);
+              rsp[i & 3] = f2_add(rsp[i & 3], f2_pack(p0, p1));
+              pk[i] = pack2<kBF16>(p0, p1);
+            }
+            tmem_st_x16(s_addr + 32 * half + 16 * c, pk);
+          }
+          float rs;
+          {
+            float a0, a1, b0, b1;
+            f2_unpack(f2_add(rsp[0], rsp[1]), a0, a1);
+            f2_unpack(f2_add(rsp[2], rsp[3]), b0, b1);
+            rs = (a0 + b0) + (a1 + b1);
+          }
+          l_run[x] = l_run[x] * factor + rs;  // this half's keys; both halves apply the same factors
+          m_run[x] = m_new;
+          tc::wait_st();
+          // last tile of the unit: V rows at or past kv_end must be finite
+          // (zero) before PV_A reads them (PV_B is issued after PV_A)
+          if (x == 0 && j == ui.ntiles - 1) {
+            const int z0 = ui.kv_end - j * kKeys;
+            if (z0 < kKeys) {
+              const int s = t % kKvStages;
+              if (!pwait(bars.vfull + s, static_cast<uint32_t>((t / kKvStages) & 1), abort_flag, p.status)) {
+                ok = false;
+                break;
+              }
+              uint8_t* vd = sV + s * kTileBytes;
+              const int nchunks = (kKeys - z0) * 16;  // 16-byte chunks over both regions
+              for (int i = ctid; i < nchunks; i += 256) {
+                const int rr = z0 + (i >> 4);
+                const int region = (i >> 3) & 1;
+                *reinterpret_cast<uint4*>(vd + region * kRegionBytes + rr * 128 + (i & 7) * 16) =
+                    make_uint4(0u, 0u, 0u, 0u);
+              }
+              fence_proxy_async_smem();  // generic writes before the tensor core reads V
+            }
+          }
+          tc::fence_before_sync();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bars.p_full + x);
         }
-        tc::fence_before_sync();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(bars.p_full + x);
       }
       if (!ok) break;
-      // ---- epilogue: O / l -> global ----
-      if (!pwait(bars.pv_done + x, static_cast<uint32_t>((t - 1) & 1), abort_flag, p.status)) break;
+      // ---- epilogue: O / l -> global; each half writes its 64 dims ----
+      bool done_ok = true;
+#pragma unroll
+      for (int x = 0; x < 2; ++x) {
+        if (!pwait(bars.pv_done + x, static_cast<uint32_t>((t - 1) & 1), abort_flag, p.status)) done_ok = false;
+        s_l[(x * 2 + half) * 128 + row] = l_run[x];
+      }
+      if (!done_ok) break;
       tc::fence_after_sync();
-      const bool zero = (l_run == 0.f) || (l_run != l_run);
-      const float inv = zero ? 0.f : v_scale / l_run;
-      const int qh = ui.h * G + hin;
-      const int64_t orow = static_cast<int64_t>(ui.qrow0 + tok);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bars.ep_full);
+      if (!pwait(bars.ep_full, static_cast<uint32_t>(uit & 1), abort_flag, p.status)) break;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        tc::ld_32x32b_x32(o_addr + c * 32, r);
-        tc::wait_ld();
-        if (row_valid) {
-          uint8_t* dst = reinterpret_cast<uint8_t*>(p.out) +
-                         (orow * p.o_st + static_cast<int64_t>(qh) * p.o_sh + c * 32) * 2;
+      for (int x = 0; x < 2; ++x) {
+        const float l_tot = l_run[x] + s_l[(x * 2 + (half ^ 1)) * 128 + row];
+        const bool zero = (l_tot == 0.f) || (l_tot != l_tot);
+        const float inv = zero ? 0.f : v_scale / l_tot;
+        const int qh = ui.h * G + hin;
+        const int64_t orow = static_cast<int64_t>(ui.qrow0 + tok[x]);
+        const uint32_t o_addr = lane_addr + 256 + x * 128 + 64 * half;
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            uint4 v;
-            v.x = pack2<kBF16>(__uint_as_float(r[8 * i + 0]) * inv, __uint_as_float(r[8 * i + 1]) * inv);
-            v.y = pack2<kBF16>(__uint_as_float(r[8 * i + 2]) * inv, __uint_as_float(r[8 * i + 3]) * inv);
-            v.z = pack2<kBF16>(__uint_as_float(r[8 * i + 4]) * inv, __uint_as_float(r[8 * i + 5]) * inv);
-            v.w = pack2<kBF16>(__uint_as_float(r[8 * i + 6]) * inv, __uint_as_float(r[8 * i + 7]) * inv);
-            *reinterpret_cast<uint4*>(dst + i * 16) = v;
+        for (int c = 0; c < 2; ++c) {
+          uint32_t o[32];
+          tc::ld_32x32b_x32(o_addr + c * 32, o);
+          tc::wait_ld();
+          if (row_valid[x]) {
+            uint8_t* dst = reinterpret_cast<uint8_t*>(p.out) +
+                           (orow * p.o_st + static_cast<int64_t>(qh) * p.o_sh + 64 * half + c * 32) * 2;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              uint4 v;
+              v.x = pack2<kBF16>(__uint_as_float(o[8 * i + 0]) * inv, __uint_as_float(o[8 * i + 1]) * inv);
+              v.y = pack2<kBF16>(__uint_as_float(o[8 * i + 2]) * inv, __uint_as_float(o[8 * i + 3]) * inv);
+              v.z = pack2<kBF16>(__uint_as_float(o[8 * i + 4]) * inv, __uint_as_float(o[8 * i + 5]) * inv);
+              v.w = pack2<kBF16>(__uint_as_float(o[8 * i + 6]) * inv, __uint_as_float(o[8 * i + 7]) * inv);
+              *reinterpret_cast<uint4*>(dst + i * 16) = v;
+            }
           }
         }
+        if (half == 0 && row_valid[x] && p.lse != nullptr)
+          p.lse[static_cast<int64_t>(qh) * p.lse_sh + orow * p.lse_st] =
+              zero ? -INFINITY : (m_run[x] + __log2f(l_tot)) * 0.6931471805599453f;
       }
-      if (row_valid && p.lse != nullptr)
-        p.lse[static_cast<int64_t>(qh) * p.lse_sh + orow * p.lse_st] =
-            zero ? -INFINITY : (m_run + __log2f(l_run)) * 0.6931471805599453f;
       tc::fence_before_sync();
       u = next_unit(p, bars, s_unit, u, uit, abort_flag, false, lane);
     }
   }
-
   // ---- teardown: every role done; TMEM owner frees it ----
   tc::fence_before_sync();
   __syncthreads();
