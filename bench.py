@@ -362,17 +362,29 @@ class Arm:
         if sampler is not None:
             sampler.start()
             time.sleep(0.25)
-        n_ev = len(self.runs) + 1
-        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(n_ev)] for _ in range(steps)]
+        # the timed region: K steps back to back, events only at its ends
         t0 = torch.cuda.Event(enable_timing=True)
         t1 = torch.cuda.Event(enable_timing=True)
         with torch.cuda.stream(self.stream):
             t0.record(self.stream)
-            for i in range(steps):
-                self.step(evs[i])
+            for _ in range(steps):
+                self.step()
             t1.record(self.stream)
         torch.cuda.synchronize(dev)
         elapsed_ms = t0.elapsed_time(t1)
+        if len(self.runs) == 1:
+            # one launch per step: its average duration is the step's
+            phase_ms = {self.names[0]: elapsed_ms / steps}
+        else:
+            # several launches per step: a second pass of K steps with an
+            # event between launches gives each launch's duration
+            n_ev = len(self.runs) + 1
+            evs = [[torch.cuda.Event(enable_timing=True) for _ in range(n_ev)] for _ in range(steps)]
+            with torch.cuda.stream(self.stream):
+                for i in range(steps):
+                    self.step(evs[i])
+            torch.cuda.synchronize(dev)
+            phase_ms = {n: sum(e[i].elapsed_time(e[i + 1]) for e in evs) / steps for i, n in enumerate(self.names)}
         clocks = None
         if sampler is not None:
             # keep the same load on the GPU for ~1.5 s so the sampler sees it
@@ -384,7 +396,6 @@ class Arm:
                     self.stream.synchronize()
             clocks = sampler.stop()
         elapsed_ms = _all_max(elapsed_ms, world, dev)
-        phase_ms = {n: sum(e[i].elapsed_time(e[i + 1]) for e in evs) / steps for i, n in enumerate(self.names)}
         assert self.ws.status() == 0, f"device status {self.ws.status():#x}"
         return {"elapsed_ms": elapsed_ms, "ms": elapsed_ms / steps, "phase_ms": phase_ms, "clocks": clocks}
 
@@ -440,17 +451,23 @@ def prefill_roofline(arm: Arm, prefill_ms: float) -> dict:
 # vLLM's FA4 path on the same inputs (the GPU bar)
 # ----------------------------------------------------------------------------
 def _median_ms(fn, stream, n: int) -> float:
+    """Average duration of ``fn`` over n back-to-back calls (the way the
+    timed region runs our steps), the median of three such runs."""
+    runs = []
     with torch.cuda.stream(stream):
         for _ in range(3):
             fn()
         stream.synchronize()
-        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
-        for a, b in evs:
+        for _ in range(3):
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
             a.record(stream)
-            fn()
+            for _ in range(n):
+                fn()
             b.record(stream)
-    stream.synchronize()
-    return statistics.median(a.elapsed_time(b) for a, b in evs)
+            stream.synchronize()
+            runs.append(a.elapsed_time(b) / n)
+    return statistics.median(runs)
 
 
 def fa4_compare(arm: Arm, steps: int, ours_step_ms: float, ours_phase_ms: dict) -> dict:

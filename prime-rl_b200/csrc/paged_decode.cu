@@ -928,7 +928,7 @@ __device__ __forceinline__ int stream_range(const DecodeParams& p, const CUtenso
 #pragma unroll
           for (int j = 0; j < 2; ++j) {
             const int col = nt * 8 + 2 * t + j;
-            if (col < kRec) {
+            if (col < ncols) {  // the rows a combine reads: the segment's query columns
               float* po = slot_o<kRec>(p, slot, col);
 #pragma unroll
               for (int mi = 0; mi < 8; ++mi) {
