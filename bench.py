@@ -107,12 +107,16 @@ def profile_traffic(kernel_tag: str):
     return None
 
 
-def config_dict(cfg: int) -> dict:
+def config_dict(cfg: int, max_seqs: int | None = None) -> dict:
     """The workload description shared by both arms (no device needed)."""
     from ps_attn import workloads
 
     q_lens, seq_lens, kw = workloads.config_lengths(cfg)
-    return {"workload": CONFIG_NAMES[cfg], "num_seqs": len(seq_lens), "num_q_heads": kw["num_q_heads"],
+    name = CONFIG_NAMES[cfg]
+    if max_seqs is not None:  # a profiling subset, not a benchmark line
+        q_lens, seq_lens = q_lens[:max_seqs], seq_lens[:max_seqs]
+        name += f" -- first {len(seq_lens)} sequences only"
+    return {"workload": name, "num_seqs": len(seq_lens), "num_q_heads": kw["num_q_heads"],
             "num_kv_heads": kw["num_kv_heads"], "head_size": 128, "block_size": 16,
             "kv_tokens": int(sum(seq_lens)), "new_tokens_per_step": int(sum(q_lens))}
 
@@ -201,7 +205,7 @@ class Arm:
     each replayed from its own CUDA graph so CUDA events can bracket it."""
 
     def __init__(self, cfg, dev, world=1, rank=0, *, kv_fp8=False, cascade=False, fused=True,
-                 gather="peer", use_graph=True):
+                 gather="peer", use_graph=True, max_seqs=None):
         from ps_attn import ops, workloads
 
         self.cfg, self.dev, self.world, self.rank = cfg, dev, world, rank
@@ -209,9 +213,10 @@ class Arm:
         self.kv_fp8, self.fused, self.use_graph = kv_fp8, fused, use_graph
         if self.sharded:
             per = 8 // world
-            batch = workloads.make_config(cfg, device=dev, kv_heads_slice=(rank * per, (rank + 1) * per))
+            batch = workloads.make_config(cfg, device=dev, kv_heads_slice=(rank * per, (rank + 1) * per),
+                                          max_seqs=max_seqs)
         else:
-            batch = workloads.make_config(cfg, device=dev, seed=rank if cfg != 5 else 0)
+            batch = workloads.make_config(cfg, device=dev, seed=rank if cfg != 5 else 0, max_seqs=max_seqs)
         self.batch = batch
         B = self.B = batch.num_seqs
         self.hq, self.hkv = batch.q.shape[1], batch.kv_cache.shape[3]
@@ -679,7 +684,7 @@ def run_ours(args):
     _lib.load(build_if_stale=False)
     cfg = args.config
     arm = Arm(cfg, dev, world, rank, kv_fp8=args.kv_fp8, cascade=args.cascade, fused=not args.unfused,
-              gather=args.gather, use_graph=not args.no_graph)
+              gather=args.gather, use_graph=not args.no_graph, max_seqs=args.max_seqs)
     arm.setup()
     sampler = None if args.quick else ClockSampler(local)
     t = arm.time(args.steps, args.warmup, sampler)
@@ -697,7 +702,7 @@ def run_ours(args):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
         "higher_is_better": True, "scaling": "strong" if arm.sharded else "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": config_dict(cfg),
+        "config": config_dict(cfg, args.max_seqs),
         "setup": {
             "parallelism": (f"kv-head tp{world} + " + ("NVLink peer-memory head gather (ps_head_gather)"
                                                        if arm.peer_gather else "NCCL all-gather") if arm.sharded else
@@ -733,7 +738,8 @@ def run_ours(args):
             res["fa4"] = fa4_compare(arm, args.steps, ms, pm)
         if rank == 0:
             res["cpu_baseline"] = cpu_baseline(cfg, budget_s=args.cpu_budget)
-    if world == 1 and not args.quick and not args.no_side and cfg == DEFAULT_CONFIG and not args.kv_fp8:
+    if (world == 1 and not args.quick and not args.no_side and cfg == DEFAULT_CONFIG and not args.kv_fp8
+            and args.max_seqs is None):
         arm.close()
         del arm
         torch.cuda.empty_cache()
@@ -1038,6 +1044,8 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--no-fa4", action="store_true", help="skip the vLLM FA4 comparison")
     ap.add_argument("--no-side", action="store_true", help="N=1: skip configs 2-4 after the headline")
+    ap.add_argument("--max-seqs", type=int, default=None,
+                    help="profiling: a seeded prefix subset of the config's sequences (not a benchmark line)")
     ap.add_argument("--quick", action="store_true",
                     help="timed steps only: no end-to-end, CPU baseline, FA4, side configs or clock sampling")
     args = ap.parse_args()
