@@ -6,11 +6,14 @@
 //   block = slot / block_size, offset = slot % block_size   (:50-51)
 //   cache[block, offset, h, :] = src[t, h, :] for all heads (:78-87, :112-123)
 //
-// B200 layout: a CTA handles one token per iteration (grid-stride over
-// tokens); its threads walk the token's 2 * num_heads head rows in VEC-byte
-// vectors, head_size bytes contiguous per head row, so each warp moves whole
-// 512-byte runs (16-byte vectors) on both the load and the store side.  The
+// B200 layout: a CTA handles kAppendTokens tokens per iteration (grid-stride
+// over tokens); its threads walk each token's 2 * num_heads head rows in
+// VEC-byte vectors, head_size bytes contiguous per head row, so each warp
+// moves whole 512-byte runs (16-byte vectors) on both the load and the store
+// side.  The
 // payload is never touched by arithmetic: the copy is bit-exact.
+#include <climits>
+
 #include "ps_common.cuh"
 #include "ps_launch.h"
 
@@ -35,6 +38,11 @@ struct VecT<2> {
   using T = uint16_t;
 };
 
+// Tokens per CTA iteration: their slot loads and row loads are all issued
+// before any store, so a thread keeps kAppendTokens 16-byte rows in flight
+// instead of one dependent slot -> row round trip per token.
+constexpr int kAppendTokens = 4;
+
 template <int VEC>
 __global__ void __launch_bounds__(256) kv_append_kernel(AppendArgs a) {
   using V = typename VecT<VEC>::T;
@@ -42,28 +50,52 @@ __global__ void __launch_bounds__(256) kv_append_kernel(AppendArgs a) {
   // still waits for this grid's completion before reading the cache
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  constexpr int U = kAppendTokens;
   const int per_tensor = a.num_heads * a.vecs_per_head;
   const int per_token = 2 * per_tensor;
-  for (int64_t t = blockIdx.x; t < a.num_tokens; t += gridDim.x) {
-    const int64_t slot = __ldg(a.slot_mapping + t);
-    if (slot < 0) continue;  // padding token
-    if (slot >= a.num_slots) {
-      if (threadIdx.x == 0) set_status(a.status, PS_DEV_SLOT_OUT_OF_RANGE);
-      continue;
-    }
-    const int64_t blk = slot / a.block_size;
-    const int64_t off = slot - blk * a.block_size;
-    const int64_t dst_tok = blk * a.c_sblock + off * a.c_sslot;
+  // a slot that passes the range check fits in 32 bits whenever the pool
+  // does; the block / offset split is then a 32-bit division
+  const bool narrow = a.num_slots <= INT32_MAX;
+  for (int64_t t0 = static_cast<int64_t>(blockIdx.x) * U; t0 < a.num_tokens;
+       t0 += static_cast<int64_t>(gridDim.x) * U) {
+    int64_t slot[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) slot[u] = t0 + u < a.num_tokens ? __ldg(a.slot_mapping + t0 + u) : -1;
     for (int j = threadIdx.x; j < per_token; j += blockDim.x) {
       const bool is_v = j >= per_tensor;
       const int r = is_v ? j - per_tensor : j;
       const int h = r / a.vecs_per_head;
       const int c = r - h * a.vecs_per_head;
-      const char* src = is_v ? a.value + t * a.val_st + h * a.val_sh
-                             : a.key + t * a.key_st + h * a.key_sh;
-      char* dst = (is_v ? a.value_cache : a.key_cache) + dst_tok + h * a.c_shead;
-      const V v = __ldg(reinterpret_cast<const V*>(src) + c);
-      reinterpret_cast<V*>(dst)[c] = v;
+      const char* src0 = is_v ? a.value + h * a.val_sh : a.key + h * a.key_sh;
+      const int64_t sst = is_v ? a.val_st : a.key_st;
+      // every row of a token below num_tokens is readable (padding tokens
+      // included), so the row loads do not wait for the slots
+      V v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (t0 + u < a.num_tokens) v[u] = __ldg(reinterpret_cast<const V*>(src0 + (t0 + u) * sst) + c);
+      char* base = (is_v ? a.value_cache : a.key_cache) + h * a.c_shead;
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int64_t sl = slot[u];
+        if (sl < 0 || sl >= a.num_slots) continue;  // padding token / recorded below
+        int64_t blk, off;
+        if (narrow) {
+          const uint32_t s32 = static_cast<uint32_t>(sl), bs = static_cast<uint32_t>(a.block_size);
+          const uint32_t b32 = s32 / bs;
+          blk = b32;
+          off = s32 - b32 * bs;
+        } else {
+          blk = sl / a.block_size;
+          off = sl - blk * a.block_size;
+        }
+        reinterpret_cast<V*>(base + blk * a.c_sblock + off * a.c_sslot)[c] = v[u];
+      }
+    }
+    if (threadIdx.x == 0) {
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (slot[u] >= a.num_slots) set_status(a.status, PS_DEV_SLOT_OUT_OF_RANGE);
     }
   }
 }
@@ -73,7 +105,7 @@ __global__ void __launch_bounds__(256) kv_append_kernel(AppendArgs a) {
 int ps_launch_kv_append(const ps::AppendArgs& a, int vec, int sm_count, cudaStream_t stream) {
   if (a.num_tokens == 0) return 0;
   const int threads = 256;
-  int64_t blocks = a.num_tokens;
+  int64_t blocks = (a.num_tokens + ps::kAppendTokens - 1) / ps::kAppendTokens;
   const int64_t cap = static_cast<int64_t>(sm_count) * 8;
   if (blocks > cap) blocks = cap;
   switch (vec) {
@@ -138,7 +170,7 @@ __global__ void __launch_bounds__(256) kv_append_fp8_kernel(AppendArgs a, const 
 int ps_launch_kv_append_fp8(const ps::AppendArgs& a, const float* k_scale, const float* v_scale,
                             int dtype_bf16, int sm_count, cudaStream_t stream) {
   if (a.num_tokens == 0) return 0;
-  int64_t blocks = a.num_tokens;
+  int64_t blocks = (a.num_tokens + ps::kAppendTokens - 1) / ps::kAppendTokens;
   const int64_t cap = static_cast<int64_t>(sm_count) * 8;
   if (blocks > cap) blocks = cap;
   if (dtype_bf16)
