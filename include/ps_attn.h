@@ -211,12 +211,10 @@ int ps_paged_decode(const ps_paged_problem* problem, void* workspace, int64_t wo
  * ps_paged_decode, but no workspace argument: the split counters and partials
  * live in a 16 MiB array inside the library, of which every GPU that loads it
  * holds one copy until the process exits.  A problem is rejected with
- * PS_ERR_WORKSPACE when the decode scratch of its own cache dtype exceeds
- * 16 MiB: the 16-bit kernel keeps a split record per warp of 8 warps per SM,
- * the fp8 kernel per warp of 12 (with 8 KV heads, GQA group <= 8 and 148
- * SMs: at most 352 sequences per call with a 16-bit cache, 278 with an fp8
- * cache; ps_paged_decode_workspace_size, which serves both, is the larger
- * fp8 size).  Allocates nothing (no cudaMalloc / cudaFree).  The
+ * PS_ERR_WORKSPACE when its decode scratch (ps_paged_decode_workspace_size:
+ * a split record per warp, 8 warps per SM with either cache dtype, plus one
+ * per (sequence, kv head)) exceeds 16 MiB -- with 8 KV heads, GQA group <= 8
+ * and 148 SMs, at most 352 sequences per call.  Allocates nothing (no cudaMalloc / cudaFree).  The
  * first call on a device looks up the array's device address for that device;
  * make that first call before any stream capture.  All calls share the one
  * array: calls that can overlap on the GPU (other streams, other threads)

@@ -7,10 +7,10 @@
 // and FA4's zero-sum guard (cute/softmax.py:147-158).
 //
 // Work decomposition ("stream-K" over page-heads):
-//   A unit of work is one 16-token page of one KV head of one sequence.  The
-//   page-heads of the batch are laid out in (sequence, kv head, page) order and
-//   cut into equal contiguous ranges, one per warp of a persistent grid of one
-//   CTA per SM.  A warp therefore streams an exactly equal share of the KV
+//   A unit of work is one 16-token page of one KV head of one sequence (two
+//   consecutive pages with an fp8 cache).  The units ("page-heads") of the
+//   batch are laid out in (sequence, kv head, page) order and cut into equal
+//   contiguous ranges, one per warp of a persistent grid of one CTA per SM.  A warp therefore streams an exactly equal share of the KV
 //   bytes.  Where a warp's range crosses a (sequence, kv head) boundary it
 //   finishes that segment as a split: it writes a normalised fp32 partial and
 //   its LSE, bumps a per-(sequence, kv head) counter, and the warp that brings
@@ -76,7 +76,7 @@ __device__ __forceinline__ float* slot_lse(const DecodeParams& p, int64_t slot, 
 
 // Shared-memory tables built by the prologue.
 struct Tables {
-  const int* prefix;  // [B+1] exclusive scan of each sequence's own pages
+  const int* prefix;  // [B+1] exclusive scan of each sequence's own units (pages; fp8: page pairs)
   const int* soff;    // [B]   cascade: pages of the sequence covered by its group prefix
   const int* gph;     // [G+1] cascade: exclusive scan of pages * passes per group
   const int* gu;      // [G+1] cascade: exclusive scan of passes per group
@@ -436,9 +436,17 @@ __host__ __device__ constexpr int decode_qslot_bytes() {
   return 8 * NT * kQRowBytes;
 }
 
-// Page stages per warp and their size.  An fp8 page-head is half the bytes,
-// so the fp8 kernels keep about as many bytes in flight with more stages
-// (4 with 8 query columns; 3 with 16, whose query slots are twice the size).
+// Pages of one work unit.  An fp8 page-head is half the bytes of a 16-bit one
+// and its per-page instruction stream (conversions, softmax, the MMA issue)
+// sets the pace, so an fp8 unit is two consecutive pages of one (sequence, kv
+// head): one stage holds both (8 KB, as a 16-bit page), one online-softmax
+// update and one max/rescale cover 32 tokens, and the list, the stream-K cut
+// and the split records count units.
+template <bool kFP8>
+__host__ __device__ constexpr int unit_pages() {
+  return kFP8 ? 2 : 1;
+}
+// Stages per warp and their size.
 template <bool kFP8, int kQNT>
 __host__ __device__ constexpr int decode_stages() {
   return kFP8 ? kDecodeFp8Stages : kDecodeStages;
@@ -449,7 +457,7 @@ __host__ __device__ constexpr int decode_warps() {
 }
 template <bool kFP8>
 __host__ __device__ constexpr int decode_stage_bytes() {
-  return kFP8 ? 2 * kBoxBytesF8 : kStageBytes;
+  return kFP8 ? 4 * kBoxBytesF8 : kStageBytes;  // fp8: K page 0, K page 1, V page 0, V page 1
 }
 
 template <int kQNT, bool kFP8 = false>
@@ -510,6 +518,8 @@ __device__ __forceinline__ int stream_range(const DecodeParams& p, const CUtenso
                                             int lane) {
   constexpr int D = decode_stages<kFP8, kQNT>();
   constexpr int SB = decode_stage_bytes<kFP8>();
+  constexpr int kUP = unit_pages<kFP8>();        // pages per unit
+  constexpr int kUnitTokens = kPageTokens * kUP;
   // MMA operand type: the model dtype, or f16 for an fp8 cache (e4m3 codes
   // convert to f16 exactly)
   constexpr bool kMathBF16 = kBF16 && !kFP8;
@@ -538,15 +548,27 @@ __device__ __forceinline__ int stream_range(const DecodeParams& p, const CUtenso
   // Issue the TMA loads of page-head c into `stage` (warp-collective).
   // `seg_start`: c begins a segment for this warp -> also bring its query rows.
   auto issue = [&](int stage, const Cursor& c, bool seg_start) {
-    const int pg = c.p + c.off;
+    const int pg = (c.p + c.off) * kUP;  // first page of the unit
     const int e = pg / sub_per_block;
-    if (c.b != bt_b || e < bt_e0 || e >= bt_e0 + 32) {
+    const int e_last = (pg + kUP - 1) / sub_per_block;
+    if (c.b != bt_b || e < bt_e0 || e_last >= bt_e0 + 32) {
       bt_b = c.b;
       bt_e0 = e;
       const int idx = e + lane;
       bt_reg = idx < p.max_blocks_per_seq ? __ldg(p.block_table + c.b * p.bt_stride + idx) : 0;
     }
     int blk = __shfl_sync(0xffffffffu, bt_reg, e - bt_e0);
+    int blk1 = 0;
+    bool has1 = false;  // fp8: the unit's second page exists
+    if constexpr (kFP8) {
+      blk1 = __shfl_sync(0xffffffffu, bt_reg, e_last - bt_e0);
+      has1 = true;
+      if (c.p == c.P - 1) {  // only a sequence's last unit can hold one page
+        const int L = max(__ldg(p.seq_lens + c.b), 0);
+        const int npg = min((L + kPageTokens - 1) / kPageTokens, p.max_blocks_per_seq * sub_per_block);
+        has1 = pg + 1 < npg;
+      }
+    }
     const int sub = pg - e * sub_per_block;
     uint8_t* dst = wsm + stage * SB;
     uint64_t* bar = wbar + stage;
@@ -557,12 +579,24 @@ __device__ __forceinline__ int stream_range(const DecodeParams& p, const CUtenso
         set_status(p.status, PS_DEV_BLOCK_OUT_OF_RANGE);
         blk = 0;
       }
-      mbar_arrive_expect_tx(bar, SB + qbytes);
       const int tok = sub * kPageTokens;
       if constexpr (kFP8) {
+        // K page 0 | K page 1 | V page 0 | V page 1; a missing second page
+        // leaves its boxes stale (every token of it is masked)
+        mbar_arrive_expect_tx(bar, (has1 ? 4 : 2) * kBoxBytesF8 + qbytes);
         tma_load_4d(dst, kmap, bar, 0, c.h, tok, blk);
-        tma_load_4d(dst + kBoxBytesF8, vmap, bar, 0, c.h, tok, blk);
+        tma_load_4d(dst + 2 * kBoxBytesF8, vmap, bar, 0, c.h, tok, blk);
+        if (has1) {
+          if (blk1 < 0 || blk1 >= p.num_blocks) {
+            set_status(p.status, PS_DEV_BLOCK_OUT_OF_RANGE);
+            blk1 = 0;
+          }
+          const int tok1 = (pg + 1 - e_last * sub_per_block) * kPageTokens;
+          tma_load_4d(dst + kBoxBytesF8, kmap, bar, 0, c.h, tok1, blk1);
+          tma_load_4d(dst + 3 * kBoxBytesF8, vmap, bar, 0, c.h, tok1, blk1);
+        }
       } else {
+        mbar_arrive_expect_tx(bar, SB + qbytes);
         tma_load_4d(dst + 0 * kBoxBytes, kmap, bar, 0, c.h, tok, blk);
         tma_load_4d(dst + 1 * kBoxBytes, kmap, bar, 64, c.h, tok, blk);
         tma_load_4d(dst + 2 * kBoxBytes, vmap, bar, 0, c.h, tok, blk);
@@ -635,7 +669,7 @@ __device__ __forceinline__ int stream_range(const DecodeParams& p, const CUtenso
     // ---- segment start: query fragments from the slot, reset state ------------
     if (k == 0 || cc.p == 0) {
       if constexpr (kMode == kCasPrefix) {
-        L = cc.P * kPageTokens;  // shared pages are complete for every member
+        L = cc.P * kUnitTokens;  // shared pages are complete for every member
         ncols = cc.ncols;
       } else {
         L = __ldg(p.seq_lens + cc.b);
@@ -691,9 +725,9 @@ __device__ __forceinline__ int stream_range(const DecodeParams& p, const CUtenso
       }
     }
 
-    const int valid = min(kPageTokens, L - (cc.p + cc.off) * kPageTokens);
+    const int valid = min(kUnitTokens, L - (cc.p + cc.off) * kUnitTokens);
 
-    // ---- fused append: the sequence's last page carries the new token -----
+    // ---- fused append: the sequence's last unit carries the new token -----
     if (fused && cc.p == cc.P - 1 && new_slot >= 0) {
       const int pos = L - 1;
       const int bidx = pos / p.block_size;
@@ -706,9 +740,10 @@ __device__ __forceinline__ int stream_range(const DecodeParams& p, const CUtenso
         const int64_t blk = new_slot / p.block_size, off = new_slot - blk * p.block_size;
         if constexpr (kFP8) {
           // this lane's 8 elements (dims 8c..8c+7) as e4m3(x / scale), as
-          // ps_kv_append_fp8 stores them
+          // ps_kv_append_fp8 stores them, into page u of the unit
+          const int u = (pos & (kUnitTokens - 1)) / kPageTokens;
           const uint2 q8 = quantize8_e4m3<kBF16>(new_row, lane < 16 ? k_scale : v_scale);
-          *reinterpret_cast<uint2*>(st + (lane < 16 ? 0 : kBoxBytesF8) + r * 128 +
+          *reinterpret_cast<uint2*>(st + (lane < 16 ? 0 : 2 * kBoxBytesF8) + u * kBoxBytesF8 + r * 128 +
                                     ((((c >> 1) ^ (r & 7)) << 4) | ((c & 1) << 3))) = q8;
           uint8_t* dst = reinterpret_cast<uint8_t*>(lane < 16 ? p.key_cache : p.value_cache) +
                          blk * p.c_sblock + off * p.c_sslot + cc.h * p.c_shead;
@@ -727,10 +762,12 @@ __device__ __forceinline__ int stream_range(const DecodeParams& p, const CUtenso
       __syncwarp();
     }
 
-    // ---- S^T = K Q^T -----------------------------------------------------------
-    float s[NT][4];
+    // ---- S^T = K Q^T (per page u of the unit) ----------------------------------
+    float s[kUP][NT][4];
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+    for (int u = 0; u < kUP; ++u)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) s[u][nt][0] = s[u][nt][1] = s[u][nt][2] = s[u][nt][3] = 0.f;
     const uint32_t kbase = smem_u32(st);
     if constexpr (kFP8) {
       // one ldmatrix.x4 per two 16-dim steps: matrices (tokens 0-7 | 8-15) x
@@ -738,22 +775,24 @@ __device__ __forceinline__ int stream_range(const DecodeParams& p, const CUtenso
       // of token g (or g+8), converted to the f16 pairs (4t, 4t+1) and
       // (4t+2, 4t+3) that match the permuted query fragments
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int chunk = 2 * j + k_chk;
-        const uint32_t addr = kbase + k_row * 128 + ((chunk ^ (k_row & 7)) << 4);
-        uint32_t r0, r1, r2, r3;
-        ldsm_x4(addr, r0, r1, r2, r3);
-        uint32_t k0l, k0h, k1l, k1h, k2l, k2h, k3l, k3h;
-        e4m3x4_to_f16x2x2(r0, k0l, k0h);
-        e4m3x4_to_f16x2x2(r1, k1l, k1h);
-        e4m3x4_to_f16x2x2(r2, k2l, k2h);
-        e4m3x4_to_f16x2x2(r3, k3l, k3h);
+      for (int u = 0; u < kUP; ++u)
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-          mma_16816<false>(s[nt], k0l, k1l, k0h, k1h, qf[nt][2 * j][0], qf[nt][2 * j][1]);
-          mma_16816<false>(s[nt], k2l, k3l, k2h, k3h, qf[nt][2 * j + 1][0], qf[nt][2 * j + 1][1]);
+        for (int j = 0; j < 4; ++j) {
+          const int chunk = 2 * j + k_chk;
+          const uint32_t addr = kbase + u * kBoxBytesF8 + k_row * 128 + ((chunk ^ (k_row & 7)) << 4);
+          uint32_t r0, r1, r2, r3;
+          ldsm_x4(addr, r0, r1, r2, r3);
+          uint32_t k0l, k0h, k1l, k1h, k2l, k2h, k3l, k3h;
+          e4m3x4_to_f16x2x2(r0, k0l, k0h);
+          e4m3x4_to_f16x2x2(r1, k1l, k1h);
+          e4m3x4_to_f16x2x2(r2, k2l, k2h);
+          e4m3x4_to_f16x2x2(r3, k3l, k3h);
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            mma_16816<false>(s[u][nt], k0l, k1l, k0h, k1h, qf[nt][2 * j][0], qf[nt][2 * j][1]);
+            mma_16816<false>(s[u][nt], k2l, k3l, k2h, k3h, qf[nt][2 * j + 1][0], qf[nt][2 * j + 1][1]);
+          }
         }
-      }
     } else {
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks) {
@@ -763,34 +802,49 @@ __device__ __forceinline__ int stream_range(const DecodeParams& p, const CUtenso
         uint32_t a0, a1, a2, a3;
         ldsm_x4(addr, a0, a1, a2, a3);
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) mma_16816<kBF16>(s[nt], a0, a1, a2, a3, qf[nt][ks][0], qf[nt][ks][1]);
+        for (int nt = 0; nt < NT; ++nt) mma_16816<kBF16>(s[0][nt], a0, a1, a2, a3, qf[nt][ks][0], qf[nt][ks][1]);
       }
     }
 
-    // ---- online softmax (exp2 domain) ----------------------------------------
-    const bool v0 = g < valid, v1 = (g + 8) < valid;
-    uint32_t pb[NT][2];
+    // ---- online softmax (exp2 domain), one max/rescale per unit ---------------
+    uint32_t pb[kUP][NT][2];
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) {
-      s[nt][0] = v0 ? s[nt][0] * scale_log2 : -INFINITY;
-      s[nt][1] = v0 ? s[nt][1] * scale_log2 : -INFINITY;
-      s[nt][2] = v1 ? s[nt][2] * scale_log2 : -INFINITY;
-      s[nt][3] = v1 ? s[nt][3] * scale_log2 : -INFINITY;
+#pragma unroll
+      for (int u = 0; u < kUP; ++u) {
+        const bool v0 = u * kPageTokens + g < valid, v1 = u * kPageTokens + g + 8 < valid;
+        s[u][nt][0] = v0 ? s[u][nt][0] * scale_log2 : -INFINITY;
+        s[u][nt][1] = v0 ? s[u][nt][1] * scale_log2 : -INFINITY;
+        s[u][nt][2] = v1 ? s[u][nt][2] * scale_log2 : -INFINITY;
+        s[u][nt][3] = v1 ? s[u][nt][3] * scale_log2 : -INFINITY;
+      }
       float alpha[2];
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
-        float mx = fmaxf(s[nt][j], s[nt][j + 2]);
+        float mx = fmaxf(s[0][nt][j], s[0][nt][j + 2]);
+#pragma unroll
+        for (int u = 1; u < kUP; ++u) mx = fmaxf(mx, fmaxf(s[u][nt][j], s[u][nt][j + 2]));
         mx = warp_max_xor(mx, 0);
         const float mnew = fmaxf(m[nt][j], mx);
         alpha[j] = ex2(m[nt][j] - mnew);  // m = -inf -> 0
         m[nt][j] = mnew;
       }
-      const float p0 = ex2(s[nt][0] - m[nt][0]);
-      const float p1 = ex2(s[nt][1] - m[nt][1]);
-      const float p2 = ex2(s[nt][2] - m[nt][0]);
-      const float p3 = ex2(s[nt][3] - m[nt][1]);
-      l[nt][0] = l[nt][0] * alpha[0] + p0 + p2;
-      l[nt][1] = l[nt][1] * alpha[1] + p1 + p3;
+#pragma unroll
+      for (int u = 0; u < kUP; ++u) {
+        const float p0 = ex2(s[u][nt][0] - m[nt][0]);
+        const float p1 = ex2(s[u][nt][1] - m[nt][1]);
+        const float p2 = ex2(s[u][nt][2] - m[nt][0]);
+        const float p3 = ex2(s[u][nt][3] - m[nt][1]);
+        if (u == 0) {
+          l[nt][0] = l[nt][0] * alpha[0] + p0 + p2;
+          l[nt][1] = l[nt][1] * alpha[1] + p1 + p3;
+        } else {
+          l[nt][0] += p0 + p2;
+          l[nt][1] += p1 + p3;
+        }
+        pb[u][nt][0] = movmatrix_t(pack2<kMathBF16>(p0, p1));
+        pb[u][nt][1] = movmatrix_t(pack2<kMathBF16>(p2, p3));
+      }
       if (alpha[0] != 1.f || alpha[1] != 1.f) {
 #pragma unroll
         for (int mi = 0; mi < 8; ++mi) {
@@ -800,48 +854,52 @@ __device__ __forceinline__ int stream_range(const DecodeParams& p, const CUtenso
           o[nt][mi][3] *= alpha[1];
         }
       }
-      pb[nt][0] = movmatrix_t(pack2<kMathBF16>(p0, p1));
-      pb[nt][1] = movmatrix_t(pack2<kMathBF16>(p2, p3));
     }
 
     // ---- O^T += V^T P^T ------------------------------------------------------
-    const bool tail = valid < kPageTokens;
-    const bool z0 = 2 * t >= valid, z1 = 2 * t + 1 >= valid;
-    const bool z2 = 2 * t + 8 >= valid, z3 = 2 * t + 9 >= valid;
+    const bool tail = valid < kUnitTokens;
     if constexpr (kFP8) {
       // ldmatrix.trans over byte pairs: a lane receives dims (2g, 2g+1) of
       // tokens (2t, 2t+1) [or 8+...]; one byte permute splits them into the
       // token pairs of dim 2g and of dim 2g+1, which become accumulator rows
       // g and g+8 (the output rows of each 16-dim tile are permuted; the
       // epilogue writes them back in order)
-      const uint32_t vbase = kbase + kBoxBytesF8;
-      const uint32_t m01 = (z0 ? 0u : 0xffffu) | (z1 ? 0u : 0xffff0000u);
-      const uint32_t m23 = (z2 ? 0u : 0xffffu) | (z3 ? 0u : 0xffff0000u);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int chunk = 2 * j + k_chk;
-        const uint32_t addr = vbase + k_row * 128 + ((chunk ^ (k_row & 7)) << 4);
-        uint32_t r0, r1, r2, r3;
-        ldsm_x4_t(addr, r0, r1, r2, r3);
+      for (int u = 0; u < kUP; ++u) {
+        const uint32_t vbase = kbase + 2 * kBoxBytesF8 + u * kBoxBytesF8;
+        const int vu = valid - u * kPageTokens;  // valid tokens of page u (may be <= 0)
+        const bool z0 = 2 * t >= vu, z1 = 2 * t + 1 >= vu;
+        const bool z2 = 2 * t + 8 >= vu, z3 = 2 * t + 9 >= vu;
+        const uint32_t m01 = (z0 ? 0u : 0xffffu) | (z1 ? 0u : 0xffff0000u);
+        const uint32_t m23 = (z2 ? 0u : 0xffffu) | (z3 ? 0u : 0xffff0000u);
 #pragma unroll
-        for (int h2 = 0; h2 < 2; ++h2) {
-          const uint32_t lo = __byte_perm(h2 ? r2 : r0, 0u, 0x3120);  // tokens 2t, 2t+1
-          const uint32_t hi = __byte_perm(h2 ? r3 : r1, 0u, 0x3120);  // tokens 2t+8, 2t+9
-          uint32_t a0, a1, a2, a3;
-          e4m3x4_to_f16x2x2(lo, a0, a1);
-          e4m3x4_to_f16x2x2(hi, a2, a3);
-          if (tail) {  // stale rows past seq_len: P is 0 there, keep NaN codes out too
-            a0 &= m01;
-            a1 &= m01;
-            a2 &= m23;
-            a3 &= m23;
+        for (int j = 0; j < 4; ++j) {
+          const int chunk = 2 * j + k_chk;
+          const uint32_t addr = vbase + k_row * 128 + ((chunk ^ (k_row & 7)) << 4);
+          uint32_t r0, r1, r2, r3;
+          ldsm_x4_t(addr, r0, r1, r2, r3);
+#pragma unroll
+          for (int h2 = 0; h2 < 2; ++h2) {
+            const uint32_t lo = __byte_perm(h2 ? r2 : r0, 0u, 0x3120);  // tokens 2t, 2t+1
+            const uint32_t hi = __byte_perm(h2 ? r3 : r1, 0u, 0x3120);  // tokens 2t+8, 2t+9
+            uint32_t a0, a1, a2, a3;
+            e4m3x4_to_f16x2x2(lo, a0, a1);
+            e4m3x4_to_f16x2x2(hi, a2, a3);
+            if (tail) {  // stale rows past seq_len: P is 0 there, keep NaN codes out too
+              a0 &= m01;
+              a1 &= m01;
+              a2 &= m23;
+              a3 &= m23;
+            }
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+              mma_16816<false>(o[nt][2 * j + h2], a0, a1, a2, a3, pb[u][nt][0], pb[u][nt][1]);
           }
-#pragma unroll
-          for (int nt = 0; nt < NT; ++nt)
-            mma_16816<false>(o[nt][2 * j + h2], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
         }
       }
     } else {
+    const bool z0 = 2 * t >= valid, z1 = 2 * t + 1 >= valid;
+    const bool z2 = 2 * t + 8 >= valid, z3 = 2 * t + 9 >= valid;
     const uint32_t vbase = kbase + 2 * kBoxBytes;
 #pragma unroll
     for (int mi = 0; mi < 8; ++mi) {
@@ -859,7 +917,7 @@ __device__ __forceinline__ int stream_range(const DecodeParams& p, const CUtenso
         a3 &= (mlo1 | mhi1);
       }
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) mma_16816<kBF16>(o[nt][mi], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
+      for (int nt = 0; nt < NT; ++nt) mma_16816<kBF16>(o[nt][mi], a0, a1, a2, a3, pb[0][nt][0], pb[0][nt][1]);
     }
     }
     __syncwarp();
@@ -1094,7 +1152,7 @@ __global__ void __launch_bounds__(decode_warps<kFP8>() * 32, kDecodeCtasPerSm)
   tb.wo = 1;
   tb.Qc = 1;
 
-  // ---- prologue: pages per sequence and their exclusive prefix sum ----------
+  // ---- prologue: units per sequence and their exclusive prefix sum ----------
   const int per = (B + blockDim.x - 1) / blockDim.x;
   const int b_lo = min(B, tid * per), b_hi = min(B, b_lo + per);
   int bad = 0;
@@ -1182,10 +1240,11 @@ __global__ void __launch_bounds__(decode_warps<kFP8>() * 32, kDecodeCtasPerSm)
     tb.pre_units = static_cast<int64_t>(tot_u) * Hkv;
   }
 
-  // own pages per sequence (after the group prefix in cascade mode)
+  // own units per sequence (after the group prefix in cascade mode)
+  constexpr int kUP = unit_pages<kFP8>();
   int local = 0;
   for (int b = b_lo; b < b_hi; ++b) {
-    int P = own_pages_of(p, b, sub_per_block);
+    int P = (own_pages_of(p, b, sub_per_block) + kUP - 1) / kUP;
     if constexpr (kCascade) {
       const int gsb = G > 0 ? __ldg(p.cas_seq_group + b) : -1;
       const int off = gsb >= 0 ? __ldg(p.cas_group_pages + gsb) : 0;
@@ -1198,7 +1257,7 @@ __global__ void __launch_bounds__(decode_warps<kFP8>() * 32, kDecodeCtasPerSm)
   int run = block_exclusive_scan(local, s_warp_tot, &total_own);
   for (int b = b_lo; b < b_hi; ++b) {
     prefix[b] = run;
-    int P = own_pages_of(p, b, sub_per_block);
+    int P = (own_pages_of(p, b, sub_per_block) + kUP - 1) / kUP;
     if constexpr (kCascade) P -= soff[b];
     run += P;
   }

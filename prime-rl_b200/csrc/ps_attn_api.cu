@@ -61,7 +61,11 @@ EncodeTiledFn encode_fn() {
 // Tensor map over one cache half viewed as [num_blocks][block_size][Hkv][128]
 // 16-bit elements; box = one 16-token page of one head, 64 dims (128 B) wide,
 // 128-byte swizzle.  elem_bytes = 1 (fp8 cache): the box is all 128 dims,
-// again 128 bytes wide.
+// again 128 bytes wide.  L2 promotion: 256 B for a 16-bit cache (a head's row,
+// whose other half the next box reads), 128 B for fp8, whose head row is 128 B:
+// a 256-byte promotion would pull in the neighbouring head's row, which
+// another warp streams much later (measured: 1.31x the algorithmic DRAM bytes
+// and a 23% slower config-5 step).
 int make_page_map(CUtensorMap* map, const void* base, int64_t num_blocks, int block_size,
                   int num_kv_heads, int64_t s_block, int64_t s_slot, int64_t s_head,
                   int elem_bytes = 2) {
@@ -77,7 +81,8 @@ int make_page_map(CUtensorMap* map, const void* base, int64_t num_blocks, int bl
   CUresult r = fn(map, elem_bytes == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_UINT16,
                   4, const_cast<void*>(base), dims, strides,
                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                  elem_bytes == 1 ? CU_TENSOR_MAP_L2_PROMOTION_L2_128B : CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return fail(PS_ERR_INVALID_ARGUMENT,
                 "cuTensorMapEncodeTiled failed (%d): cache strides must be multiples of 16 "

@@ -82,14 +82,14 @@ struct DecodeParams {
 #define PS_DECODE_CTAS_PER_SM 1
 #endif
 #ifndef PS_DECODE_FP8_WARPS
-#define PS_DECODE_FP8_WARPS 12
+#define PS_DECODE_FP8_WARPS 8
 #endif
 #ifndef PS_DECODE_FP8_STAGES
 #define PS_DECODE_FP8_STAGES 2
 #endif
 constexpr int kDecodeWarps = PS_DECODE_WARPS;           // warps per CTA
-// fp8 caches: a page-head is half the bytes and the per-warp instruction
-// stream, not HBM, sets the pace, so more warps with fewer stages each
+// fp8 caches: a unit is two pages (the same 8 KB per stage as a 16-bit page),
+// so the same warps and stages as the 16-bit kernel
 constexpr int kDecodeFp8Warps = PS_DECODE_FP8_WARPS;
 constexpr int kDecodeFp8Stages = PS_DECODE_FP8_STAGES;
 constexpr int kDecodeMaxWarps = kDecodeWarps > kDecodeFp8Warps ? kDecodeWarps : kDecodeFp8Warps;

@@ -134,13 +134,12 @@ def test_static_scratch_rejects_oversized_problem(cuda_device):
 
 @pytest.mark.parametrize("fp8", [False, True])
 def test_static_scratch_size_limit(cuda_device, fp8):
-    """The static scratch takes every problem whose decode scratch for its
-    cache dtype fits in 16 MiB: the 16-bit kernel keeps a split slot per warp
-    of 8 warps per SM, the fp8 kernel of 12 (352 and 278 sequences at 8 KV
-    heads on 148 SMs)."""
+    """The static scratch takes every problem whose decode scratch fits in
+    16 MiB: a split slot per warp of 8 warps per SM with either cache dtype,
+    plus one per (sequence, kv head) (352 sequences at 8 KV heads on 148
+    SMs)."""
     lib = _lib.load()
-    warps = 12 if fp8 else 8
-    nwarps = torch.cuda.get_device_properties(cuda_device).multi_processor_count * warps
+    nwarps = torch.cuda.get_device_properties(cuda_device).multi_processor_count * 8
     part_off = 256 + 2 * 4096 * 8 * 4
     limit = (STATIC_BYTES - part_off) // (8 * 129 * 4) - nwarps
     max_seqs = limit // 8
