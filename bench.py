@@ -725,7 +725,10 @@ def run_ours(args):
     tokens = arm.batch.num_tokens  # every rank produces all tokens (its heads when sharded)
     value = tokens * (1 if arm.sharded else world) / (ms / 1e3)
     step_bytes = workloads.hbm_bytes(arm.batch)
-    traffic = None if args.kv_fp8 or arm.sharded else profile_traffic(f"paged_decode_cfg{cfg}")
+    # DRAM bytes of a full launch from the committed ncu summary (none for a
+    # profiling subset or a KV-head shard, whose launches are smaller)
+    traffic = (None if arm.sharded or args.max_seqs is not None
+               else profile_traffic(f"paged_decode_{'fp8_' if args.kv_fp8 else ''}cfg{cfg}"))
     res = {
         "metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),

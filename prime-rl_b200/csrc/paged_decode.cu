@@ -547,6 +547,8 @@ __device__ __forceinline__ int stream_range(const DecodeParams& p, const CUtenso
 
   // Issue the TMA loads of page-head c into `stage` (warp-collective).
   // `seg_start`: c begins a segment for this warp -> also bring its query rows.
+  // KV pages are read once: evict them from L2 first
+  const uint64_t kv_policy = l2_policy_evict_first();
   auto issue = [&](int stage, const Cursor& c, bool seg_start) {
     const int pg = (c.p + c.off) * kUP;  // first page of the unit
     const int e = pg / sub_per_block;
@@ -584,23 +586,23 @@ __device__ __forceinline__ int stream_range(const DecodeParams& p, const CUtenso
         // K page 0 | K page 1 | V page 0 | V page 1; a missing second page
         // leaves its boxes stale (every token of it is masked)
         mbar_arrive_expect_tx(bar, (has1 ? 4 : 2) * kBoxBytesF8 + qbytes);
-        tma_load_4d(dst, kmap, bar, 0, c.h, tok, blk);
-        tma_load_4d(dst + 2 * kBoxBytesF8, vmap, bar, 0, c.h, tok, blk);
+        tma_load_4d_hint(dst, kmap, bar, 0, c.h, tok, blk, kv_policy);
+        tma_load_4d_hint(dst + 2 * kBoxBytesF8, vmap, bar, 0, c.h, tok, blk, kv_policy);
         if (has1) {
           if (blk1 < 0 || blk1 >= p.num_blocks) {
             set_status(p.status, PS_DEV_BLOCK_OUT_OF_RANGE);
             blk1 = 0;
           }
           const int tok1 = (pg + 1 - e_last * sub_per_block) * kPageTokens;
-          tma_load_4d(dst + kBoxBytesF8, kmap, bar, 0, c.h, tok1, blk1);
-          tma_load_4d(dst + 3 * kBoxBytesF8, vmap, bar, 0, c.h, tok1, blk1);
+          tma_load_4d_hint(dst + kBoxBytesF8, kmap, bar, 0, c.h, tok1, blk1, kv_policy);
+          tma_load_4d_hint(dst + 3 * kBoxBytesF8, vmap, bar, 0, c.h, tok1, blk1, kv_policy);
         }
       } else {
         mbar_arrive_expect_tx(bar, SB + qbytes);
-        tma_load_4d(dst + 0 * kBoxBytes, kmap, bar, 0, c.h, tok, blk);
-        tma_load_4d(dst + 1 * kBoxBytes, kmap, bar, 64, c.h, tok, blk);
-        tma_load_4d(dst + 2 * kBoxBytes, vmap, bar, 0, c.h, tok, blk);
-        tma_load_4d(dst + 3 * kBoxBytes, vmap, bar, 64, c.h, tok, blk);
+        tma_load_4d_hint(dst + 0 * kBoxBytes, kmap, bar, 0, c.h, tok, blk, kv_policy);
+        tma_load_4d_hint(dst + 1 * kBoxBytes, kmap, bar, 64, c.h, tok, blk, kv_policy);
+        tma_load_4d_hint(dst + 2 * kBoxBytes, vmap, bar, 0, c.h, tok, blk, kv_policy);
+        tma_load_4d_hint(dst + 3 * kBoxBytes, vmap, bar, 64, c.h, tok, blk, kv_policy);
       }
     }
     if (seg_start) {
