@@ -12,7 +12,9 @@ metric is quoted on at 1/2/4/8 GPUs.  Inputs (KV pool 23 GB) exceed the
 
 N > 1 (torchrun, one process per GPU): config 5 shards KV heads across the
 GPUs (rank r: KV heads [r*8/N, (r+1)*8/N) and their query heads) and
-all-gathers the head outputs over NVLink peer memory (``ps_head_gather``;
+all-gathers the head outputs over NVLink peer memory inside the decode launch
+(``ps_paged_decode_head_gather``: rows stored into the peers as they are
+finished; ``--gather peer`` for the separate pull launch ``ps_head_gather``,
 ``--gather nccl`` for NCCL's all_gather) -- strong scaling, every rank checks
 sampled gathered rows against a torch fp32 attention of the same rows.
 Configs 2-4 at N > 1 run as independent replicas (sequence-batch sharding,
@@ -205,11 +207,12 @@ class Arm:
     each replayed from its own CUDA graph so CUDA events can bracket it."""
 
     def __init__(self, cfg, dev, world=1, rank=0, *, kv_fp8=False, cascade=False, fused=True,
-                 gather="peer", use_graph=True, max_seqs=None):
+                 gather="fused", use_graph=True, max_seqs=None):
         from ps_attn import ops, workloads
 
         self.cfg, self.dev, self.world, self.rank = cfg, dev, world, rank
         self.sharded = cfg == 5 and world > 1
+        self.gather_kind = gather
         self.kv_fp8, self.fused, self.use_graph = kv_fp8, fused, use_graph
         if self.sharded:
             per = 8 // world
@@ -254,13 +257,15 @@ class Arm:
         self.gathered = None
         if self.sharded:
             self.full_out = torch.empty(B, self.hq * world, 128, dtype=batch.q.dtype, device=dev)
-            if gather == "peer":
-                # head outputs exchanged over NVLink peer memory (ps_head_gather)
+            if gather in ("fused", "peer"):
+                # head outputs exchanged over NVLink peer memory: stored into
+                # the peers by the decode itself (ps_paged_decode_head_gather),
+                # or pulled by a separate launch (ps_head_gather)
                 from ps_attn import sharding
 
                 shard = sharding.HeadShard(world, rank, self.hq * world, self.hkv * world)
-                self.peer_gather = sharding.PeerHeadGather.from_process_group(
-                    shard, B, batch.q.dtype, device=dev)
+                cls = sharding.FusedHeadGather if gather == "fused" else sharding.PeerHeadGather
+                self.peer_gather = cls.from_process_group(shard, B, batch.q.dtype, device=dev)
             else:
                 self.gathered = torch.empty(world, B, self.hq, 128, dtype=batch.q.dtype, device=dev)
         self.stream = torch.cuda.Stream(dev)
@@ -289,7 +294,7 @@ class Arm:
         if self.cascade:  # the per-step plan (an engine builds it once per step for all layers)
             ph.append(("plan", lambda: ops.cascade_plan(inp["block_table"], inp["seq_lens"], self.hq, self.hkv,
                                                         16, query_start_loc=inp["query_start_loc"], plan=plan)))
-        if self.peer_gather is not None:  # this rank's heads into its slab
+        if self.peer_gather is not None:  # this rank's heads (fused: and the exchange)
             ph.append(("decode", lambda: self.peer_gather.decode(
                 inp["q"], kc, vc, inp["block_table"], inp["seq_lens"], scale, self.full_out, lse=lse,
                 query_start_loc=inp["query_start_loc"], workspace=ws, **fkw, **skw)))
@@ -305,7 +310,9 @@ class Arm:
                 inp["q"], kc, vc, inp["block_table"][nd:], inp["seq_lens"][nd:], inp["query_start_loc"][nd:],
                 scale, out, lse=lse, workspace=ws)))
         if self.sharded:
-            if self.peer_gather is not None:
+            if self.gather_kind == "fused":
+                pass  # inside the decode launch
+            elif self.peer_gather is not None:
                 ph.append(("gather", lambda: self.peer_gather.gather(self.B, self.full_out)))
             else:
                 def nccl_gather():
@@ -327,6 +334,12 @@ class Arm:
         the eager phases and there are no graphs."""
         ph = self.phases(self.inputs() if inp is None else inp)
         names = [n for n, _ in ph]
+        if self.sharded:
+            # the ranks reach their first exchange together (its waits are bounded)
+            import torch.distributed as dist
+
+            torch.cuda.synchronize(self.stream.device)
+            dist.barrier()
         with torch.cuda.stream(self.stream):
             for _ in range(3):
                 for _, fn in ph:
@@ -736,8 +749,11 @@ def run_ours(args):
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": config_dict(cfg, args.max_seqs),
         "setup": {
-            "parallelism": (f"kv-head tp{world} + " + ("NVLink peer-memory head gather (ps_head_gather)"
-                                                       if arm.peer_gather else "NCCL all-gather") if arm.sharded else
+            "parallelism": (f"kv-head tp{world} + " + {
+                "fused": "head all-gather fused into the decode over NVLink peer memory "
+                         "(ps_paged_decode_head_gather)",
+                "peer": "NVLink peer-memory head gather (ps_head_gather)",
+                "nccl": "NCCL all-gather"}[arm.gather_kind] if arm.sharded else
                             (f"batch replicas x{world}" if world > 1 else "single GPU")),
             "heads_this_gpu": {"q": arm.hq, "kv": arm.hkv},
             "kv_pool_bytes_this_gpu": arm.batch.kv_cache.numel() * arm.batch.kv_cache.element_size(),
@@ -757,9 +773,15 @@ def run_ours(args):
         "clocks": t["clocks"],
     }
     if arm.sharded:
-        res["gather"] = {"kind": "peer" if arm.peer_gather else "nccl", "ms_per_step": round(pm["gather"], 5),
-                         "share_of_step": round(pm["gather"] / ms, 4),
-                         "bytes_received_per_gpu": (world - 1) * arm.B * arm.hq * 128 * arm.batch.q.element_size()}
+        rx = (world - 1) * arm.B * arm.hq * 128 * arm.batch.q.element_size()
+        if arm.gather_kind == "fused":
+            res["gather"] = {"kind": "fused into the decode launch (ps_paged_decode_head_gather)",
+                             "ms_per_step": None, "bytes_received_per_gpu": rx,
+                             "note": "rows stored into the peers over NVLink as the decode finishes them; "
+                                     "the decode phase includes the closing barrier and the local copy"}
+        else:
+            res["gather"] = {"kind": arm.gather_kind, "ms_per_step": round(pm["gather"], 5),
+                             "share_of_step": round(pm["gather"] / ms, 4), "bytes_received_per_gpu": rx}
         res["check"] = check
     if arm.cascade:
         res["cascade"] = {"groups": int(arm.plan.views()["num_groups"].item()),
@@ -1067,8 +1089,9 @@ def main():
                     help="config 3: shared-prefix (cascade) decode with a per-step plan")
     ap.add_argument("--dcp", action="store_true",
                     help="config 5 under decode context parallelism (tokens sharded, not heads)")
-    ap.add_argument("--gather", default="peer", choices=["nccl", "peer"],
-                    help="config 5 on N GPUs: head outputs all-gathered by NCCL or over peer memory")
+    ap.add_argument("--gather", default="fused", choices=["fused", "nccl", "peer"],
+                    help="config 5 on N GPUs: head outputs stored into the peers by the decode itself "
+                         "(fused), pulled over peer memory by a separate launch (peer), or all-gathered by NCCL")
     ap.add_argument("--kv-fp8", action="store_true",
                     help="decode configs over an fp8 (e4m3) KV cache, fused quantizing append")
     ap.add_argument("--interleave", type=int, default=1,

@@ -469,6 +469,37 @@ int ps_head_gather(const ps_head_gather_problem* problem, void* stream);
    k+1 for any. */
 int ps_head_gather_phase(const ps_head_gather_problem* problem, int32_t phase, void* stream);
 
+/*
+ * KV-head-sharded decode with the head all-gather fused in: one launch per
+ * rank does ps_paged_decode (with the fused append when the problem asks for
+ * it) and ps_head_gather's exchange, so the NVLink transfers overlap the
+ * decode instead of following it.  The reference has no single counterpart:
+ * it is tensor-parallel attention (vLLM splits heads over ranks,
+ * vllm/model_executor/models/qwen3.py:78-107) followed by
+ * all_gather_into_tensor of the head outputs, in one kernel.
+ *
+ * problem: this rank's decode (its query heads, num_q_heads == gather->hq_local,
+ * and its KV heads' caches); problem->out and its strides are ignored -- the
+ * rows go to gather->out at heads [rank * hq_local, (rank + 1) * hq_local),
+ * and every finished row is also stored over NVLink into each peer's slab,
+ * [max_tokens, world * hq_local, 128] at byte offset 256.  At the end every
+ * rank copies the peers' rows from its own slab into gather->out, so when
+ * the launch completes gather->out holds [num_tokens, world * hq_local, 128]
+ * on every rank.  Slabs: ps_dcp_slab_alloc of
+ * ps_decode_head_gather_slab_bytes(max_tokens, world * hq_local), mapped in
+ * the peers with ps_dcp_ipc_handle / ps_dcp_ipc_open, one per rank, reused
+ * by every call (not shared with ps_head_gather's slabs).  Every rank makes
+ * the same calls in the same order; a rank's query rows must be < num_tokens
+ * (else PS_DEV_BAD_METADATA and the row is not sent).  Two flag rounds per
+ * call (rows written; rows copied, so that no rank's next call overwrites
+ * rows a peer has not copied), bounded as in ps_dcp_decode:
+ * PS_DEV_WAIT_TIMEOUT in *gather->status.  Plain decode only (no cascade
+ * plan); 16-bit or fp8 caches.
+ */
+int64_t ps_decode_head_gather_slab_bytes(int32_t max_tokens, int32_t num_q_heads);
+int ps_paged_decode_head_gather(const ps_paged_problem* problem, void* workspace, int64_t workspace_bytes,
+                                const ps_head_gather_problem* gather, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -42,6 +42,17 @@
 //   online softmax per head column (exp2 domain; 3 xor-shuffles per max)
 //   P^T -> B fragment      via movmatrix.trans (no shared-memory round trip)
 //   O^T[128 dims, 8 heads] += V^T[128, 16 tok] . P^T        (8 mma, V via ldmatrix.trans)
+//
+// Fused head all-gather (KV-head-sharded groups, DecodeParams::gather_world):
+//   every output row is also stored into each peer GPU's slab over NVLink as
+//   it is finished -- by the combine (one 256-byte row per warp store) or, for
+//   a segment one warp streamed alone, from the accumulators transposed by
+//   movmatrix -- so the exchange overlaps the streaming of the remaining pages.  At the end
+//   each CTA waits (bounded) for every rank's "rows written" flag and copies
+//   the peers' rows from this GPU's slab into the output; a second flag round
+//   ("rows copied") keeps the next call from overwriting rows a peer has not
+//   copied yet.
+#include "peer_sync.cuh"
 #include "ps_common.cuh"
 #include "ps_launch.h"
 
@@ -268,6 +279,20 @@ __device__ __noinline__ void combine_rows(const DecodeParams& p, int64_t slot0, 
       else
         *reinterpret_cast<uint2*>(reinterpret_cast<__half*>(p.out) + obase) = packed;
       if (lane == 0 && p.lse != nullptr) p.lse[qh * p.lse_sh + qrow * p.lse_st] = lse;
+      if (p.gather_world > 0) {
+        // the same row into every peer's slab (the warp's 8-byte lane stores
+        // form one 256-byte row); a row past the slabs' tokens is refused
+        if (qrow < p.gather_tokens) {
+#pragma unroll
+          for (int r = 0; r < 8; ++r) {
+            char* dst = r < p.gather_world ? p.gather_rows[r] : nullptr;
+            if (dst != nullptr)
+              *reinterpret_cast<uint2*>(dst + qrow * p.gather_row_st + qh * 256 + lane * 8) = packed;
+          }
+        } else if (lane == 0) {
+          set_status(p.gather_status, PS_DEV_BAD_METADATA);
+        }
+      }
     }
   };
   if (kRec == 8 && ntot <= 4 && nrows <= 4) {
@@ -510,7 +535,47 @@ __device__ __forceinline__ int out_row(int g, int hi) {
   return kFP8 ? 2 * g + hi : g + 8 * hi;
 }
 
-template <bool kBF16, int NT, int kRec, int kQNT, int kMode, bool kFP8 = false>
+// Fused head all-gather, segments one warp streams alone: the segment's
+// output rows (o * inv rounded as the direct store rounds them) into every
+// peer's slab.  For each 16-dim tile mi and half, the accumulators form an
+// m8n8 b16 matrix with dims on rows and query heads on columns;
+// movmatrix.trans hands lane (g, t) two dims of head g: 16-bit caches dims
+// 16mi + 8 half + 2t, +1; fp8 caches (rows permuted, see out_row) dims
+// 16mi + 4t, +2 and 16mi + 4t + 1, +3, interleaved into 4 consecutive dims.
+// Each warp store then moves 16- (16-bit) or 32-byte (fp8) runs of 8 rows.
+template <bool kBF16, bool kFP8, int NT>
+__device__ __forceinline__ void push_rows_direct(const DecodeParams& p, const float (&o)[NT][8][4],
+                                                 const float (&inv)[NT][2], int qrow, int h, int g,
+                                                 int t, int lane) {
+  if (qrow >= p.gather_tokens) {
+    if (lane == 0) set_status(p.gather_status, PS_DEV_BAD_METADATA);
+    return;
+  }
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const bool ok = nt * 8 + g < p.group;  // this lane's head after the transpose
+    const int64_t row = qrow * p.gather_row_st + static_cast<int64_t>(h * p.group + nt * 8 + g) * 256;
+#pragma unroll
+    for (int mi = 0; mi < 8; ++mi) {
+      const uint32_t a = movmatrix_t(pack2<kBF16>(o[nt][mi][0] * inv[nt][0], o[nt][mi][1] * inv[nt][1]));
+      const uint32_t b = movmatrix_t(pack2<kBF16>(o[nt][mi][2] * inv[nt][0], o[nt][mi][3] * inv[nt][1]));
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        char* dst = r < p.gather_world ? p.gather_rows[r] : nullptr;
+        if (!ok || dst == nullptr) continue;
+        if constexpr (kFP8) {
+          *reinterpret_cast<uint2*>(dst + row + (16 * mi + 4 * t) * 2) =
+              make_uint2(__byte_perm(a, b, 0x5410), __byte_perm(a, b, 0x7632));
+        } else {
+          *reinterpret_cast<uint32_t*>(dst + row + (16 * mi + 2 * t) * 2) = a;
+          *reinterpret_cast<uint32_t*>(dst + row + (16 * mi + 8 + 2 * t) * 2) = b;
+        }
+      }
+    }
+  }
+}
+
+template <bool kBF16, int NT, int kRec, int kQNT, int kMode, bool kFP8 = false, bool kGather = false>
 __device__ __forceinline__ int stream_range(const DecodeParams& p, const CUtensorMap* kmap,
                                             const CUtensorMap* vmap, const Tables& tb,
                                             int64_t start, int64_t end, int64_t gw,
@@ -981,6 +1046,7 @@ __device__ __forceinline__ int stream_range(const DecodeParams& p, const CUtenso
               if (g == 0 && p.lse) p.lse[qh * p.lse_sh + qrow * p.lse_st] = lse[nt][j];
             }
           }
+        if constexpr (kGather) push_rows_direct<kBF16, kFP8, NT>(p, o, inv, qrow, h, g, t, lane);
       } else {
         const int64_t slot = gw + unit;
 #pragma unroll
@@ -1102,7 +1168,47 @@ __device__ __forceinline__ int own_pages_of(const DecodeParams& p, int b, int su
   return min(P, p.max_blocks_per_seq * sub_per_block);
 }
 
-template <bool kBF16, int NT, bool kCascade, bool kFP8>
+// Fused head all-gather, after this CTA's streaming (the whole CTA).  Rows
+// written: every CTA's peer stores precede its arrival (a system-scope fence
+// per thread); the CTA that arrives last publishes "rows written" to every
+// rank.  Each CTA then waits for every rank's flag and copies a share of the
+// peers' rows from this rank's slab into gather_out; the last CTA to finish
+// copying publishes "rows copied" and waits for every rank's, so that when
+// the kernel completes no peer still needs the rows this rank will push in
+// its next call.  All waits are bounded (status PS_DEV_WAIT_TIMEOUT).
+__device__ __noinline__ void gather_tail(const DecodeParams& p) {
+  char* own = p.gather_slab[p.gather_rank];
+  const int32_t e = peer::call_epoch(own);
+  __threadfence_system();
+  if (peer::last_cta(own)) peer::signal(p.gather_slab, p.gather_world, p.gather_rank, 0, e);
+  if (peer::wait_all(own, p.gather_world, 0, e, p.gather_status)) {
+    const int hq = p.gather_hq_local;
+    const int64_t row_vecs = static_cast<int64_t>(p.gather_world) * hq * 16;  // 16-byte vectors per token
+    const int64_t peer_vecs = row_vecs - static_cast<int64_t>(hq) * 16;
+    const int64_t nvec = static_cast<int64_t>(p.gather_tokens) * peer_vecs;
+    const char* rows = own + kDecodeGatherRowsOffset;
+    const int own_lo = p.gather_rank * hq;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < nvec;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+      const int64_t t = i / peer_vecs;
+      const int rem = static_cast<int>(i - t * peer_vecs);
+      const int c = rem & 15;
+      const int hp = rem >> 4;
+      const int hg = hp < own_lo ? hp : hp + hq;  // this rank's heads are already in gather_out
+      const uint4 v = *reinterpret_cast<const uint4*>(rows + t * p.gather_row_st + hg * 256 + c * 16);
+      *reinterpret_cast<uint4*>(p.gather_out + t * p.gather_o_st + hg * p.gather_o_sh + c * 16) = v;
+    }
+  }
+  if (peer::last_cta(own, kDecodeGatherDone2Word)) {
+    peer::signal(p.gather_slab, p.gather_world, p.gather_rank, 1, e);
+    peer::wait_all(own, p.gather_world, 1, e, p.gather_status);
+    peer::close_call(own, e);
+  }
+}
+
+// kGather: the fused head all-gather is compiled in (plain decode only); the
+// kernels without it carry none of its code
+template <bool kBF16, int NT, bool kCascade, bool kFP8, bool kGather = false>
 __global__ void __launch_bounds__(decode_warps<kFP8>() * 32, kDecodeCtasPerSm)
     paged_decode_kernel(const __grid_constant__ DecodeParams p,
                         const __grid_constant__ CUtensorMap kmap,
@@ -1285,32 +1391,45 @@ __global__ void __launch_bounds__(decode_warps<kFP8>() * 32, kDecodeCtasPerSm)
     const int qrow = p.qsl ? __ldg(p.qsl + b) : b;
     for (int d = 0; d < kHeadDim; ++d) store_out2<kBF16>(p.out, qrow * p.o_st + qh * p.o_sh + d, 0.f);
     if (p.lse) p.lse[qh * p.lse_sh + qrow * p.lse_st] = -INFINITY;
+    if constexpr (kGather) {
+      if (qrow < p.gather_tokens) {
+        for (int r = 0; r < p.gather_world; ++r)
+          if (p.gather_rows[r] != nullptr)
+            for (int c = 0; c < 16; ++c)
+              reinterpret_cast<uint4*>(p.gather_rows[r] + qrow * p.gather_row_st + qh * 256)[c] =
+                  make_uint4(0u, 0u, 0u, 0u);
+      } else {
+        set_status(p.gather_status, PS_DEV_BAD_METADATA);
+      }
+    }
   }
 
   const int64_t gw = static_cast<int64_t>(blockIdx.x) * W + warp;
   const int64_t start = min(total, list_at_cost(tb, gw * tb.Qc));
   const int64_t end = min(total, list_at_cost(tb, (gw + 1) * tb.Qc));
-  if (start >= end) return;
 
-  uint8_t* wsm = smem + warp * D * SB;
-  uint8_t* wq = qslots + warp * D * decode_qslot_bytes<kQNT>();
-  uint64_t* wbar = bars + warp * D;
+  if (start < end) {
+    uint8_t* wsm = smem + warp * D * SB;
+    uint8_t* wq = qslots + warp * D * decode_qslot_bytes<kQNT>();
+    uint64_t* wbar = bars + warp * D;
 
-  if constexpr (kCascade) {
-    int k = 0;
-    if (start < tb.pre_total)
-      k = stream_range<kBF16, kPrefixNT, kRec, kQNT, kCasPrefix>(
-          p, &kmap, &vmap, tb, start, min(end, tb.pre_total), gw, wsm, wq, wbar, 0, lane);
-    if (k >= 0 && end > tb.pre_total)
-      stream_range<kBF16, NT, kRec, kQNT, kCasSuffix>(p, &kmap, &vmap, tb, max(start, tb.pre_total),
-                                                      end, gw, wsm, wq, wbar, k, lane);
-  } else {
-    stream_range<kBF16, NT, kRec, kQNT, kPlain, kFP8>(p, &kmap, &vmap, tb, start, end, gw, wsm, wq,
-                                                      wbar, 0, lane);
+    if constexpr (kCascade) {
+      int k = 0;
+      if (start < tb.pre_total)
+        k = stream_range<kBF16, kPrefixNT, kRec, kQNT, kCasPrefix>(
+            p, &kmap, &vmap, tb, start, min(end, tb.pre_total), gw, wsm, wq, wbar, 0, lane);
+      if (k >= 0 && end > tb.pre_total)
+        stream_range<kBF16, NT, kRec, kQNT, kCasSuffix>(p, &kmap, &vmap, tb, max(start, tb.pre_total),
+                                                        end, gw, wsm, wq, wbar, k, lane);
+    } else {
+      stream_range<kBF16, NT, kRec, kQNT, kPlain, kFP8, kGather>(p, &kmap, &vmap, tb, start, end, gw, wsm,
+                                                                 wq, wbar, 0, lane);
+    }
   }
+  if constexpr (kGather) gather_tail(p);  // every warp of the CTA
 }
 
-template <bool kBF16, int NT, bool kCascade, bool kFP8 = false>
+template <bool kBF16, int NT, bool kCascade, bool kFP8 = false, bool kGather = false>
 static int launch_t(const DecodeParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap,
                     int sm_count, cudaStream_t stream) {
   constexpr int kQNT = kCascade ? kPrefixNT : NT;
@@ -1327,7 +1446,7 @@ static int launch_t(const DecodeParams& p, const CUtensorMap& kmap, const CUtens
   if (cudaGetDevice(&dev) != cudaSuccess || dev >= 64) return static_cast<int>(cudaErrorInvalidDevice);
   if (!configured[dev]) {
     const cudaError_t e = cudaFuncSetAttribute(
-        paged_decode_kernel<kBF16, NT, kCascade, kFP8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        paged_decode_kernel<kBF16, NT, kCascade, kFP8, kGather>, cudaFuncAttributeMaxDynamicSharedMemorySize,
         static_cast<int>(1024 + decode_smem_bytes_before_table<kQNT, kFP8>() +
                          static_cast<size_t>(table_ints(max_seqs, max_seqs / 2)) * 4));
     if (e != cudaSuccess) return static_cast<int>(e);
@@ -1343,7 +1462,8 @@ static int launch_t(const DecodeParams& p, const CUtensorMap& kmap, const CUtens
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, paged_decode_kernel<kBF16, NT, kCascade, kFP8>, p, kmap, vmap);
+  const cudaError_t e =
+      cudaLaunchKernelEx(&cfg, paged_decode_kernel<kBF16, NT, kCascade, kFP8, kGather>, p, kmap, vmap);
   return static_cast<int>(e != cudaSuccess ? e : cudaGetLastError());
 }
 
@@ -1357,25 +1477,36 @@ int64_t ps_decode_partial_slots(int num_seqs, int num_kv_heads, int sm_count, in
              (fp8 ? ps::kDecodeFp8Warps : ps::kDecodeWarps) + units;
 }
 
+namespace ps {
+// Plain decode (no cascade plan): cache dtype x I/O dtype x query-column tiles.
+template <bool kGather>
+static int launch_plain(const DecodeParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap,
+                        int dtype_bf16, int sm_count, cudaStream_t stream, int fp8_cache, int nt) {
+  if (fp8_cache) {
+    if (dtype_bf16)
+      return nt == 1 ? launch_t<true, 1, false, true, kGather>(p, kmap, vmap, sm_count, stream)
+                     : launch_t<true, 2, false, true, kGather>(p, kmap, vmap, sm_count, stream);
+    return nt == 1 ? launch_t<false, 1, false, true, kGather>(p, kmap, vmap, sm_count, stream)
+                   : launch_t<false, 2, false, true, kGather>(p, kmap, vmap, sm_count, stream);
+  }
+  if (dtype_bf16)
+    return nt == 1 ? launch_t<true, 1, false, false, kGather>(p, kmap, vmap, sm_count, stream)
+                   : launch_t<true, 2, false, false, kGather>(p, kmap, vmap, sm_count, stream);
+  return nt == 1 ? launch_t<false, 1, false, false, kGather>(p, kmap, vmap, sm_count, stream)
+                 : launch_t<false, 2, false, false, kGather>(p, kmap, vmap, sm_count, stream);
+}
+}  // namespace ps
+
 int ps_launch_paged_decode(const ps::DecodeParams& p, const CUtensorMap& kmap,
                            const CUtensorMap& vmap, int dtype_bf16, int sm_count,
                            cudaStream_t stream, int fp8_cache) {
   const int nt = p.group <= 8 ? 1 : 2;
-  if (fp8_cache) {  // plain decode only (checked by the caller)
-    if (dtype_bf16)
-      return nt == 1 ? ps::launch_t<true, 1, false, true>(p, kmap, vmap, sm_count, stream)
-                     : ps::launch_t<true, 2, false, true>(p, kmap, vmap, sm_count, stream);
-    return nt == 1 ? ps::launch_t<false, 1, false, true>(p, kmap, vmap, sm_count, stream)
-                   : ps::launch_t<false, 2, false, true>(p, kmap, vmap, sm_count, stream);
-  }
-  if (p.cas_num_groups != nullptr) {  // cascade: group <= 8 (checked by the caller)
+  if (p.cas_num_groups != nullptr && !fp8_cache && p.gather_world == 0) {
+    // cascade: group <= 8 (checked by the caller)
     return dtype_bf16 ? ps::launch_t<true, 1, true>(p, kmap, vmap, sm_count, stream)
                       : ps::launch_t<false, 1, true>(p, kmap, vmap, sm_count, stream);
   }
-  if (dtype_bf16) {
-    return nt == 1 ? ps::launch_t<true, 1, false>(p, kmap, vmap, sm_count, stream)
-                   : ps::launch_t<true, 2, false>(p, kmap, vmap, sm_count, stream);
-  }
-  return nt == 1 ? ps::launch_t<false, 1, false>(p, kmap, vmap, sm_count, stream)
-                 : ps::launch_t<false, 2, false>(p, kmap, vmap, sm_count, stream);
+  if (p.gather_world > 0)  // plain decode only (checked by the caller)
+    return ps::launch_plain<true>(p, kmap, vmap, dtype_bf16, sm_count, stream, fp8_cache, nt);
+  return ps::launch_plain<false>(p, kmap, vmap, dtype_bf16, sm_count, stream, fp8_cache, nt);
 }

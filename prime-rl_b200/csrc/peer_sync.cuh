@@ -7,6 +7,7 @@
 //                        remotely, st.release.sys)
 //   int32 word 32        epoch: calls completed on this rank (local)
 //   int32 word 33        done: CTAs of the current kernel that finished (local)
+//   int32 word 34        done, second round (a kernel that counts arrivals twice)
 // A call's epoch is one more than the calls completed, so every kernel of a
 // call agrees on it without host state (CUDA graphs replay the same
 // launches).  Waits are bounded (1 s of %globaltimer) and report
@@ -90,15 +91,16 @@ __device__ __forceinline__ bool wait_all(char* own, int world, int ph, int32_t e
 }
 
 // CTA-wide: whether this CTA is the last of the grid to get here (the
-// counter in `own`'s header is reset by that CTA).  Contains __syncthreads.
-__device__ __forceinline__ bool last_cta(char* own) {
+// counter, word `word` of `own`'s header, is reset by that CTA).  Contains
+// __syncthreads.
+__device__ __forceinline__ bool last_cta(char* own, int word = kDoneWord) {
   __shared__ int s_last;
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
-    const int old = atomicAdd(words(own) + kDoneWord, 1);
+    const int old = atomicAdd(words(own) + word, 1);
     s_last = old == static_cast<int>(gridDim.x) - 1;
-    if (s_last) words(own)[kDoneWord] = 0;
+    if (s_last) words(own)[word] = 0;
   }
   __syncthreads();
   return s_last != 0;

@@ -191,7 +191,8 @@ int validate_problem(const ps_paged_problem* pr, bool decode) {
 }
 
 int decode_impl(const ps_paged_problem* pr, const void* plan, int64_t plan_bytes, void* workspace,
-                int64_t workspace_bytes, void* stream, bool cascade) {
+                int64_t workspace_bytes, void* stream, bool cascade,
+                const ps_head_gather_problem* gather = nullptr) {
   int rc = validate_problem(pr, true);
   if (rc != PS_OK) return rc;
   if (pr->num_seqs == 0) return PS_OK;
@@ -227,7 +228,7 @@ int decode_impl(const ps_paged_problem* pr, const void* plan, int64_t plan_bytes
                      pr->cache_stride_block, pr->cache_stride_slot, pr->cache_stride_head, fp8 ? 1 : 2);
   if (rc != PS_OK) return rc;
   char* ws = static_cast<char*>(workspace);
-  ps::DecodeParams p;
+  ps::DecodeParams p = {};  // every optional feature off
   p.q = pr->q;
   p.q_st = pr->q_stride_token;
   p.q_sh = pr->q_stride_head;
@@ -288,6 +289,25 @@ int decode_impl(const ps_paged_problem* pr, const void* plan, int64_t plan_bytes
     if (!aligned(pr->new_key, 16) || !aligned(pr->new_value, 16) || pr->new_key_stride_token % 8 ||
         pr->new_key_stride_head % 8 || pr->new_value_stride_token % 8 || pr->new_value_stride_head % 8)
       return fail(PS_ERR_INVALID_ARGUMENT, "new key/value rows must be 16-byte aligned");
+  }
+  if (gather != nullptr) {
+    const int hq = gather->hq_local;
+    p.gather_world = gather->world;
+    p.gather_rank = gather->rank;
+    p.gather_hq_local = hq;
+    p.gather_tokens = gather->num_tokens;
+    p.gather_row_st = static_cast<int64_t>(gather->world) * hq * 256;
+    for (int r = 0; r < gather->world; ++r) {
+      char* slab = static_cast<char*>(gather->slabs[r]);
+      p.gather_slab[r] = slab;
+      p.gather_rows[r] = r == gather->rank
+                             ? nullptr
+                             : slab + ps::kDecodeGatherRowsOffset + static_cast<int64_t>(gather->rank) * hq * 256;
+    }
+    p.gather_out = static_cast<char*>(gather->out);
+    p.gather_o_st = gather->out_stride_token * 2;
+    p.gather_o_sh = gather->out_stride_head * 2;
+    p.gather_status = gather->status;
   }
   const int e = ps_launch_paged_decode(p, kmap, vmap, pr->dtype == PS_DTYPE_BF16, sms,
                                        static_cast<cudaStream_t>(stream), fp8 ? 1 : 0);
@@ -862,7 +882,7 @@ int ps_dcp_decode_phase(const ps_dcp_problem* problem, int32_t phase, void* work
 
 // ------------------------------------------------------------ head gather
 namespace {
-int head_gather_impl(const ps_head_gather_problem* hp, int which, void* stream) {
+int validate_gather(const ps_head_gather_problem* hp) {
   if (!hp) return fail(PS_ERR_INVALID_ARGUMENT, "problem is NULL");
   if (hp->world < 1 || hp->world > PS_DCP_MAX_WORLD || hp->rank < 0 || hp->rank >= hp->world)
     return fail(PS_ERR_INVALID_ARGUMENT, "world %d / rank %d invalid (world <= %d)", hp->world, hp->rank,
@@ -878,6 +898,12 @@ int head_gather_impl(const ps_head_gather_problem* hp, int which, void* stream) 
   if (!hp->out || !aligned(hp->out, 16) || hp->out_stride_token % 8 || hp->out_stride_head % 8)
     return fail(PS_ERR_INVALID_ARGUMENT, "out base/strides must be 16-byte aligned");
   if (!hp->status) return fail(PS_ERR_INVALID_ARGUMENT, "head gather needs a device status word");
+  return PS_OK;
+}
+
+int head_gather_impl(const ps_head_gather_problem* hp, int which, void* stream) {
+  const int rc = validate_gather(hp);
+  if (rc != PS_OK) return rc;
   if (hp->num_tokens == 0) return PS_OK;
   const int sms = sm_count_current(nullptr);
   if (sms <= 0) return fail(PS_ERR_CUDA, "no CUDA device");
@@ -910,6 +936,38 @@ int64_t ps_head_gather_slab_bytes(int32_t max_tokens, int32_t hq_local) {
 
 int ps_head_gather(const ps_head_gather_problem* problem, void* stream) {
   return head_gather_impl(problem, 0, stream);
+}
+
+int64_t ps_decode_head_gather_slab_bytes(int32_t max_tokens, int32_t num_q_heads) {
+  if (max_tokens < 1 || num_q_heads < 1) {
+    fail(PS_ERR_INVALID_ARGUMENT, "decode head gather slab size: bad shape");
+    return -1;
+  }
+  return round_up(ps::kDecodeGatherRowsOffset + static_cast<int64_t>(max_tokens) * num_q_heads * 256, 256);
+}
+
+int ps_paged_decode_head_gather(const ps_paged_problem* problem, void* workspace, int64_t workspace_bytes,
+                                const ps_head_gather_problem* gather, void* stream) {
+  int rc = validate_gather(gather);
+  if (rc != PS_OK) return rc;
+  if (!problem) return fail(PS_ERR_INVALID_ARGUMENT, "problem is NULL");
+  if (problem->num_q_heads != gather->hq_local)
+    return fail(PS_ERR_INVALID_ARGUMENT, "problem's %d query heads != the gather's hq_local %d",
+                problem->num_q_heads, gather->hq_local);
+  if (problem->dtype != gather->dtype)
+    return fail(PS_ERR_INVALID_ARGUMENT, "problem dtype %d != gather dtype %d", problem->dtype, gather->dtype);
+  if (problem->num_seqs > gather->num_tokens)
+    return fail(PS_ERR_INVALID_ARGUMENT, "%d sequences > the gather's %d tokens", problem->num_seqs,
+                gather->num_tokens);
+  if (gather->num_tokens == 0 || problem->num_seqs == 0)
+    return fail(PS_ERR_INVALID_ARGUMENT, "an empty step has no rows to gather (every rank must skip it)");
+  // this rank's heads of the group's output
+  ps_paged_problem local = *problem;
+  local.out = static_cast<char*>(gather->out) +
+              static_cast<int64_t>(gather->rank) * gather->hq_local * gather->out_stride_head * 2;
+  local.out_stride_token = gather->out_stride_token;
+  local.out_stride_head = gather->out_stride_head;
+  return decode_impl(&local, nullptr, 0, workspace, workspace_bytes, stream, false, gather);
 }
 
 int ps_head_gather_phase(const ps_head_gather_problem* problem, int32_t phase, void* stream) {

@@ -68,6 +68,20 @@ struct DecodeParams {
   // V * v_scale (an fp8 cache's dequantization)
   const float* k_scale;
   const float* v_scale;
+  // fused head all-gather of a KV-head-sharded group (gather_world == 0: off).
+  // `out` is then this rank's first head of the group's [T, Hq, 128] output;
+  // every finished row is also stored into each peer's slab rows region
+  // (gather_rows[r]: peer r's region offset to this rank's first head,
+  // nullptr for this rank; token t at + t * gather_row_st bytes, local head j
+  // at + j * 256).  The kernel's tail waits for every peer's rows and copies
+  // them from this rank's slab into gather_out.
+  int32_t gather_world, gather_rank, gather_hq_local, gather_tokens;
+  char* gather_slab[8];   // every rank's slab (barrier header at byte 0)
+  char* gather_rows[8];
+  int64_t gather_row_st;  // bytes per token row of a slab's rows region
+  char* gather_out;       // [T, world * hq_local, 128] (this rank's `out` is inside it)
+  int64_t gather_o_st, gather_o_sh;  // bytes
+  int32_t* gather_status;
 };
 
 // Static sizing of the decode kernel, shared by the workspace-size query.
@@ -199,6 +213,7 @@ struct RopeArgs {
 // Decode context parallelism: one rank's view of its group and of one call.
 // Byte strides unless noted.
 constexpr int kDcpMaxWorld = 8;
+static_assert(kDcpMaxWorld == 8, "DecodeParams' gather arrays hold kDcpMaxWorld ranks");
 struct DcpArgs {
   int32_t world, rank, interleave;
   char* slab[kDcpMaxWorld];  // every rank's slab as addressed from this GPU
@@ -252,6 +267,11 @@ struct DequantArgs {
 
 // Head all-gather over peer memory (KV-head-sharded decode).  Byte strides.
 constexpr int64_t kHeadGatherRowsOffset = 256;  // this rank's rows in its slab
+// The fused decode + head gather: the group's rows [T, Hq, 128] in every
+// rank's slab at this offset; slab header word 34 counts the second round of
+// CTA arrivals (word 33 the first).
+constexpr int64_t kDecodeGatherRowsOffset = 256;
+constexpr int kDecodeGatherDone2Word = 34;
 struct HeadGatherArgs {
   int32_t world, rank;
   char* slab[kDcpMaxWorld];

@@ -60,6 +60,8 @@ EXPORTED_SYMBOLS = (
     "ps_head_gather_slab_bytes",
     "ps_head_gather",
     "ps_head_gather_phase",
+    "ps_decode_head_gather_slab_bytes",
+    "ps_paged_decode_head_gather",
     "ps_kv_dequant_gather",
     "ps_merge_attn_states",
 )
@@ -279,6 +281,11 @@ def _declare(lib):
     lib.ps_head_gather.argtypes = [c.POINTER(HeadGatherProblem), c.c_void_p]
     lib.ps_head_gather_phase.restype = c.c_int
     lib.ps_head_gather_phase.argtypes = [c.POINTER(HeadGatherProblem), c.c_int32, c.c_void_p]
+    lib.ps_decode_head_gather_slab_bytes.restype = c.c_int64
+    lib.ps_decode_head_gather_slab_bytes.argtypes = [c.c_int32, c.c_int32]
+    lib.ps_paged_decode_head_gather.restype = c.c_int
+    lib.ps_paged_decode_head_gather.argtypes = [c.POINTER(PagedProblem), c.c_void_p, c.c_int64,
+                                                c.POINTER(HeadGatherProblem), c.c_void_p]
     lib.ps_dcp_decode_phase.restype = c.c_int
     lib.ps_dcp_decode_phase.argtypes = [c.POINTER(DcpProblem), c.c_int32, c.c_void_p, c.c_int64,
                                         c.c_void_p]

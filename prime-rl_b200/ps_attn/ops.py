@@ -384,7 +384,8 @@ def paged_decode(q: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Te
                  new_key: torch.Tensor | None = None, new_value: torch.Tensor | None = None,
                  slot_mapping: torch.Tensor | None = None,
                  cascade: CascadePlan | None = None, k_scale: torch.Tensor | None = None,
-                 v_scale: torch.Tensor | None = None, out_address: int | None = None) -> torch.Tensor:
+                 v_scale: torch.Tensor | None = None, out_address: int | None = None,
+                 head_gather: "_lib.HeadGatherProblem | None" = None) -> torch.Tensor:
     """Decode attention, one query row per sequence, written into ``out``.
 
     q/out: [T, Hq, D]; caches [num_blocks, block_size, Hkv, D]; block_table
@@ -408,6 +409,12 @@ def paged_decode(q: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Te
     contiguous [T, Hq, D] in ``out``'s dtype (``out`` then only supplies the
     dtype and shape) -- a peer-memory slab for :mod:`ps_attn.sharding`'s
     NVLink head gather.
+
+    ``head_gather``: a filled ``ps_head_gather_problem`` -- this call is then
+    one rank's part of a KV-head-sharded group and runs
+    ``ps_paged_decode_head_gather`` (the group's rows land in
+    ``head_gather.out`` on every rank; ``out`` only supplies shape and dtype).
+    Used by :class:`ps_attn.sharding.FusedHeadGather`.
     """
     lib = _lib.load()
     B = seq_lens.shape[0]
@@ -445,7 +452,13 @@ def paged_decode(q: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Te
         pr.new_value = new_value.data_ptr()
         pr.new_value_stride_token, pr.new_value_stride_head = new_value.stride(0), new_value.stride(1)
         pr.slot_mapping = slot_mapping.data_ptr()
-    if cascade is not None:
+    if head_gather is not None:
+        if cascade is not None or out_address is not None:
+            raise ValueError("the fused head gather runs the plain decode into its own output")
+        _lib.check(lib.ps_paged_decode_head_gather(ctypes.byref(pr), workspace.buffer.data_ptr(),
+                                                   workspace.nbytes, ctypes.byref(head_gather),
+                                                   _stream_ptr(q.device)))
+    elif cascade is not None:
         _lib.check(lib.ps_paged_decode_cascade(ctypes.byref(pr), cascade.buffer.data_ptr(),
                                                cascade.nbytes, workspace.buffer.data_ptr(),
                                                workspace.nbytes, _stream_ptr(q.device)))

@@ -206,6 +206,59 @@ class PeerHeadGather:
         self.slabs.close()
 
 
+class FusedHeadGather(PeerHeadGather):
+    """KV-head-sharded decode with the head all-gather fused into the decode
+    launch (``ps_paged_decode_head_gather``): the decode stores every output
+    row into each peer's slab over NVLink as it finishes the row, so the
+    exchange overlaps the rest of the decode, and the launch ends with the
+    group's ``[T, Hq, D]`` output in ``out`` on every rank -- no separate
+    gather launch.  Slabs hold the group's rows ``[max_tokens, Hq, D]``.
+
+    Every rank's launch waits for the others', so the ranks must be separate
+    GPUs (one process per GPU, :meth:`from_process_group`); there is no
+    one-GPU emulation of a whole group.
+    """
+
+    @staticmethod
+    def slab_bytes(max_tokens: int, num_q_heads: int) -> int:
+        from . import _lib
+
+        n = _lib.load().ps_decode_head_gather_slab_bytes(max_tokens, num_q_heads)
+        if n < 0:
+            _lib.check(_lib.PS_ERR_INVALID_ARGUMENT)
+        return int(n)
+
+    @classmethod
+    def from_process_group(cls, shard: HeadShard, max_tokens: int, dtype, group=None, device=None):
+        from .peer import PeerSlabs
+
+        slabs = PeerSlabs.from_process_group(cls.slab_bytes(max_tokens, shard.num_q_heads), group, device)
+        status = torch.zeros(1, dtype=torch.int32, device=slabs.device)
+        return cls(shard, max_tokens, dtype, slabs, status)
+
+    @classmethod
+    def emulated(cls, *args, **kwargs):
+        raise NotImplementedError("the fused gather's ranks wait on one another: one GPU per rank")
+
+    def decode(self, q_local, key_cache, value_cache, block_table, seq_lens, softmax_scale,
+               out: torch.Tensor, **kw) -> torch.Tensor:
+        """This rank's decode and the exchange: ``out[:T]`` ([>= T, Hq, D])
+        holds every rank's heads when the launch completes (same call on
+        every rank)."""
+        from . import ops
+
+        T = q_local.shape[0]
+        if T > self.max_tokens:
+            raise ValueError(f"{T} tokens > the slabs' {self.max_tokens}")
+        hp = self._problem(T, out)
+        ops.paged_decode(q_local, key_cache, value_cache, block_table, seq_lens, softmax_scale,
+                         out[:T, :self.shard.q_per_rank], head_gather=hp, **kw)
+        return out
+
+    def gather(self, num_tokens: int, out: torch.Tensor) -> torch.Tensor:
+        raise RuntimeError("the fused head gather has no separate gather step: decode() does it")
+
+
 def gather_group(gathers: list, num_tokens: int, outs: list) -> None:
     """The head gather of an emulated group (:meth:`PeerHeadGather.emulated`):
     phase k for every rank before phase k+1 for any."""

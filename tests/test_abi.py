@@ -170,3 +170,34 @@ def test_head_gather_struct_and_validation():
     hp.dtype, hp.num_tokens = _lib.PS_DTYPE_BF16, 9  # more rows than the slabs hold
     assert lib.ps_head_gather(ctypes.byref(hp), None) == _lib.PS_ERR_INVALID_ARGUMENT
     assert lib.ps_head_gather_phase(ctypes.byref(hp), 3, None) == _lib.PS_ERR_INVALID_ARGUMENT
+
+
+def test_fused_decode_head_gather_validation():
+    """ps_paged_decode_head_gather: slab size and host-side refusals (no
+    kernel launched)."""
+    lib = _lib.load()
+    # the group's rows [max_tokens, num_q_heads, 128] after the 256-byte header
+    assert lib.ps_decode_head_gather_slab_bytes(512, 64) == 256 + 512 * 64 * 256
+    assert lib.ps_decode_head_gather_slab_bytes(0, 64) == -1
+    assert lib.ps_paged_decode_head_gather(None, None, 0, None, None) == _lib.PS_ERR_INVALID_ARGUMENT
+    hp = _lib.HeadGatherProblem()
+    hp.world, hp.rank, hp.num_tokens, hp.hq_local, hp.max_tokens = 2, 1, 4, 8, 8
+    hp.dtype = _lib.PS_DTYPE_BF16
+    hp.slabs[0], hp.slabs[1] = 256, 512
+    hp.out, hp.out_stride_token, hp.out_stride_head = 1024, 16 * 128, 128
+    hp.status = 4096
+    pr = _lib.PagedProblem()
+    assert lib.ps_paged_decode_head_gather(None, None, 0, ctypes.byref(hp), None) == _lib.PS_ERR_INVALID_ARGUMENT
+    pr.num_q_heads, pr.num_kv_heads, pr.dtype, pr.num_seqs = 16, 2, _lib.PS_DTYPE_BF16, 4
+    rc = lib.ps_paged_decode_head_gather(ctypes.byref(pr), None, 0, ctypes.byref(hp), None)
+    assert rc == _lib.PS_ERR_INVALID_ARGUMENT and b"hq_local" in lib.ps_last_error()
+    pr.num_q_heads = 8
+    pr.dtype = _lib.PS_DTYPE_FP16
+    rc = lib.ps_paged_decode_head_gather(ctypes.byref(pr), None, 0, ctypes.byref(hp), None)
+    assert rc == _lib.PS_ERR_INVALID_ARGUMENT and b"dtype" in lib.ps_last_error()
+    pr.dtype, pr.num_seqs = _lib.PS_DTYPE_BF16, 5  # more sequences than the gather's rows
+    rc = lib.ps_paged_decode_head_gather(ctypes.byref(pr), None, 0, ctypes.byref(hp), None)
+    assert rc == _lib.PS_ERR_INVALID_ARGUMENT
+    pr.num_seqs = 0  # every rank must skip an empty step rather than launch
+    rc = lib.ps_paged_decode_head_gather(ctypes.byref(pr), None, 0, ctypes.byref(hp), None)
+    assert rc == _lib.PS_ERR_INVALID_ARGUMENT and b"empty" in lib.ps_last_error()

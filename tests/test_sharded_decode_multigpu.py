@@ -95,7 +95,7 @@ def test_kv_head_sharded_decode_equals_single_gpu():
     assert_attn_close(to_np32(got), to_np32(ref))
 
 
-def _peer_rank(rank, world, port, q):
+def _peer_rank(rank, world, port, q, fused=False):
     import datetime
     import sys
     from pathlib import Path
@@ -115,18 +115,23 @@ def _peer_rank(rank, world, port, q):
         full = workloads.make_config(5, device="cpu", max_seqs=24)
         shard = sharding.HeadShard(world, rank, 64, 8)
         T = full.q.shape[0]
-        gth = sharding.PeerHeadGather.from_process_group(shard, T, torch.bfloat16, device=dev)
+        cls = sharding.FusedHeadGather if fused else sharding.PeerHeadGather
+        gth = cls.from_process_group(shard, T, torch.bfloat16, device=dev)
         kv = shard.shard_cache(full.kv_cache).to(dev)
         qd = shard.shard_q(full.q).contiguous().to(dev)
         kd = shard.shard_kv_rows(full.key).contiguous().to(dev)
         vd = shard.shard_kv_rows(full.value).contiguous().to(dev)
         bt, sl, slots = full.block_table.to(dev), full.seq_lens.to(dev), full.slot_mapping.to(dev)
-        ops.kv_append(kd, vd, kv[0], kv[1], slots)
+        # fused: the append rides in the decode launch (the same rows every call)
+        fkw = dict(new_key=kd, new_value=vd, slot_mapping=slots) if fused else {}
+        if not fused:
+            ops.kv_append(kd, vd, kv[0], kv[1], slots)
         outs = []
         for _ in range(3):  # the same slabs, consecutive calls
             out = torch.full((T, 64, 128), float("nan"), dtype=torch.bfloat16, device=dev)
-            gth.decode(qd, kv[0], kv[1], bt, sl, full.softmax_scale, out)
-            gth.gather(T, out)
+            gth.decode(qd, kv[0], kv[1], bt, sl, full.softmax_scale, out, **fkw)
+            if not fused:
+                gth.gather(T, out)
             outs.append(out)
         torch.cuda.synchronize()
         assert int(gth.status.item()) == 0
@@ -143,10 +148,14 @@ def _peer_rank(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_kv_head_sharded_decode_with_peer_head_gather():
+@pytest.mark.parametrize("fused", [False, True], ids=["pull_launch", "fused_into_decode"])
+def test_kv_head_sharded_decode_with_peer_head_gather(fused):
     """The same sharded decode with the head outputs exchanged over NVLink
-    peer memory (ps_head_gather) instead of NCCL: every rank holds the whole
-    output, equal to the single-GPU decode."""
+    peer memory instead of NCCL -- pulled by a separate launch
+    (ps_head_gather), or stored into the peers by the decode launch itself
+    (ps_paged_decode_head_gather, with the append fused too): every rank
+    holds the whole output, equal to the single-GPU decode, three calls in a
+    row over the same slabs."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     import torch.multiprocessing as mp
@@ -157,7 +166,7 @@ def test_kv_head_sharded_decode_with_peer_head_gather():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_peer_rank, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_peer_rank, args=(r, world, port, q, fused)) for r in range(world)]
     for p in procs:
         p.start()
     got = dict(q.get(timeout=300) for _ in range(world))
