@@ -604,6 +604,32 @@ def check_gathered(arm: Arm, nseq: int = 4) -> dict:
             "reference": "torch fp32 attention over the gathered pages, every rank's heads all-gathered"}
 
 
+def time_local_decode(arm: Arm, n: int = 20) -> float:
+    """KV-head-sharded runs with the gather fused in: this rank's decode alone
+    (the plain kernel over the same shard and inputs, into a scratch output),
+    ``n`` launches back to back with CUDA events at the ends; max over ranks.
+    The fused step minus this is what the exchange costs."""
+    from ps_attn import ops
+
+    b, scale = arm.batch, arm.batch.softmax_scale
+    scratch = torch.empty(arm.B, arm.hq, 128, dtype=b.q.dtype, device=arm.dev)
+    kw = dict(query_start_loc=b.query_start_loc, workspace=arm.ws, **arm.skw)
+
+    def run():
+        ops.paged_decode(b.q, arm.kc, arm.vc, b.block_table, b.seq_lens, scale, scratch, **kw)
+
+    with torch.cuda.stream(arm.stream):
+        for _ in range(3):
+            run()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(arm.stream)
+        for _ in range(n):
+            run()
+        e1.record(arm.stream)
+    e1.synchronize()
+    return _all_max(e0.elapsed_time(e1) / n, arm.world, arm.dev)
+
+
 # ----------------------------------------------------------------------------
 # end to end through the public ops
 # ----------------------------------------------------------------------------
@@ -733,6 +759,7 @@ def run_ours(args):
     ms = t["ms"]
     pm = t["phase_ms"]
     check = check_gathered(arm) if arm.sharded else None
+    alone_ms = time_local_decode(arm) if arm.sharded and arm.gather_kind == "fused" else None
     e2e = None if args.quick else run_e2e(arm, args.steps)
 
     tokens = arm.batch.num_tokens  # every rank produces all tokens (its heads when sharded)
@@ -775,10 +802,13 @@ def run_ours(args):
     if arm.sharded:
         rx = (world - 1) * arm.B * arm.hq * 128 * arm.batch.q.element_size()
         if arm.gather_kind == "fused":
+            extra = ms - alone_ms
             res["gather"] = {"kind": "fused into the decode launch (ps_paged_decode_head_gather)",
-                             "ms_per_step": None, "bytes_received_per_gpu": rx,
+                             "ms_per_step": round(extra, 5), "share_of_step": round(extra / ms, 4),
+                             "decode_alone_ms": round(alone_ms, 5), "bytes_received_per_gpu": rx,
                              "note": "rows stored into the peers over NVLink as the decode finishes them; "
-                                     "the decode phase includes the closing barrier and the local copy"}
+                                     "ms_per_step = the fused step minus this rank's decode alone (the plain "
+                                     "kernel on the same shard, timed back to back after the run, max over ranks)"}
         else:
             res["gather"] = {"kind": arm.gather_kind, "ms_per_step": round(pm["gather"], 5),
                              "share_of_step": round(pm["gather"] / ms, 4), "bytes_received_per_gpu": rx}
